@@ -1,0 +1,330 @@
+"""Three-layer GAT forward throughput on B200 (the reference's headline metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: config c4 (products-shaped seeded power-law graph, 2,449,029 nodes,
+126,167,053 edges incl. self loops, 100 -> 8x32 -> 8x32 -> 1x47, BF16 with FP32
+softmax state). One step = one full three-layer forward. Metric: GEdges/s =
+3*E / t_forward (every layer traverses all E edges); ms_per_step is the
+forward time. Prints ONE JSON line (rank 0).
+
+  value    device-resident inputs, CUDA events on the launch stream, max over ranks
+  e2e      the same forward through the C-ABI model call with pinned HOST input
+           (FP32 X) and HOST logits: H2D + forward + D2H inside the timed region
+  roofline the aggregation kernel (the dominant one): algorithmic bytes per
+           launch / its CUDA-event duration inside the timed region vs the
+           measured HBM copy bandwidth
+  cpu_baseline  the reference's own B0 BF16 path (oracle/_ref/gat_baseline,
+           built from the reference sources) on this host's cores, bounded sample
+
+--impl reference times that reference CPU implementation alone on the same
+workload and prints its line (rank 0 only under torchrun).
+
+Multi-GPU: destination rows are partitioned by edge count; every layer's
+projected features are exchanged with one NCCL all-gather.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "gat-tfs_b200"))
+
+TMP = Path(os.environ.get("GAT_B200_TMP", "/tmp"))
+REF_BIN = ROOT / "oracle" / "_ref" / "gat_baseline"
+CONFIG = "c4"
+METRIC = "3-layer GAT fwd GEdges/s (2.45M nodes/126M edges, BF16)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", default=CONFIG, choices=["c1", "c2", "c4"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# --------------------------------------------------------------------- clocks
+class Clocks:
+    """nvidia-smi samples (every 200 ms) while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.device)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=5)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------- reference (CPU)
+def write_reference_inputs(cfg) -> tuple[Path, Path]:
+    import gatb200 as G
+    g = TMP / f"gat_b200_{cfg.name}.gatbin"
+    w = TMP / f"gat_b200_{cfg.name}.gatwgt"
+    want = 32 + 8 * (cfg.graph.n + 1) + 4 * cfg.graph.e + 4 * cfg.graph.n * cfg.graph.din
+    if not g.exists() or g.stat().st_size != want:
+        G.save_graph(cfg.graph, g)
+    G.save_model(cfg.model, w)
+    return g, w
+
+
+def physical_cores() -> int:
+    try:
+        out = subprocess.run(["lscpu", "-p=CORE,SOCKET"], capture_output=True, text=True, timeout=10).stdout
+        cores = {l for l in out.splitlines() if l and not l.startswith("#")}
+        return max(1, len(cores))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def run_reference(cfg, warmups: int, repeats: int, timeout_s: int = 900) -> dict:
+    """The reference's B0 BF16 path (baseline/bench/main.cpp benchmark mode)."""
+    if not REF_BIN.exists():
+        return {"unavailable": "oracle/_ref/gat_baseline was not built (reference tree absent at build time)"}
+    g, w = write_reference_inputs(cfg)
+    threads = physical_cores()
+    env = dict(os.environ, OMP_NUM_THREADS=str(threads), OMP_PROC_BIND="close", OMP_PLACES="cores")
+    cmd = [str(REF_BIN), "--graph", str(g), "--weights", str(w), "--path", "standard_bf16", "--mode", "benchmark",
+           "--threads", str(threads), "--warmups", str(warmups), "--repeats", str(repeats)]
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=timeout_s)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": f"reference B0 run exceeded {timeout_s} s"}
+    if r.returncode != 0:
+        return {"unavailable": f"reference B0 exited {r.returncode}: {(r.stderr or r.stdout).strip()[-200:]}"}
+    totals = [float(m) for m in re.findall(r"^E2E path=\S+ rep=\d+ layer=0 total_ms=([0-9.eE+-]+)", r.stdout, re.M)]
+    if not totals:
+        return {"unavailable": "no E2E lines in reference output"}
+    med = statistics.median(totals)
+    return {"median_ms": med, "totals_ms": totals, "threads": threads}
+
+
+# ------------------------------------------------------------------ our arm
+def agg_bytes(n, e, heads, dim, out_bytes_per_elem):
+    """Algorithmic bytes of one aggregation launch: rowptr, col, L of the row,
+    R of every edge's source, H row of every edge's source (BF16), the output."""
+    return 8 * (n + 1) + 4 * e + 4 * n * heads + 4 * e * heads + 2 * e * heads * dim + out_bytes_per_elem * n * heads * dim
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    import configs
+
+    if args.impl == "reference":
+        # Rank 0 alone times the reference CPU implementation; the others exit.
+        if rank != 0:
+            return 0
+        cfg = configs.make(args.config)
+        w = max(1, min(args.warmup, 1))
+        k = max(1, min(args.steps, 5))
+        res = run_reference(cfg, w, k)
+        e3 = 3 * cfg.graph.e
+        if "unavailable" in res:
+            print(json.dumps({"impl": "reference", "unavailable": res["unavailable"]}))
+            return 0
+        v = e3 / (res["median_ms"] * 1e-3) / 1e9
+        sample = (f"full {args.config} forward per step, median of {len(res['totals_ms'])} timed forwards "
+                  f"after {w} warm-up (bounded)")
+        line = {"impl": "reference", "metric": METRIC, "value": round(v, 5), "unit": "GEdges/s", "n_gpus": 0,
+                "steps": len(res["totals_ms"]), "warmup": w, "ms_per_step": round(res["median_ms"], 3),
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic", "config": {"workload": args.config, "path": "reference B0 standard_bf16 (CPU)"},
+                "cpu_baseline": {"value": round(v, 5), "unit": "GEdges/s", "cores": res["threads"],
+                                 "kind": "reference", "sample": sample},
+                "e2e": {"value": round(v, 5), "unit": "GEdges/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return 0
+
+    import numpy as np
+    import torch
+    import gatb200 as G
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+
+    cfg = configs.make(args.config)
+    n, e = cfg.graph.n, cfg.graph.e
+    stream = torch.cuda.current_stream()
+    g = G.DeviceGraph(cfg.graph.row, cfg.graph.col, stream)
+    layers = [G.DeviceLayer(p) for p in cfg.model]
+    model = G.DeviceModel(g, layers, G.PATH_STANDARD_BF16)
+    x_dev = torch.from_numpy(cfg.graph.x).cuda()
+    logits = torch.empty((n, model.classes), dtype=torch.float32, device="cuda")
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    for _ in range(max(args.warmup, 3)):
+        model.forward(x_dev, logits, False, False, stream)
+    torch.cuda.synchronize()
+    G.check_device()
+
+    model.enable_timing(args.steps)
+    clocks = Clocks(local)
+    clocks.start()
+    barrier()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        model.forward(x_dev, logits, False, False, stream)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    G.check_device()
+    ms = t0.elapsed_time(t1) / args.steps
+    if dist is not None:
+        tt = torch.tensor([ms], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    stages = model.stage_times()  # [steps, 9]
+    launches = model.launches()
+    model.enable_timing(0)
+
+    # roofline of the aggregation kernel (three launches per step)
+    agg_ms = [float(stages[:, k].mean()) for k in (3, 5, 7)]
+    b = [agg_bytes(n, e, 8, 32, 2), agg_bytes(n, e, 8, 32, 2), agg_bytes(n, e, 1, cfg.model[2].dim, 4)]
+    achieved = sum(b) / (sum(agg_ms) * 1e-3) / 1e9
+    peak, peak_kind = peaks()
+    traffic = None
+    prof = ROOT / "profiles" / "aggregate_c4_traffic.json"
+    if prof.exists():
+        traffic = json.loads(prof.read_text()).get("bytes_per_launch_avg")
+
+    # e2e through the model call with pinned host buffers
+    x_host = torch.from_numpy(cfg.graph.x).pin_memory()
+    l_host = torch.empty((n, model.classes), dtype=torch.float32).pin_memory()
+    for _ in range(2):
+        model.forward(x_host, l_host, True, True, stream)
+    e_steps = max(1, min(args.steps, 5))
+    barrier()
+    torch.cuda.synchronize()
+    t0.record(stream)
+    for _ in range(e_steps):
+        model.forward(x_host, l_host, True, True, stream)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = t0.elapsed_time(t1) / e_steps
+    if dist is not None:
+        tt = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_ms = float(tt.item())
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res = run_reference(cfg, 1, 2)
+        if "unavailable" in res:
+            cpu = {"value": None, "unit": "GEdges/s", "cores": physical_cores(), "kind": "reference",
+                   "sample": res["unavailable"]}
+        else:
+            cpu = {"value": round(3 * e / (res["median_ms"] * 1e-3) / 1e9, 5), "unit": "GEdges/s",
+                   "cores": res["threads"], "kind": "reference",
+                   "sample": f"full {args.config} forward, median of {len(res['totals_ms'])} after 1 warm-up "
+                             f"(reference B0 standard_bf16, {res['median_ms']:.1f} ms)"}
+
+    if rank == 0:
+        value = 3 * e / (ms * 1e-3) / 1e9
+        line = {
+            "metric": METRIC, "value": round(value, 4), "unit": "GEdges/s", "n_gpus": world, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"{args.config}: products-shaped power-law graph, N={n}, E={e}, "
+                                   f"{cfg.graph.din}->8x32->8x32->1x{cfg.model[2].dim}",
+                       "nodes": n, "edges": e, "l2": "inputs larger than L2 (H is 1.25 GB per layer)",
+                       "parallelism": f"rows{world}" if world > 1 else "single"},
+            "stage_ms": {k: round(float(stages[:, i].mean()), 4) for i, k in enumerate(G.DeviceModel.STAGES)
+                         if k not in ("h2d", "d2h")},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
+                         "kernel": "edge-softmax aggregation (3 launches/step)",
+                         "algorithmic_bytes_per_launch": int(sum(b) / 3)},
+            "e2e": {"value": round(3 * e / (e2e_ms * 1e-3) / 1e9, 4), "unit": "GEdges/s",
+                    "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": n * cfg.graph.din * 4,
+                    "d2h_bytes_per_step": n * model.classes * 4},
+            "gpu_launches": launches * args.steps,
+            "clocks": clk,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line))
+    model.close()
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

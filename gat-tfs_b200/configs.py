@@ -1,0 +1,51 @@
+"""Seeded synthetic stand-ins for the benchmark configurations.
+
+The reference measures on ogbn-arxiv / ogbn-products GATBIN1 files that are not
+available here. These configurations reproduce their shapes (node and edge
+counts, degree tails, feature widths, classes) with seeded generators
+(gat_b200_synth_*), so every run builds bit-identical inputs.
+
+  c1  tiny: 1,024 nodes, 15 uniform distinct sources + self loop per row,
+      X ~ N(0,1) 1024x128, 128 -> 8x32 -> 8x32 -> 1x40, Glorot weights.
+  c2  arxiv-like: 169,343 nodes, 2,484,941 edges incl. self loops, power-law
+      degrees (gamma 2.1, max 13,162), X ~ N(0,1) x128, classes 40.
+  c3  layer-2 micro on the c2 graph: H ~ N(0,1) 169,343x256, a ~ U(-0.1,0.1),
+      W 256x256 Glorot.
+  c4  products-like: 2,449,029 nodes, 126,167,053 edges incl. self loops,
+      power-law degrees (gamma 2.1, max 17,482), X ~ N(0,1) x100, classes 47.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+
+import gatb200 as G
+
+SPECS = {
+    "c1": dict(kind="uniform", n=1024, sources=15, din=128, classes=40, seed=1),
+    "c2": dict(kind="powerlaw", n=169_343, e=2_484_941, max_degree=13_162, gamma=2.1, din=128, classes=40, seed=2),
+    "c4": dict(kind="powerlaw", n=2_449_029, e=126_167_053, max_degree=17_482, gamma=2.1, din=100, classes=47, seed=4),
+}
+
+
+@dataclass
+class Config:
+    name: str
+    graph: G.Graph
+    model: list
+
+
+def make_graph(name: str, features: bool = True) -> G.Graph:
+    s = SPECS[name]
+    if s["kind"] == "uniform":
+        row, col = G.synth_uniform_graph(s["n"], s["sources"], s["seed"])
+    else:
+        row, col = G.synth_powerlaw_graph(s["n"], s["e"], s["max_degree"], s["gamma"], s["seed"])
+    x = G.synth_normal((s["n"], s["din"]), s["seed"], 1) if features else np.zeros((0, s["din"]), np.float32)
+    return G.Graph(s["n"], len(col), s["din"], s["classes"], row, col, x)
+
+
+def make(name: str, features: bool = True) -> Config:
+    s = SPECS[name]
+    return Config(name, make_graph(name, features), G.glorot_model(s["din"], s["classes"], s["seed"]))

@@ -1,0 +1,33 @@
+// Internal declarations shared by the host (.cpp) and device (.cu) sources of
+// libgat_b200.so. Not part of the C-ABI (that is include/gat_b200.h).
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <string>
+
+#include "../../include/gat_b200.h"
+
+namespace gatb {
+
+// Thread-local last error (gat_b200_last_error). fail() records the message and
+// returns GAT_B200_EINVAL; fail_code() lets the caller choose the status.
+int fail(const std::string& msg);
+int fail_code(int code, const std::string& msg);
+void clear_error();
+
+// Row stride (in elements) used for every device feature buffer of `width`
+// columns: rows start on 16-byte boundaries (TMA and 128-bit gathers need it)
+// and the padding columns are kept at zero.
+inline int padded_ld(int width, int elem_bytes) {
+    int per16 = 16 / elem_bytes;
+    return (width + per16 - 1) / per16 * per16;
+}
+
+// Synthetic inputs (synth.cpp).
+int synth_uniform_graph(uint64_t n, uint32_t sources, uint64_t seed, uint64_t* row, uint32_t* col);
+int synth_powerlaw_graph(uint64_t n, uint64_t e_target, uint64_t max_degree, double gamma,
+                         uint64_t seed, uint64_t* row, uint32_t* col);
+int synth_normal(uint64_t count, double scale, uint64_t seed, uint64_t stream, float* out);
+int synth_uniform(uint64_t count, double lo, double hi, uint64_t seed, uint64_t stream, float* out);
+
+}  // namespace gatb

@@ -1,0 +1,495 @@
+// Tensor-core projection with fused attention dots (sm_100a tcgen05 + TMA).
+//
+// Replaces gat::projection + gat::lr_from_z of the B0 BF16 path
+// (baseline/src/baseline_standard.cpp:3-20):
+//   Z = BF16(X) . BF16(W)  (FP32 accumulate)
+//   left[i][h] = Z_ih . aL_h,  right[i][h] = Z_ih . aR_h   (from the FP32 Z)
+//   H = BF16 RNE(Z)        (the gathered feature rows of the aggregation)
+//
+// Persistent kernel, one CTA per SM, 6 warps with fixed roles:
+//   warp 0  TMA producer: W^T once (resident in shared memory for the whole
+//           kernel), then 128-row x 64-column tiles of X through an S-stage ring.
+//   warp 1  TMEM owner and MMA issuer: 128 x NP x 16 tcgen05.mma (kind::f16,
+//           BF16 x BF16 -> FP32) into one of two TMEM accumulators, so the
+//           epilogue of tile t overlaps the MMAs of tile t+1.
+//   warps 2-5 epilogue: tcgen05.ld 16 columns at a time (thread = row),
+//           L/R dot products in FP32, BF16 pack into a 128B-swizzled staging
+//           buffer, TMA store of 32 x 64 boxes.
+// No cluster launch, no multicast: every CTA loads its own tiles.
+//
+// Every mbarrier wait is bounded: after ~1 s without progress the CTA records
+// GAT_B200_ETIMEOUT in a device flag, waits (bounded) for its own copies and
+// MMAs in flight, frees its TMEM and exits.
+#include <cuda.h>
+
+#include "device.cuh"
+#include "graph.cuh"
+
+namespace gatb {
+
+__device__ unsigned g_proj_error = 0;
+
+namespace {
+
+constexpr int kTileM = 128;
+constexpr int kKBlock = 64;                       // BF16 elements per 128-byte swizzle row
+constexpr int kABytes = kTileM * kKBlock * 2;     // 16 KB per A stage
+constexpr int kStageRows = 32;                    // epilogue store box rows (one warp)
+constexpr int kStageBytes = kStageRows * 128;     // 4 KB
+constexpr int kThreads = 192;
+
+struct ProjArgs {
+    uint64_t n;
+    int heads, dim, width, np, kb;
+    int stages;
+    uint32_t tmem_cols;  // two accumulators, tmem_cols/2 columns apart
+    float* left;
+    float* right;
+    float* z;       // optional FP32 Z [n][ldz]
+    int ldz;
+    int lr_vec;     // left/right allow float4 stores (heads == 8, aligned)
+    int store_h;    // 1: BF16 H through TMA stores (0: only z / left / right)
+    const float* al;
+    const float* ar;
+};
+
+// ---- PTX wrappers ----------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait. Returns false (and raises the CTA's abort flag) on timeout or
+// when another role of this CTA has already aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+    if (mbar_try(bar, parity)) return true;
+    const long long start = clock64();
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_try(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if ((it & 63) == 63) {
+            __nanosleep(128);
+            if (clock64() - start > (1ll << 31)) {  // ~1 s at the B200 clock
+                *abort_flag = 1;
+                atomicOr(&g_proj_error, 1u);
+                return false;
+            }
+        }
+    }
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+                 ::"l"(map), "r"(smem_u32(src)), "r"(x), "r"(y)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// K-major operand in the 128-byte swizzle layout: rows of 128 bytes, 8-row
+// groups 1024 bytes apart (SBO = 1024), descriptor version 1 (sm_100).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= uint64_t((saddr >> 4) & 0x3fff);
+    d |= uint64_t(1) << 16;               // LBO (unused for swizzled K-major)
+    d |= uint64_t(1024 >> 4) << 32;       // SBO
+    d |= uint64_t(1) << 46;               // version
+    d |= uint64_t(2) << 61;               // SWIZZLE_128B
+    return d;
+}
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+    uint32_t r[16];
+    // Load and wait in one asm statement: the registers are defined only after
+    // the wait, so no use of them can be scheduled before it.
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <bool ALIGNED16>
+__global__ void __launch_bounds__(kThreads, 1)
+    proj_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                   const __grid_constant__ CUtensorMap tm_h, const ProjArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // 1024-byte alignment for the swizzled tiles.
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int S = a.stages, NP = a.np, KB = a.kb;
+    uint8_t* w_s = smem;                                         // KB x [NP x 128 B]
+    uint8_t* a_s = w_s + size_t(KB) * NP * 128;                   // S x 16 KB
+    uint8_t* st_s = a_s + size_t(S) * kABytes;                    // 4 warps x 2 x 4 KB
+    float* al_s = reinterpret_cast<float*>(st_s + 8 * kStageBytes);  // [NP]
+    float* ar_s = al_s + NP;                                      // [NP]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(ar_s + NP);
+    uint64_t* full = bars;              // [S]
+    uint64_t* empty = bars + S;         // [S]
+    uint64_t* w_full = bars + 2 * S;    // 1
+    uint64_t* acc_full = w_full + 1;    // [2]
+    uint64_t* acc_empty = acc_full + 2; // [2]
+    uint64_t* mma_done = acc_empty + 2; // 1
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint64_t ntiles = (a.n + kTileM - 1) / kTileM;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, 1);
+        }
+        mbar_init(w_full, 1);
+        mbar_init(acc_full + 0, 1);
+        mbar_init(acc_full + 1, 1);
+        mbar_init(acc_empty + 0, 4);
+        mbar_init(acc_empty + 1, 4);
+        mbar_init(mma_done, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    for (int c = threadIdx.x; c < NP; c += kThreads) {
+        al_s[c] = c < a.width ? a.al[c] : 0.f;
+        ar_s[c] = c < a.width ? a.ar[c] : 0.f;
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                     "r"(a.tmem_cols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---- TMA producer ----
+            mbar_expect_tx(w_full, uint32_t(KB) * NP * 128);
+            for (int k = 0; k < KB; ++k) tma_load_2d(w_s + size_t(k) * NP * 128, &tm_w, w_full, k * kKBlock, 0);
+            uint64_t kc = 0;
+            bool ok = true;
+            for (uint64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                for (int k = 0; k < KB; ++k, ++kc) {
+                    const int s = int(kc % S);
+                    const uint32_t ph = uint32_t(kc / S) & 1u;
+                    if (!mbar_wait(empty + s, ph ^ 1u, abort_flag)) { ok = false; break; }
+                    mbar_expect_tx(full + s, kABytes);
+                    tma_load_2d(a_s + size_t(s) * kABytes, &tm_x, full + s, k * kKBlock, int(t * kTileM));
+                }
+            }
+            // Wait (bounded) until every load this thread issued has landed.
+            mbar_wait(w_full, 0, abort_flag);
+            for (int s = 0; s < S; ++s) {
+                if (kc > uint64_t(s)) {
+                    uint64_t last = kc - 1 - ((kc - 1 - s) % S);  // last k-block index that used stage s
+                    mbar_wait(full + s, uint32_t(last / S) & 1u, abort_flag);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---- MMA issuer ----
+            const uint32_t idesc = (1u << 4)            // D = F32
+                                   | (1u << 7)          // A = BF16
+                                   | (1u << 10)         // B = BF16
+                                   | (uint32_t(NP >> 3) << 17)  // N
+                                   | (uint32_t(kTileM >> 4) << 24);  // M
+            bool ok = mbar_wait(w_full, 0, abort_flag);
+            tc_fence_after();
+            uint64_t kc = 0;
+            uint32_t t_local = 0;
+            for (uint64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++t_local) {
+                const uint32_t buf = t_local & 1u, use = t_local >> 1;
+                if (!mbar_wait(acc_empty + buf, (use & 1u) ^ 1u, abort_flag)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + buf * (a.tmem_cols / 2);
+                for (int k = 0; k < KB; ++k, ++kc) {
+                    const int s = int(kc % S);
+                    if (!mbar_wait(full + s, uint32_t(kc / S) & 1u, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(a_s + size_t(s) * kABytes);
+                    const uint32_t b_addr = smem_u32(w_s + size_t(k) * NP * 128);
+#pragma unroll
+                    for (int kk = 0; kk < kKBlock / 16; ++kk)
+                        mma_bf16(d_tmem, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), idesc,
+                                 (k | kk) ? 1u : 0u);
+                    mma_commit(empty + s);
+                }
+                if (!ok) break;
+                mma_commit(acc_full + buf);
+            }
+            // All MMAs issued so far complete before this barrier fires.
+            mma_commit(mma_done);
+            mbar_wait(mma_done, 0, abort_flag);
+        }
+    } else {
+        // ---- epilogue: warps 2..5, TMEM lane quarter = warp % 4 ----
+        const int q = warp & 3;
+        const int ew = warp - 2;  // staging slot
+        uint8_t* stage0 = st_s + size_t(ew) * 2 * kStageBytes;
+        uint32_t toggle = 0;
+        uint32_t t_local = 0;
+        for (uint64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++t_local) {
+            const uint32_t buf = t_local & 1u, use = t_local >> 1;
+            if (!mbar_wait(acc_full + buf, use & 1u, abort_flag)) break;
+            tc_fence_after();
+            const uint64_t row = t * kTileM + uint64_t(q) * 32 + lane;
+            const uint32_t taddr = tmem_base + (uint32_t(q * 32) << 16) + buf * (a.tmem_cols / 2);
+            float L[8], R[8];
+#pragma unroll
+            for (int h = 0; h < 8; ++h) { L[h] = 0.f; R[h] = 0.f; }
+            for (int g = 0; g < NP; g += 64) {
+                uint8_t* sb = stage0 + toggle * kStageBytes;
+                if (lane == 0 && a.store_h) bulk_wait_read<1>();
+                __syncwarp();
+                for (int cc = 0; cc < 4 && g + cc * 16 < NP; ++cc) {
+                    const int c = g + cc * 16;
+                    float v[16];
+                    tmem_ld16(taddr + uint32_t(c), v);
+                    if constexpr (ALIGNED16) {
+                        float pl = 0.f, pr = 0.f;
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            pl = fmaf(v[j], al_s[c + j], pl);
+                            pr = fmaf(v[j], ar_s[c + j], pr);
+                        }
+                        const int hh = c / a.dim;
+#pragma unroll
+                        for (int h = 0; h < 8; ++h)
+                            if (h == hh) { L[h] += pl; R[h] += pr; }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const int hh = (c + j) / a.dim;
+                            const float xl = v[j] * al_s[c + j], xr = v[j] * ar_s[c + j];
+#pragma unroll
+                            for (int h = 0; h < 8; ++h)
+                                if (h == hh) { L[h] += xl; R[h] += xr; }
+                        }
+                    }
+                    if (a.z && row < a.n) {
+                        float* zr = a.z + row * uint64_t(a.ldz) + c;
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            if (c + j < a.width) zr[j] = v[j];
+                    }
+                    if (!a.store_h) continue;
+                    uint32_t pk[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) pk[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+                    // 16-byte chunks 2cc and 2cc+1 of this row, 128B swizzle.
+                    const int c0 = (2 * cc) ^ (lane & 7), c1 = (2 * cc + 1) ^ (lane & 7);
+                    *reinterpret_cast<uint4*>(sb + lane * 128 + c0 * 16) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                    *reinterpret_cast<uint4*>(sb + lane * 128 + c1 * 16) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                }
+                if (!a.store_h) continue;
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(&tm_h, sb, g, int(t * kTileM) + q * 32);
+                    bulk_commit();
+                }
+                toggle ^= 1u;
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty + buf);
+            if (row < a.n) {
+                if (a.lr_vec) {
+                    float4* lp = reinterpret_cast<float4*>(a.left + row * 8);
+                    float4* rp = reinterpret_cast<float4*>(a.right + row * 8);
+                    if (a.left) { lp[0] = make_float4(L[0], L[1], L[2], L[3]); lp[1] = make_float4(L[4], L[5], L[6], L[7]); }
+                    if (a.right) { rp[0] = make_float4(R[0], R[1], R[2], R[3]); rp[1] = make_float4(R[4], R[5], R[6], R[7]); }
+                } else {
+#pragma unroll
+                    for (int h = 0; h < 8; ++h)
+                        if (h < a.heads) {
+                            if (a.left) a.left[row * a.heads + h] = L[h];
+                            if (a.right) a.right[row * a.heads + h] = R[h];
+                        }
+                }
+            }
+        }
+        if (lane == 0) bulk_wait_all();
+        __syncwarp();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(a.tmem_cols));
+    }
+}
+
+// ---- host side -------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// 2-D BF16 tensor map: inner extent `cols`, `rows` rows, row pitch `ld` elements.
+int make_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint64_t ld, uint32_t box_cols,
+             uint32_t box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail_code(GAT_B200_ECUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {ld * 2};
+    cuuint32_t box[2] = {box_cols, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail_code(GAT_B200_ECUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+    return 0;
+}
+
+}  // namespace
+
+// Returns GAT_B200_EUNSUPPORTED when the shape is outside the kernel (the
+// caller then uses the CUDA-core projection).
+int projection_tc_launch(const gat_b200_layer* p, uint64_t n, const uint16_t* x, int ldx, uint16_t* h, int ldh,
+                         float* z, int ldz, float* left, float* right, cudaStream_t st) {
+    if (p->np > 256 || p->kp > 256) return GAT_B200_EUNSUPPORTED;
+    if (n == 0) return 0;
+    if (n > uint64_t(INT32_MAX)) return fail("projection: too many rows");
+    if ((reinterpret_cast<uintptr_t>(x) & 15) || (uint64_t(ldx) * 2) % 16) return fail("projection: X rows must be 16-byte aligned");
+    if (h && ((reinterpret_cast<uintptr_t>(h) & 15) || (uint64_t(ldh) * 2) % 16 || ldh < p->width))
+        return fail("projection: H rows must be 16-byte aligned and hold the width");
+    if (z && ldz < p->width) return fail("projection: Z row stride smaller than the width");
+    ProjArgs a{};
+    a.n = n;
+    a.heads = p->heads;
+    a.dim = p->dim;
+    a.width = p->width;
+    a.np = p->np;
+    a.kb = p->kp / kKBlock;
+    a.left = left;
+    a.right = right;
+    a.z = z;
+    a.ldz = ldz;
+    a.al = p->al;
+    a.ar = p->ar;
+    a.store_h = h != nullptr;
+    a.lr_vec = p->heads == 8 && (reinterpret_cast<uintptr_t>(left) & 15) == 0 &&
+               (reinterpret_cast<uintptr_t>(right) & 15) == 0;
+    uint32_t cols = 32;
+    while (cols < uint32_t(2 * p->np)) cols <<= 1;
+    a.tmem_cols = cols;
+    const size_t fixed = size_t(a.kb) * p->np * 128 + 8 * kStageBytes + 2 * size_t(p->np) * 4 + 512 + 1024;
+    const size_t limit = 227 * 1024;
+    int S = int((limit - fixed) / kABytes);
+    S = S > 8 ? 8 : S;
+    if (S < 2) return GAT_B200_EUNSUPPORTED;
+    a.stages = S;
+    size_t smem = fixed + size_t(S) * kABytes;
+    // 512 TMEM columns are only safe with one CTA per SM: make the shared
+    // memory request rule out a second resident CTA.
+    if (cols > 256 && smem < 120 * 1024) smem = 120 * 1024;
+
+    CUtensorMap tm_x, tm_w, tm_h;
+    int rc;
+    if ((rc = make_map(&tm_x, x, uint64_t(p->in), n, uint64_t(ldx), kKBlock, kTileM))) return rc;
+    if ((rc = make_map(&tm_w, p->wt_bf16, uint64_t(p->kp), uint64_t(p->np), uint64_t(p->kp), kKBlock, uint32_t(p->np)))) return rc;
+    if (h) {
+        if ((rc = make_map(&tm_h, h, uint64_t(ldh), n, uint64_t(ldh), 64, kStageRows))) return rc;
+    } else {
+        tm_h = tm_x;  // never used when store_h == 0
+    }
+
+    int dev = 0, sms = 0;
+    GATB_CUDA(cudaGetDevice(&dev));
+    GATB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const uint64_t ntiles = (n + kTileM - 1) / kTileM;
+    const unsigned grid = unsigned(ntiles < uint64_t(sms) ? ntiles : uint64_t(sms));
+    if (p->dim % 16 == 0) {
+        auto k = proj_tc_kernel<true>;
+        GATB_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+        k<<<grid, kThreads, smem, st>>>(tm_x, tm_w, tm_h, a);
+    } else {
+        auto k = proj_tc_kernel<false>;
+        GATB_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+        k<<<grid, kThreads, smem, st>>>(tm_x, tm_w, tm_h, a);
+    }
+    GATB_LAUNCH("projection (tcgen05) kernel");
+    return 0;
+}
+
+int projection_tc_check_error() {
+    unsigned e = 0;
+    GATB_CUDA(cudaMemcpyFromSymbol(&e, g_proj_error, sizeof(e)));
+    if (e) {
+        unsigned z = 0;
+        cudaMemcpyToSymbol(g_proj_error, &z, sizeof(z));
+        return fail_code(GAT_B200_ETIMEOUT, "projection kernel: a bounded wait timed out");
+    }
+    return 0;
+}
+
+}  // namespace gatb

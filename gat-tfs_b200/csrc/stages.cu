@@ -1,0 +1,214 @@
+// Small stage kernels: FP32->BF16 convert, max prescan, finish, and the
+// CUDA-core projection (FP32 path, and the BF16 path for shapes outside the
+// tensor-core kernel).
+#include "device.cuh"
+#include "graph.cuh"
+
+namespace gatb {
+namespace {
+
+// baseline/src/common.cpp:85-93: FP32 -> BF16 RNE, here with a padded output
+// stride whose padding columns are written as zero.
+__global__ void convert_kernel(uint64_t n, int width, const float* __restrict__ in, int ld_in,
+                               uint16_t* __restrict__ out, int ld_out) {
+    const uint64_t total = n * uint64_t(ld_out / 2);  // pairs of output columns
+    for (uint64_t t = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; t < total;
+         t += uint64_t(gridDim.x) * blockDim.x) {
+        uint64_t r = t / uint64_t(ld_out / 2);
+        int c = int(t % uint64_t(ld_out / 2)) * 2;
+        const float* src = in + r * uint64_t(ld_in);
+        float a = c < width ? src[c] : 0.f;
+        float b = c + 1 < width ? src[c + 1] : 0.f;
+        reinterpret_cast<uint32_t*>(out + r * uint64_t(ld_out))[c / 2] = pack_bf16x2(a, b);
+    }
+}
+
+// baseline/src/baseline_standard.cpp:44-51 (one warp per row).
+__global__ void max_prescan_kernel(const uint64_t* __restrict__ row, const uint32_t* __restrict__ col,
+                                   uint64_t n, int heads, const float* __restrict__ left,
+                                   const float* __restrict__ right, float* __restrict__ max) {
+    const int lane = threadIdx.x & 31;
+    for (uint64_t i = (blockIdx.x * uint64_t(blockDim.x) + threadIdx.x) >> 5; i < n;
+         i += (uint64_t(gridDim.x) * blockDim.x) >> 5) {
+        float mr[8];
+#pragma unroll
+        for (int h = 0; h < 8; ++h) mr[h] = -INFINITY;
+        for (uint64_t e = row[i] + lane; e < row[i + 1]; e += 32) {
+            uint32_t s = col[e];
+#pragma unroll
+            for (int h = 0; h < 8; ++h)
+                if (h < heads) mr[h] = fmaxf(mr[h], right[uint64_t(s) * heads + h]);
+        }
+#pragma unroll
+        for (int h = 0; h < 8; ++h) mr[h] = warp_max(mr[h]);
+        const bool empty = row[i] == row[i + 1];
+#pragma unroll
+        for (int h = 0; h < 8; ++h)
+            if (h < heads && lane == h) max[i * heads + h] = empty ? 0.f : leaky(mr[h] + left[i * heads + h]);
+    }
+}
+
+// baseline/src/baseline_standard.cpp:85-97
+__global__ void finish_kernel(uint64_t n, int heads, int dim, const float* __restrict__ den, int hidden,
+                              float* __restrict__ out, int ldo) {
+    const int width = heads * dim;
+    const uint64_t total = n * uint64_t(width);
+    for (uint64_t t = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; t < total;
+         t += uint64_t(gridDim.x) * blockDim.x) {
+        uint64_t r = t / width;
+        int c = int(t % width);
+        float d = den[r * heads + c / dim];
+        float v = out[r * ldo + c] * (d > 0.f ? 1.f / d : 0.f);
+        if (hidden) v = elu(v);
+        out[r * ldo + c] = v;
+    }
+}
+
+// CUDA-core projection: Z = X W (FP32 accumulate over k ascending in blocks of
+// 32), left/right = Z_h . aL_h / aR_h, Z stored as FP32 or BF16 RNE.
+// Block: kRows rows x all `width` columns, 256 threads.
+constexpr int kRows = 32;
+constexpr int kKb = 32;
+template <class XT>
+__global__ void __launch_bounds__(256) projection_simt_kernel(
+    uint64_t n, int in, int heads, int dim, const XT* __restrict__ x, int ldx, const float* __restrict__ w,
+    int quantize_w, const float* __restrict__ al, const float* __restrict__ ar, void* __restrict__ h,
+    int h_bf16, int ldh, float* __restrict__ left, float* __restrict__ right) {
+    extern __shared__ float smem[];
+    const int width = heads * dim;
+    float* xs = smem;                 // [kRows][kKb]
+    float* ws = xs + kRows * kKb;     // [kKb][width]
+    float* zs = ws + kKb * width;     // [kRows][width+1]
+    const int zld = width + 1;
+    const uint64_t r0 = blockIdx.x * uint64_t(kRows);
+    const int tid = threadIdx.x;
+    constexpr int CPT = 2;  // columns per thread (width <= 512)
+    float acc[CPT][kRows];
+#pragma unroll
+    for (int j = 0; j < CPT; ++j)
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) acc[j][r] = 0.f;
+    for (int k0 = 0; k0 < in; k0 += kKb) {
+        for (int t = tid; t < kRows * kKb; t += 256) {
+            int r = t / kKb, k = t % kKb;
+            float v = 0.f;
+            if (r0 + r < n && k0 + k < in) {
+                if constexpr (sizeof(XT) == 2)
+                    v = __uint_as_float(uint32_t(x[(r0 + r) * ldx + k0 + k]) << 16);
+                else
+                    v = x[(r0 + r) * ldx + k0 + k];
+            }
+            xs[t] = v;
+        }
+        for (int t = tid; t < kKb * width; t += 256) {
+            int k = t / width, c = t % width;
+            float v = k0 + k < in ? w[uint64_t(k0 + k) * width + c] : 0.f;
+            if (quantize_w) v = __uint_as_float((pack_bf16x2(v, 0.f) & 0xffffu) << 16);
+            ws[t] = v;
+        }
+        __syncthreads();
+        const int kmax = min(kKb, in - k0);
+        for (int k = 0; k < kmax; ++k) {
+            float wv[CPT];
+#pragma unroll
+            for (int j = 0; j < CPT; ++j) {
+                int c = tid + j * 256;
+                wv[j] = c < width ? ws[k * width + c] : 0.f;
+            }
+#pragma unroll
+            for (int r = 0; r < kRows; ++r) {
+                float xv = xs[r * kKb + k];
+#pragma unroll
+                for (int j = 0; j < CPT; ++j) acc[j][r] = fmaf(xv, wv[j], acc[j][r]);
+            }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) {
+        int c = tid + j * 256;
+        if (c < width)
+#pragma unroll
+            for (int r = 0; r < kRows; ++r) zs[r * zld + c] = acc[j][r];
+    }
+    __syncthreads();
+    // Attention dots, sequential over the head's columns (lr_from_z scalar form).
+    for (int t = tid; t < kRows * heads; t += 256) {
+        int r = t / heads, hh = t % heads;
+        if (r0 + r >= n) continue;
+        float l = 0.f, rr = 0.f;
+        for (int d = 0; d < dim; ++d) {
+            float z = zs[r * zld + hh * dim + d];
+            l = fmaf(z, al[hh * dim + d], l);
+            rr = fmaf(z, ar[hh * dim + d], rr);
+        }
+        if (left) left[(r0 + r) * heads + hh] = l;
+        if (right) right[(r0 + r) * heads + hh] = rr;
+    }
+    if (h) {
+        for (int t = tid; t < kRows * ldh; t += 256) {
+            int r = t / ldh, c = t % ldh;
+            if (r0 + r >= n) continue;
+            float z = c < width ? zs[r * zld + c] : 0.f;
+            if (h_bf16)
+                static_cast<uint16_t*>(h)[(r0 + r) * ldh + c] = uint16_t(pack_bf16x2(z, 0.f) & 0xffffu);
+            else
+                static_cast<float*>(h)[(r0 + r) * ldh + c] = z;
+        }
+    }
+}
+
+unsigned grid_for(uint64_t work, int per_block) {
+    uint64_t b = (work + per_block - 1) / per_block;
+    if (b > 148ull * 64) b = 148ull * 64;
+    return unsigned(b ? b : 1);
+}
+
+}  // namespace
+
+int convert_launch(uint64_t n, int width, const float* in, int ld_in, uint16_t* out, int ld_out, cudaStream_t st) {
+    if (!in || !out) return fail("convert: null buffer");
+    if (ld_in < width || ld_out < width || (ld_out & 1)) return fail("convert: bad row strides");
+    convert_kernel<<<grid_for(n * uint64_t(ld_out / 2), 256), 256, 0, st>>>(n, width, in, ld_in, out, ld_out);
+    GATB_LAUNCH("convert kernel");
+    return 0;
+}
+
+int max_prescan_launch(const gat_b200_graph* g, int heads, const float* left, const float* right, float* max,
+                       cudaStream_t st) {
+    if (!g || !left || !right || !max) return fail("max_prescan: null buffer");
+    if (heads < 1 || heads > 8) return fail("invalid parameter shape (heads <=8, head_dim <=64)");
+    max_prescan_kernel<<<grid_for(g->n * 32, 256), 256, 0, st>>>(g->row, g->col, g->n, heads, left, right, max);
+    GATB_LAUNCH("max prescan kernel");
+    return 0;
+}
+
+int finish_launch(uint64_t n, int heads, int dim, const float* den, int hidden, float* out, int ldo, cudaStream_t st) {
+    if (!den || !out) return fail("finish: null buffer");
+    if (heads < 1 || heads > 8 || dim < 1 || dim > 64) return fail("invalid parameter shape (heads <=8, head_dim <=64)");
+    if (ldo < heads * dim) return fail("finish: row stride smaller than the width");
+    finish_kernel<<<grid_for(n * uint64_t(heads * dim), 256), 256, 0, st>>>(n, heads, dim, den, hidden, out, ldo);
+    GATB_LAUNCH("finish kernel");
+    return 0;
+}
+
+int projection_simt_launch(const gat_b200_layer* p, uint64_t n, const void* x, int x_bf16, int ldx, void* h,
+                           int h_bf16, int ldh, float* left, float* right, cudaStream_t st) {
+    const size_t smem = (size_t(kRows) * kKb + size_t(kKb) * p->width + size_t(kRows) * (p->width + 1)) * sizeof(float);
+    unsigned blocks = unsigned((n + kRows - 1) / kRows);
+    if (x_bf16) {
+        auto k = projection_simt_kernel<uint16_t>;
+        GATB_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+        k<<<blocks, 256, smem, st>>>(n, p->in, p->heads, p->dim, static_cast<const uint16_t*>(x), ldx, p->w, 1,
+                                     p->al, p->ar, h, h_bf16, ldh, left, right);
+    } else {
+        auto k = projection_simt_kernel<float>;
+        GATB_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+        k<<<blocks, 256, smem, st>>>(n, p->in, p->heads, p->dim, static_cast<const float*>(x), ldx, p->w, 0,
+                                     p->al, p->ar, h, h_bf16, ldh, left, right);
+    }
+    GATB_LAUNCH("projection (CUDA cores) kernel");
+    return 0;
+}
+
+}  // namespace gatb

@@ -1,0 +1,411 @@
+"""Python host mirror of the reference's GAT API over libgat_b200.so (ctypes).
+
+The reference's C++ surface (baseline/include/gat.hpp) is mirrored by name:
+Graph / Param / Model, load_graph / save_graph, load_model / save_model,
+random_model, degree_schedule, projection, max_prescan, standard_aggregate,
+finish, standard_layer, plus the fused layer and the three-layer model that
+the benchmark runs. Errors raise GatError (the reference raises
+std::runtime_error with the same messages).
+
+Device buffers are torch CUDA tensors; torch is only used for device memory,
+streams and the process group, never for the computation. The library is the
+in-tree build gat-tfs_b200/libgat_b200.so; importing this module fails if it is
+missing (there is no fallback path).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass, field
+from pathlib import Path
+from typing import List, Optional, Sequence
+
+import numpy as np
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = Path(os.environ.get("GAT_B200_LIB", _PKG / "libgat_b200.so"))
+if not LIB_PATH.exists():
+    raise ImportError(f"{LIB_PATH} is missing: build it with `python gat-tfs_b200/build.py`")
+_lib = C.CDLL(str(LIB_PATH))
+
+F32, BF16 = 0, 1
+PATH_STANDARD_BF16, PATH_STANDARD_FP32 = 0, 1
+PATHS = {"standard_bf16": PATH_STANDARD_BF16, "standard_fp32": PATH_STANDARD_FP32}
+OK, EINVAL, ECUDA, EUNSUPPORTED, ETIMEOUT, EIO = range(6)
+
+_u64p = C.POINTER(C.c_uint64)
+_u32p = C.POINTER(C.c_uint32)
+_u16p = C.POINTER(C.c_uint16)
+_f32p = C.POINTER(C.c_float)
+_vp = C.c_void_p
+
+# (name, restype, argtypes) of every exported entry point, as declared in
+# include/gat_b200.h.
+SIGNATURES = [
+    ("gat_b200_last_error", C.c_char_p, []),
+    ("gat_b200_version", C.c_int, []),
+    ("gat_b200_padded_ld", C.c_int, [C.c_int, C.c_int]),
+    ("gat_b200_rne", C.c_uint16, [C.c_float]),
+    ("gat_b200_convert_host", C.c_int, [_f32p, _u16p, C.c_uint64]),
+    ("gat_b200_validate_csr", C.c_int, [C.c_uint64, C.c_uint64, _u64p, _u32p]),
+    ("gat_b200_read_graph_header", C.c_int, [C.c_char_p, _u64p, _u64p, _u32p, _u32p]),
+    ("gat_b200_read_graph", C.c_int, [C.c_char_p, C.c_uint64, C.c_uint64, C.c_uint32, _u64p, _u32p, _f32p]),
+    ("gat_b200_write_graph", C.c_int, [C.c_char_p, C.c_uint64, C.c_uint64, C.c_uint32, C.c_uint32, _u64p, _u32p, _f32p]),
+    ("gat_b200_read_weights", C.c_int, [C.c_char_p, C.c_int, C.c_int, C.POINTER(_f32p), C.POINTER(_f32p), C.POINTER(_f32p)]),
+    ("gat_b200_write_weights", C.c_int, [C.c_char_p, C.c_int, C.c_int, C.POINTER(_f32p), C.POINTER(_f32p), C.POINTER(_f32p)]),
+    ("gat_b200_random_model", C.c_int, [C.c_int, C.c_int, C.c_int, C.POINTER(_f32p), C.POINTER(_f32p), C.POINTER(_f32p)]),
+    ("gat_b200_synth_uniform_graph", C.c_int, [C.c_uint64, C.c_uint32, C.c_uint64, _u64p, _u32p]),
+    ("gat_b200_synth_powerlaw_graph", C.c_int, [C.c_uint64, C.c_uint64, C.c_uint64, C.c_double, C.c_uint64, _u64p, _u32p]),
+    ("gat_b200_synth_normal", C.c_int, [C.c_uint64, C.c_double, C.c_uint64, C.c_uint64, _f32p]),
+    ("gat_b200_synth_uniform", C.c_int, [C.c_uint64, C.c_double, C.c_double, C.c_uint64, C.c_uint64, _f32p]),
+    ("gat_b200_graph_create", C.c_int, [C.c_uint64, C.c_uint64, _u64p, _u32p, _vp, C.POINTER(_vp)]),
+    ("gat_b200_graph_destroy", C.c_int, [_vp]),
+    ("gat_b200_graph_schedule", C.c_int, [_vp, _u32p, _u64p]),
+    ("gat_b200_graph_device_csr", C.c_int, [_vp, C.POINTER(_vp), C.POINTER(_vp)]),
+    ("gat_b200_graph_info", C.c_int, [_vp, _u64p, _u64p, _u32p, _u32p, _u32p, _u32p]),
+    ("gat_b200_layer_create", C.c_int, [C.c_int, C.c_int, C.c_int, _f32p, _f32p, _f32p, C.POINTER(_vp)]),
+    ("gat_b200_layer_destroy", C.c_int, [_vp]),
+    ("gat_b200_convert", C.c_int, [C.c_uint64, C.c_int, _vp, C.c_int, _vp, C.c_int, _vp]),
+    ("gat_b200_projection", C.c_int, [_vp, C.c_uint64, _vp, C.c_int, C.c_int, _vp, C.c_int, C.c_int, _vp, _vp, _vp]),
+    ("gat_b200_max_prescan", C.c_int, [_vp, C.c_int, _vp, _vp, _vp, _vp]),
+    ("gat_b200_standard_aggregate", C.c_int, [_vp, C.c_int, C.c_int, _vp, C.c_int, C.c_int, _vp, _vp, _vp, _vp, _vp, C.c_int, _vp, _vp, _vp]),
+    ("gat_b200_finish", C.c_int, [C.c_uint64, C.c_int, C.c_int, _vp, C.c_int, _vp, C.c_int, _vp]),
+    ("gat_b200_aggregate_fused", C.c_int, [_vp, C.c_int, C.c_int, _vp, C.c_int, C.c_int, _vp, _vp, C.c_int, _vp, C.c_int, C.c_int, _vp]),
+    ("gat_b200_standard_layer", C.c_int, [_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp, _vp, C.c_int, C.c_int, _vp]),
+    ("gat_b200_check_device", C.c_int, []),
+    ("gat_b200_model_create", C.c_int, [_vp, C.POINTER(_vp), C.c_int, C.POINTER(_vp)]),
+    ("gat_b200_model_destroy", C.c_int, [_vp]),
+    ("gat_b200_model_forward", C.c_int, [_vp, _vp, C.c_int, _vp, C.c_int, _vp]),
+    ("gat_b200_model_enable_timing", C.c_int, [_vp, C.c_int]),
+    ("gat_b200_model_stage_times", C.c_int, [_vp, _f32p]),
+    ("gat_b200_model_launches", C.c_int, [_vp]),
+]
+for _name, _res, _args in SIGNATURES:
+    _fn = getattr(_lib, _name)
+    _fn.restype = _res
+    _fn.argtypes = _args
+
+
+class GatError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(msg)
+        self.code = code
+
+
+def _check(rc: int):
+    if rc != 0:
+        raise GatError(rc, _lib.gat_b200_last_error().decode())
+
+
+def _p(a: np.ndarray, t):
+    return a.ctypes.data_as(t)
+
+
+def _ptr(t) -> Optional[int]:
+    """Device pointer of a torch tensor (or int / None)."""
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return t
+    return t.data_ptr()
+
+
+def _stream(s) -> Optional[int]:
+    if s is None:
+        return None
+    return s.cuda_stream if hasattr(s, "cuda_stream") else int(s)
+
+
+def version() -> int:
+    return _lib.gat_b200_version()
+
+
+def padded_ld(width: int, dtype: int) -> int:
+    return _lib.gat_b200_padded_ld(width, dtype)
+
+
+# ---------------------------------------------------------------- host side
+@dataclass
+class Graph:
+    """Destination-row CSR + FP32 features (baseline/include/gat.hpp:32-39)."""
+    n: int
+    e: int
+    din: int
+    classes: int
+    row: np.ndarray  # u64 [n+1]
+    col: np.ndarray  # u32 [e]
+    x: np.ndarray    # f32 [n, din]
+
+    def validate(self):
+        _check(_lib.gat_b200_validate_csr(self.n, self.e, _p(self.row, _u64p), _p(self.col, _u32p)))
+        if not np.isfinite(self.x).all():
+            raise GatError(EINVAL, "nonfinite graph input")
+
+
+@dataclass
+class Param:
+    """One layer (baseline/include/gat.hpp:42-47): W[in][heads*dim], aL, aR."""
+    in_: int
+    heads: int
+    dim: int
+    w: np.ndarray
+    al: np.ndarray
+    ar: np.ndarray
+
+    @property
+    def width(self) -> int:
+        return self.heads * self.dim
+
+
+def rne(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.shape, dtype=np.uint16)
+    _check(_lib.gat_b200_convert_host(_p(x, _f32p), _p(out, _u16p), x.size))
+    return out
+
+
+def bf16_to_f32(b: np.ndarray) -> np.ndarray:
+    return (b.astype(np.uint32) << 16).view(np.float32)
+
+
+def load_graph(path) -> Graph:
+    n, e, d, c = C.c_uint64(), C.c_uint64(), C.c_uint32(), C.c_uint32()
+    bpath = str(path).encode()
+    _check(_lib.gat_b200_read_graph_header(bpath, C.byref(n), C.byref(e), C.byref(d), C.byref(c)))
+    row = np.empty(n.value + 1, np.uint64)
+    col = np.empty(max(e.value, 1), np.uint32)[: e.value]
+    x = np.empty((n.value, d.value), np.float32)
+    _check(_lib.gat_b200_read_graph(bpath, n.value, e.value, d.value, _p(row, _u64p), _p(col, _u32p), _p(x, _f32p)))
+    return Graph(n.value, e.value, d.value, c.value, row, col, x)
+
+
+def save_graph(g: Graph, path):
+    _check(_lib.gat_b200_write_graph(str(path).encode(), g.n, g.e, g.din, g.classes,
+                                     _p(np.ascontiguousarray(g.row, np.uint64), _u64p),
+                                     _p(np.ascontiguousarray(g.col, np.uint32), _u32p),
+                                     _p(np.ascontiguousarray(g.x, np.float32), _f32p)))
+
+
+def model_shapes(din: int, classes: int):
+    """Layer shapes of the reference model (baseline/src/common.cpp:53)."""
+    return [(din, 8, 32), (256, 8, 32), (256, 1, classes)]
+
+
+def _empty_model(din, classes) -> List[Param]:
+    return [Param(i, h, d, np.empty((i, h * d), np.float32), np.empty(h * d, np.float32), np.empty(h * d, np.float32))
+            for i, h, d in model_shapes(din, classes)]
+
+
+def _arrays(model):
+    arr = lambda xs: (_f32p * 3)(*[_p(x, _f32p) for x in xs])
+    return arr([p.w for p in model]), arr([p.al for p in model]), arr([p.ar for p in model])
+
+
+def random_model(din: int, classes: int, seed: int) -> List[Param]:
+    """The reference's seeded untrained model (baseline/src/common.cpp:50-62)."""
+    m = _empty_model(din, classes)
+    _check(_lib.gat_b200_random_model(din, classes, seed, *_arrays(m)))
+    return m
+
+
+def glorot_model(din: int, classes: int, seed: int) -> List[Param]:
+    """Glorot-uniform W (fan_in=in, fan_out=heads*dim) and a (fan = heads+dim)."""
+    m = _empty_model(din, classes)
+    for l, p in enumerate(m):
+        lw = float(np.sqrt(6.0 / (p.in_ + p.width)))
+        la = float(np.sqrt(6.0 / (p.heads + p.dim)))
+        _check(_lib.gat_b200_synth_uniform(p.w.size, -lw, lw, seed, 100 + 3 * l, _p(p.w, _f32p)))
+        _check(_lib.gat_b200_synth_uniform(p.width, -la, la, seed, 101 + 3 * l, _p(p.al, _f32p)))
+        _check(_lib.gat_b200_synth_uniform(p.width, -la, la, seed, 102 + 3 * l, _p(p.ar, _f32p)))
+    return m
+
+
+def load_model(path, din: int, classes: int) -> List[Param]:
+    m = _empty_model(din, classes)
+    _check(_lib.gat_b200_read_weights(str(path).encode(), din, classes, *_arrays(m)))
+    return m
+
+
+def save_model(model: Sequence[Param], path):
+    din, classes = model[0].in_, model[2].dim
+    _check(_lib.gat_b200_write_weights(str(path).encode(), din, classes, *_arrays(model)))
+
+
+def synth_uniform_graph(n: int, sources: int, seed: int):
+    row = np.empty(n + 1, np.uint64)
+    col = np.empty(n * (sources + 1), np.uint32)
+    _check(_lib.gat_b200_synth_uniform_graph(n, sources, seed, _p(row, _u64p), _p(col, _u32p)))
+    return row, col
+
+
+def synth_powerlaw_graph(n: int, e: int, max_degree: int, gamma: float, seed: int):
+    row = np.empty(n + 1, np.uint64)
+    col = np.empty(e, np.uint32)
+    _check(_lib.gat_b200_synth_powerlaw_graph(n, e, max_degree, gamma, seed, _p(row, _u64p), _p(col, _u32p)))
+    return row, col
+
+
+def synth_normal(shape, seed: int, stream: int, scale: float = 1.0) -> np.ndarray:
+    out = np.empty(shape, np.float32)
+    _check(_lib.gat_b200_synth_normal(out.size, scale, seed, stream, _p(out, _f32p)))
+    return out
+
+
+def synth_uniform(shape, lo: float, hi: float, seed: int, stream: int) -> np.ndarray:
+    out = np.empty(shape, np.float32)
+    _check(_lib.gat_b200_synth_uniform(out.size, lo, hi, seed, stream, _p(out, _f32p)))
+    return out
+
+
+# -------------------------------------------------------------- device side
+class DeviceGraph:
+    """CSR uploaded to the current CUDA device with its degree schedule."""
+
+    def __init__(self, row: np.ndarray, col: np.ndarray, stream=None):
+        row = np.ascontiguousarray(row, np.uint64)
+        col = np.ascontiguousarray(col, np.uint32)
+        self.n = len(row) - 1
+        self.e = len(col)
+        h = _vp()
+        _check(_lib.gat_b200_graph_create(self.n, self.e, _p(row, _u64p), _p(col, _u32p), _stream(stream), C.byref(h)))
+        self.handle = h
+
+    def schedule(self):
+        """(perm, neighbor_steps) as gat::degree_schedule (common.cpp:120-125)."""
+        perm = np.empty(self.n, np.uint32)
+        steps = C.c_uint64()
+        _check(_lib.gat_b200_graph_schedule(self.handle, _p(perm, _u32p), C.byref(steps)))
+        return perm, steps.value
+
+    def info(self) -> dict:
+        n, e = C.c_uint64(), C.c_uint64()
+        md, nh, ns, se = C.c_uint32(), C.c_uint32(), C.c_uint32(), C.c_uint32()
+        _check(_lib.gat_b200_graph_info(self.handle, C.byref(n), C.byref(e), C.byref(md), C.byref(nh),
+                                        C.byref(ns), C.byref(se)))
+        return dict(n=n.value, e=e.value, max_degree=md.value, n_hub=nh.value, n_seg=ns.value,
+                    seg_edges=se.value)
+
+    def close(self):
+        if getattr(self, "handle", None):
+            _lib.gat_b200_graph_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class DeviceLayer:
+    """Prepared layer parameters on the device (gat::prepare, common.cpp:97-119)."""
+
+    def __init__(self, p: Param):
+        self.param = p
+        self.in_, self.heads, self.dim, self.width = p.in_, p.heads, p.dim, p.width
+        h = _vp()
+        w = np.ascontiguousarray(p.w, np.float32)
+        al = np.ascontiguousarray(p.al, np.float32)
+        ar = np.ascontiguousarray(p.ar, np.float32)
+        _check(_lib.gat_b200_layer_create(p.in_, p.heads, p.dim, _p(w, _f32p), _p(al, _f32p), _p(ar, _f32p), C.byref(h)))
+        self.handle = h
+
+    def close(self):
+        if getattr(self, "handle", None):
+            _lib.gat_b200_layer_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def check_device():
+    _check(_lib.gat_b200_check_device())
+
+
+def convert(n, width, x, ld_in, out, ld_out, stream=None):
+    _check(_lib.gat_b200_convert(n, width, _ptr(x), ld_in, _ptr(out), ld_out, _stream(stream)))
+
+
+def projection(layer: DeviceLayer, n, x, ldx, precision, h=None, h_dtype=BF16, ldh=0, left=None, right=None,
+               stream=None):
+    _check(_lib.gat_b200_projection(layer.handle, n, _ptr(x), ldx, precision, _ptr(h), h_dtype, ldh, _ptr(left),
+                                    _ptr(right), _stream(stream)))
+
+
+def max_prescan(g: DeviceGraph, heads, left, right, mx, stream=None):
+    _check(_lib.gat_b200_max_prescan(g.handle, heads, _ptr(left), _ptr(right), _ptr(mx), _stream(stream)))
+
+
+def standard_aggregate(g: DeviceGraph, heads, dim, h, h_dtype, ldh, left, right, out, ldo, den, mx=None,
+                       fixed_p=None, fixed_den=None, stream=None):
+    _check(_lib.gat_b200_standard_aggregate(g.handle, heads, dim, _ptr(h), h_dtype, ldh, _ptr(left), _ptr(right),
+                                            _ptr(fixed_p), _ptr(fixed_den), _ptr(out), ldo, _ptr(den), _ptr(mx),
+                                            _stream(stream)))
+
+
+def finish(n, heads, dim, den, hidden, out, ldo, stream=None):
+    _check(_lib.gat_b200_finish(n, heads, dim, _ptr(den), int(hidden), _ptr(out), ldo, _stream(stream)))
+
+
+def aggregate_fused(g: DeviceGraph, heads, dim, h, h_dtype, ldh, left, right, hidden, out, out_dtype, ldo,
+                    stream=None):
+    _check(_lib.gat_b200_aggregate_fused(g.handle, heads, dim, _ptr(h), h_dtype, ldh, _ptr(left), _ptr(right),
+                                         int(hidden), _ptr(out), out_dtype, ldo, _stream(stream)))
+
+
+def standard_layer(g: DeviceGraph, layer: DeviceLayer, x, ldx, path, hidden, h, left, right, out, out_dtype, ldo,
+                   stream=None):
+    _check(_lib.gat_b200_standard_layer(g.handle, layer.handle, _ptr(x), ldx, path, int(hidden), _ptr(h), _ptr(left),
+                                        _ptr(right), _ptr(out), out_dtype, ldo, _stream(stream)))
+
+
+class DeviceModel:
+    """The three-layer forward (bench/main.cpp:171-172) with all buffers preallocated."""
+
+    def __init__(self, g: DeviceGraph, layers: Sequence[DeviceLayer], path: int = PATH_STANDARD_BF16):
+        self.g = g
+        self.layers = list(layers)
+        arr = (_vp * 3)(*[l.handle for l in self.layers])
+        h = _vp()
+        _check(_lib.gat_b200_model_create(g.handle, arr, path, C.byref(h)))
+        self.handle = h
+        self.classes = self.layers[2].width
+        self.din = self.layers[0].in_
+
+    def forward(self, x, logits, x_on_host: bool, logits_on_host: bool, stream=None):
+        """x, logits: torch tensors (pinned host or device) or raw pointers."""
+        _check(_lib.gat_b200_model_forward(self.handle, _ptr(x), int(x_on_host), _ptr(logits), int(logits_on_host),
+                                           _stream(stream)))
+
+    STAGES = ("h2d", "convert", "projection_l1", "aggregate_l1", "projection_l2", "aggregate_l2",
+              "projection_l3", "aggregate_l3", "d2h")
+
+    def enable_timing(self, steps: int):
+        _check(_lib.gat_b200_model_enable_timing(self.handle, steps))
+        self._timing_steps = steps
+
+    def stage_times(self) -> np.ndarray:
+        """[sets, 9] milliseconds per stage (see STAGES)."""
+        buf = np.zeros((max(1, self._timing_steps), len(self.STAGES)), np.float32)
+        k = _lib.gat_b200_model_stage_times(self.handle, _p(buf, _f32p))
+        if k < 0:
+            _check(k)
+        return buf[:k]
+
+    def launches(self) -> int:
+        return _lib.gat_b200_model_launches(self.handle)
+
+    def close(self):
+        if getattr(self, "handle", None):
+            _lib.gat_b200_model_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

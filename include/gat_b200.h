@@ -1,0 +1,246 @@
+/*
+ * gat_b200.h -- C-ABI of libgat_b200.so, the B200 (sm_100a) implementation of
+ * the three-layer multi-head GAT forward of huamiao123/GAT-TFS.
+ *
+ * Plain C: opaque handles, plain pointers and sizes, int status codes. No C++
+ * exceptions cross this boundary; gat_b200_last_error() returns the message of
+ * the calling thread's last failure (the reference throws std::runtime_error
+ * with the same kind of message, e.g. baseline/src/common.cpp:24-28).
+ *
+ * Each entry point names the reference interface it replaces (file:line inside
+ * the reference project). Reference layouts are kept: destination-row CSR with
+ * u64 row pointers and u32 source ids, row-major features, W[in][heads*dim]
+ * with head-major columns, per-row/head arrays [n][heads], per-edge arrays
+ * [e][heads]. Device feature buffers use a row stride `ld` (elements) that the
+ * caller passes; gat_b200_padded_ld() gives the stride the library uses itself
+ * (rows start on 16-byte boundaries, padding columns hold zeros).
+ *
+ * Streams are passed as `void*` (a cudaStream_t; NULL = legacy default stream).
+ * Device-pointer arguments must be device memory of the current device.
+ */
+#ifndef GAT_B200_H
+#define GAT_B200_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define GAT_B200_OK 0
+#define GAT_B200_EINVAL 1       /* bad argument, shape or input data */
+#define GAT_B200_ECUDA 2        /* CUDA runtime / driver error */
+#define GAT_B200_EUNSUPPORTED 3 /* shape outside what the kernels implement */
+#define GAT_B200_ETIMEOUT 4     /* a bounded device-side wait gave up */
+#define GAT_B200_EIO 5          /* file open/read/write failure */
+
+/* ---- element types, paths ---------------------------------------------- */
+#define GAT_B200_F32 0
+#define GAT_B200_BF16 1
+
+/* Layer paths, named after the reference's --path values
+ * (baseline/bench/main.cpp:30, baseline/src/common.cpp:126-134). */
+#define GAT_B200_PATH_STANDARD_BF16 0 /* B0: BF16 X/W on tcgen05, FP32 softmax state */
+#define GAT_B200_PATH_STANDARD_FP32 1 /* B0 FP32 projection, FP32 features         */
+
+/* Message of this thread's last failure ("" if none). */
+const char* gat_b200_last_error(void);
+/* Library version: major*10000 + minor*100 + patch. */
+int gat_b200_version(void);
+/* Row stride (elements) the library uses for `width` columns of elem_dtype. */
+int gat_b200_padded_ld(int width, int elem_dtype);
+
+/* ======================================================================== *
+ *  Host utilities (no GPU needed)                                          *
+ * ======================================================================== */
+
+/* FP32 -> BF16 round-to-nearest-even, NaN quieted.
+ * Replaces gat::rne (baseline/src/common.cpp:80-83). */
+uint16_t gat_b200_rne(float x);
+/* Replaces gat::convert (baseline/src/common.cpp:85-93), host side. */
+int gat_b200_convert_host(const float* in, uint16_t* out, uint64_t count);
+
+/* Replaces gat::Graph::validate (baseline/src/common.cpp:23-30) for the CSR
+ * part: row[0]==0, row[n]==e, monotone rows, col < n, 0 < n <= INT32_MAX. */
+int gat_b200_validate_csr(uint64_t n, uint64_t e, const uint64_t* row, const uint32_t* col);
+
+/* GATBIN1 graph files. Replaces gat::load_graph / save_graph
+ * (baseline/src/common.cpp:31-44). Read the header first, then the arrays into
+ * caller buffers of row[n+1], col[e], x[n*din]. */
+int gat_b200_read_graph_header(const char* path, uint64_t* n, uint64_t* e, uint32_t* din,
+                               uint32_t* classes);
+int gat_b200_read_graph(const char* path, uint64_t n, uint64_t e, uint32_t din, uint64_t* row,
+                        uint32_t* col, float* x);
+int gat_b200_write_graph(const char* path, uint64_t n, uint64_t e, uint32_t din, uint32_t classes,
+                         const uint64_t* row, const uint32_t* col, const float* x);
+
+/* GATWGT1 checkpoints for the 3-layer model din -> 8x32 -> 8x32 -> 1xclasses.
+ * Replaces gat::load_model / save_model (baseline/src/common.cpp:63-79).
+ * w[l], al[l], ar[l] are caller buffers of in_l*width_l, width_l, width_l. */
+int gat_b200_read_weights(const char* path, int din, int classes, float* const* w,
+                          float* const* al, float* const* ar);
+int gat_b200_write_weights(const char* path, int din, int classes, const float* const* w,
+                           const float* const* al, const float* const* ar);
+
+/* Seeded untrained model with the reference's generator: mt19937(seed+11*l),
+ * W ~ N(0,1)/sqrt(in), a ~ N(0,1)/sqrt(dim). Replaces gat::random_model
+ * (baseline/src/common.cpp:50-62); bit-identical with the same C++ library. */
+int gat_b200_random_model(int din, int classes, int seed, float* const* w, float* const* al,
+                          float* const* ar);
+
+/* Seeded synthetic inputs (no reference counterpart: the reference reads
+ * prepared OGB files, implementation/tools/prepare_arxiv.py:28-52).
+ *  - uniform: every row has `sources` distinct uniform sources != self, plus
+ *    the self loop; e = n*(sources+1).
+ *  - powerlaw: row degrees follow a power law of exponent gamma with the given
+ *    maximum and exactly e edges (self loops included); sources are drawn by
+ *    the same popularity law.
+ *  - normal / uniform: count floats ~ N(0,scale^2) / U(lo,hi) from (seed,stream). */
+int gat_b200_synth_uniform_graph(uint64_t n, uint32_t sources, uint64_t seed, uint64_t* row,
+                                 uint32_t* col);
+int gat_b200_synth_powerlaw_graph(uint64_t n, uint64_t e, uint64_t max_degree, double gamma,
+                                  uint64_t seed, uint64_t* row, uint32_t* col);
+int gat_b200_synth_normal(uint64_t count, double scale, uint64_t seed, uint64_t stream, float* out);
+int gat_b200_synth_uniform(uint64_t count, double lo, double hi, uint64_t seed, uint64_t stream,
+                           float* out);
+
+/* ======================================================================== *
+ *  Device: graph and degree schedule                                       *
+ * ======================================================================== */
+
+typedef struct gat_b200_graph gat_b200_graph;
+
+/* Uploads a destination-row CSR (host arrays) to the current device, checks it
+ * on the device (the CSR checks of Graph::validate, baseline/src/common.cpp:24-28)
+ * and builds the degree schedule (replaces gat::degree_schedule,
+ * baseline/src/common.cpp:120-125): the stable (degree, row id) ascending
+ * permutation and neighbor_steps, computed on the device by a stable radix sort.
+ * The kernels walk that permutation from the largest degree down and give rows
+ * above a degree threshold a whole CTA. */
+int gat_b200_graph_create(uint64_t n, uint64_t e, const uint64_t* row, const uint32_t* col,
+                          void* stream, gat_b200_graph** out);
+int gat_b200_graph_destroy(gat_b200_graph* g);
+/* Copies the schedule back: perm[n] (may be NULL) and neighbor_steps (may be NULL). */
+int gat_b200_graph_schedule(const gat_b200_graph* g, uint32_t* perm, uint64_t* neighbor_steps);
+/* Device pointers of the uploaded CSR (row[n+1] u64, col[e] u32). */
+int gat_b200_graph_device_csr(const gat_b200_graph* g, const uint64_t** row, const uint32_t** col);
+/* Schedule statistics: rows, edges, largest degree, number of rows split into
+ * segments of at most seg_edges edges (n_hub), and those segments (n_seg). */
+int gat_b200_graph_info(const gat_b200_graph* g, uint64_t* n, uint64_t* e, uint32_t* max_degree,
+                        uint32_t* n_hub, uint32_t* n_seg, uint32_t* seg_edges);
+
+/* ======================================================================== *
+ *  Device: prepared layer parameters                                       *
+ * ======================================================================== */
+
+typedef struct gat_b200_layer gat_b200_layer;
+
+/* Replaces gat::prepare (baseline/src/common.cpp:97-119) and Param::validate
+ * (common.cpp:45-49): heads in [1,8], dim in [1,64]. Uploads BF16 RNE(W) in the
+ * tensor-core layout, FP32 W, aL, aR and blr = W.a ([in][2*heads],
+ * common.cpp:100-108). Host input arrays. */
+int gat_b200_layer_create(int in, int heads, int dim, const float* w, const float* al,
+                          const float* ar, gat_b200_layer** out);
+int gat_b200_layer_destroy(gat_b200_layer* p);
+
+/* ======================================================================== *
+ *  Device: stage kernels (device pointers, caller-owned buffers)           *
+ * ======================================================================== */
+
+/* FP32 [n][width] (row stride ld_in) -> BF16 RNE [n][ld_out], padding zeroed.
+ * Replaces gat::convert (baseline/src/common.cpp:85-93). */
+int gat_b200_convert(uint64_t n, int width, const float* in, int ld_in, uint16_t* out, int ld_out,
+                     void* stream);
+
+/* Projection with fused attention dots. Replaces gat::projection followed by
+ * gat::lr_from_z (baseline/src/baseline_standard.cpp:3-20):
+ *   Z = X W (FP32 accumulate), left[i][h] = Z_ih . aL_h, right[i][h] = Z_ih . aR_h.
+ * precision BF16: x must be BF16 [n][ldx] and the product runs on tcgen05
+ *   tensor cores (BF16 RNE(W)); FP32: x FP32 [n][ldx], FP32 CUDA-core GEMM.
+ * Outputs (each may be NULL): h = Z in h_dtype [n][ldh] (BF16 RNE or FP32),
+ * left/right FP32 [n][heads]. */
+int gat_b200_projection(const gat_b200_layer* p, uint64_t n, const void* x, int ldx, int precision,
+                        void* h, int h_dtype, int ldh, float* left, float* right, void* stream);
+
+/* m[i][h] = leaky(L_ih + max_{j in N(i)} R_jh), 0 for empty rows.
+ * Replaces gat::max_prescan (baseline/src/baseline_standard.cpp:44-51). */
+int gat_b200_max_prescan(const gat_b200_graph* g, int heads, const float* left, const float* right,
+                         float* max, void* stream);
+
+/* Edge softmax + weighted aggregation writing the UNNORMALIZED out[n][heads*dim]
+ * (FP32, stride ldo) and den[n][heads] (and max[n][heads] if not NULL).
+ * Replaces gat::standard_aggregate (baseline/src/baseline_standard.cpp:52-84).
+ * With fixed_p ([e][heads]) the weights come from it and den from fixed_den,
+ * as the reference's fixed-p mode (baseline/bench/main.cpp:132). */
+int gat_b200_standard_aggregate(const gat_b200_graph* g, int heads, int dim, const void* h,
+                                int h_dtype, int ldh, const float* left, const float* right,
+                                const float* fixed_p, const float* fixed_den, float* out, int ldo,
+                                float* den, float* max, void* stream);
+
+/* out *= (den>0 ? 1/den : 0), then ELU if hidden. Replaces gat::finish
+ * (baseline/src/baseline_standard.cpp:85-97). FP32 out [n][ldo]. */
+int gat_b200_finish(uint64_t n, int heads, int dim, const float* den, int hidden, float* out,
+                    int ldo, void* stream);
+
+/* The fused hot kernel: edge softmax with an online (running max/sum) update,
+ * weighted aggregation, normalisation, ELU when hidden, and the store in
+ * out_dtype (BF16 RNE = the next layer's input, which equals the reference's
+ * convert() of its FP32 output). Replaces the sequence max_prescan +
+ * standard_aggregate + finish (+ convert of the next layer) of gat::standard_layer
+ * (baseline/src/baseline_standard.cpp:98-108). */
+int gat_b200_aggregate_fused(const gat_b200_graph* g, int heads, int dim, const void* h,
+                             int h_dtype, int ldh, const float* left, const float* right,
+                             int hidden, void* out, int out_dtype, int ldo, void* stream);
+
+/* One full layer on device buffers. Replaces gat::standard_layer
+ * (baseline/src/baseline_standard.cpp:98-108) for path STANDARD_BF16 (x BF16)
+ * or STANDARD_FP32 (x FP32). Scratch: h [n][ldh] (BF16 for STANDARD_BF16, FP32
+ * otherwise, ldh = gat_b200_padded_ld(heads*dim, that dtype)), left/right
+ * [n][heads]. Output as in gat_b200_aggregate_fused. */
+int gat_b200_standard_layer(const gat_b200_graph* g, const gat_b200_layer* p, const void* x,
+                            int ldx, int path, int hidden, void* h, float* left, float* right,
+                            void* out, int out_dtype, int ldo, void* stream);
+
+/* Reports (and clears) a device-side failure recorded by an earlier kernel:
+ * GAT_B200_ETIMEOUT if a bounded wait inside a kernel gave up. Synchronizes
+ * with the device. */
+int gat_b200_check_device(void);
+
+/* ======================================================================== *
+ *  Device: three-layer model (the benchmarked forward)                     *
+ * ======================================================================== */
+
+typedef struct gat_b200_model gat_b200_model;
+
+/* Binds a graph and the three prepared layers, allocating every device buffer
+ * the forward needs up front (the reference allocates all workspaces before
+ * timing, baseline/bench/main.cpp:156). The layers must chain:
+ * in(l+1) == heads(l)*dim(l). */
+int gat_b200_model_create(const gat_b200_graph* g, const gat_b200_layer* const* layers, int path,
+                          gat_b200_model** out);
+int gat_b200_model_destroy(gat_b200_model* m);
+/* Three-layer forward: layers 1-2 hidden (ELU), layer 3 logits, as the
+ * reference's model loop (baseline/bench/main.cpp:171-172). x: FP32 [n][din]
+ * (dense rows) in host memory (x_on_host=1) or device memory; logits: FP32
+ * [n][classes] (dense rows) in host or device memory. Host buffers should be
+ * pinned for asynchronous copies. Work is enqueued on `stream`; when logits
+ * are in host memory the call returns after the copy completed. */
+int gat_b200_model_forward(gat_b200_model* m, const float* x, int x_on_host, float* logits,
+                           int logits_on_host, void* stream);
+/* Per-stage timing, the device counterpart of the reference's Times and its
+ * per-layer JSON fields (baseline/include/gat.hpp:68-76, common.cpp:155-170).
+ * enable_timing(m, k) records CUDA events around every stage of the next
+ * forwards into a ring of k sets (0 disables). stage_times waits for them and
+ * writes ms[set*9 + stage] for stages {h2d, convert, projection L1, aggregation
+ * L1, projection L2, aggregation L2, projection L3, aggregation L3, d2h};
+ * returns the number of sets written (or a negative status on error). */
+int gat_b200_model_enable_timing(gat_b200_model* m, int steps);
+int gat_b200_model_stage_times(gat_b200_model* m, float* ms);
+/* Number of kernels the last forward launched. */
+int gat_b200_model_launches(const gat_b200_model* m);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,145 @@
+// Golden-vector harness (test infrastructure): links the reference's own
+// sources, compiled in place by oracle/Makefile, calls the reference functions
+// and writes their outputs as raw little-endian files for
+// tests/golden/make_golden.py. Nothing here is part of libgat_b200.so.
+//
+//   ref_dump boundary OUTDIR          64 D/K/d cases of baseline/tests/boundaries.cpp
+//   ref_dump chain GRAPH WEIGHTS OUTDIR   three-layer chains on a GATBIN1 graph;
+//                                     WEIGHTS = GATWGT1 path or "seed:N" (random_model)
+#include "gat.hpp"
+
+#include <cstdio>
+#include <iostream>
+#include <random>
+
+using namespace gat;
+
+static void dump(const std::string& path, const void* data, size_t bytes) {
+    std::ofstream f(path, std::ios::binary);
+    f.write(static_cast<const char*>(data), std::streamsize(bytes));
+    if (!f) throw std::runtime_error("cannot write " + path);
+}
+template <class T>
+static void dumpv(const std::string& path, const std::vector<T>& v) { dump(path, v.data(), v.size() * sizeof(T)); }
+
+// Test inputs of baseline/tests/boundaries.cpp:8-13 (restated: that file keeps
+// them in static functions). 35 nodes, degrees cycling through
+// {0,1,2,15,16,17,31,32,33,63,64,65,129}, x = 0.5 sin(0.17 i).
+static Param boundary_params(int D, int K, int d) {
+    Param p;
+    p.in = D; p.heads = K; p.dim = d;
+    p.w.resize(size_t(D) * K * d); p.al.resize(size_t(K) * d); p.ar.resize(size_t(K) * d);
+    std::mt19937 rng(D + K + d);
+    std::uniform_real_distribution<float> rnd(-.3, .3);
+    for (auto& x : p.w) x = rnd(rng);
+    for (auto& x : p.al) x = rnd(rng);
+    for (auto& x : p.ar) x = rnd(rng);
+    return p;
+}
+static Graph boundary_graph(int D) {
+    Graph g;
+    g.n = 35; g.din = D; g.classes = 40; g.row = {0};
+    const int deg[] = {0, 1, 2, 15, 16, 17, 31, 32, 33, 63, 64, 65, 129};
+    for (uint64_t i = 0; i < g.n; ++i) {
+        int count = deg[i % 13];
+        for (int e = 0; e < count; ++e) g.col.push_back(uint32_t((i * 3 + e * 7) % g.n));
+        g.row.push_back(g.col.size());
+    }
+    g.e = g.col.size();
+    g.x.resize(g.n * D);
+    for (size_t i = 0; i < g.x.size(); ++i) g.x[i] = std::sin(float(i) * .17f) * .5f;
+    g.validate();
+    return g;
+}
+
+static int boundary(const std::string& out) {
+    for (int D : {17, 33, 128, 256})
+        for (int K : {1, 2, 4, 8})
+            for (int d : {7, 32, 40, 47}) {
+                Graph g = boundary_graph(D);
+                Param p = boundary_params(D, K, d);
+                Prepared q = prepare(p);
+                Workspace r, b, f;
+                r.allocate(g, p, "ref_fp32");
+                b.allocate(g, p, "standard_bf16");
+                f.allocate(g, p, "standard_fp32");
+                Times t;
+                ref_layer(g, p, g.x, r, false, t);
+                standard_layer(g, p, q, g.x, b, false, t, false);
+                standard_layer(g, p, q, g.x, f, false, t, true);
+                std::string pre = out + "/bnd_" + std::to_string(D) + "_" + std::to_string(K) + "_" + std::to_string(d);
+                dumpv(pre + "_ref.f32", r.out);
+                dumpv(pre + "_b0bf16.f32", b.out);
+                dumpv(pre + "_b0fp32.f32", f.out);
+                dumpv(pre + "_w.f32", p.w);
+                dumpv(pre + "_al.f32", p.al);
+                dumpv(pre + "_ar.f32", p.ar);
+            }
+    Graph g = boundary_graph(17);
+    Schedule s = degree_schedule(g);
+    dumpv(out + "/bnd_perm.u32", s.perm);
+    dump(out + "/bnd_steps.u64", &s.neighbor_steps, 8);
+    dumpv(out + "/bnd_row.u64", g.row);
+    dumpv(out + "/bnd_col.u32", g.col);
+    std::cout << "BOUNDARY_DUMP cases=64\n";
+    return 0;
+}
+
+static int chain(const std::string& graph, const std::string& weights, const std::string& out) {
+    Graph g = load_graph(graph);
+    Model model;
+    if (weights.rfind("seed:", 0) == 0) {
+        model = random_model(g.din, g.classes, std::stoi(weights.substr(5)));
+        save_model(model, out + "/weights.gatwgt");
+    } else {
+        model = load_model(weights, g.din, g.classes);
+    }
+    Schedule s = degree_schedule(g);
+    dumpv(out + "/perm.u32", s.perm);
+    dump(out + "/steps.u64", &s.neighbor_steps, 8);
+    // R0 chain with per-layer intermediates.
+    std::vector<float> input = g.x;
+    for (int l = 0; l < 3; ++l) {
+        Workspace w;
+        w.allocate(g, model[l], "ref_fp32");
+        Times t;
+        ref_layer(g, model[l], input, w, l < 2, t);
+        std::string pre = out + "/ref_l" + std::to_string(l + 1);
+        dumpv(pre + "_left.f32", w.left);
+        dumpv(pre + "_right.f32", w.right);
+        dumpv(pre + "_max.f32", w.max);
+        dumpv(pre + "_den.f32", w.den);
+        dumpv(pre + "_out.f32", w.out);
+        input = std::move(w.out);
+    }
+    // B0 chains (each path consumes its own previous output, bench/main.cpp:95-96).
+    for (bool fp32 : {false, true}) {
+        std::vector<Prepared> prep;
+        for (const auto& p : model) prep.push_back(prepare(p));
+        std::vector<float> in = g.x;
+        for (int l = 0; l < 3; ++l) {
+            Workspace w;
+            w.allocate(g, model[l], fp32 ? "standard_fp32" : "standard_bf16");
+            Times t;
+            standard_layer(g, model[l], prep[l], in, w, l < 2, t, fp32);
+            in = std::move(w.out);
+        }
+        dumpv(out + (fp32 ? "/b0fp32_out.f32" : "/b0bf16_out.f32"), in);
+    }
+    std::cout << "CHAIN_DUMP n=" << g.n << " e=" << g.e << "\n";
+    return 0;
+}
+
+int main(int argc, char** argv) {
+    try {
+        omp_set_num_threads(8);
+        std::string mode = argc > 1 ? argv[1] : "";
+        if (mode == "boundary" && argc == 3) return boundary(argv[2]);
+        if (mode == "chain" && argc == 5) return chain(argv[2], argv[3], argv[4]);
+        std::cerr << "usage: ref_dump boundary OUTDIR | ref_dump chain GRAPH WEIGHTS OUTDIR\n";
+        return 2;
+    } catch (const std::exception& e) {
+        std::cerr << "FAIL " << e.what() << "\n";
+        return 1;
+    }
+}

@@ -1,0 +1,137 @@
+"""Regenerates the golden fixtures in tests/golden/ from the reference itself.
+
+Run in a container where the reference tree exists (REF, default
+/root/reference) after `make -C oracle all ref`:
+
+    python tests/golden/make_golden.py
+
+What it records (all produced by the reference's own code, compiled from its
+sources in place by oracle/Makefile; nothing here is hand-written):
+  * smoke1024.gatbin: the reference's committed test graph
+    (implementation/data/smoke1024.gatbin). It is regenerated here with the
+    reference's own algorithm (implementation/tools/prepare_smoke.py:9-23,
+    numpy default_rng(20260928)) and must hash to the committed file.
+  * smoke1024_seed11.npz: R0 three-layer chain on smoke1024 with the
+    reference's random_model(seed 11): per-layer left/right/max/den, final
+    logits, B0 BF16 / FP32 chain logits, degree_schedule perm and
+    neighbor_steps, and the hash of the GATWGT1 file the reference saved.
+  * config1.npz: the same dumps for the c1 graph and Glorot weights produced
+    by this repository's generator (GATBIN1 / GATWGT1 hashes recorded).
+  * boundary.npz: R0 (and for a subset B0 BF16) outputs of the 64 D/K/d
+    cases of baseline/tests/boundaries.cpp, plus its degree schedule.
+"""
+import hashlib
+import json
+import os
+import struct
+import subprocess
+import sys
+import tempfile
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parents[2]
+sys.path.insert(0, str(ROOT / "gat-tfs_b200"))
+import configs  # noqa: E402
+import gatb200 as G  # noqa: E402
+
+REF = Path(os.environ.get("REF", "/root/reference"))
+OUT = Path(__file__).resolve().parent
+DUMP = ROOT / "oracle" / "_ref" / "ref_dump"
+
+
+def sha256(path) -> str:
+    return hashlib.sha256(Path(path).read_bytes()).hexdigest()
+
+
+def write_smoke1024(path: Path):
+    """Same draws, in the same order, as implementation/tools/prepare_smoke.py:9-23."""
+    rng = np.random.default_rng(20260928)
+    n, d, c = 1024, 128, 40
+    degrees = [1, 2, 7, 15, 16, 17, 31, 32, 33, 63, 64, 65, 96, 127]
+    row, col = [0], []
+    for i in range(n):
+        deg = degrees[i % len(degrees)]
+        neighbors = rng.choice(n, size=deg - 1, replace=False).astype(np.uint32).tolist()
+        col.extend([i] + neighbors)
+        row.append(len(col))
+    x = rng.normal(0, 0.5, size=(n, d)).astype("<f4")
+    with path.open("wb") as f:
+        f.write(struct.pack("<8sQQII", b"GATBIN1\0", n, len(col), d, c))
+        np.asarray(row, dtype="<u8").tofile(f)
+        np.asarray(col, dtype="<u4").tofile(f)
+        x.tofile(f)
+
+
+def load(d: Path, name: str, dtype=np.float32):
+    return np.fromfile(d / name, dtype=dtype)
+
+
+def chain_npz(d: Path, n: int, classes: int) -> dict:
+    out = dict(perm=load(d, "perm.u32", np.uint32), steps=load(d, "steps.u64", np.uint64))
+    for l, k in ((1, 8), (2, 8), (3, 1)):
+        for s in ("left", "right", "max", "den"):
+            out[f"ref_l{l}_{s}"] = load(d, f"ref_l{l}_{s}.f32").reshape(n, k)
+    out["ref_logits"] = load(d, "ref_l3_out.f32").reshape(n, classes)
+    out["b0bf16_logits"] = load(d, "b0bf16_out.f32").reshape(n, classes)
+    out["b0fp32_logits"] = load(d, "b0fp32_out.f32").reshape(n, classes)
+    return out
+
+
+def main():
+    if not DUMP.exists():
+        sys.exit("build the reference harness first: make -C oracle all ref")
+    manifest = {}
+    with tempfile.TemporaryDirectory() as tmp:
+        tmp = Path(tmp)
+        # smoke1024
+        smoke = tmp / "smoke1024.gatbin"
+        write_smoke1024(smoke)
+        manifest["smoke1024_gatbin_sha256"] = sha256(smoke)
+        ref_file = REF / "implementation" / "data" / "smoke1024.gatbin"
+        if ref_file.exists():
+            assert sha256(ref_file) == manifest["smoke1024_gatbin_sha256"], "smoke1024 regeneration differs"
+            manifest["smoke1024_matches_reference_file"] = True
+        d = tmp / "smoke"
+        d.mkdir()
+        subprocess.run([str(DUMP), "chain", str(smoke), "seed:11", str(d)], check=True)
+        manifest["smoke1024_seed11_gatwgt_sha256"] = sha256(d / "weights.gatwgt")
+        np.savez_compressed(OUT / "smoke1024_seed11.npz", **chain_npz(d, 1024, 40))
+
+        # c1 from this repository's generator
+        cfg = configs.make("c1")
+        g1, w1 = tmp / "c1.gatbin", tmp / "c1.gatwgt"
+        G.save_graph(cfg.graph, g1)
+        G.save_model(cfg.model, w1)
+        manifest["config1_gatbin_sha256"] = sha256(g1)
+        manifest["config1_gatwgt_sha256"] = sha256(w1)
+        d = tmp / "c1"
+        d.mkdir()
+        subprocess.run([str(DUMP), "chain", str(g1), str(w1), str(d)], check=True)
+        np.savez_compressed(OUT / "config1.npz", **chain_npz(d, 1024, 40))
+
+        # boundaries.cpp cases
+        d = tmp / "bnd"
+        d.mkdir()
+        subprocess.run([str(DUMP), "boundary", str(d)], check=True)
+        b = dict(perm=load(d, "bnd_perm.u32", np.uint32), steps=load(d, "bnd_steps.u64", np.uint64),
+                 row=load(d, "bnd_row.u64", np.uint64), col=load(d, "bnd_col.u32", np.uint32))
+        for D in (17, 33, 128, 256):
+            for K in (1, 2, 4, 8):
+                for dd in (7, 32, 40, 47):
+                    key = f"{D}_{K}_{dd}"
+                    b["ref_" + key] = load(d, f"bnd_{key}_ref.f32").reshape(35, K * dd)
+                    if D in (17, 256) and K in (1, 8):
+                        b["b0bf16_" + key] = load(d, f"bnd_{key}_b0bf16.f32").reshape(35, K * dd)
+                    # Pins oracle_boundary_params to the reference's draws.
+                    b["wsum_" + key] = np.array([load(d, f"bnd_{key}_w.f32").astype(np.float64).sum(),
+                                                 load(d, f"bnd_{key}_al.f32").astype(np.float64).sum(),
+                                                 load(d, f"bnd_{key}_ar.f32").astype(np.float64).sum()])
+        np.savez_compressed(OUT / "boundary.npz", **b)
+    (OUT / "MANIFEST.json").write_text(json.dumps(manifest, indent=1, sort_keys=True) + "\n")
+    print(json.dumps(manifest, indent=1))
+
+
+if __name__ == "__main__":
+    main()
