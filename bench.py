@@ -51,14 +51,14 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", default=CONFIG, choices=["c1", "c2", "c4"])
+    ap.add_argument("--config", default=CONFIG, choices=["c1", "c2", "c4", "c4s"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
 
 # --------------------------------------------------------------------- clocks
 class Clocks:
-    """nvidia-smi samples (every 200 ms) while the timed region runs."""
+    """nvidia-smi samples (every 100 ms) while the timed region runs."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -72,7 +72,7 @@ class Clocks:
     def start(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
                  "-i", str(self.device)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()

@@ -13,6 +13,7 @@ counts, degree tails, feature widths, classes) with seeded generators
       W 256x256 Glorot.
   c4  products-like: 2,449,029 nodes, 126,167,053 edges incl. self loops,
       power-law degrees (gamma 2.1, max 17,482), X ~ N(0,1) x100, classes 47.
+  c4s c4 scaled down 4x (profiler captures only).
 """
 from __future__ import annotations
 
@@ -26,6 +27,9 @@ SPECS = {
     "c1": dict(kind="uniform", n=1024, sources=15, din=128, classes=40, seed=1),
     "c2": dict(kind="powerlaw", n=169_343, e=2_484_941, max_degree=13_162, gamma=2.1, din=128, classes=40, seed=2),
     "c4": dict(kind="powerlaw", n=2_449_029, e=126_167_053, max_degree=17_482, gamma=2.1, din=100, classes=47, seed=4),
+    # c4 scaled down 4x in nodes and edges (same mean degree and model) for
+    # profiler captures: its features (0.3 GB per layer) still exceed L2.
+    "c4s": dict(kind="powerlaw", n=612_257, e=31_541_763, max_degree=8_000, gamma=2.1, din=100, classes=47, seed=4),
 }
 
 
