@@ -126,186 +126,284 @@ __device__ __forceinline__ float finalize(const AggArgs& a, int c, float acc, fl
     return a.hidden ? elu(v) : v;
 }
 
+// ---- asynchronous pipeline -------------------------------------------------
+__device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+enum : int { kValid = 1, kFirst = 2, kLast = 4, kPartial = 8 };
+
+// One chunk (at most C edges) of a work item, identical in every lane.
+struct Rec {
+    uint64_t item;  // work item: segment index (< n_seg) or row item
+    uint64_t pos;   // first edge of the chunk
+    uint32_t r;     // destination row
+    int cnt;        // edges in the chunk (0 for an empty row)
+    int flags;
+};
+
+// Per-chunk record handed from the scoring stage to the consuming stage.
+template <int C, int KM>
+struct __align__(16) Slot {
+    float p[C * KM];  // p[t*KM + h]
+    float sc[8];      // rescale of the running sums before this chunk
+    float den[8];     // final sums (last chunk of an item)
+    float m[8];       // final maxima (last chunk of an item)
+    uint32_t src[C];
+    uint64_t item;
+    uint32_t r;
+    int cnt;
+    int flags;
+};
+
+// Walks this warp's work items (gw, gw+G, ...) chunk by chunk. Item metadata
+// is fetched two items ahead (segment or permutation entry) and one item
+// ahead (row pointers), so a new item's bounds are in registers when needed.
+template <int C>
+struct Gen {
+    uint64_t total, G;
+    uint64_t item, beg, pos, end;
+    uint32_t r;
+    bool partial, have;
+    uint64_t n_item, n_beg, n_end;  // next item
+    uint32_t n_r;
+    bool n_partial, n_have;
+    uint64_t nn_item, nn_beg, nn_end;  // item after next (stage 1 only for rows)
+    uint32_t nn_r;
+    bool nn_partial, nn_have;
+
+    __device__ __forceinline__ void stage1(const AggArgs& a, uint64_t it, uint32_t& rr, uint64_t& b, uint64_t& e,
+                                           bool& part, bool& hv) {
+        hv = it < total;
+        part = false;
+        b = e = 0;
+        rr = 0;
+        if (!hv) return;
+        if (it < a.n_seg) {
+            const Segment* sg = a.segs + it;
+            rr = sg->row;
+            b = sg->beg;
+            e = sg->end;
+            part = true;
+        } else {
+            rr = a.perm[a.n - 1 - a.n_hub - (it - a.n_seg)];
+        }
+    }
+    __device__ __forceinline__ void stage2(const AggArgs& a, uint32_t rr, uint64_t& b, uint64_t& e, bool part,
+                                           bool hv) {
+        if (hv && !part) {
+            b = a.row[rr];
+            e = a.row[rr + 1];
+        }
+    }
+    __device__ __forceinline__ void init(const AggArgs& a, uint64_t gw, uint64_t g_, uint64_t tot) {
+        total = tot;
+        G = g_;
+        item = gw;
+        stage1(a, item, r, beg, end, partial, have);
+        stage2(a, r, beg, end, partial, have);
+        pos = beg;
+        n_item = gw + G;
+        stage1(a, n_item, n_r, n_beg, n_end, n_partial, n_have);
+        stage2(a, n_r, n_beg, n_end, n_partial, n_have);
+        nn_item = gw + 2 * G;
+        stage1(a, nn_item, nn_r, nn_beg, nn_end, nn_partial, nn_have);
+    }
+    __device__ __forceinline__ Rec next(const AggArgs& a) {
+        Rec rec;
+        rec.flags = 0;
+        rec.cnt = 0;
+        rec.item = item;
+        rec.pos = pos;
+        rec.r = r;
+        if (!have) return rec;
+        const uint64_t rem = end - pos;
+        rec.cnt = int(rem < uint64_t(C) ? rem : uint64_t(C));
+        rec.flags = kValid | (pos == beg ? kFirst : 0) | (rem <= uint64_t(C) ? kLast : 0) | (partial ? kPartial : 0);
+        pos += C;
+        if (pos >= end) {  // move to the next item
+            item = n_item; r = n_r; beg = n_beg; end = n_end; partial = n_partial; have = n_have;
+            pos = beg;
+            n_item = nn_item; n_r = nn_r; n_beg = nn_beg; n_end = nn_end; n_partial = nn_partial; n_have = nn_have;
+            stage2(a, n_r, n_beg, n_end, n_partial, n_have);
+            nn_item = n_item + G;
+            stage1(a, nn_item, nn_r, nn_beg, nn_end, nn_partial, nn_have);
+        }
+        return rec;
+    }
+};
+
 // KT: heads known at compile time (1 or 8), 0 = runtime heads <= 8.
-// LPE lanes share one edge's feature row; VPL 16-byte vectors per lane.
-// MIXED: a vector may straddle heads (dim not a multiple of the vector width).
-template <class HT, int KT, int LPE, int VPL, bool MIXED>
-__global__ void __launch_bounds__(kWarps * 32) agg_kernel(const AggArgs a) {
+// C: edges per chunk. LPE lanes share one feature row in the gather; VPL
+// 16-byte vectors per lane. MIXED: a vector may straddle two heads.
+//
+// Per warp, per loop iteration (one chunk k):
+//   1. scores of chunk k (col and R were prefetched one and two iterations
+//      earlier), running max / sum update, p and the rescale factor to shared
+//      memory;
+//   2. cp.async of chunk k's feature rows into shared-memory buffer k%2;
+//   3. prefetch: R of chunk k+1, col of chunk k+2, metadata of later items;
+//   4. consume chunk k-1 from buffer (k-1)%2 (waiting only for that group).
+// Each lane copies exactly the 16-byte vectors it later consumes, so a lane
+// waits only for its own copies.
+template <class HT, int KT, int C, int LPE, int VPL, bool MIXED>
+__global__ void __launch_bounds__(256) agg_kernel(const AggArgs a) {
     using V = Vec<HT>;
     constexpr int VEC = V::N;
     constexpr int KM = KT ? KT : 8;
-    constexpr int EPS = 32 / LPE;               // edges per warp step
-    constexpr int U = (VPL == 1) ? 8 : (VPL == 2 ? 4 : 2);  // unroll: 8 loads in flight per lane
-    __shared__ float s_p[kWarps][32 * KM];
-    __shared__ uint32_t s_src[kWarps][32];
+    constexpr int SPL = 32 / C;                 // score lanes per edge
+    constexpr int KS = (KM + SPL - 1) / SPL;    // heads per score lane
+    constexpr int EPS = 32 / LPE;               // edges per consume step
+    constexpr int RV = LPE * VPL;               // 16-byte vectors per buffered row
+    constexpr int NT = C / EPS;                 // consume steps per chunk
+    static_assert(C * SPL == 32 && EPS * LPE == 32 && C % EPS == 0, "bad tiling");
+    using SlotT = Slot<C, KM>;
 
+    extern __shared__ __align__(16) uint8_t agg_smem[];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-    const int K = KT ? KT : a.heads;
-    const int es = lane / LPE, vl = lane % LPE;
-    const int nvec = (a.width + VEC - 1) / VEC;
-    float* sp = s_p[wib];
-    uint32_t* ss = s_src[wib];
-    const HT* H = static_cast<const HT*>(a.h);
+    const size_t warp_bytes = 2 * sizeof(SlotT) + size_t(2) * C * RV * 16;
+    uint8_t* wbase = agg_smem + wib * warp_bytes;
+    SlotT* slots = reinterpret_cast<SlotT*>(wbase);
+    uint4* bufs = reinterpret_cast<uint4*>(wbase + 2 * sizeof(SlotT));
+    const uint32_t bufs_s = static_cast<uint32_t>(__cvta_generic_to_shared(bufs));
 
-    // Head owning each of this lane's vectors (or elements when MIXED).
+    const int K = KT ? KT : a.heads;
+    const int t = lane % C, hs = lane / C;      // scoring role
+    const int es = lane / LPE, vl = lane % LPE; // gather / consume role
+    const int nvec = (a.width + VEC - 1) / VEC;
+    const HT* H = static_cast<const HT*>(a.h);
+    const bool fixed = a.fixed_p != nullptr;
+
     int hv[VPL];
     int hk[VPL][MIXED ? VEC : 1];
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
-        int v = vl + j * LPE;
+        const int v = vl + j * LPE;
         hv[j] = KT == 1 ? 0 : min((v * VEC) / a.dim, K - 1);
 #pragma unroll
         for (int k = 0; k < (MIXED ? VEC : 1); ++k) hk[j][k] = min((v * VEC + k) / a.dim, K - 1);
     }
 
     const uint64_t total = uint64_t(a.n_seg) + (a.n - a.n_hub);
-    const uint64_t gw = blockIdx.x * uint64_t(kWarps) + wib;
-    const uint64_t G = uint64_t(gridDim.x) * kWarps;
-    for (uint64_t item = gw; item < total; item += G) {
-        uint64_t beg, end, r;
-        bool partial = item < a.n_seg;
-        if (partial) {
-            Segment sg = a.segs[item];
-            r = sg.row;
-            beg = sg.beg;
-            end = sg.end;
-        } else {
-            r = a.perm[a.n - 1 - a.n_hub - (item - a.n_seg)];
-            beg = a.row[r];
-            end = a.row[r + 1];
-        }
-        float Lr[KM], m[KM], ls[KM];
-        bool have_l = false;
-        if constexpr (KT == 8) {
-            if (!a.fixed_p) {
-                float4 l0 = *reinterpret_cast<const float4*>(a.left + r * 8);
-                float4 l1 = *reinterpret_cast<const float4*>(a.left + r * 8 + 4);
-                Lr[0] = l0.x; Lr[1] = l0.y; Lr[2] = l0.z; Lr[3] = l0.w;
-                Lr[4] = l1.x; Lr[5] = l1.y; Lr[6] = l1.z; Lr[7] = l1.w;
-                have_l = true;
-            }
-        }
-        if (!have_l) {
-#pragma unroll
-            for (int h = 0; h < KM; ++h) Lr[h] = (h < K && !a.fixed_p) ? a.left[r * K + h] : 0.f;
-        }
-#pragma unroll
-        for (int h = 0; h < KM; ++h) {
-            m[h] = a.fixed_p ? 0.f : -INFINITY;
-            ls[h] = 0.f;
-        }
-        float acc[VPL][VEC];
-#pragma unroll
-        for (int j = 0; j < VPL; ++j)
-#pragma unroll
-            for (int k = 0; k < VEC; ++k) acc[j][k] = 0.f;
+    const uint64_t G = uint64_t(gridDim.x) * (blockDim.x >> 5);
+    const uint64_t gw = blockIdx.x * uint64_t(blockDim.x >> 5) + wib;
+    Gen<C> gen;
+    gen.init(a, gw, G, total);
 
-        for (uint64_t c0 = beg; c0 < end; c0 += 32) {
-            const int cnt = int(end - c0 < 32 ? end - c0 : 32);
-            // ---- scores of up to 32 edges, one per lane ----
-            float s[KM];
-            uint32_t src = 0;
-            if (lane < cnt) {
-                src = ldg_stream_u32(a.col + c0 + lane);
-                if (a.fixed_p) {
+    // Prefetch helpers (lane t of chunk rec).
+    auto load_col = [&](const Rec& rc) -> uint32_t {
+        return (rc.flags & kValid) && t < rc.cnt ? ldg_stream_u32(a.col + rc.pos + t) : 0u;
+    };
+    auto load_r = [&](const Rec& rc, uint32_t src, float (&o)[KS]) {
+        const bool ok = (rc.flags & kValid) && t < rc.cnt;
+        if (fixed) {
 #pragma unroll
-                    for (int h = 0; h < KM; ++h) s[h] = h < K ? a.fixed_p[(c0 + lane) * K + h] : 0.f;
-                } else if constexpr (KT == 8) {
-                    float4 r0 = __ldg(reinterpret_cast<const float4*>(a.right + uint64_t(src) * 8));
-                    float4 r1 = __ldg(reinterpret_cast<const float4*>(a.right + uint64_t(src) * 8 + 4));
-                    float rr[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
-#pragma unroll
-                    for (int h = 0; h < 8; ++h) s[h] = leaky(Lr[h] + rr[h]);
-                } else {
-#pragma unroll
-                    for (int h = 0; h < KM; ++h)
-                        s[h] = h < K ? leaky(Lr[h] + __ldg(a.right + uint64_t(src) * K + h)) : 0.f;
-                }
-            } else {
-#pragma unroll
-                for (int h = 0; h < KM; ++h) s[h] = a.fixed_p ? 0.f : -INFINITY;
+            for (int j = 0; j < KS; ++j) {
+                const int h = hs * KS + j;
+                o[j] = ok && h < K ? a.fixed_p[(rc.pos + t) * K + h] : 0.f;
             }
-            float sc[KM];
-            if (a.fixed_p) {
-#pragma unroll
-                for (int h = 0; h < KM; ++h) {
-                    sc[h] = 1.f;
-                    ls[h] += s[h];
-                    sp[lane * KM + h] = s[h];
-                }
-            } else {
-#pragma unroll
-                for (int h = 0; h < KM; ++h) {
-                    float nm = fmaxf(m[h], warp_max(s[h]));
-                    sc[h] = expf(m[h] - nm);  // exp(-inf) = 0 on the first chunk
-                    m[h] = nm;
-                    float p = lane < cnt ? expf(s[h] - nm) : 0.f;
-                    ls[h] = ls[h] * sc[h] + p;
-                    sp[lane * KM + h] = p;
-                }
-#pragma unroll
-                for (int j = 0; j < VPL; ++j) {
-                    if constexpr (MIXED) {
-#pragma unroll
-                        for (int k = 0; k < VEC; ++k) acc[j][k] *= pick(sc, hk[j][k]);
-                    } else {
-                        float f = pick(sc, hv[j]);
-#pragma unroll
-                        for (int k = 0; k < VEC; ++k) acc[j][k] *= f;
-                    }
-                }
-            }
-            ss[lane] = src;
-            __syncwarp();
-            // ---- weighted gather of the feature rows ----
-            for (int t0 = 0; t0 < cnt; t0 += EPS * U) {
-                uint4 raw[U][VPL];
-                float pw[U][VPL][MIXED ? VEC : 1];
-#pragma unroll
-                for (int u = 0; u < U; ++u) {
-                    const int t = t0 + u * EPS + es;
-                    const bool ok = t < cnt;
-                    const uint32_t sidx = ok ? ss[t] : 0u;
-#pragma unroll
-                    for (int j = 0; j < VPL; ++j) {
-                        const int v = vl + j * LPE;
-                        if (ok && v < nvec)
-                            raw[u][j] = ldg_nc_v4(H + uint64_t(sidx) * a.ldh + v * VEC);
-                        else
-                            raw[u][j] = make_uint4(0, 0, 0, 0);
-#pragma unroll
-                        for (int k = 0; k < (MIXED ? VEC : 1); ++k)
-                            pw[u][j][k] = ok ? sp[t * KM + (MIXED ? hk[j][k] : hv[j])] : 0.f;
-                    }
-                }
-#pragma unroll
-                for (int u = 0; u < U; ++u)
-#pragma unroll
-                    for (int j = 0; j < VPL; ++j) {
-                        float f[VEC];
-                        V::unpack(raw[u][j], f);
-#pragma unroll
-                        for (int k = 0; k < VEC; ++k) acc[j][k] = fmaf(pw[u][j][MIXED ? k : 0], f[k], acc[j][k]);
-                    }
-            }
-            __syncwarp();
+            return;
         }
-        // ---- combine edge slots and lanes ----
+        if constexpr (KT == 8 && KS == 4) {
+            if (ok) {
+                const float4 v = __ldg(reinterpret_cast<const float4*>(a.right + uint64_t(src) * 8 + hs * 4));
+                o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w;
+            } else {
 #pragma unroll
-        for (int o = LPE; o < 32; o <<= 1)
+                for (int j = 0; j < KS; ++j) o[j] = 0.f;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < KS; ++j) {
+                const int h = hs * KS + j;
+                o[j] = ok && h < K ? __ldg(a.right + uint64_t(src) * K + h) : 0.f;
+            }
+        }
+    };
+    auto load_l = [&](const Rec& rc, float (&o)[KS]) {
+        const bool ok = (rc.flags & kValid) && (rc.flags & kFirst) && !fixed;
+#pragma unroll
+        for (int j = 0; j < KS; ++j) {
+            const int h = hs * KS + j;
+            o[j] = ok && h < K ? a.left[uint64_t(rc.r) * K + h] : 0.f;
+        }
+    };
+
+    Rec P1 = gen.next(a);
+    Rec P2 = gen.next(a);
+    uint32_t colP1 = load_col(P1);
+    float RP1[KS], LP1[KS];
+    load_r(P1, colP1, RP1);
+    load_l(P1, LP1);
+    uint32_t colP2 = load_col(P2);
+
+    float m[KS], ls[KS], Lr[KS];
+#pragma unroll
+    for (int j = 0; j < KS; ++j) { m[j] = -INFINITY; ls[j] = 0.f; Lr[j] = 0.f; }
+    float acc[VPL][VEC];
+#pragma unroll
+    for (int j = 0; j < VPL; ++j)
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) acc[j][k] = 0.f;
+
+    // Consumes the chunk in slot `sl` (its copies must be complete).
+    auto consume = [&](int sl) {
+        const SlotT& S = slots[sl];
+        const int flags = S.flags, cnt = S.cnt;
+        if (flags & kFirst) {
 #pragma unroll
             for (int j = 0; j < VPL; ++j)
 #pragma unroll
-                for (int k = 0; k < VEC; ++k) acc[j][k] += __shfl_xor_sync(kFull, acc[j][k], o);
-        float den[KM];
+                for (int k = 0; k < VEC; ++k) acc[j][k] = 0.f;
+        } else if (!fixed) {
 #pragma unroll
-        for (int h = 0; h < KM; ++h) den[h] = warp_sum(ls[h]);
-
-        if (partial) {
-            float* st = a.seg_state + item * kSegStateFloats;
+            for (int j = 0; j < VPL; ++j)
+#pragma unroll
+                for (int k = 0; k < VEC; ++k) acc[j][k] *= S.sc[MIXED ? hk[j][k] : hv[j]];
+        }
+        const uint4* buf = bufs + size_t(sl) * C * RV;
+#pragma unroll 4
+        for (int i = 0; i < NT; ++i) {
+            const int tt = es + i * EPS;
+            if (tt >= cnt) break;
+#pragma unroll
+            for (int j = 0; j < VPL; ++j) {
+                const int v = vl + j * LPE;
+                if (v >= nvec) continue;
+                float f[VEC];
+                V::unpack(buf[tt * RV + v], f);
+                if constexpr (MIXED) {
+#pragma unroll
+                    for (int k = 0; k < VEC; ++k) acc[j][k] = fmaf(S.p[tt * KM + hk[j][k]], f[k], acc[j][k]);
+                } else {
+                    const float pw = S.p[tt * KM + hv[j]];
+#pragma unroll
+                    for (int k = 0; k < VEC; ++k) acc[j][k] = fmaf(pw, f[k], acc[j][k]);
+                }
+            }
+        }
+        if (!(flags & kLast)) return;
+        // ---- item complete: combine edge slots, then store ----
+        float out[VPL][VEC];
+#pragma unroll
+        for (int j = 0; j < VPL; ++j)
+#pragma unroll
+            for (int k = 0; k < VEC; ++k) {
+                float v = acc[j][k];
+#pragma unroll
+                for (int o = LPE; o < 32; o <<= 1) v += __shfl_xor_sync(kFull, v, o);
+                out[j][k] = v;
+            }
+        if (flags & kPartial) {
+            float* st = a.seg_state + S.item * kSegStateFloats;
             if (lane < K) {
-                st[lane] = pick(m, lane);
-                st[8 + lane] = pick(den, lane);
+                st[lane] = S.m[lane];
+                st[8 + lane] = S.den[lane];
             }
             if (es == 0)
 #pragma unroll
@@ -313,14 +411,14 @@ __global__ void __launch_bounds__(kWarps * 32) agg_kernel(const AggArgs a) {
                     const int v = vl + j * LPE;
                     if (v < nvec)
 #pragma unroll
-                        for (int k = 0; k < VEC; ++k) st[16 + v * VEC + k] = acc[j][k];
+                        for (int k = 0; k < VEC; ++k) st[16 + v * VEC + k] = out[j][k];
                 }
-            continue;
+            return;
         }
-        const bool empty = beg == end;
+        const uint64_t r = S.r;
         if (a.unnorm && lane < K) {
-            a.den_out[r * K + lane] = a.fixed_den ? a.fixed_den[r * K + lane] : pick(den, lane);
-            if (a.max_out && !a.fixed_p) a.max_out[r * K + lane] = empty ? 0.f : pick(m, lane);
+            a.den_out[r * K + lane] = a.fixed_den ? a.fixed_den[r * K + lane] : S.den[lane];
+            if (a.max_out && !fixed) a.max_out[r * K + lane] = S.m[lane];
         }
         if (es == 0) {
 #pragma unroll
@@ -330,12 +428,110 @@ __global__ void __launch_bounds__(kWarps * 32) agg_kernel(const AggArgs a) {
                 float o[VEC];
 #pragma unroll
                 for (int k = 0; k < VEC; ++k) {
-                    int hh = MIXED ? hk[j][k] : hv[j];
-                    o[k] = finalize(a, v * VEC + k, acc[j][k], pick(den, hh));
+                    const int hh = MIXED ? hk[j][k] : hv[j];
+                    o[k] = finalize(a, v * VEC + k, out[j][k], S.den[hh]);
                 }
                 store_out<VEC>(a, r, v * VEC, o);
             }
         }
+    };
+
+    int prev = -1;
+    for (int k = 0;; ++k) {
+        const Rec S = P1;
+        if (!(S.flags & kValid)) break;
+        const uint32_t colS = colP1;
+        float RS[KS], LS[KS];
+#pragma unroll
+        for (int j = 0; j < KS; ++j) { RS[j] = RP1[j]; LS[j] = LP1[j]; }
+        // ---- advance the prefetch pipeline ----
+        P1 = P2;
+        colP1 = colP2;
+        load_r(P1, colP1, RP1);
+        load_l(P1, LP1);
+        P2 = gen.next(a);
+        colP2 = load_col(P2);
+
+        // ---- 1. scores of chunk k ----
+        const int sl = k & 1;
+        SlotT& SL = slots[sl];
+        __syncwarp();
+        if (S.flags & kFirst) {
+#pragma unroll
+            for (int j = 0; j < KS; ++j) {
+                m[j] = fixed ? 0.f : -INFINITY;
+                ls[j] = 0.f;
+                Lr[j] = LS[j];
+            }
+        }
+        const bool ok = t < S.cnt;
+#pragma unroll
+        for (int j = 0; j < KS; ++j) {
+            const int h = hs * KS + j;
+            float p, sc;
+            if (fixed) {
+                p = ok ? RS[j] : 0.f;
+                sc = 1.f;
+            } else {
+                const float s = ok ? leaky(Lr[j] + RS[j]) : -INFINITY;
+                float cm = s;
+#pragma unroll
+                for (int o = 1; o < C; o <<= 1) cm = fmaxf(cm, __shfl_xor_sync(kFull, cm, o));
+                const float nm = fmaxf(m[j], cm);
+                sc = nm == -INFINITY ? 1.f : __expf(m[j] - nm);
+                p = ok ? __expf(s - nm) : 0.f;
+                m[j] = nm;
+            }
+            ls[j] = ls[j] * sc + p;
+            if (h < KM) SL.p[t * KM + h] = p;
+            if (t == 0 && h < 8) SL.sc[h] = sc;
+        }
+        if (S.flags & kLast) {
+#pragma unroll
+            for (int j = 0; j < KS; ++j) {
+                const int h = hs * KS + j;
+                float d = ls[j];
+#pragma unroll
+                for (int o = 1; o < C; o <<= 1) d += __shfl_xor_sync(kFull, d, o);
+                if (t == 0 && h < 8) {
+                    SL.den[h] = d;
+                    SL.m[h] = (S.cnt == 0 || fixed) ? 0.f : m[j];
+                }
+            }
+        }
+        if (hs == 0) SL.src[t] = colS;
+        if (lane == 0) {
+            SL.item = S.item;
+            SL.r = S.r;
+            SL.cnt = S.cnt;
+            SL.flags = S.flags;
+        }
+        __syncwarp();
+        // ---- 2. gather chunk k's feature rows ----
+        const uint32_t bs = bufs_s + uint32_t(sl) * C * RV * 16;
+#pragma unroll
+        for (int i = 0; i < NT; ++i) {
+            const int tt = es + i * EPS;
+            if (tt < S.cnt) {
+                const HT* row = H + uint64_t(SL.src[tt]) * a.ldh;
+#pragma unroll
+                for (int j = 0; j < VPL; ++j) {
+                    const int v = vl + j * LPE;
+                    if (v < nvec) cp_async16(bs + uint32_t(tt * RV + v) * 16, row + v * VEC);
+                }
+            }
+        }
+        cp_commit();
+        // ---- 4. consume chunk k-1 ----
+        if (prev >= 0) {
+            cp_wait<1>();
+            consume(prev);
+        }
+        prev = sl;
+    }
+    if (prev >= 0) {
+        cp_wait<0>();
+        consume(prev);
     }
 }
 
@@ -383,22 +579,28 @@ __global__ void __launch_bounds__(kWarps * 32) hub_merge_kernel(const AggArgs a)
     }
 }
 
-template <class HT, int KT, int LPE, int VPL, bool MIXED>
+template <class HT, int KT, int C, int LPE, int VPL, bool MIXED>
 int launch_agg(const AggArgs& a, cudaStream_t st) {
+    constexpr int KM = KT ? KT : 8;
+    constexpr size_t warp_bytes = 2 * sizeof(Slot<C, KM>) + size_t(2) * C * LPE * VPL * 16;
+    // Warps per block: up to 8 within ~100 KB of shared memory per block.
+    constexpr int wpb = warp_bytes * 8 <= 100 * 1024 ? 8 : (warp_bytes * 4 <= 100 * 1024 ? 4 : 2);
+    constexpr size_t smem = warp_bytes * wpb;
+    auto kern = agg_kernel<HT, KT, C, LPE, VPL, MIXED>;
     static int grid = 0;  // resident blocks (per process; all B200s are alike)
     if (!grid) {
         int dev = 0, sms = 0, per_sm = 0;
         GATB_CUDA(cudaGetDevice(&dev));
         GATB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-        GATB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, agg_kernel<HT, KT, LPE, VPL, MIXED>,
-                                                                kWarps * 32, 0));
+        GATB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+        GATB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, wpb * 32, smem));
         grid = sms * (per_sm > 0 ? per_sm : 1);
     }
     uint64_t items = uint64_t(a.n_seg) + (a.n - a.n_hub);
-    uint64_t need = (items + kWarps - 1) / kWarps;
+    uint64_t need = (items + wpb - 1) / wpb;
     unsigned blocks = unsigned(need < uint64_t(grid) ? need : uint64_t(grid));
     if (blocks == 0) blocks = 1;
-    agg_kernel<HT, KT, LPE, VPL, MIXED><<<blocks, kWarps * 32, 0, st>>>(a);
+    kern<<<blocks, wpb * 32, smem, st>>>(a);
     GATB_LAUNCH("edge-softmax aggregation kernel");
     if (a.n_hub) {
         hub_merge_kernel<<<(a.n_hub + kWarps - 1) / kWarps, kWarps * 32, 0, st>>>(a);
@@ -457,15 +659,15 @@ int aggregate_dispatch(const gat_b200_graph* g, int heads, int dim, const void* 
     if (h_dtype == GAT_B200_BF16) {
         if (heads == 8 && dim == 32 && (reinterpret_cast<uintptr_t>(left) & 15) == 0 &&
             (reinterpret_cast<uintptr_t>(right) & 15) == 0)
-            return launch_agg<uint16_t, 8, 32, 1, false>(a, st);
-        if (heads == 1 && width <= 64) return launch_agg<uint16_t, 1, 8, 1, false>(a, st);
-        return launch_agg<uint16_t, 0, 32, 2, true>(a, st);
+            return launch_agg<uint16_t, 8, 16, 32, 1, false>(a, st);
+        if (heads == 1 && width <= 64) return launch_agg<uint16_t, 1, 32, 8, 1, false>(a, st);
+        return launch_agg<uint16_t, 0, 16, 32, 2, true>(a, st);
     }
     if (heads == 8 && dim == 32 && (reinterpret_cast<uintptr_t>(left) & 15) == 0 &&
         (reinterpret_cast<uintptr_t>(right) & 15) == 0)
-        return launch_agg<float, 8, 32, 2, false>(a, st);
-    if (heads == 1 && width <= 64) return launch_agg<float, 1, 16, 1, false>(a, st);
-    return launch_agg<float, 0, 32, 4, true>(a, st);
+        return launch_agg<float, 8, 16, 32, 2, false>(a, st);
+    if (heads == 1 && width <= 64) return launch_agg<float, 1, 32, 16, 1, false>(a, st);
+    return launch_agg<float, 0, 16, 32, 4, true>(a, st);
 }
 
 }  // namespace gatb
