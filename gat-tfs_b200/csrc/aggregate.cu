@@ -58,6 +58,32 @@ struct AggArgs {
     float* max_out;
 };
 
+// Packed FP32 pair (sm_100 f32x2 arithmetic; each half rounds like the scalar op).
+struct F2 {
+    unsigned long long v;
+};
+__device__ __forceinline__ F2 f2make(float lo, float hi) {
+    F2 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r.v) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ F2 f2zero() { return F2{0ull}; }
+__device__ __forceinline__ F2 f2fma(F2 a, F2 b, F2 c) {
+    F2 r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r.v) : "l"(a.v), "l"(b.v), "l"(c.v));
+    return r;
+}
+__device__ __forceinline__ F2 f2mul(F2 a, F2 b) {
+    F2 r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+    return r;
+}
+__device__ __forceinline__ float f2get(F2 a, int hi) {
+    float lo_f, hi_f;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo_f), "=f"(hi_f) : "l"(a.v));
+    return hi ? hi_f : lo_f;
+}
+
 template <class HT>
 struct Vec;
 template <>
@@ -123,7 +149,8 @@ __device__ __forceinline__ float finalize(const AggArgs& a, int c, float acc, fl
     if (c >= a.width) return 0.f;  // padding columns stay zero
     if (a.unnorm) return acc;
     float v = acc * (den > 0.f ? 1.f / den : 0.f);  // baseline_standard.cpp:115-117
-    return a.hidden ? elu(v) : v;
+    // ELU (gat.hpp:53): exp(x)-1 for x < 0, |error| < 3e-7 (values are >= -1).
+    return (a.hidden && v < 0.f) ? __expf(v) - 1.f : v;
 }
 
 // ---- asynchronous pipeline -------------------------------------------------
@@ -150,11 +177,10 @@ struct Rec {
 // Per-chunk record handed from the scoring stage to the consuming stage.
 template <int C, int KM>
 struct __align__(16) Slot {
-    float p[C * KM];  // p[t*KM + h]
+    float p[KM * (C + 1)];  // p[h*(C+1) + t]: conflict-free stores and reads
     float sc[8];      // rescale of the running sums before this chunk
     float den[8];     // final sums (last chunk of an item)
     float m[8];       // final maxima (last chunk of an item)
-    uint32_t src[C];
     uint64_t item;
     uint32_t r;
     int cnt;
@@ -251,7 +277,7 @@ struct Gen {
 //   4. consume chunk k-1 from buffer (k-1)%2 (waiting only for that group).
 // Each lane copies exactly the 16-byte vectors it later consumes, so a lane
 // waits only for its own copies.
-template <class HT, int KT, int C, int LPE, int VPL, bool MIXED>
+template <class HT, int KT, int C, int LPE, int VPL, bool MIXED, int NVC>
 __global__ void __launch_bounds__(256) agg_kernel(const AggArgs a) {
     using V = Vec<HT>;
     constexpr int VEC = V::N;
@@ -261,7 +287,10 @@ __global__ void __launch_bounds__(256) agg_kernel(const AggArgs a) {
     constexpr int EPS = 32 / LPE;               // edges per consume step
     constexpr int RV = LPE * VPL;               // 16-byte vectors per buffered row
     constexpr int NT = C / EPS;                 // consume steps per chunk
+    constexpr int CPL = (RV + SPL - 1) / SPL;   // vectors each lane copies per edge
+    constexpr int PS = C + 1;                   // p row stride (padding)
     static_assert(C * SPL == 32 && EPS * LPE == 32 && C % EPS == 0, "bad tiling");
+    static_assert(VEC % 2 == 0, "packed pairs");
     using SlotT = Slot<C, KM>;
 
     extern __shared__ __align__(16) uint8_t agg_smem[];
@@ -275,7 +304,7 @@ __global__ void __launch_bounds__(256) agg_kernel(const AggArgs a) {
     const int K = KT ? KT : a.heads;
     const int t = lane % C, hs = lane / C;      // scoring role
     const int es = lane / LPE, vl = lane % LPE; // gather / consume role
-    const int nvec = (a.width + VEC - 1) / VEC;
+    const int nvec = NVC ? NVC : (a.width + VEC - 1) / VEC;
     const HT* H = static_cast<const HT*>(a.h);
     const bool fixed = a.fixed_p != nullptr;
 
@@ -345,13 +374,14 @@ __global__ void __launch_bounds__(256) agg_kernel(const AggArgs a) {
     float m[KS], ls[KS], Lr[KS];
 #pragma unroll
     for (int j = 0; j < KS; ++j) { m[j] = -INFINITY; ls[j] = 0.f; Lr[j] = 0.f; }
-    float acc[VPL][VEC];
+    // Accumulators as packed FP32 pairs (fma.rn.f32x2 rounds each half like fmaf).
+    F2 acc[VPL][VEC / 2];
 #pragma unroll
     for (int j = 0; j < VPL; ++j)
 #pragma unroll
-        for (int k = 0; k < VEC; ++k) acc[j][k] = 0.f;
+        for (int k = 0; k < VEC / 2; ++k) acc[j][k] = f2zero();
 
-    // Consumes the chunk in slot `sl` (its copies must be complete).
+    // Consumes the chunk in slot `sl` (its copies must be complete and visible).
     auto consume = [&](int sl) {
         const SlotT& S = slots[sl];
         const int flags = S.flags, cnt = S.cnt;
@@ -359,31 +389,40 @@ __global__ void __launch_bounds__(256) agg_kernel(const AggArgs a) {
 #pragma unroll
             for (int j = 0; j < VPL; ++j)
 #pragma unroll
-                for (int k = 0; k < VEC; ++k) acc[j][k] = 0.f;
+                for (int k = 0; k < VEC / 2; ++k) acc[j][k] = f2zero();
         } else if (!fixed) {
 #pragma unroll
             for (int j = 0; j < VPL; ++j)
 #pragma unroll
-                for (int k = 0; k < VEC; ++k) acc[j][k] *= S.sc[MIXED ? hk[j][k] : hv[j]];
+                for (int k = 0; k < VEC / 2; ++k) {
+                    const float s0 = S.sc[MIXED ? hk[j][2 * k] : hv[j]];
+                    const float s1 = S.sc[MIXED ? hk[j][2 * k + 1] : hv[j]];
+                    acc[j][k] = f2mul(acc[j][k], f2make(s0, s1));
+                }
         }
         const uint4* buf = bufs + size_t(sl) * C * RV;
-#pragma unroll 4
+#pragma unroll
         for (int i = 0; i < NT; ++i) {
             const int tt = es + i * EPS;
-            if (tt >= cnt) break;
+            if (tt < cnt) {
 #pragma unroll
-            for (int j = 0; j < VPL; ++j) {
-                const int v = vl + j * LPE;
-                if (v >= nvec) continue;
-                float f[VEC];
-                V::unpack(buf[tt * RV + v], f);
-                if constexpr (MIXED) {
+                for (int j = 0; j < VPL; ++j) {
+                    const int v = vl + j * LPE;
+                    if (NVC == 0 && v >= nvec) continue;
+                    float f[VEC];
+                    V::unpack(buf[tt * RV + v], f);
+                    if constexpr (MIXED) {
 #pragma unroll
-                    for (int k = 0; k < VEC; ++k) acc[j][k] = fmaf(S.p[tt * KM + hk[j][k]], f[k], acc[j][k]);
-                } else {
-                    const float pw = S.p[tt * KM + hv[j]];
+                        for (int k = 0; k < VEC / 2; ++k)
+                            acc[j][k] = f2fma(f2make(f[2 * k], f[2 * k + 1]),
+                                              f2make(S.p[hk[j][2 * k] * PS + tt], S.p[hk[j][2 * k + 1] * PS + tt]),
+                                              acc[j][k]);
+                    } else {
+                        const float pw = S.p[hv[j] * PS + tt];
+                        const F2 pp = f2make(pw, pw);
 #pragma unroll
-                    for (int k = 0; k < VEC; ++k) acc[j][k] = fmaf(pw, f[k], acc[j][k]);
+                        for (int k = 0; k < VEC / 2; ++k) acc[j][k] = f2fma(f2make(f[2 * k], f[2 * k + 1]), pp, acc[j][k]);
+                    }
                 }
             }
         }
@@ -394,7 +433,7 @@ __global__ void __launch_bounds__(256) agg_kernel(const AggArgs a) {
         for (int j = 0; j < VPL; ++j)
 #pragma unroll
             for (int k = 0; k < VEC; ++k) {
-                float v = acc[j][k];
+                float v = f2get(acc[j][k / 2], k & 1);
 #pragma unroll
                 for (int o = LPE; o < 32; o <<= 1) v += __shfl_xor_sync(kFull, v, o);
                 out[j][k] = v;
@@ -409,7 +448,7 @@ __global__ void __launch_bounds__(256) agg_kernel(const AggArgs a) {
 #pragma unroll
                 for (int j = 0; j < VPL; ++j) {
                     const int v = vl + j * LPE;
-                    if (v < nvec)
+                    if (NVC != 0 || v < nvec)
 #pragma unroll
                         for (int k = 0; k < VEC; ++k) st[16 + v * VEC + k] = out[j][k];
                 }
@@ -483,7 +522,7 @@ __global__ void __launch_bounds__(256) agg_kernel(const AggArgs a) {
                 m[j] = nm;
             }
             ls[j] = ls[j] * sc + p;
-            if (h < KM) SL.p[t * KM + h] = p;
+            if (h < KM) SL.p[h * PS + t] = p;
             if (t == 0 && h < 8) SL.sc[h] = sc;
         }
         if (S.flags & kLast) {
@@ -499,38 +538,35 @@ __global__ void __launch_bounds__(256) agg_kernel(const AggArgs a) {
                 }
             }
         }
-        if (hs == 0) SL.src[t] = colS;
         if (lane == 0) {
             SL.item = S.item;
             SL.r = S.r;
             SL.cnt = S.cnt;
             SL.flags = S.flags;
         }
-        __syncwarp();
-        // ---- 2. gather chunk k's feature rows ----
-        const uint32_t bs = bufs_s + uint32_t(sl) * C * RV * 16;
+        // ---- 2. gather chunk k's feature rows: lane (t, hs) copies vectors
+        // hs, hs+SPL, ... of edge t's row into buffer k%2 ----
+        if (ok) {
+            const HT* row = H + uint64_t(colS) * a.ldh;
+            const uint32_t dst = bufs_s + uint32_t(sl) * C * RV * 16 + uint32_t(t) * RV * 16;
 #pragma unroll
-        for (int i = 0; i < NT; ++i) {
-            const int tt = es + i * EPS;
-            if (tt < S.cnt) {
-                const HT* row = H + uint64_t(SL.src[tt]) * a.ldh;
-#pragma unroll
-                for (int j = 0; j < VPL; ++j) {
-                    const int v = vl + j * LPE;
-                    if (v < nvec) cp_async16(bs + uint32_t(tt * RV + v) * 16, row + v * VEC);
-                }
+            for (int i = 0; i < CPL; ++i) {
+                const int v = hs + i * SPL;
+                if (v < RV && (NVC != 0 || v < nvec)) cp_async16(dst + uint32_t(v) * 16, row + v * VEC);
             }
         }
         cp_commit();
         // ---- 4. consume chunk k-1 ----
         if (prev >= 0) {
             cp_wait<1>();
+            __syncwarp();
             consume(prev);
         }
         prev = sl;
     }
     if (prev >= 0) {
         cp_wait<0>();
+        __syncwarp();
         consume(prev);
     }
 }
@@ -579,14 +615,14 @@ __global__ void __launch_bounds__(kWarps * 32) hub_merge_kernel(const AggArgs a)
     }
 }
 
-template <class HT, int KT, int C, int LPE, int VPL, bool MIXED>
+template <class HT, int KT, int C, int LPE, int VPL, bool MIXED, int NVC>
 int launch_agg(const AggArgs& a, cudaStream_t st) {
     constexpr int KM = KT ? KT : 8;
     constexpr size_t warp_bytes = 2 * sizeof(Slot<C, KM>) + size_t(2) * C * LPE * VPL * 16;
     // Warps per block: up to 8 within ~100 KB of shared memory per block.
     constexpr int wpb = warp_bytes * 8 <= 100 * 1024 ? 8 : (warp_bytes * 4 <= 100 * 1024 ? 4 : 2);
     constexpr size_t smem = warp_bytes * wpb;
-    auto kern = agg_kernel<HT, KT, C, LPE, VPL, MIXED>;
+    auto kern = agg_kernel<HT, KT, C, LPE, VPL, MIXED, NVC>;
     static int grid = 0;  // resident blocks (per process; all B200s are alike)
     if (!grid) {
         int dev = 0, sms = 0, per_sm = 0;
@@ -659,15 +695,15 @@ int aggregate_dispatch(const gat_b200_graph* g, int heads, int dim, const void* 
     if (h_dtype == GAT_B200_BF16) {
         if (heads == 8 && dim == 32 && (reinterpret_cast<uintptr_t>(left) & 15) == 0 &&
             (reinterpret_cast<uintptr_t>(right) & 15) == 0)
-            return launch_agg<uint16_t, 8, 16, 32, 1, false>(a, st);
-        if (heads == 1 && width <= 64) return launch_agg<uint16_t, 1, 32, 8, 1, false>(a, st);
-        return launch_agg<uint16_t, 0, 16, 32, 2, true>(a, st);
+            return launch_agg<uint16_t, 8, 16, 32, 1, false, 32>(a, st);
+        if (heads == 1 && width <= 64) return launch_agg<uint16_t, 1, 32, 8, 1, false, 0>(a, st);
+        return launch_agg<uint16_t, 0, 16, 32, 2, true, 0>(a, st);
     }
     if (heads == 8 && dim == 32 && (reinterpret_cast<uintptr_t>(left) & 15) == 0 &&
         (reinterpret_cast<uintptr_t>(right) & 15) == 0)
-        return launch_agg<float, 8, 16, 32, 2, false>(a, st);
-    if (heads == 1 && width <= 64) return launch_agg<float, 1, 32, 16, 1, false>(a, st);
-    return launch_agg<float, 0, 16, 32, 4, true>(a, st);
+        return launch_agg<float, 8, 16, 32, 2, false, 64>(a, st);
+    if (heads == 1 && width <= 64) return launch_agg<float, 1, 32, 16, 1, false, 0>(a, st);
+    return launch_agg<float, 0, 16, 32, 4, true, 0>(a, st);
 }
 
 }  // namespace gatb
