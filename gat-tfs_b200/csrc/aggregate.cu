@@ -58,32 +58,6 @@ struct AggArgs {
     float* max_out;
 };
 
-// Packed FP32 pair (sm_100 f32x2 arithmetic; each half rounds like the scalar op).
-struct F2 {
-    unsigned long long v;
-};
-__device__ __forceinline__ F2 f2make(float lo, float hi) {
-    F2 r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r.v) : "f"(lo), "f"(hi));
-    return r;
-}
-__device__ __forceinline__ F2 f2zero() { return F2{0ull}; }
-__device__ __forceinline__ F2 f2fma(F2 a, F2 b, F2 c) {
-    F2 r;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r.v) : "l"(a.v), "l"(b.v), "l"(c.v));
-    return r;
-}
-__device__ __forceinline__ F2 f2mul(F2 a, F2 b) {
-    F2 r;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
-    return r;
-}
-__device__ __forceinline__ float f2get(F2 a, int hi) {
-    float lo_f, hi_f;
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo_f), "=f"(hi_f) : "l"(a.v));
-    return hi ? hi_f : lo_f;
-}
-
 template <class HT>
 struct Vec;
 template <>
@@ -153,7 +127,9 @@ __device__ __forceinline__ float finalize(const AggArgs& a, int c, float acc, fl
     return (a.hidden && v < 0.f) ? __expf(v) - 1.f : v;
 }
 
-// ---- asynchronous pipeline -------------------------------------------------
+// Kept for gat_b200_check_device (this kernel has no waits that can time out).
+__device__ unsigned g_agg_error = 0;
+
 __device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g) : "memory");
 }
@@ -163,48 +139,63 @@ __device__ __forceinline__ void cp_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// Packed FP32 pair: sm_100 f32x2 arithmetic, each half rounded like fmaf.
+__device__ __forceinline__ unsigned long long pk(float lo, float hi) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ unsigned long long ffma2(unsigned long long a, unsigned long long b, unsigned long long c) {
+    unsigned long long r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ unsigned long long fmul2(unsigned long long a, unsigned long long b) {
+    unsigned long long r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ float2 upk(unsigned long long a) {
+    float2 f;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(f.x), "=f"(f.y) : "l"(a));
+    return f;
+}
+
 enum : int { kValid = 1, kFirst = 2, kLast = 4, kPartial = 8 };
 
-// One chunk (at most C edges) of a work item, identical in every lane.
+// One chunk of at most C edges of a work item (identical in every lane).
 struct Rec {
-    uint64_t item;  // work item: segment index (< n_seg) or row item
-    uint64_t pos;   // first edge of the chunk
-    uint32_t r;     // destination row
-    int cnt;        // edges in the chunk (0 for an empty row)
-    int flags;
+    uint32_t item, r, pos;
+    int cnt, flags;
 };
 
-// Per-chunk record handed from the scoring stage to the consuming stage.
+// Chunk record handed from scoring to consuming through shared memory.
 template <int C, int KM>
 struct __align__(16) Slot {
-    float p[KM * (C + 1)];  // p[h*(C+1) + t]: conflict-free stores and reads
-    float sc[8];      // rescale of the running sums before this chunk
-    float den[8];     // final sums (last chunk of an item)
-    float m[8];       // final maxima (last chunk of an item)
-    uint64_t item;
-    uint32_t r;
-    int cnt;
-    int flags;
+    float p[KM * (C + 1)];  // p[h*(C+1) + t]: conflict-free
+    float sc[8];            // rescale of the running sums before this chunk
+    float den[8];           // final sums (last chunk of an item)
+    float m[8];             // final maxima (last chunk of an item)
+    uint32_t item, r;
+    int cnt, flags;
 };
 
-// Walks this warp's work items (gw, gw+G, ...) chunk by chunk. Item metadata
-// is fetched two items ahead (segment or permutation entry) and one item
-// ahead (row pointers), so a new item's bounds are in registers when needed.
+// Walks this warp's work items (gw, gw+G, ...) chunk by chunk: items below
+// n_seg are hub-row segments, the rest rows in descending degree order. The
+// bounds of the next item are prefetched one item ahead and the permutation
+// entry of the item after it two items ahead. Edge positions fit 32 bits.
 template <int C>
 struct Gen {
-    uint64_t total, G;
-    uint64_t item, beg, pos, end;
-    uint32_t r;
+    uint32_t total, G;
+    uint32_t item, r, beg, pos, end;
     bool partial, have;
-    uint64_t n_item, n_beg, n_end;  // next item
-    uint32_t n_r;
+    uint32_t n_item, n_r, n_beg, n_end;
     bool n_partial, n_have;
-    uint64_t nn_item, nn_beg, nn_end;  // item after next (stage 1 only for rows)
-    uint32_t nn_r;
+    uint32_t nn_item, nn_r, nn_beg, nn_end;
     bool nn_partial, nn_have;
 
-    __device__ __forceinline__ void stage1(const AggArgs& a, uint64_t it, uint32_t& rr, uint64_t& b, uint64_t& e,
-                                           bool& part, bool& hv) {
+    __device__ __forceinline__ void stage1(const AggArgs& a, uint32_t it, uint32_t& rr, uint32_t& b, uint32_t& e,
+                                           bool& part, bool& hv) const {
         hv = it < total;
         part = false;
         b = e = 0;
@@ -213,21 +204,21 @@ struct Gen {
         if (it < a.n_seg) {
             const Segment* sg = a.segs + it;
             rr = sg->row;
-            b = sg->beg;
-            e = sg->end;
+            b = uint32_t(sg->beg);
+            e = uint32_t(sg->end);
             part = true;
         } else {
             rr = a.perm[a.n - 1 - a.n_hub - (it - a.n_seg)];
         }
     }
-    __device__ __forceinline__ void stage2(const AggArgs& a, uint32_t rr, uint64_t& b, uint64_t& e, bool part,
-                                           bool hv) {
+    __device__ __forceinline__ void stage2(const AggArgs& a, uint32_t rr, uint32_t& b, uint32_t& e, bool part,
+                                           bool hv) const {
         if (hv && !part) {
-            b = a.row[rr];
-            e = a.row[rr + 1];
+            b = uint32_t(a.row[rr]);
+            e = uint32_t(a.row[rr + 1]);
         }
     }
-    __device__ __forceinline__ void init(const AggArgs& a, uint64_t gw, uint64_t g_, uint64_t tot) {
+    __device__ __forceinline__ void init(const AggArgs& a, uint32_t gw, uint32_t g_, uint32_t tot) {
         total = tot;
         G = g_;
         item = gw;
@@ -237,22 +228,22 @@ struct Gen {
         n_item = gw + G;
         stage1(a, n_item, n_r, n_beg, n_end, n_partial, n_have);
         stage2(a, n_r, n_beg, n_end, n_partial, n_have);
-        nn_item = gw + 2 * G;
+        nn_item = n_item + G;
         stage1(a, nn_item, nn_r, nn_beg, nn_end, nn_partial, nn_have);
     }
     __device__ __forceinline__ Rec next(const AggArgs& a) {
         Rec rec;
-        rec.flags = 0;
-        rec.cnt = 0;
         rec.item = item;
-        rec.pos = pos;
         rec.r = r;
+        rec.pos = pos;
+        rec.cnt = 0;
+        rec.flags = 0;
         if (!have) return rec;
-        const uint64_t rem = end - pos;
-        rec.cnt = int(rem < uint64_t(C) ? rem : uint64_t(C));
-        rec.flags = kValid | (pos == beg ? kFirst : 0) | (rem <= uint64_t(C) ? kLast : 0) | (partial ? kPartial : 0);
+        const uint32_t rem = end - pos;
+        rec.cnt = int(rem < uint32_t(C) ? rem : uint32_t(C));
+        rec.flags = kValid | (pos == beg ? kFirst : 0) | (rem <= uint32_t(C) ? kLast : 0) | (partial ? kPartial : 0);
         pos += C;
-        if (pos >= end) {  // move to the next item
+        if (rem <= uint32_t(C)) {  // item finished: move to the next one
             item = n_item; r = n_r; beg = n_beg; end = n_end; partial = n_partial; have = n_have;
             pos = beg;
             n_item = nn_item; n_r = nn_r; n_beg = nn_beg; n_end = nn_end; n_partial = nn_partial; n_have = nn_have;
@@ -265,46 +256,51 @@ struct Gen {
 };
 
 // KT: heads known at compile time (1 or 8), 0 = runtime heads <= 8.
-// C: edges per chunk. LPE lanes share one feature row in the gather; VPL
-// 16-byte vectors per lane. MIXED: a vector may straddle two heads.
+// C: edges per chunk. LPE lanes share a feature row when copying and
+// consuming it, VPL 16-byte vectors each. MIXED: a vector may straddle heads.
 //
-// Per warp, per loop iteration (one chunk k):
-//   1. scores of chunk k (col and R were prefetched one and two iterations
-//      earlier), running max / sum update, p and the rescale factor to shared
-//      memory;
-//   2. cp.async of chunk k's feature rows into shared-memory buffer k%2;
-//   3. prefetch: R of chunk k+1, col of chunk k+2, metadata of later items;
-//   4. consume chunk k-1 from buffer (k-1)%2 (waiting only for that group).
-// Each lane copies exactly the 16-byte vectors it later consumes, so a lane
-// waits only for its own copies.
-template <class HT, int KT, int C, int LPE, int VPL, bool MIXED, int NVC>
-__global__ void __launch_bounds__(256) agg_kernel(const AggArgs a) {
+// Scoring layout: lane = (edge offset eo, head slot h). With 8 head slots 4
+// edges are scored per group (C/4 groups), so a head's chunk max and its row
+// sum need 2 shuffle steps; with one head every lane scores its own edge.
+//
+// Per warp and loop iteration (chunk k):
+//   1. scores of chunk k from col/R prefetched one and two iterations ago;
+//      running max, rescale factor and p to the chunk's shared-memory slot;
+//   2. cp.async of chunk k's feature rows into buffer k%2: lane (es, vl)
+//      copies vector vl (+LPE...) of edges es, es+32/LPE, ..., the source id
+//      arriving by shuffle from the scoring lane;
+//   3. prefetch R of chunk k+1 and col of chunk k+2;
+//   4. consume chunk k-1 (waiting only for this lane's own copies: a lane
+//      consumes exactly the vectors it copied).
+template <class HT, int KT, int C, int LPE, int VPL, bool MIXED>
+__global__ void __launch_bounds__(128) agg_kernel(const AggArgs a) {
     using V = Vec<HT>;
     constexpr int VEC = V::N;
     constexpr int KM = KT ? KT : 8;
-    constexpr int SPL = 32 / C;                 // score lanes per edge
-    constexpr int KS = (KM + SPL - 1) / SPL;    // heads per score lane
-    constexpr int EPS = 32 / LPE;               // edges per consume step
-    constexpr int RV = LPE * VPL;               // 16-byte vectors per buffered row
-    constexpr int NT = C / EPS;                 // consume steps per chunk
-    constexpr int CPL = (RV + SPL - 1) / SPL;   // vectors each lane copies per edge
-    constexpr int PS = C + 1;                   // p row stride (padding)
-    static_assert(C * SPL == 32 && EPS * LPE == 32 && C % EPS == 0, "bad tiling");
-    static_assert(VEC % 2 == 0, "packed pairs");
+    constexpr int HS = KT == 1 ? 1 : 8;  // score lanes per edge
+    constexpr int EG = 32 / HS;          // edges per score group
+    constexpr int NG = C / EG;           // score groups per chunk
+    constexpr int EPS = 32 / LPE;        // edges per copy/consume step
+    constexpr int NT = C / EPS;          // copy/consume steps per chunk
+    constexpr int RV = LPE * VPL;        // 16-byte vectors per buffered row
+    constexpr int PS = C + 1;            // p row stride
+    static_assert(NG >= 1 && NG * EG == C && NT * EPS == C, "bad tiling");
+    static_assert(HS == 1 || LPE == 32, "8 head slots need whole-warp rows");
     using SlotT = Slot<C, KM>;
 
     extern __shared__ __align__(16) uint8_t agg_smem[];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-    const size_t warp_bytes = 2 * sizeof(SlotT) + size_t(2) * C * RV * 16;
-    uint8_t* wbase = agg_smem + wib * warp_bytes;
+    constexpr size_t kWarpBytes = 2 * sizeof(SlotT) + size_t(2) * C * RV * 16;
+    uint8_t* wbase = agg_smem + wib * kWarpBytes;
     SlotT* slots = reinterpret_cast<SlotT*>(wbase);
-    uint4* bufs = reinterpret_cast<uint4*>(wbase + 2 * sizeof(SlotT));
+    const uint4* bufs = reinterpret_cast<const uint4*>(wbase + 2 * sizeof(SlotT));
     const uint32_t bufs_s = static_cast<uint32_t>(__cvta_generic_to_shared(bufs));
 
     const int K = KT ? KT : a.heads;
-    const int t = lane % C, hs = lane / C;      // scoring role
-    const int es = lane / LPE, vl = lane % LPE; // gather / consume role
-    const int nvec = NVC ? NVC : (a.width + VEC - 1) / VEC;
+    const int eo = lane / HS, hh = lane % HS;    // scoring role
+    const bool hok = hh < K;
+    const int es = lane / LPE, vl = lane % LPE;  // copy / consume role
+    const int nvec = (a.width + VEC - 1) / VEC;
     const HT* H = static_cast<const HT*>(a.h);
     const bool fixed = a.fixed_p != nullptr;
 
@@ -318,70 +314,49 @@ __global__ void __launch_bounds__(256) agg_kernel(const AggArgs a) {
         for (int k = 0; k < (MIXED ? VEC : 1); ++k) hk[j][k] = min((v * VEC + k) / a.dim, K - 1);
     }
 
-    const uint64_t total = uint64_t(a.n_seg) + (a.n - a.n_hub);
-    const uint64_t G = uint64_t(gridDim.x) * (blockDim.x >> 5);
-    const uint64_t gw = blockIdx.x * uint64_t(blockDim.x >> 5) + wib;
+    const uint32_t total = uint32_t(a.n_seg + (a.n - a.n_hub));
+    const uint32_t G = gridDim.x * (blockDim.x >> 5);
     Gen<C> gen;
-    gen.init(a, gw, G, total);
+    gen.init(a, blockIdx.x * (blockDim.x >> 5) + wib, G, total);
 
-    // Prefetch helpers (lane t of chunk rec).
-    auto load_col = [&](const Rec& rc) -> uint32_t {
-        return (rc.flags & kValid) && t < rc.cnt ? ldg_stream_u32(a.col + rc.pos + t) : 0u;
-    };
-    auto load_r = [&](const Rec& rc, uint32_t src, float (&o)[KS]) {
-        const bool ok = (rc.flags & kValid) && t < rc.cnt;
-        if (fixed) {
+    auto load_col = [&](const Rec& rc, uint32_t (&o)[NG]) {
 #pragma unroll
-            for (int j = 0; j < KS; ++j) {
-                const int h = hs * KS + j;
-                o[j] = ok && h < K ? a.fixed_p[(rc.pos + t) * K + h] : 0.f;
-            }
-            return;
-        }
-        if constexpr (KT == 8 && KS == 4) {
-            if (ok) {
-                const float4 v = __ldg(reinterpret_cast<const float4*>(a.right + uint64_t(src) * 8 + hs * 4));
-                o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w;
-            } else {
-#pragma unroll
-                for (int j = 0; j < KS; ++j) o[j] = 0.f;
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < KS; ++j) {
-                const int h = hs * KS + j;
-                o[j] = ok && h < K ? __ldg(a.right + uint64_t(src) * K + h) : 0.f;
-            }
+        for (int g = 0; g < NG; ++g) {
+            const int e = g * EG + eo;
+            o[g] = (rc.flags & kValid) && e < rc.cnt ? ldg_stream_u32(a.col + rc.pos + e) : 0u;
         }
     };
-    auto load_l = [&](const Rec& rc, float (&o)[KS]) {
-        const bool ok = (rc.flags & kValid) && (rc.flags & kFirst) && !fixed;
+    auto load_r = [&](const Rec& rc, const uint32_t (&c)[NG], float (&o)[NG]) {
 #pragma unroll
-        for (int j = 0; j < KS; ++j) {
-            const int h = hs * KS + j;
-            o[j] = ok && h < K ? a.left[uint64_t(rc.r) * K + h] : 0.f;
+        for (int g = 0; g < NG; ++g) {
+            const int e = g * EG + eo;
+            const bool ok = (rc.flags & kValid) && e < rc.cnt && hok;
+            if (fixed)
+                o[g] = ok ? a.fixed_p[(uint64_t(rc.pos) + e) * K + hh] : 0.f;
+            else
+                o[g] = ok ? __ldg(a.right + uint64_t(c[g]) * K + hh) : 0.f;
         }
+    };
+    auto load_l = [&](const Rec& rc) -> float {
+        return (rc.flags & kValid) && (rc.flags & kFirst) && hok && !fixed ? a.left[uint64_t(rc.r) * K + hh] : 0.f;
     };
 
     Rec P1 = gen.next(a);
     Rec P2 = gen.next(a);
-    uint32_t colP1 = load_col(P1);
-    float RP1[KS], LP1[KS];
+    uint32_t colP1[NG], colP2[NG];
+    float RP1[NG];
+    load_col(P1, colP1);
     load_r(P1, colP1, RP1);
-    load_l(P1, LP1);
-    uint32_t colP2 = load_col(P2);
+    float LP1 = load_l(P1);
+    load_col(P2, colP2);
 
-    float m[KS], ls[KS], Lr[KS];
-#pragma unroll
-    for (int j = 0; j < KS; ++j) { m[j] = -INFINITY; ls[j] = 0.f; Lr[j] = 0.f; }
-    // Accumulators as packed FP32 pairs (fma.rn.f32x2 rounds each half like fmaf).
-    F2 acc[VPL][VEC / 2];
+    float m = fixed ? 0.f : -INFINITY, ls = 0.f, Lr = 0.f;
+    unsigned long long acc[VPL][VEC / 2];
 #pragma unroll
     for (int j = 0; j < VPL; ++j)
 #pragma unroll
-        for (int k = 0; k < VEC / 2; ++k) acc[j][k] = f2zero();
+        for (int k = 0; k < VEC / 2; ++k) acc[j][k] = 0ull;
 
-    // Consumes the chunk in slot `sl` (its copies must be complete and visible).
     auto consume = [&](int sl) {
         const SlotT& S = slots[sl];
         const int flags = S.flags, cnt = S.cnt;
@@ -389,57 +364,61 @@ __global__ void __launch_bounds__(256) agg_kernel(const AggArgs a) {
 #pragma unroll
             for (int j = 0; j < VPL; ++j)
 #pragma unroll
-                for (int k = 0; k < VEC / 2; ++k) acc[j][k] = f2zero();
+                for (int k = 0; k < VEC / 2; ++k) acc[j][k] = 0ull;
         } else if (!fixed) {
 #pragma unroll
             for (int j = 0; j < VPL; ++j)
 #pragma unroll
-                for (int k = 0; k < VEC / 2; ++k) {
-                    const float s0 = S.sc[MIXED ? hk[j][2 * k] : hv[j]];
-                    const float s1 = S.sc[MIXED ? hk[j][2 * k + 1] : hv[j]];
-                    acc[j][k] = f2mul(acc[j][k], f2make(s0, s1));
-                }
+                for (int k = 0; k < VEC / 2; ++k)
+                    acc[j][k] = fmul2(acc[j][k], pk(S.sc[MIXED ? hk[j][2 * k] : hv[j]],
+                                                    S.sc[MIXED ? hk[j][2 * k + 1] : hv[j]]));
         }
         const uint4* buf = bufs + size_t(sl) * C * RV;
-#pragma unroll
+#pragma unroll 4
         for (int i = 0; i < NT; ++i) {
             const int tt = es + i * EPS;
+            if (i * EPS >= cnt) break;
             if (tt < cnt) {
 #pragma unroll
                 for (int j = 0; j < VPL; ++j) {
                     const int v = vl + j * LPE;
-                    if (NVC == 0 && v >= nvec) continue;
+                    if (v >= nvec) continue;
                     float f[VEC];
                     V::unpack(buf[tt * RV + v], f);
                     if constexpr (MIXED) {
 #pragma unroll
                         for (int k = 0; k < VEC / 2; ++k)
-                            acc[j][k] = f2fma(f2make(f[2 * k], f[2 * k + 1]),
-                                              f2make(S.p[hk[j][2 * k] * PS + tt], S.p[hk[j][2 * k + 1] * PS + tt]),
+                            acc[j][k] = ffma2(pk(f[2 * k], f[2 * k + 1]),
+                                              pk(S.p[hk[j][2 * k] * PS + tt], S.p[hk[j][2 * k + 1] * PS + tt]),
                                               acc[j][k]);
                     } else {
                         const float pw = S.p[hv[j] * PS + tt];
-                        const F2 pp = f2make(pw, pw);
+                        const unsigned long long pp = pk(pw, pw);
 #pragma unroll
-                        for (int k = 0; k < VEC / 2; ++k) acc[j][k] = f2fma(f2make(f[2 * k], f[2 * k + 1]), pp, acc[j][k]);
+                        for (int k = 0; k < VEC / 2; ++k) acc[j][k] = ffma2(pk(f[2 * k], f[2 * k + 1]), pp, acc[j][k]);
                     }
                 }
             }
         }
         if (!(flags & kLast)) return;
-        // ---- item complete: combine edge slots, then store ----
+        // ---- item complete ----
         float out[VPL][VEC];
 #pragma unroll
         for (int j = 0; j < VPL; ++j)
 #pragma unroll
-            for (int k = 0; k < VEC; ++k) {
-                float v = f2get(acc[j][k / 2], k & 1);
-#pragma unroll
-                for (int o = LPE; o < 32; o <<= 1) v += __shfl_xor_sync(kFull, v, o);
-                out[j][k] = v;
+            for (int k = 0; k < VEC / 2; ++k) {
+                const float2 f = upk(acc[j][k]);
+                out[j][2 * k] = f.x;
+                out[j][2 * k + 1] = f.y;
             }
+#pragma unroll
+        for (int o = LPE; o < 32; o <<= 1)
+#pragma unroll
+            for (int j = 0; j < VPL; ++j)
+#pragma unroll
+                for (int k = 0; k < VEC; ++k) out[j][k] += __shfl_xor_sync(kFull, out[j][k], o);
         if (flags & kPartial) {
-            float* st = a.seg_state + S.item * kSegStateFloats;
+            float* st = a.seg_state + uint64_t(S.item) * kSegStateFloats;
             if (lane < K) {
                 st[lane] = S.m[lane];
                 st[8 + lane] = S.den[lane];
@@ -448,7 +427,7 @@ __global__ void __launch_bounds__(256) agg_kernel(const AggArgs a) {
 #pragma unroll
                 for (int j = 0; j < VPL; ++j) {
                     const int v = vl + j * LPE;
-                    if (NVC != 0 || v < nvec)
+                    if (v < nvec)
 #pragma unroll
                         for (int k = 0; k < VEC; ++k) st[16 + v * VEC + k] = out[j][k];
                 }
@@ -466,10 +445,8 @@ __global__ void __launch_bounds__(256) agg_kernel(const AggArgs a) {
                 if (v * VEC >= a.ldo) continue;
                 float o[VEC];
 #pragma unroll
-                for (int k = 0; k < VEC; ++k) {
-                    const int hh = MIXED ? hk[j][k] : hv[j];
-                    o[k] = finalize(a, v * VEC + k, out[j][k], S.den[hh]);
-                }
+                for (int k = 0; k < VEC; ++k)
+                    o[k] = finalize(a, v * VEC + k, out[j][k], S.den[MIXED ? hk[j][k] : hv[j]]);
                 store_out<VEC>(a, r, v * VEC, o);
             }
         }
@@ -479,63 +456,65 @@ __global__ void __launch_bounds__(256) agg_kernel(const AggArgs a) {
     for (int k = 0;; ++k) {
         const Rec S = P1;
         if (!(S.flags & kValid)) break;
-        const uint32_t colS = colP1;
-        float RS[KS], LS[KS];
+        uint32_t colS[NG];
+        float RS[NG];
 #pragma unroll
-        for (int j = 0; j < KS; ++j) { RS[j] = RP1[j]; LS[j] = LP1[j]; }
+        for (int g = 0; g < NG; ++g) { colS[g] = colP1[g]; RS[g] = RP1[g]; }
+        const float LS = LP1;
         // ---- advance the prefetch pipeline ----
         P1 = P2;
-        colP1 = colP2;
+#pragma unroll
+        for (int g = 0; g < NG; ++g) colP1[g] = colP2[g];
         load_r(P1, colP1, RP1);
-        load_l(P1, LP1);
+        LP1 = load_l(P1);
         P2 = gen.next(a);
-        colP2 = load_col(P2);
+        load_col(P2, colP2);
 
         // ---- 1. scores of chunk k ----
         const int sl = k & 1;
         SlotT& SL = slots[sl];
         __syncwarp();
         if (S.flags & kFirst) {
-#pragma unroll
-            for (int j = 0; j < KS; ++j) {
-                m[j] = fixed ? 0.f : -INFINITY;
-                ls[j] = 0.f;
-                Lr[j] = LS[j];
-            }
+            m = fixed ? 0.f : -INFINITY;
+            ls = 0.f;
+            Lr = LS;
         }
-        const bool ok = t < S.cnt;
+        float p[NG];
+        float sc = 1.f;
+        if (fixed) {
 #pragma unroll
-        for (int j = 0; j < KS; ++j) {
-            const int h = hs * KS + j;
-            float p, sc;
-            if (fixed) {
-                p = ok ? RS[j] : 0.f;
-                sc = 1.f;
-            } else {
-                const float s = ok ? leaky(Lr[j] + RS[j]) : -INFINITY;
-                float cm = s;
+            for (int g = 0; g < NG; ++g) p[g] = RS[g];
+        } else {
+            float s[NG];
+            float mx = -INFINITY;
 #pragma unroll
-                for (int o = 1; o < C; o <<= 1) cm = fmaxf(cm, __shfl_xor_sync(kFull, cm, o));
-                const float nm = fmaxf(m[j], cm);
-                sc = nm == -INFINITY ? 1.f : __expf(m[j] - nm);
-                p = ok ? __expf(s - nm) : 0.f;
-                m[j] = nm;
+            for (int g = 0; g < NG; ++g) {
+                const bool ok = g * EG + eo < S.cnt && hok;
+                s[g] = ok ? leaky(Lr + RS[g]) : -INFINITY;
+                mx = fmaxf(mx, s[g]);
             }
-            ls[j] = ls[j] * sc + p;
-            if (h < KM) SL.p[h * PS + t] = p;
-            if (t == 0 && h < 8) SL.sc[h] = sc;
+#pragma unroll
+            for (int o = HS; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+            const float nm = fmaxf(m, mx);
+            sc = nm == -INFINITY ? 1.f : __expf(m - nm);  // 0 on an item's first chunk
+            m = nm;
+#pragma unroll
+            for (int g = 0; g < NG; ++g) p[g] = s[g] == -INFINITY ? 0.f : __expf(s[g] - nm);
         }
+        ls *= sc;
+#pragma unroll
+        for (int g = 0; g < NG; ++g) {
+            ls += p[g];
+            if (hh < KM) SL.p[hh * PS + g * EG + eo] = p[g];
+        }
+        if (eo == 0 && hh < 8) SL.sc[hh] = sc;
         if (S.flags & kLast) {
+            float d = ls;
 #pragma unroll
-            for (int j = 0; j < KS; ++j) {
-                const int h = hs * KS + j;
-                float d = ls[j];
-#pragma unroll
-                for (int o = 1; o < C; o <<= 1) d += __shfl_xor_sync(kFull, d, o);
-                if (t == 0 && h < 8) {
-                    SL.den[h] = d;
-                    SL.m[h] = (S.cnt == 0 || fixed) ? 0.f : m[j];
-                }
+            for (int o = HS; o < 32; o <<= 1) d += __shfl_xor_sync(kFull, d, o);
+            if (eo == 0 && hh < 8) {
+                SL.den[hh] = d;
+                SL.m[hh] = (S.cnt == 0 || fixed) ? 0.f : m;
             }
         }
         if (lane == 0) {
@@ -544,29 +523,33 @@ __global__ void __launch_bounds__(256) agg_kernel(const AggArgs a) {
             SL.cnt = S.cnt;
             SL.flags = S.flags;
         }
-        // ---- 2. gather chunk k's feature rows: lane (t, hs) copies vectors
-        // hs, hs+SPL, ... of edge t's row into buffer k%2 ----
-        if (ok) {
-            const HT* row = H + uint64_t(colS) * a.ldh;
-            const uint32_t dst = bufs_s + uint32_t(sl) * C * RV * 16 + uint32_t(t) * RV * 16;
+        // ---- 2. copy chunk k's feature rows ----
+        const uint32_t bs = bufs_s + uint32_t(sl) * C * RV * 16;
 #pragma unroll
-            for (int i = 0; i < CPL; ++i) {
-                const int v = hs + i * SPL;
-                if (v < RV && (NVC != 0 || v < nvec)) cp_async16(dst + uint32_t(v) * 16, row + v * VEC);
+        for (int i = 0; i < NT; ++i) {
+            const int tt = es + i * EPS;
+            const int g = (i * EPS) / EG;  // static: EPS == 1 or NG == 1
+            const uint32_t c = __shfl_sync(kFull, colS[g], (tt % EG) * HS);
+            if (tt < S.cnt) {
+                const HT* row = H + uint64_t(c) * a.ldh;
+#pragma unroll
+                for (int j = 0; j < VPL; ++j) {
+                    const int v = vl + j * LPE;
+                    if (v < nvec) cp_async16(bs + uint32_t(tt * RV + v) * 16, row + v * VEC);
+                }
             }
         }
         cp_commit();
+        __syncwarp();
         // ---- 4. consume chunk k-1 ----
         if (prev >= 0) {
             cp_wait<1>();
-            __syncwarp();
             consume(prev);
         }
         prev = sl;
     }
     if (prev >= 0) {
         cp_wait<0>();
-        __syncwarp();
         consume(prev);
     }
 }
@@ -615,14 +598,14 @@ __global__ void __launch_bounds__(kWarps * 32) hub_merge_kernel(const AggArgs a)
     }
 }
 
-template <class HT, int KT, int C, int LPE, int VPL, bool MIXED, int NVC>
+template <class HT, int KT, int C, int LPE, int VPL, bool MIXED>
 int launch_agg(const AggArgs& a, cudaStream_t st) {
     constexpr int KM = KT ? KT : 8;
     constexpr size_t warp_bytes = 2 * sizeof(Slot<C, KM>) + size_t(2) * C * LPE * VPL * 16;
-    // Warps per block: up to 8 within ~100 KB of shared memory per block.
-    constexpr int wpb = warp_bytes * 8 <= 100 * 1024 ? 8 : (warp_bytes * 4 <= 100 * 1024 ? 4 : 2);
+    // Up to 4 warps per block within 200 KB of shared memory.
+    constexpr int wpb = warp_bytes * 4 <= 200 * 1024 ? 4 : (warp_bytes * 2 <= 200 * 1024 ? 2 : 1);
     constexpr size_t smem = warp_bytes * wpb;
-    auto kern = agg_kernel<HT, KT, C, LPE, VPL, MIXED, NVC>;
+    auto kern = agg_kernel<HT, KT, C, LPE, VPL, MIXED>;
     static int grid = 0;  // resident blocks (per process; all B200s are alike)
     if (!grid) {
         int dev = 0, sms = 0, per_sm = 0;
@@ -647,6 +630,17 @@ int launch_agg(const AggArgs& a, cudaStream_t st) {
 
 }  // namespace
 
+int aggregate_check_error() {
+    unsigned e = 0;
+    GATB_CUDA(cudaMemcpyFromSymbol(&e, g_agg_error, sizeof(e)));
+    if (e) {
+        unsigned z = 0;
+        cudaMemcpyToSymbol(g_agg_error, &z, sizeof(z));
+        return fail_code(GAT_B200_ETIMEOUT, "aggregation kernel: a bounded wait on a row copy timed out");
+    }
+    return 0;
+}
+
 int aggregate_dispatch(const gat_b200_graph* g, int heads, int dim, const void* h, int h_dtype, int ldh,
                        const float* left, const float* right, const float* fixed_p, const float* fixed_den,
                        int unnorm, int hidden, void* out, int out_bf16, int ldo, float* den, float* max,
@@ -662,6 +656,7 @@ int aggregate_dispatch(const gat_b200_graph* g, int heads, int dim, const void* 
     if ((reinterpret_cast<uintptr_t>(h) & 15) || (uint64_t(ldh) * elem) % 16)
         return fail("aggregate: feature rows must start on 16-byte boundaries");
     if ((fixed_p == nullptr) != (fixed_den == nullptr)) return fail("aggregate: fixed_p and fixed_den go together");
+    if (g->e >= (1ull << 32) - 64) return fail_code(GAT_B200_EUNSUPPORTED, "aggregate: more than 2^32 edges");
     AggArgs a{};
     a.row = g->row;
     a.col = g->col;
@@ -695,15 +690,15 @@ int aggregate_dispatch(const gat_b200_graph* g, int heads, int dim, const void* 
     if (h_dtype == GAT_B200_BF16) {
         if (heads == 8 && dim == 32 && (reinterpret_cast<uintptr_t>(left) & 15) == 0 &&
             (reinterpret_cast<uintptr_t>(right) & 15) == 0)
-            return launch_agg<uint16_t, 8, 16, 32, 1, false, 32>(a, st);
-        if (heads == 1 && width <= 64) return launch_agg<uint16_t, 1, 32, 8, 1, false, 0>(a, st);
-        return launch_agg<uint16_t, 0, 16, 32, 2, true, 0>(a, st);
+            return launch_agg<uint16_t, 8, 16, 32, 1, false>(a, st);
+        if (heads == 1 && width <= 64) return launch_agg<uint16_t, 1, 32, 8, 1, false>(a, st);
+        return launch_agg<uint16_t, 0, 16, 32, 2, true>(a, st);
     }
     if (heads == 8 && dim == 32 && (reinterpret_cast<uintptr_t>(left) & 15) == 0 &&
         (reinterpret_cast<uintptr_t>(right) & 15) == 0)
-        return launch_agg<float, 8, 16, 32, 2, false, 64>(a, st);
-    if (heads == 1 && width <= 64) return launch_agg<float, 1, 32, 16, 1, false, 0>(a, st);
-    return launch_agg<float, 0, 16, 32, 4, true, 0>(a, st);
+        return launch_agg<float, 8, 16, 32, 2, false>(a, st);
+    if (heads == 1 && width <= 64) return launch_agg<float, 1, 32, 16, 1, false>(a, st);
+    return launch_agg<float, 0, 16, 32, 4, true>(a, st);
 }
 
 }  // namespace gatb

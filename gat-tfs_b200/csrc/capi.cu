@@ -23,6 +23,12 @@ int projection_simt_launch(const gat_b200_layer* p, uint64_t n, const void* x, i
 int projection_tc_launch(const gat_b200_layer* p, uint64_t n, const uint16_t* x, int ldx, uint16_t* h, int ldh,
                          float* z, int ldz, float* left, float* right, cudaStream_t st);
 int projection_tc_check_error();
+int aggregate_check_error();
+int device_check_errors() {
+    int rc = projection_tc_check_error();
+    int rc2 = aggregate_check_error();
+    return rc ? rc : rc2;
+}
 
 namespace {
 int dmalloc(void** p, size_t bytes) {
@@ -282,7 +288,7 @@ int gat_b200_standard_layer(const gat_b200_graph* g, const gat_b200_layer* p, co
 
 int gat_b200_check_device(void) {
     clear_error();
-    return projection_tc_check_error();
+    return device_check_errors();
 }
 
 int gat_b200_model_create(const gat_b200_graph* g, const gat_b200_layer* const* layers, int path,
@@ -405,7 +411,7 @@ int gat_b200_model_forward(gat_b200_model* m, const float* x, int x_on_host, flo
     ++m->forwards;
     if (logits_on_host) {
         GATB_CUDA(cudaStreamSynchronize(st));
-        return projection_tc_check_error();
+        return device_check_errors();
     }
     return 0;
 }
