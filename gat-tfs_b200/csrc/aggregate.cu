@@ -130,8 +130,9 @@ __device__ __forceinline__ float finalize(const AggArgs& a, int c, float acc, fl
 // Kept for gat_b200_check_device (this kernel has no waits that can time out).
 __device__ unsigned g_agg_error = 0;
 
-__device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g) : "memory");
+// 16-byte cp.async; src_bytes = 0 reads nothing and zero-fills the slot.
+__device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(saddr), "l"(g), "r"(src_bytes) : "memory");
 }
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
@@ -172,7 +173,7 @@ struct Rec {
 // Chunk record handed from scoring to consuming through shared memory.
 template <int C, int KM>
 struct __align__(16) Slot {
-    float p[KM * (C + 1)];  // p[h*(C+1) + t]: conflict-free
+    float p[KM * (C + 4)];  // p[h*(C+4) + t]: conflict-free stores and reads
     float sc[8];            // rescale of the running sums before this chunk
     float den[8];           // final sums (last chunk of an item)
     float m[8];             // final maxima (last chunk of an item)
@@ -272,7 +273,7 @@ struct Gen {
 //   3. prefetch R of chunk k+1 and col of chunk k+2;
 //   4. consume chunk k-1 (waiting only for this lane's own copies: a lane
 //      consumes exactly the vectors it copied).
-template <class HT, int KT, int C, int LPE, int VPL, bool MIXED>
+template <class HT, int KT, int C, int LPE, int VPL, bool MIXED, int NVC>
 __global__ void __launch_bounds__(128) agg_kernel(const AggArgs a) {
     using V = Vec<HT>;
     constexpr int VEC = V::N;
@@ -283,7 +284,7 @@ __global__ void __launch_bounds__(128) agg_kernel(const AggArgs a) {
     constexpr int EPS = 32 / LPE;        // edges per copy/consume step
     constexpr int NT = C / EPS;          // copy/consume steps per chunk
     constexpr int RV = LPE * VPL;        // 16-byte vectors per buffered row
-    constexpr int PS = C + 1;            // p row stride
+    constexpr int PS = C + 4;            // p row stride (Slot::p): conflict-free for 8 heads x 4 offsets
     static_assert(NG >= 1 && NG * EG == C && NT * EPS == C, "bad tiling");
     static_assert(HS == 1 || LPE == 32, "8 head slots need whole-warp rows");
     using SlotT = Slot<C, KM>;
@@ -298,10 +299,11 @@ __global__ void __launch_bounds__(128) agg_kernel(const AggArgs a) {
 
     const int K = KT ? KT : a.heads;
     const int eo = lane / HS, hh = lane % HS;    // scoring role
-    const bool hok = hh < K;
+    const bool hok = KT == 8 || hh < K;
     const int es = lane / LPE, vl = lane % LPE;  // copy / consume role
-    const int nvec = (a.width + VEC - 1) / VEC;
-    const HT* H = static_cast<const HT*>(a.h);
+    const int nvec = NVC ? NVC : (a.width + VEC - 1) / VEC;
+    const uint64_t row_bytes = uint64_t(a.ldh) * sizeof(HT);
+    const char* hbase = reinterpret_cast<const char*>(a.h) + vl * 16;
     const bool fixed = a.fixed_p != nullptr;
 
     int hv[VPL];
@@ -374,15 +376,18 @@ __global__ void __launch_bounds__(128) agg_kernel(const AggArgs a) {
                                                     S.sc[MIXED ? hk[j][2 * k + 1] : hv[j]]));
         }
         const uint4* buf = bufs + size_t(sl) * C * RV;
-#pragma unroll 4
-        for (int i = 0; i < NT; ++i) {
-            const int tt = es + i * EPS;
-            if (i * EPS >= cnt) break;
-            if (tt < cnt) {
+        // Slots past cnt hold zero rows and p = 0, so groups of 4 steps run
+        // without per-edge predicates.
+#pragma unroll
+        for (int i0 = 0; i0 < NT; i0 += 4) {
+            if (i0 * EPS >= cnt) break;
+#pragma unroll
+            for (int u = 0; u < 4 && i0 + u < NT; ++u) {
+                const int tt = es + (i0 + u) * EPS;
 #pragma unroll
                 for (int j = 0; j < VPL; ++j) {
                     const int v = vl + j * LPE;
-                    if (v >= nvec) continue;
+                    if (NVC == 0 && v >= nvec) continue;
                     float f[VEC];
                     V::unpack(buf[tt * RV + v], f);
                     if constexpr (MIXED) {
@@ -490,16 +495,18 @@ __global__ void __launch_bounds__(128) agg_kernel(const AggArgs a) {
 #pragma unroll
             for (int g = 0; g < NG; ++g) {
                 const bool ok = g * EG + eo < S.cnt && hok;
-                s[g] = ok ? leaky(Lr + RS[g]) : -INFINITY;
+                const float x = Lr + RS[g];
+                s[g] = ok ? fmaxf(x, 0.2f * x) : -INFINITY;  // leaky (gat.hpp:52), exactly
                 mx = fmaxf(mx, s[g]);
             }
 #pragma unroll
             for (int o = HS; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
             const float nm = fmaxf(m, mx);
-            sc = nm == -INFINITY ? 1.f : __expf(m - nm);  // 0 on an item's first chunk
+            const float nms = nm == -INFINITY ? 0.f : nm;  // a chunk without edges
+            sc = __expf(m - nms);  // 0 on an item's first chunk
             m = nm;
 #pragma unroll
-            for (int g = 0; g < NG; ++g) p[g] = s[g] == -INFINITY ? 0.f : __expf(s[g] - nm);
+            for (int g = 0; g < NG; ++g) p[g] = __expf(s[g] - nms);  // exp(-inf) = 0 for empty slots
         }
         ls *= sc;
 #pragma unroll
@@ -523,20 +530,21 @@ __global__ void __launch_bounds__(128) agg_kernel(const AggArgs a) {
             SL.cnt = S.cnt;
             SL.flags = S.flags;
         }
-        // ---- 2. copy chunk k's feature rows ----
-        const uint32_t bs = bufs_s + uint32_t(sl) * C * RV * 16;
+        // ---- 2. copy chunk k's feature rows (every slot: rows past cnt are
+        // zero-filled without reading memory) ----
+        const uint32_t bs = bufs_s + uint32_t(sl) * C * RV * 16 + uint32_t(vl) * 16;
 #pragma unroll
         for (int i = 0; i < NT; ++i) {
             const int tt = es + i * EPS;
             const int g = (i * EPS) / EG;  // static: EPS == 1 or NG == 1
             const uint32_t c = __shfl_sync(kFull, colS[g], (tt % EG) * HS);
-            if (tt < S.cnt) {
-                const HT* row = H + uint64_t(c) * a.ldh;
+            const uint32_t nb = tt < S.cnt ? 16u : 0u;
+            const char* src = hbase + uint64_t(c) * row_bytes;
 #pragma unroll
-                for (int j = 0; j < VPL; ++j) {
-                    const int v = vl + j * LPE;
-                    if (v < nvec) cp_async16(bs + uint32_t(tt * RV + v) * 16, row + v * VEC);
-                }
+            for (int j = 0; j < VPL; ++j) {
+                const int v = vl + j * LPE;
+                if (NVC != 0 || v < nvec)
+                    cp_async16(bs + uint32_t(tt * RV + j * LPE) * 16, src + j * LPE * 16, nb);
             }
         }
         cp_commit();
@@ -598,14 +606,14 @@ __global__ void __launch_bounds__(kWarps * 32) hub_merge_kernel(const AggArgs a)
     }
 }
 
-template <class HT, int KT, int C, int LPE, int VPL, bool MIXED>
+template <class HT, int KT, int C, int LPE, int VPL, bool MIXED, int NVC>
 int launch_agg(const AggArgs& a, cudaStream_t st) {
     constexpr int KM = KT ? KT : 8;
     constexpr size_t warp_bytes = 2 * sizeof(Slot<C, KM>) + size_t(2) * C * LPE * VPL * 16;
     // Up to 4 warps per block within 200 KB of shared memory.
     constexpr int wpb = warp_bytes * 4 <= 200 * 1024 ? 4 : (warp_bytes * 2 <= 200 * 1024 ? 2 : 1);
     constexpr size_t smem = warp_bytes * wpb;
-    auto kern = agg_kernel<HT, KT, C, LPE, VPL, MIXED>;
+    auto kern = agg_kernel<HT, KT, C, LPE, VPL, MIXED, NVC>;
     static int grid = 0;  // resident blocks (per process; all B200s are alike)
     if (!grid) {
         int dev = 0, sms = 0, per_sm = 0;
@@ -690,15 +698,15 @@ int aggregate_dispatch(const gat_b200_graph* g, int heads, int dim, const void* 
     if (h_dtype == GAT_B200_BF16) {
         if (heads == 8 && dim == 32 && (reinterpret_cast<uintptr_t>(left) & 15) == 0 &&
             (reinterpret_cast<uintptr_t>(right) & 15) == 0)
-            return launch_agg<uint16_t, 8, 16, 32, 1, false>(a, st);
-        if (heads == 1 && width <= 64) return launch_agg<uint16_t, 1, 32, 8, 1, false>(a, st);
-        return launch_agg<uint16_t, 0, 16, 32, 2, true>(a, st);
+            return launch_agg<uint16_t, 8, 16, 32, 1, false, 32>(a, st);
+        if (heads == 1 && width <= 64) return launch_agg<uint16_t, 1, 32, 8, 1, false, 0>(a, st);
+        return launch_agg<uint16_t, 0, 16, 32, 2, true, 0>(a, st);
     }
     if (heads == 8 && dim == 32 && (reinterpret_cast<uintptr_t>(left) & 15) == 0 &&
         (reinterpret_cast<uintptr_t>(right) & 15) == 0)
-        return launch_agg<float, 8, 16, 32, 2, false>(a, st);
-    if (heads == 1 && width <= 64) return launch_agg<float, 1, 32, 16, 1, false>(a, st);
-    return launch_agg<float, 0, 16, 32, 4, true>(a, st);
+        return launch_agg<float, 8, 16, 32, 2, false, 64>(a, st);
+    if (heads == 1 && width <= 64) return launch_agg<float, 1, 32, 16, 1, false, 0>(a, st);
+    return launch_agg<float, 0, 16, 32, 4, true, 0>(a, st);
 }
 
 }  // namespace gatb
