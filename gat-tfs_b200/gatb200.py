@@ -71,6 +71,7 @@ SIGNATURES = [
     ("gat_b200_standard_aggregate", C.c_int, [_vp, C.c_int, C.c_int, _vp, C.c_int, C.c_int, _vp, _vp, _vp, _vp, _vp, C.c_int, _vp, _vp, _vp]),
     ("gat_b200_finish", C.c_int, [C.c_uint64, C.c_int, C.c_int, _vp, C.c_int, _vp, C.c_int, _vp]),
     ("gat_b200_aggregate_fused", C.c_int, [_vp, C.c_int, C.c_int, _vp, C.c_int, C.c_int, _vp, _vp, C.c_int, _vp, C.c_int, C.c_int, _vp]),
+    ("gat_b200_aggregate_fused_noalloc", C.c_int, [C.c_uint64, C.c_uint64, _vp, _vp, C.c_int, C.c_int, _vp, C.c_int, C.c_int, _vp, _vp, C.c_int, _vp, C.c_int, C.c_int, _vp]),
     ("gat_b200_standard_layer", C.c_int, [_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp, _vp, C.c_int, C.c_int, _vp]),
     ("gat_b200_check_device", C.c_int, []),
     ("gat_b200_model_create", C.c_int, [_vp, C.POINTER(_vp), C.c_int, C.POINTER(_vp)]),
@@ -355,6 +356,14 @@ def aggregate_fused(g: DeviceGraph, heads, dim, h, h_dtype, ldh, left, right, hi
                     stream=None):
     _check(_lib.gat_b200_aggregate_fused(g.handle, heads, dim, _ptr(h), h_dtype, ldh, _ptr(left), _ptr(right),
                                          int(hidden), _ptr(out), out_dtype, ldo, _stream(stream)))
+
+
+def aggregate_fused_noalloc(n, e, row, col, heads, dim, h, h_dtype, ldh, left, right, hidden, out, out_dtype, ldo,
+                            stream=None):
+    """The fused aggregation without any device allocation (CSR given as device pointers)."""
+    _check(_lib.gat_b200_aggregate_fused_noalloc(n, e, _ptr(row), _ptr(col), heads, dim, _ptr(h), h_dtype, ldh,
+                                                 _ptr(left), _ptr(right), int(hidden), _ptr(out), out_dtype, ldo,
+                                                 _stream(stream)))
 
 
 def standard_layer(g: DeviceGraph, layer: DeviceLayer, x, ldx, path, hidden, h, left, right, out, out_dtype, ldo,

@@ -193,6 +193,26 @@ int gat_b200_aggregate_fused(const gat_b200_graph* g, int heads, int dim, const 
                              int h_dtype, int ldh, const float* left, const float* right,
                              int hidden, void* out, int out_dtype, int ldo, void* stream);
 
+/* No counterpart in the reference. The fused aggregation above for callers
+ * that cannot allocate device memory themselves: a plugin inside another
+ * framework whose allocator owns the GPU's memory, or a serving loop where
+ * cudaMalloc would synchronize the device and stall other streams. It takes
+ * the destination-row CSR as device pointers (no gat_b200_graph handle, no
+ * degree schedule: rows are split into equal edge ranges instead) and keeps
+ * its scratch in a 32 MiB array compiled into the library, which every GPU
+ * that loads the library's module keeps until the process exits. Limits:
+ * at most 7936 * 65536 = 520,093,696 edges (larger graphs get
+ * GAT_B200_EUNSUPPORTED), heads <= 8, dim <= 64. The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress) with that device
+ * current; make that first call before any stream capture. All calls share the
+ * array: calls whose kernels can overlap on the GPU (other streams, other host
+ * threads) race on it and must be serialized by the caller. Arguments and
+ * output as in gat_b200_aggregate_fused. */
+int gat_b200_aggregate_fused_noalloc(uint64_t n, uint64_t e, const uint64_t* row,
+                                     const uint32_t* col, int heads, int dim, const void* h,
+                                     int h_dtype, int ldh, const float* left, const float* right,
+                                     int hidden, void* out, int out_dtype, int ldo, void* stream);
+
 /* One full layer on device buffers. Replaces gat::standard_layer
  * (baseline/src/baseline_standard.cpp:98-108) for path STANDARD_BF16 (x BF16)
  * or STANDARD_FP32 (x FP32). Scratch: h [n][ldh] (BF16 for STANDARD_BF16, FP32
