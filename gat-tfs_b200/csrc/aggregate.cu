@@ -532,19 +532,26 @@ __global__ void __launch_bounds__(128) agg_kernel(const AggArgs a) {
         }
         // ---- 2. copy chunk k's feature rows (every slot: rows past cnt are
         // zero-filled without reading memory) ----
+        // Groups of 4 steps, as in consume: slots up to the end of the last
+        // group holding an edge are written, later groups are skipped.
         const uint32_t bs = bufs_s + uint32_t(sl) * C * RV * 16 + uint32_t(vl) * 16;
 #pragma unroll
-        for (int i = 0; i < NT; ++i) {
-            const int tt = es + i * EPS;
-            const int g = (i * EPS) / EG;  // static: EPS == 1 or NG == 1
-            const uint32_t c = __shfl_sync(kFull, colS[g], (tt % EG) * HS);
-            const uint32_t nb = tt < S.cnt ? 16u : 0u;
-            const char* src = hbase + uint64_t(c) * row_bytes;
+        for (int i0 = 0; i0 < NT; i0 += 4) {
+            if (i0 * EPS >= S.cnt) break;
 #pragma unroll
-            for (int j = 0; j < VPL; ++j) {
-                const int v = vl + j * LPE;
-                if (NVC != 0 || v < nvec)
-                    cp_async16(bs + uint32_t(tt * RV + j * LPE) * 16, src + j * LPE * 16, nb);
+            for (int u = 0; u < 4 && i0 + u < NT; ++u) {
+                const int i = i0 + u;
+                const int tt = es + i * EPS;
+                const int g = (i * EPS) / EG;  // static: EPS == 1 or NG == 1
+                const uint32_t c = __shfl_sync(kFull, colS[g], (tt % EG) * HS);
+                const uint32_t nb = tt < S.cnt ? 16u : 0u;
+                const char* src = hbase + uint64_t(c) * row_bytes;
+#pragma unroll
+                for (int j = 0; j < VPL; ++j) {
+                    const int v = vl + j * LPE;
+                    if (NVC != 0 || v < nvec)
+                        cp_async16(bs + uint32_t(tt * RV + j * LPE) * 16, src + j * LPE * 16, nb);
+                }
             }
         }
         cp_commit();
