@@ -210,78 +210,110 @@ def main():
         import datetime
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
-
-    cfg = configs.make(args.config)
-    n, e = cfg.graph.n, cfg.graph.e
     stream = torch.cuda.current_stream()
-    g = G.DeviceGraph(cfg.graph.row, cfg.graph.col, stream)
-    layers = [G.DeviceLayer(p) for p in cfg.model]
-    model = G.DeviceModel(g, layers, G.PATH_STANDARD_BF16)
-    x_dev = torch.from_numpy(cfg.graph.x).cuda()
-    logits = torch.empty((n, model.classes), dtype=torch.float32, device="cuda")
+    warm = max(args.warmup, 3)
 
     def barrier():
         if dist is not None:
             dist.barrier()
 
-    for _ in range(max(args.warmup, 3)):
-        model.forward(x_dev, logits, False, False, stream)
-    torch.cuda.synchronize()
-    G.check_device()
+    def max_over_ranks(v):
+        if dist is None:
+            return v
+        t = torch.tensor([v], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
 
-    model.enable_timing(args.steps)
-    clocks = Clocks(local)
-    clocks.start()
-    barrier()
-    torch.cuda.synchronize()
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    for _ in range(args.steps):
-        model.forward(x_dev, logits, False, False, stream)
-    t1.record(stream)
-    torch.cuda.synchronize()
-    barrier()
-    clk = clocks.stop()
-    G.check_device()
-    ms = t0.elapsed_time(t1) / args.steps
-    if dist is not None:
-        tt = torch.tensor([ms], device="cuda")
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms = float(tt.item())
-    stages = model.stage_times()  # [steps, 9]
-    launches = model.launches()
-    model.enable_timing(0)
+    def timed(step, k):
+        """ms per step of k calls of step(), CUDA events on the launch stream, max over ranks."""
+        barrier()
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(k):
+            step()
+        t1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(t0.elapsed_time(t1) / k)
 
-    # roofline of the aggregation kernel (three launches per step)
-    agg_ms = [float(stages[:, k].mean()) for k in (3, 5, 7)]
-    b = [agg_bytes(n, e, 8, 32, 2), agg_bytes(n, e, 8, 32, 2), agg_bytes(n, e, 1, cfg.model[2].dim, 4)]
+    if world == 1:
+        # ---- one GPU: the C-ABI three-layer model ----
+        cfg = configs.make(args.config)
+        n, e, din = cfg.graph.n, cfg.graph.e, cfg.graph.din
+        n_loc, e_loc = n, e
+        g = G.DeviceGraph(cfg.graph.row, cfg.graph.col, stream)
+        layers = [G.DeviceLayer(p) for p in cfg.model]
+        model = G.DeviceModel(g, layers, G.PATH_STANDARD_BF16)
+        classes = model.classes
+        x_rows = cfg.graph.x
+        x_dev = torch.from_numpy(x_rows).cuda()
+        logits = torch.empty((n, classes), dtype=torch.float32, device="cuda")
+        fwd = lambda x, y, xh, yh: model.forward(x, y, xh, yh, stream)
+        for _ in range(warm):
+            fwd(x_dev, logits, False, False)
+        torch.cuda.synchronize()
+        G.check_device()
+        model.enable_timing(args.steps)
+        clocks = Clocks(local)
+        clocks.start()
+        ms = timed(lambda: fwd(x_dev, logits, False, False), args.steps)
+        clk = clocks.stop()
+        G.check_device()
+        st = model.stage_times()
+        stage_ms = {k: float(st[:, i].mean()) for i, k in enumerate(G.DeviceModel.STAGES) if k not in ("h2d", "d2h")}
+        launches = model.launches()
+        model.enable_timing(0)
+        parallelism = "single"
+    else:
+        # ---- N GPUs: destination rows partitioned by edge count, NCCL all-gather ----
+        import dist as gdist
+        part = configs.make_part(args.config, rank, world)
+        n, e, din = len(part.row) - 1, part.e, part.din
+        pm = gdist.PartitionedModel(part.row, part.col_rows, part.model, rank, world, stream, dist, part.cuts)
+        n_loc, e_loc = pm.n_loc, pm.e_loc
+        classes = pm.classes
+        x_rows = part.x_rows
+        x_dev = torch.from_numpy(x_rows).cuda()
+        logits = torch.empty((n_loc, classes), dtype=torch.float32, device="cuda")
+        fwd = pm.forward
+        for _ in range(warm):
+            fwd(x_dev, logits, False, False)
+        torch.cuda.synchronize()
+        G.check_device()
+        pm.enable_timing(True)
+        clocks = Clocks(local)
+        clocks.start()
+        ms = timed(lambda: fwd(x_dev, logits, False, False), args.steps)
+        clk = clocks.stop()
+        G.check_device()
+        stage_ms = pm.stage_times()  # last timed step
+        pm.enable_timing(False)
+        launches = 1 + 3 * (2 + (1 if pm.g.info()["n_hub"] else 0))
+        parallelism = f"rows{world}: destination rows split by edge count, NCCL all-gather of H and R per layer"
+
+    # roofline of the aggregation kernel (three launches per step, this rank's rows)
+    agg_ms = [stage_ms["aggregate_l1"], stage_ms["aggregate_l2"], stage_ms["aggregate_l3"]]
+    b = [agg_bytes(n_loc, e_loc, 8, 32, 2), agg_bytes(n_loc, e_loc, 8, 32, 2), agg_bytes(n_loc, e_loc, 1, classes, 4)]
     achieved = sum(b) / (sum(agg_ms) * 1e-3) / 1e9
     peak, peak_kind = peaks()
     traffic = None
     prof = ROOT / "profiles" / "aggregate_c4_traffic.json"
-    if prof.exists():
+    if prof.exists() and world == 1 and args.config == "c4":
         traffic = json.loads(prof.read_text()).get("bytes_per_launch_avg")
 
-    # e2e through the model call with pinned host buffers
-    x_host = torch.from_numpy(cfg.graph.x).pin_memory()
-    l_host = torch.empty((n, model.classes), dtype=torch.float32).pin_memory()
+    # e2e: the same forward with pinned HOST input rows and HOST logits
+    x_host = torch.from_numpy(x_rows).pin_memory()
+    l_host = torch.empty((n_loc, classes), dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        fwd(x_host, l_host, True, True)
+
     for _ in range(2):
-        model.forward(x_host, l_host, True, True, stream)
-    e_steps = max(1, min(args.steps, 5))
-    barrier()
+        e2e_step()
     torch.cuda.synchronize()
-    t0.record(stream)
-    for _ in range(e_steps):
-        model.forward(x_host, l_host, True, True, stream)
-    t1.record(stream)
-    torch.cuda.synchronize()
-    barrier()
-    e2e_ms = t0.elapsed_time(t1) / e_steps
-    if dist is not None:
-        tt = torch.tensor([e2e_ms], device="cuda")
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        e2e_ms = float(tt.item())
+    e2e_ms = timed(e2e_step, max(1, min(args.steps, 5)))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -299,29 +331,30 @@ def main():
         value = 3 * e / (ms * 1e-3) / 1e9
         line = {
             "metric": METRIC, "value": round(value, 4), "unit": "GEdges/s", "n_gpus": world, "steps": args.steps,
-            "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "warmup": warm, "ms_per_step": round(ms, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": f"{args.config}: products-shaped power-law graph, N={n}, E={e}, "
-                                   f"{cfg.graph.din}->8x32->8x32->1x{cfg.model[2].dim}",
+                                   f"{din}->8x32->8x32->1x{classes}",
                        "nodes": n, "edges": e, "l2": "inputs larger than L2 (H is 1.25 GB per layer)",
-                       "parallelism": f"rows{world}" if world > 1 else "single"},
-            "stage_ms": {k: round(float(stages[:, i].mean()), 4) for i, k in enumerate(G.DeviceModel.STAGES)
-                         if k not in ("h2d", "d2h")},
+                       "parallelism": parallelism},
+            "stage_ms": {k: round(float(v), 4) for k, v in stage_ms.items()},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
-                         "kernel": "edge-softmax aggregation (3 launches/step)",
+                         "kernel": "edge-softmax aggregation (3 launches/step" + (", rank 0 rows)" if world > 1 else ")"),
                          "algorithmic_bytes_per_launch": int(sum(b) / 3)},
             "e2e": {"value": round(3 * e / (e2e_ms * 1e-3) / 1e9, 4), "unit": "GEdges/s",
-                    "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": n * cfg.graph.din * 4,
-                    "d2h_bytes_per_step": n * model.classes * 4},
+                    "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": n * din * 4,
+                    "d2h_bytes_per_step": n * classes * 4},
             "gpu_launches": launches * args.steps,
             "clocks": clk,
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line))
-    model.close()
-    if dist is not None:
+    if world == 1:
+        model.close()
+    else:
+        pm.close()
         dist.destroy_process_group()
     return 0
 

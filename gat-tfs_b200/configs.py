@@ -53,3 +53,34 @@ def make_graph(name: str, features: bool = True) -> G.Graph:
 def make(name: str, features: bool = True) -> Config:
     s = SPECS[name]
     return Config(name, make_graph(name, features), G.glorot_model(s["din"], s["classes"], s["seed"]))
+
+
+@dataclass
+class Part:
+    """This rank's share of a power-law configuration (multi-GPU runs)."""
+    name: str
+    row: np.ndarray      # all n+1 row pointers
+    col_rows: np.ndarray  # sources of rows [lo, hi)
+    x_rows: np.ndarray    # features of rows [lo, hi)
+    cuts: np.ndarray
+    lo: int
+    hi: int
+    e: int
+    din: int
+    model: list
+
+
+def make_part(name: str, rank: int, world: int) -> Part:
+    """Generates only what rank `rank` of `world` needs: every rank builds the
+    row pointers, then the sources and features of its own rows."""
+    import dist
+    s = SPECS[name]
+    if s["kind"] != "powerlaw":
+        raise ValueError("make_part needs a power-law configuration")
+    row = G.synth_powerlaw_rowptr(s["n"], s["e"], s["max_degree"], s["gamma"], s["seed"])
+    cuts = dist.partition(row, world)
+    lo, hi = int(cuts[rank]), int(cuts[rank + 1])
+    col = G.synth_powerlaw_cols(s["n"], s["e"], s["max_degree"], s["gamma"], s["seed"], row, lo, hi)
+    x = G.synth_normal_range(lo * s["din"], (hi - lo, s["din"]), s["seed"], 1)
+    return Part(name, row, col, x, cuts, lo, hi, int(row[-1]), s["din"],
+                G.glorot_model(s["din"], s["classes"], s["seed"]))

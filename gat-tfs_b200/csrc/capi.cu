@@ -118,6 +118,28 @@ int gat_b200_graph_create(uint64_t n, uint64_t e, const uint64_t* row, const uin
     return 0;
 }
 
+int gat_b200_graph_create_part(uint64_t n, uint64_t n_src, uint64_t e, const uint64_t* row, const uint32_t* col,
+                               void* stream, gat_b200_graph** out) {
+    clear_error();
+    if (!out) return fail("graph_create_part: null output handle");
+    *out = nullptr;
+    if (!n || n > uint64_t(INT32_MAX) || !n_src || n_src > uint64_t(UINT32_MAX)) return fail("invalid graph sizes");
+    if (!row || (e && !col)) return fail("invalid graph sizes");
+    gat_b200_graph* g = new (std::nothrow) gat_b200_graph();
+    if (!g) return fail("graph_create_part: out of host memory");
+    g->n = n;
+    g->e = e;
+    g->n_src = n_src;
+    int rc = graph_build(g, row, col, as_stream(stream));
+    if (rc) {
+        graph_release(g);
+        delete g;
+        return rc;
+    }
+    *out = g;
+    return 0;
+}
+
 int gat_b200_graph_destroy(gat_b200_graph* g) {
     if (!g) return 0;
     graph_release(g);

@@ -27,7 +27,9 @@ inline int padded_ld(int width, int elem_bytes) {
 int synth_uniform_graph(uint64_t n, uint32_t sources, uint64_t seed, uint64_t* row, uint32_t* col);
 int synth_powerlaw_graph(uint64_t n, uint64_t e_target, uint64_t max_degree, double gamma,
                          uint64_t seed, uint64_t* row, uint32_t* col);
-int synth_normal(uint64_t count, double scale, uint64_t seed, uint64_t stream, float* out);
+int synth_powerlaw_rows(uint64_t n, uint64_t e_target, uint64_t max_degree, double gamma, uint64_t seed,
+                        uint64_t r_lo, uint64_t r_hi, uint64_t* row, uint32_t* col);
+int synth_normal(uint64_t count, double scale, uint64_t seed, uint64_t stream, float* out, uint64_t offset);
 int synth_uniform(uint64_t count, double lo, double hi, uint64_t seed, uint64_t stream, float* out);
 
 }  // namespace gatb

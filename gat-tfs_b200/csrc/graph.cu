@@ -142,7 +142,7 @@ int graph_build(gat_b200_graph* g, const uint64_t* row_h, const uint32_t* col_h,
         cudaMemsetAsync(flags, 0, sizeof(unsigned), st);
         cudaMemsetAsync(stats, 0, 3 * sizeof(unsigned long long), st);
         validate_rows<<<unsigned((n + 255) / 256), 256, 0, st>>>(g->row, n, e, deg, ids, flags);
-        if (e) validate_cols<<<1184, 256, 0, st>>>(g->col, e, n, flags);
+        if (e) validate_cols<<<1184, 256, 0, st>>>(g->col, e, g->n_src ? g->n_src : n, flags);
         unsigned hflags = 0;
         cudaMemcpyAsync(&hflags, flags, sizeof(unsigned), cudaMemcpyDeviceToHost, st);
         cudaError_t ce = cudaStreamSynchronize(st);

@@ -19,6 +19,7 @@ struct Segment {
 
 struct gat_b200_graph {
     uint64_t n = 0, e = 0;
+    uint64_t n_src = 0;       // source ids are < n_src (n for a square graph)
     int device = 0;
     uint64_t* row = nullptr;  // device [n+1]
     uint32_t* col = nullptr;  // device [e]

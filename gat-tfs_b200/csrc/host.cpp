@@ -186,7 +186,17 @@ int gat_b200_synth_powerlaw_graph(uint64_t n, uint64_t e, uint64_t max_degree, d
 }
 int gat_b200_synth_normal(uint64_t count, double scale, uint64_t seed, uint64_t stream, float* out) {
     if (!out) return fail("synth: null pointer");
-    return synth_normal(count, scale, seed, stream, out);
+    return synth_normal(count, scale, seed, stream, out, 0);
+}
+int gat_b200_synth_normal_range(uint64_t offset, uint64_t count, double scale, uint64_t seed, uint64_t stream,
+                                float* out) {
+    if (!out) return fail("synth: null pointer");
+    return synth_normal(count, scale, seed, stream, out, offset);
+}
+int gat_b200_synth_powerlaw_rows(uint64_t n, uint64_t e, uint64_t max_degree, double gamma, uint64_t seed,
+                                 uint64_t r_lo, uint64_t r_hi, uint64_t* row, uint32_t* col) {
+    if (!row) return fail("synth: null pointer");
+    return synth_powerlaw_rows(n, e, max_degree, gamma, seed, r_lo, r_hi, row, col);
 }
 int gat_b200_synth_uniform(uint64_t count, double lo, double hi, uint64_t seed, uint64_t stream, float* out) {
     if (!out) return fail("synth: null pointer");

@@ -121,8 +121,13 @@ int synth_uniform_graph(uint64_t n, uint32_t sources, uint64_t seed, uint64_t* r
 // few units of slack are spread one per row. Node ids receive ranks through a
 // seeded permutation, and the same ranks set source popularity weights, so
 // high in-degree nodes are also frequent sources (as in an undirected graph).
-int synth_powerlaw_graph(uint64_t n, uint64_t e_target, uint64_t max_degree, double gamma,
-                         uint64_t seed, uint64_t* row, uint32_t* col) {
+struct PowerLaw {
+    std::vector<uint64_t> node_deg;  // degree without the self loop
+    std::vector<double> weight;      // source popularity
+};
+
+static int powerlaw_setup(uint64_t n, uint64_t e_target, uint64_t max_degree, double gamma, uint64_t seed,
+                          PowerLaw& pl) {
     if (n < 4 || gamma <= 1.0) return fail("power-law graph: bad n/gamma");
     if (e_target < 2 * n || max_degree < 2 || max_degree > n / 2 || e_target > n * (max_degree))
         return fail("power-law graph: infeasible edge target");
@@ -165,26 +170,42 @@ int synth_powerlaw_graph(uint64_t n, uint64_t e_target, uint64_t max_degree, dou
         if (deg[r] < max_degree - 1) { ++deg[r]; ++s; }
     if (s != want) return fail("power-law graph: degree sequence did not close");
     std::vector<uint32_t> node_of_rank = permutation(n, seed, 1);
-    std::vector<uint64_t> node_deg(n);
-    std::vector<double> weight(n);
+    pl.node_deg.assign(n, 0);
+    pl.weight.assign(n, 0.0);
     for (uint64_t r = 0; r < n; ++r) {
-        node_deg[node_of_rank[r]] = deg[r];
-        weight[node_of_rank[r]] = std::pow(double(r) + r0, -beta);
+        pl.node_deg[node_of_rank[r]] = deg[r];
+        pl.weight[node_of_rank[r]] = std::pow(double(r) + r0, -beta);
     }
-    Alias table(weight);
+    return 0;
+}
+
+int synth_powerlaw_rows(uint64_t n, uint64_t e_target, uint64_t max_degree, double gamma, uint64_t seed,
+                        uint64_t r_lo, uint64_t r_hi, uint64_t* row, uint32_t* col) {
+    PowerLaw pl;
+    int rc = powerlaw_setup(n, e_target, max_degree, gamma, seed, pl);
+    if (rc) return rc;
+    if (r_lo > r_hi || r_hi > n) return fail("power-law graph: bad row range");
     row[0] = 0;
-    for (uint64_t i = 0; i < n; ++i) row[i + 1] = row[i] + node_deg[i] + 1;
+    for (uint64_t i = 0; i < n; ++i) row[i + 1] = row[i] + pl.node_deg[i] + 1;
+    if (!col) return 0;  // row pointers only
+    Alias table(pl.weight);
+    uint32_t* base = col - row[r_lo];  // col holds edges [row[r_lo], row[r_hi])
 #pragma omp parallel for schedule(dynamic, 64)
-    for (long long i = 0; i < (long long)n; ++i)
-        fill_row(uint64_t(i), node_deg[i], col + row[i], [&](uint64_t k) {
+    for (long long i = (long long)r_lo; i < (long long)r_hi; ++i)
+        fill_row(uint64_t(i), pl.node_deg[i], base + row[i], [&](uint64_t k) {
             return table.draw(rng(seed, 3ull << 40 | uint64_t(i), 2 * k), rng(seed, 3ull << 40 | uint64_t(i), 2 * k + 1));
         });
     return 0;
 }
 
-int synth_normal(uint64_t count, double scale, uint64_t seed, uint64_t stream, float* out) {
+int synth_powerlaw_graph(uint64_t n, uint64_t e_target, uint64_t max_degree, double gamma,
+                         uint64_t seed, uint64_t* row, uint32_t* col) {
+    return synth_powerlaw_rows(n, e_target, max_degree, gamma, seed, 0, n, row, col);
+}
+
+int synth_normal(uint64_t count, double scale, uint64_t seed, uint64_t stream, float* out, uint64_t offset) {
 #pragma omp parallel for schedule(static)
-    for (long long i = 0; i < (long long)count; ++i) out[i] = float(scale * normal(seed, stream, uint64_t(i)));
+    for (long long i = 0; i < (long long)count; ++i) out[i] = float(scale * normal(seed, stream, offset + uint64_t(i)));
     return 0;
 }
 

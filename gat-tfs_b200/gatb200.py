@@ -57,8 +57,11 @@ SIGNATURES = [
     ("gat_b200_synth_uniform_graph", C.c_int, [C.c_uint64, C.c_uint32, C.c_uint64, _u64p, _u32p]),
     ("gat_b200_synth_powerlaw_graph", C.c_int, [C.c_uint64, C.c_uint64, C.c_uint64, C.c_double, C.c_uint64, _u64p, _u32p]),
     ("gat_b200_synth_normal", C.c_int, [C.c_uint64, C.c_double, C.c_uint64, C.c_uint64, _f32p]),
+    ("gat_b200_synth_normal_range", C.c_int, [C.c_uint64, C.c_uint64, C.c_double, C.c_uint64, C.c_uint64, _f32p]),
+    ("gat_b200_synth_powerlaw_rows", C.c_int, [C.c_uint64, C.c_uint64, C.c_uint64, C.c_double, C.c_uint64, C.c_uint64, C.c_uint64, _u64p, _u32p]),
     ("gat_b200_synth_uniform", C.c_int, [C.c_uint64, C.c_double, C.c_double, C.c_uint64, C.c_uint64, _f32p]),
     ("gat_b200_graph_create", C.c_int, [C.c_uint64, C.c_uint64, _u64p, _u32p, _vp, C.POINTER(_vp)]),
+    ("gat_b200_graph_create_part", C.c_int, [C.c_uint64, C.c_uint64, C.c_uint64, _u64p, _u32p, _vp, C.POINTER(_vp)]),
     ("gat_b200_graph_destroy", C.c_int, [_vp]),
     ("gat_b200_graph_schedule", C.c_int, [_vp, _u32p, _u64p]),
     ("gat_b200_graph_device_csr", C.c_int, [_vp, C.POINTER(_vp), C.POINTER(_vp)]),
@@ -246,6 +249,29 @@ def synth_powerlaw_graph(n: int, e: int, max_degree: int, gamma: float, seed: in
     return row, col
 
 
+def synth_powerlaw_rowptr(n: int, e: int, max_degree: int, gamma: float, seed: int) -> np.ndarray:
+    """The n+1 row pointers of synth_powerlaw_graph (no sources)."""
+    row = np.empty(n + 1, np.uint64)
+    _check(_lib.gat_b200_synth_powerlaw_rows(n, e, max_degree, gamma, seed, 0, 0, _p(row, _u64p), None))
+    return row
+
+
+def synth_powerlaw_cols(n: int, e: int, max_degree: int, gamma: float, seed: int, row: np.ndarray, r_lo: int,
+                        r_hi: int) -> np.ndarray:
+    """The sources of rows [r_lo, r_hi) of synth_powerlaw_graph."""
+    row = np.ascontiguousarray(row, np.uint64).copy()
+    col = np.empty(int(row[r_hi] - row[r_lo]), np.uint32)
+    _check(_lib.gat_b200_synth_powerlaw_rows(n, e, max_degree, gamma, seed, r_lo, r_hi, _p(row, _u64p),
+                                             _p(col, _u32p)))
+    return col
+
+
+def synth_normal_range(offset: int, shape, seed: int, stream: int, scale: float = 1.0) -> np.ndarray:
+    out = np.empty(shape, np.float32)
+    _check(_lib.gat_b200_synth_normal_range(offset, out.size, scale, seed, stream, _p(out, _f32p)))
+    return out
+
+
 def synth_normal(shape, seed: int, stream: int, scale: float = 1.0) -> np.ndarray:
     out = np.empty(shape, np.float32)
     _check(_lib.gat_b200_synth_normal(out.size, scale, seed, stream, _p(out, _f32p)))
@@ -262,13 +288,20 @@ def synth_uniform(shape, lo: float, hi: float, seed: int, stream: int) -> np.nda
 class DeviceGraph:
     """CSR uploaded to the current CUDA device with its degree schedule."""
 
-    def __init__(self, row: np.ndarray, col: np.ndarray, stream=None):
+    def __init__(self, row: np.ndarray, col: np.ndarray, stream=None, n_src: Optional[int] = None):
+        """n_src: number of source rows when the graph is a partition slice
+        (gat_b200_graph_create_part); None for a square graph."""
         row = np.ascontiguousarray(row, np.uint64)
         col = np.ascontiguousarray(col, np.uint32)
         self.n = len(row) - 1
         self.e = len(col)
         h = _vp()
-        _check(_lib.gat_b200_graph_create(self.n, self.e, _p(row, _u64p), _p(col, _u32p), _stream(stream), C.byref(h)))
+        if n_src is None:
+            _check(_lib.gat_b200_graph_create(self.n, self.e, _p(row, _u64p), _p(col, _u32p), _stream(stream),
+                                              C.byref(h)))
+        else:
+            _check(_lib.gat_b200_graph_create_part(self.n, n_src, self.e, _p(row, _u64p), _p(col, _u32p),
+                                                   _stream(stream), C.byref(h)))
         self.handle = h
 
     def schedule(self):

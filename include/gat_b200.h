@@ -102,6 +102,16 @@ int gat_b200_synth_uniform_graph(uint64_t n, uint32_t sources, uint64_t seed, ui
 int gat_b200_synth_powerlaw_graph(uint64_t n, uint64_t e, uint64_t max_degree, double gamma,
                                   uint64_t seed, uint64_t* row, uint32_t* col);
 int gat_b200_synth_normal(uint64_t count, double scale, uint64_t seed, uint64_t stream, float* out);
+/* Rank-local pieces of the same inputs, for multi-GPU runs where no process
+ * builds the whole graph: elements [offset, offset+count) of synth_normal, and
+ * all n+1 row pointers of synth_powerlaw_graph with the sources of rows
+ * [r_lo, r_hi) only (col holds row[r_hi]-row[r_lo] entries; NULL = row
+ * pointers only). Identical values to the whole-graph calls. */
+int gat_b200_synth_normal_range(uint64_t offset, uint64_t count, double scale, uint64_t seed,
+                                uint64_t stream, float* out);
+int gat_b200_synth_powerlaw_rows(uint64_t n, uint64_t e, uint64_t max_degree, double gamma,
+                                 uint64_t seed, uint64_t r_lo, uint64_t r_hi, uint64_t* row,
+                                 uint32_t* col);
 int gat_b200_synth_uniform(uint64_t count, double lo, double hi, uint64_t seed, uint64_t stream,
                            float* out);
 
@@ -120,6 +130,13 @@ typedef struct gat_b200_graph gat_b200_graph;
  * above a degree threshold a whole CTA. */
 int gat_b200_graph_create(uint64_t n, uint64_t e, const uint64_t* row, const uint32_t* col,
                           void* stream, gat_b200_graph** out);
+/* A slice of a partitioned graph: n destination rows whose source ids index a
+ * feature table of n_src rows (the all-gathered projected features of every
+ * rank in the multi-GPU forward). No reference counterpart (the reference runs
+ * on one CPU); validation and schedule as gat_b200_graph_create, with the
+ * source bound n_src instead of n. */
+int gat_b200_graph_create_part(uint64_t n, uint64_t n_src, uint64_t e, const uint64_t* row,
+                               const uint32_t* col, void* stream, gat_b200_graph** out);
 int gat_b200_graph_destroy(gat_b200_graph* g);
 /* Copies the schedule back: perm[n] (may be NULL) and neighbor_steps (may be NULL). */
 int gat_b200_graph_schedule(const gat_b200_graph* g, uint32_t* perm, uint64_t* neighbor_steps);
