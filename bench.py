@@ -58,6 +58,74 @@ def parse():
 
 # --------------------------------------------------------------------- clocks
 class Clocks:
+    """SM clock and clock-event reasons sampled every 5 ms through NVML while
+    the timed region runs (read-only queries; no setting is changed). Falls
+    back to nvidia-smi at 100 ms when NVML cannot be opened."""
+
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap", "hw_power_brake")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.samples = []          # (sm_mhz, sm_max_mhz, reasons bitmask)
+        self.stop_ev = threading.Event()
+        self.thread = None
+        self.handle = None
+        self.nv = None
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            self.nv = nv
+            try:
+                import torch
+                pr = torch.cuda.get_device_properties(device)
+                bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+                self.handle = nv.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                self.handle = nv.nvmlDeviceGetHandleByIndex(device)
+            self.bits = {
+                "hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap,
+                "hw_power_brake": nv.nvmlClocksEventReasonHwPowerBrakeSlowdown,
+            }
+        except Exception:
+            self.handle = None
+
+    def _poll(self):
+        nv, h = self.nv, self.handle
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        while True:
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((float(sm), float(mx), int(rs)))
+            except Exception:
+                pass
+            if self.stop_ev.wait(0.005):
+                break
+
+    def start(self):
+        if self.handle is None:
+            self.smi = _SmiClocks(self.device)
+            self.smi.start()
+            return
+        self.thread = threading.Thread(target=self._poll, daemon=True)
+        self.thread.start()
+
+    def stop(self) -> dict:
+        if self.handle is None:
+            return self.smi.stop()
+        self.stop_ev.set()
+        self.thread.join(timeout=5)
+        sm = [s[0] for s in self.samples]
+        reasons = {nm for s in self.samples for nm, bit in self.bits.items() if s[2] & bit}
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(s[1] for s in self.samples) if sm else None,
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvml 5 ms"}
+
+
+class _SmiClocks:
     """nvidia-smi samples (every 100 ms) while the timed region runs."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -107,7 +175,7 @@ class Clocks:
                 if v.lower().startswith("active"):
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi 100 ms"}
 
 
 def peaks():
@@ -168,6 +236,11 @@ def agg_bytes(n, e, heads, dim, out_bytes_per_elem):
     return 8 * (n + 1) + 4 * e + 4 * n * heads + 4 * e * heads + 2 * e * heads * dim + out_bytes_per_elem * n * heads * dim
 
 
+def log(msg):
+    """Progress line on stderr, tagged with the rank (stdout carries only the JSON line)."""
+    print(f"[bench rank {os.environ.get('RANK', '0')}] {msg}", file=sys.stderr, flush=True)
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -210,6 +283,7 @@ def main():
         import datetime
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+        log("process group ready")
     stream = torch.cuda.current_stream()
     warm = max(args.warmup, 3)
 
@@ -269,9 +343,12 @@ def main():
     else:
         # ---- N GPUs: destination rows partitioned by edge count, NCCL all-gather ----
         import dist as gdist
+        log("building rank-local inputs")
         part = configs.make_part(args.config, rank, world)
+        log(f"rows [{part.lo}, {part.hi}) of {len(part.row) - 1}")
         n, e, din = len(part.row) - 1, part.e, part.din
         pm = gdist.PartitionedModel(part.row, part.col_rows, part.model, rank, world, stream, dist, part.cuts)
+        log("device model ready")
         n_loc, e_loc = pm.n_loc, pm.e_loc
         classes = pm.classes
         x_rows = part.x_rows
@@ -282,6 +359,7 @@ def main():
             fwd(x_dev, logits, False, False)
         torch.cuda.synchronize()
         G.check_device()
+        log("warm-up done")
         pm.enable_timing(True)
         clocks = Clocks(local)
         clocks.start()

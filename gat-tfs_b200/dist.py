@@ -131,7 +131,10 @@ class PartitionedModel:
             G.projection(p, n, lin, ldin, G.BF16, hs, G.BF16, ldh, self.left, rs, self.stream)
             self._mark(3 + 3 * l)
             if self.world > 1:
-                self.dist.all_gather_into_tensor(hf, hs)
+                # the feature tables hold BF16 bit patterns in int16 storage; NCCL
+                # has no 16-bit integer type, so the exchange goes through a
+                # bfloat16 view of the same bytes
+                self.dist.all_gather_into_tensor(hf.view(torch.bfloat16), hs.view(torch.bfloat16))
                 self.dist.all_gather_into_tensor(rf, rs)
             else:
                 hf, rf = hs, rs

@@ -74,7 +74,18 @@ def test_two_gpu_partitioned_forward_matches_single_gpu():
     procs = [ctx.Process(target=_rank_main, args=(r, 2, port, "c2", q)) for r in range(2)]
     for p in procs:
         p.start()
-    got = q.get(timeout=600)
+    import queue
+    import time
+    got, deadline = None, time.time() + 240
+    while got is None:
+        try:
+            got = q.get(timeout=2)
+        except queue.Empty:
+            dead = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
+            if dead or time.time() > deadline:
+                for p in procs:
+                    p.kill()
+                pytest.fail(f"rank processes failed or stalled (exit codes {[p.exitcode for p in procs]})")
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
