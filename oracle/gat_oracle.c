@@ -245,6 +245,139 @@ void oracle_standard_aggregate(uint64_t n, const uint64_t* row, const uint32_t* 
     }
 }
 
+/* V[c] += sum_k a[k] * wq[k][h*dim+c] for one neighbour step (or one block):
+ * sequential FP32 over k, the accumulation order of AMX tdpbf16ps; the
+ * products of two BF16 values are exact in FP32. */
+static void tfs_accumulate(int in, int width, int h, int dim, const float* a, const float* wq, float* v) {
+    for (int c = 0; c < dim; ++c) {
+        float acc = v[c];
+        for (int k = 0; k < in; ++k) acc = acc + a[k] * wq[(size_t)k * width + h * dim + c];
+        v[c] = acc;
+    }
+}
+
+void oracle_tfs_aggregate(uint64_t n, const uint64_t* row, const uint32_t* col, int in, int heads, int dim,
+                          const float* xq, const float* wq, const float* left, const float* right,
+                          const float* max_in, const float* fixed_p, const float* fixed_den, int rounding,
+                          int block, int threshold, float* out, float* den_out, float* max_out) {
+    const int width = heads * dim;
+    #pragma omp parallel for schedule(dynamic, 16)
+    for (long long i = 0; i < (long long)n; ++i) {
+        const uint64_t beg = row[i], deg = row[i + 1] - row[i];
+        const uint64_t B = block > 0 ? (uint64_t)block : (deg ? deg : 1);
+        float* hb = (float*)malloc((size_t)in * sizeof(float));
+        float* u = (float*)malloc((size_t)in * sizeof(float));
+        float* p = (float*)malloc((size_t)B * sizeof(float));
+        for (int h = 0; h < heads; ++h) {
+            const float L = left ? left[(size_t)i * heads + h] : 0.f;
+            float v[64];
+            for (int c = 0; c < dim; ++c) v[c] = 0.f;
+            float den = 0.f, m = -INFINITY;
+            for (uint64_t b0 = 0; b0 < deg; b0 += B) {
+                const uint64_t cnt = deg - b0 < B ? deg - b0 : B;
+                /* weights of the block */
+                if (fixed_p) {
+                    for (uint64_t b = 0; b < cnt; ++b) p[b] = fixed_p[(beg + b0 + b) * heads + h];
+                } else if (max_in) { /* baseline_tfs.cpp:55-57: exp(leaky(L+R) - prescan max) */
+                    const float mx = max_in[(size_t)i * heads + h];
+                    for (uint64_t b = 0; b < cnt; ++b)
+                        p[b] = expf(leak(L + right[(size_t)col[beg + b0 + b] * heads + h]) - mx);
+                    m = mx;
+                } else { /* icpp_online.cpp:75-135: block max, running max, rescale */
+                    float bm = -INFINITY;
+                    for (uint64_t b = 0; b < cnt; ++b) {
+                        p[b] = leak(L + right[(size_t)col[beg + b0 + b] * heads + h]);
+                        bm = p[b] > bm ? p[b] : bm;
+                    }
+                    const float prev = m;
+                    m = bm > m ? bm : m;
+                    const int changed = m > prev && den > 0.f;
+                    const float r = expf(changed ? prev - m : 0.f);
+                    den = den * r;
+                    for (uint64_t b = 0; b < cnt; ++b) p[b] = expf(p[b] - m);
+                    if (changed)
+                        for (int c = 0; c < dim; ++c) v[c] = v[c] * r;
+                }
+                for (uint64_t b = 0; b < cnt; ++b) den = den + p[b];
+                if (rounding == 0) { /* baseline_tfs.cpp:60-84: V += RNE(p*x) . W per neighbour */
+                    for (uint64_t b = 0; b < cnt; ++b) {
+                        const float* xr = xq + (size_t)col[beg + b0 + b] * in;
+                        for (int k = 0; k < in; ++k) hb[k] = oracle_expand(oracle_rne(xr[k] * p[b]));
+                        tfs_accumulate(in, width, h, dim, hb, wq, v);
+                    }
+                } else {
+                    for (int k = 0; k < in; ++k) u[k] = 0.f;
+                    if (rounding == 1 || (int64_t)cnt < (int64_t)threshold) {
+                        /* icpp_block.cpp:151-178: FP32 FMA chain over the block */
+                        for (int k = 0; k < in; ++k) {
+                            float acc = 0.f;
+                            for (uint64_t b = 0; b < cnt; ++b)
+                                acc = fmaf(p[b], xq[(size_t)col[beg + b0 + b] * in + k], acc);
+                            u[k] = acc;
+                        }
+                    } else {
+                        /* icpp_heads_hybrid.cpp:186-214: p = hi + lo (two BF16), hi pass then lo pass */
+                        for (int k = 0; k < in; ++k) {
+                            float acc = 0.f;
+                            for (uint64_t b = 0; b < cnt; ++b) {
+                                const float hi = oracle_expand(oracle_rne(p[b]));
+                                acc = acc + hi * xq[(size_t)col[beg + b0 + b] * in + k];
+                            }
+                            for (uint64_t b = 0; b < cnt; ++b) {
+                                const float hi = oracle_expand(oracle_rne(p[b]));
+                                const float lo = oracle_expand(oracle_rne(p[b] - hi));
+                                acc = acc + lo * xq[(size_t)col[beg + b0 + b] * in + k];
+                            }
+                            u[k] = acc;
+                        }
+                    }
+                    for (int k = 0; k < in; ++k) hb[k] = oracle_expand(oracle_rne(u[k])); /* icpp_block.cpp:185-188 */
+                    tfs_accumulate(in, width, h, dim, hb, wq, v);
+                }
+            }
+            for (int c = 0; c < dim; ++c) out[(size_t)i * width + h * dim + c] = v[c];
+            den_out[(size_t)i * heads + h] = fixed_den ? fixed_den[(size_t)i * heads + h] : den;
+            if (max_out) max_out[(size_t)i * heads + h] = m;
+        }
+        free(hb); free(u); free(p);
+    }
+}
+
+void oracle_prepare_blr(int in, int heads, int dim, const float* w, const float* al, const float* ar,
+                        float* blr) {
+    /* common.cpp:100-106 */
+    const int width = heads * dim;
+    for (int k = 0; k < in; ++k)
+        for (int h = 0; h < heads; ++h) {
+            float l = 0.f, r = 0.f;
+            for (int d = 0; d < dim; ++d) {
+                const float wv = w[(size_t)k * width + h * dim + d];
+                l = fmaf(wv, al[h * dim + d], l);
+                r = fmaf(wv, ar[h * dim + d], r);
+            }
+            blr[(size_t)k * 2 * heads + h] = l;
+            blr[(size_t)k * 2 * heads + heads + h] = r;
+        }
+}
+
+void oracle_lr_reordered(uint64_t n, int in, int heads, const float* x, const float* xq, const float* blr,
+                         int policy, float* left, float* right) {
+    /* baseline_standard.cpp:29-43 */
+    const int cols = 2 * heads;
+    #pragma omp parallel for schedule(static)
+    for (long long i = 0; i < (long long)n; ++i)
+        for (int c = 0; c < cols; ++c) {
+            float acc = 0.f;
+            for (int k = 0; k < in; ++k) {
+                const float b = blr[(size_t)k * cols + c];
+                acc = policy == 0 ? fmaf(xq[(size_t)i * in + k], oracle_expand(oracle_rne(b)), acc)
+                                  : fmaf(x[(size_t)i * in + k], b, acc);
+            }
+            if (c < heads) left[(size_t)i * heads + c] = acc;
+            else right[(size_t)i * heads + c - heads] = acc;
+        }
+}
+
 void oracle_finish(uint64_t n, int heads, int dim, const float* den, int hidden, float* out) {
     /* baseline_standard.cpp:85-97; activation() (gat.hpp:57-62) is exp(x)-1 for x<0. */
     const int width = heads * dim;

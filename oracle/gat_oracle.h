@@ -72,6 +72,46 @@ void oracle_standard_aggregate(uint64_t n, const uint64_t* row, const uint32_t* 
                                const float* fixed_p, const float* fixed_den,
                                float* out, float* den);
 
+/* TFS ("transform from sum") aggregation family, restated per destination
+ * row (the reference's 16-row batching does not change a row's arithmetic).
+ * xq: BF16-valued features [n][in]; wq: BF16-valued W [in][heads*dim].
+ * Every variant writes the UNNORMALIZED V[n][heads*dim], den[n][heads] and,
+ * if max_out is set, the final row maximum.
+ *
+ *  rounding 0, max given, block 0   baseline/src/baseline_tfs.cpp:16-110
+ *      (tfs_aggregate, B1): p from the prescan max, every product rounded,
+ *      V += RNE(p*x) . W in neighbour order. fixed_p/fixed_den as B0.
+ *  rounding 0, max NULL, block B    baseline/tfs_online/icpp_online.cpp:40-215
+ *      (icpp_online): running max per block of B neighbours, V and den
+ *      rescaled by exp(old-new) when it grows, products rounded as B1.
+ *  rounding 1, max NULL, block B    baseline/tfs_online/icpp_block.cpp:36-210
+ *      (icpp_block): U_B = sum_{j in block} p_j x_j (FP32 FMA chain),
+ *      V += RNE(U_B) . W.
+ *  rounding 2, max NULL, block B    baseline/tfs_online/icpp_heads_hybrid.cpp:44-290
+ *      (icpp_heads_hybrid): as rounding 1 for rows with fewer than `threshold`
+ *      neighbours in the block; otherwise U_B = sum p_hi x + sum p_lo x with
+ *      p = p_hi + p_lo split into two BF16 values (the AMX high/low path).
+ *  max given with rounding 1 or 2 uses that maximum for every block (no
+ *  rescale): the B200 tensor-core kernel's semantics. block 0 = whole row.
+ * All V accumulation is sequential FP32 in (neighbour, feature) order, the
+ * order of AMX tdpbf16ps over the reference's K blocks. */
+void oracle_tfs_aggregate(uint64_t n, const uint64_t* row, const uint32_t* col, int in, int heads, int dim,
+                          const float* xq, const float* wq, const float* left, const float* right,
+                          const float* max_in, const float* fixed_p, const float* fixed_den, int rounding,
+                          int block, int threshold, float* out, float* den, float* max_out);
+
+/* baseline/src/common.cpp:100-106 (prepare, attention=true): blr[k][h] =
+ * sum_d W[k][h*dim+d] * aL[h*dim+d] (and aR at [k][heads+h]), one FMA chain
+ * per entry (the reference is compiled with FMA contraction). */
+void oracle_prepare_blr(int in, int heads, int dim, const float* w, const float* al, const float* ar,
+                        float* blr);
+
+/* baseline/src/baseline_standard.cpp:29-43 (lr_reordered): [L|R] = X . blr.
+ * policy 0 "bf16": BF16 X (xq) times RNE(blr); 1 "fp32": FP32 X times blr.
+ * Each dot is a sequential FMA chain over the input features. */
+void oracle_lr_reordered(uint64_t n, int in, int heads, const float* x, const float* xq, const float* blr,
+                         int policy, float* left, float* right);
+
 /* baseline/src/baseline_standard.cpp:85-97 (finish): out *= 1/den (0 if den<=0),
  * then ELU (gat.hpp:53) when hidden. */
 void oracle_finish(uint64_t n, int heads, int dim, const float* den, int hidden, float* out);

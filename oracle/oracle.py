@@ -40,6 +40,10 @@ _lib.oracle_b0_layer.argtypes = _layer_args + [C.c_int, C.c_int] + [_f32p] * 6
 _lib.oracle_max_prescan.argtypes = [C.c_uint64, _u64p, _u32p, C.c_int, _f32p, _f32p, _f32p]
 _lib.oracle_standard_aggregate.argtypes = [C.c_uint64, _u64p, _u32p, C.c_int, C.c_int] + [_f32p] * 8
 _lib.oracle_finish.argtypes = [C.c_uint64, C.c_int, C.c_int, _f32p, C.c_int, _f32p]
+_lib.oracle_tfs_aggregate.argtypes = ([C.c_uint64, _u64p, _u32p, C.c_int, C.c_int, C.c_int] + [_f32p] * 7 +
+                                      [C.c_int, C.c_int, C.c_int] + [_f32p] * 3)
+_lib.oracle_prepare_blr.argtypes = [C.c_int, C.c_int, C.c_int, _f32p, _f32p, _f32p, _f32p]
+_lib.oracle_lr_reordered.argtypes = [C.c_uint64, C.c_int, C.c_int, _f32p, _f32p, _f32p, C.c_int, _f32p, _f32p]
 _lib.oracle_boundary_params.argtypes = [C.c_int, C.c_int, C.c_int, _f32p, _f32p, _f32p]
 _lib.oracle_random_layer.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, _f32p, _f32p, _f32p]
 
@@ -151,6 +155,65 @@ def finish(out, den, heads, dim, hidden):
     n = out.shape[0]
     _lib.oracle_finish(n, heads, dim, _p(_f(den), _f32p), int(hidden), _p(out, _f32p))
     return out
+
+
+TFS_EDGE, TFS_BLOCK, TFS_SPLIT = 0, 1, 2
+
+
+def tfs_aggregate(row, col, xq, wq, left, right, heads, dim, mx=None, rounding=TFS_EDGE, block=0, threshold=1,
+                  fixed_p=None, fixed_den=None):
+    """TFS aggregation family (baseline_tfs.cpp:16-110, icpp_online/icpp_block/
+    icpp_heads_hybrid; see gat_oracle.h). xq, wq: BF16-valued FP32 arrays.
+    Returns (unnormalized out [n][heads*dim], den [n][heads], max [n][heads])."""
+    row = np.ascontiguousarray(row, np.uint64)
+    col = np.ascontiguousarray(col, np.uint32)
+    xq, wq = _f(xq), _f(wq)
+    n = len(row) - 1
+    out = np.empty((n, heads * dim), np.float32)
+    den = np.empty((n, heads), np.float32)
+    mo = np.empty((n, heads), np.float32)
+    _lib.oracle_tfs_aggregate(n, _p(row, _u64p), _p(col, _u32p), xq.shape[1], heads, dim, _p(xq, _f32p),
+                              _p(wq, _f32p), _p(None if left is None else _f(left), _f32p),
+                              _p(None if right is None else _f(right), _f32p),
+                              _p(None if mx is None else _f(mx), _f32p),
+                              _p(None if fixed_p is None else _f(fixed_p), _f32p),
+                              _p(None if fixed_den is None else _f(fixed_den), _f32p), int(rounding), int(block),
+                              int(threshold), _p(out, _f32p), _p(den, _f32p), _p(mo, _f32p))
+    return out, den, mo
+
+
+def prepare_blr(w, al, ar, heads, dim):
+    """common.cpp:100-106: blr [in][2*heads] (L columns, then R columns)."""
+    w = _f(w)
+    blr = np.empty((w.shape[0], 2 * heads), np.float32)
+    _lib.oracle_prepare_blr(w.shape[0], heads, dim, _p(w, _f32p), _p(_f(al), _f32p), _p(_f(ar), _f32p),
+                            _p(blr, _f32p))
+    return blr
+
+
+def lr_reordered(x, blr, heads, policy):
+    """baseline_standard.cpp:29-43; policy 0 = "bf16" (BF16 X, RNE(blr)), 1 = "fp32"."""
+    x = _f(x)
+    xq = quantize(x)
+    n = x.shape[0]
+    left = np.empty((n, heads), np.float32)
+    right = np.empty((n, heads), np.float32)
+    _lib.oracle_lr_reordered(n, x.shape[1], heads, _p(x, _f32p), _p(xq, _f32p), _p(_f(blr), _f32p), int(policy),
+                             _p(left, _f32p), _p(right, _f32p))
+    return left, right
+
+
+def tfs_layer(row, col, x, w, al, ar, heads, dim, hidden, policy=0, rounding=TFS_EDGE, block=0, threshold=1):
+    """baseline_tfs.cpp:111-117 (tfs_layer): convert, lr_reordered, max_prescan,
+    tfs_aggregate, finish. rounding/block/threshold select the icpp_* variants
+    (their layer() functions run the same stages, icpp_block.cpp:329-352)."""
+    xq = quantize(x)
+    blr = prepare_blr(w, al, ar, heads, dim)
+    left, right = lr_reordered(x, blr, heads, policy)
+    mx = max_prescan(row, col, left, right, heads) if rounding == TFS_EDGE and block == 0 else None
+    out, den, _ = tfs_aggregate(row, col, xq, quantize(w), left, right, heads, dim, mx=mx, rounding=rounding,
+                                block=block, threshold=threshold)
+    return finish(out, den, heads, dim, hidden)
 
 
 def boundary_params(D, K, d):

@@ -6,7 +6,13 @@
 //   ref_dump boundary OUTDIR          64 D/K/d cases of baseline/tests/boundaries.cpp
 //   ref_dump chain GRAPH WEIGHTS OUTDIR   three-layer chains on a GATBIN1 graph;
 //                                     WEIGHTS = GATWGT1 path or "seed:N" (random_model)
+//   ref_dump tfs OUTDIR               TFS aggregation variants (B1, icpp_online,
+//                                     icpp_block, icpp_heads_hybrid) on the
+//                                     boundary graphs, with their inputs
 #include "gat.hpp"
+#include "icpp_block.hpp"
+#include "icpp_heads_hybrid.hpp"
+#include "icpp_online.hpp"
 
 #include <cstdio>
 #include <iostream>
@@ -85,6 +91,81 @@ static int boundary(const std::string& out) {
     return 0;
 }
 
+// The TFS family on the boundary graphs. Inputs (BF16 X, L, R from the BF16
+// lr policy, prescan max) come from the reference's own stages and are dumped
+// with the outputs, so the restatement is checked on identical inputs.
+static int tfs(const std::string& out) {
+    int cases = 0;
+    for (int D : {17, 33, 128, 256})
+        for (int K : {1, 2, 4, 8})
+            for (int d : {7, 32, 40, 47}) {
+                Graph g = boundary_graph(D);
+                Param p = boundary_params(D, K, d);
+                Prepared q = prepare(p, true, true, true);
+                Schedule s = degree_schedule(g);
+                Workspace w;
+                w.allocate(g, p, "tfs_bf16");
+                convert(g.x.data(), w.xbf.data(), g.x.size());
+                lr_reordered(g, p, q, g.x, w, "bf16");
+                std::vector<float> lbf = w.left, rbf = w.right;
+                lr_reordered(g, p, q, g.x, w, "fp32");
+                std::vector<float> l32 = w.left, r32 = w.right;
+                w.left = lbf;
+                w.right = rbf;
+                max_prescan(g, p, w);
+                Times t;
+                tfs_aggregate(g, p, q, s, w, 16, t);
+                std::string pre = out + "/tfs_" + std::to_string(D) + "_" + std::to_string(K) + "_" + std::to_string(d);
+                dumpv(pre + "_xbf.u16", w.xbf);
+                dumpv(pre + "_w.f32", p.w);
+                dumpv(pre + "_al.f32", p.al);
+                dumpv(pre + "_ar.f32", p.ar);
+                dumpv(pre + "_blr.f32", q.blr);
+                dumpv(pre + "_lbf.f32", lbf);
+                dumpv(pre + "_rbf.f32", rbf);
+                dumpv(pre + "_l32.f32", l32);
+                dumpv(pre + "_r32.f32", r32);
+                dumpv(pre + "_max.f32", w.max);
+                dumpv(pre + "_b1_out.f32", w.out);
+                dumpv(pre + "_b1_den.f32", w.den);
+                {
+                    icpp_online::Workspace o;
+                    o.allocate(g, p);
+                    o.base.xbf = w.xbf; o.base.left = lbf; o.base.right = rbf;
+                    icpp_online::Stats st;
+                    icpp_online::aggregate(g, p, q, s, o, 16, 16, st);
+                    dumpv(pre + "_online16_out.f32", o.base.out);
+                    dumpv(pre + "_online16_den.f32", o.base.den);
+                    dumpv(pre + "_online16_max.f32", o.base.max);
+                }
+                {
+                    icpp_block::Workspace b;
+                    b.allocate(g, p);
+                    auto& bb = b.original.base;
+                    bb.xbf = w.xbf; bb.left = lbf; bb.right = rbf;
+                    icpp_block::Stats st;
+                    icpp_block::aggregate(g, p, q, s, b, 32, 16, st);
+                    dumpv(pre + "_block32_out.f32", bb.out);
+                    dumpv(pre + "_block32_den.f32", bb.den);
+                    dumpv(pre + "_block32_max.f32", bb.max);
+                }
+                {
+                    icpp_heads_hybrid::Workspace hw;
+                    hw.allocate(g, p);
+                    auto& hb = hw.fallback.original.base;
+                    hb.xbf = w.xbf; hb.left = lbf; hb.right = rbf;
+                    icpp_heads_hybrid::Stats st;
+                    icpp_heads_hybrid::aggregate(g, p, q, s, hw, 32, 16, st, 0, false, 16);
+                    dumpv(pre + "_hybrid32_out.f32", hb.out);
+                    dumpv(pre + "_hybrid32_den.f32", hb.den);
+                    dumpv(pre + "_hybrid32_max.f32", hb.max);
+                }
+                ++cases;
+            }
+    std::cout << "TFS_DUMP cases=" << cases << "\n";
+    return 0;
+}
+
 static int chain(const std::string& graph, const std::string& weights, const std::string& out) {
     Graph g = load_graph(graph);
     Model model;
@@ -126,6 +207,20 @@ static int chain(const std::string& graph, const std::string& weights, const std
         }
         dumpv(out + (fp32 ? "/b0fp32_out.f32" : "/b0bf16_out.f32"), in);
     }
+    // TFS BF16 chain (bench/main.cpp:23 path tfs_bf16, lr policy bf16, panel 16).
+    {
+        std::vector<Prepared> prep;
+        for (const auto& p : model) prep.push_back(prepare(p, true, true, true));
+        std::vector<float> in = g.x;
+        for (int l = 0; l < 3; ++l) {
+            Workspace w;
+            w.allocate(g, model[l], "tfs_bf16");
+            Times t;
+            tfs_layer(g, model[l], prep[l], s, in, w, l < 2, 16, t, "bf16");
+            in = std::move(w.out);
+        }
+        dumpv(out + "/tfsbf16_out.f32", in);
+    }
     std::cout << "CHAIN_DUMP n=" << g.n << " e=" << g.e << "\n";
     return 0;
 }
@@ -136,7 +231,8 @@ int main(int argc, char** argv) {
         std::string mode = argc > 1 ? argv[1] : "";
         if (mode == "boundary" && argc == 3) return boundary(argv[2]);
         if (mode == "chain" && argc == 5) return chain(argv[2], argv[3], argv[4]);
-        std::cerr << "usage: ref_dump boundary OUTDIR | ref_dump chain GRAPH WEIGHTS OUTDIR\n";
+        if (mode == "tfs" && argc == 3) return tfs(argv[2]);
+        std::cerr << "usage: ref_dump boundary OUTDIR | ref_dump chain GRAPH WEIGHTS OUTDIR | ref_dump tfs OUTDIR\n";
         return 2;
     } catch (const std::exception& e) {
         std::cerr << "FAIL " << e.what() << "\n";

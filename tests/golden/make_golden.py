@@ -19,6 +19,11 @@ sources in place by oracle/Makefile; nothing here is hand-written):
     by this repository's generator (GATBIN1 / GATWGT1 hashes recorded).
   * boundary.npz: R0 (and for a subset B0 BF16) outputs of the 64 D/K/d
     cases of baseline/tests/boundaries.cpp, plus its degree schedule.
+  * tfs.npz: the TFS aggregation family on a subset of the boundary cases:
+    B1 tfs_aggregate, icpp_online (block 16), icpp_block (block 32) and
+    icpp_heads_hybrid (block 32, threshold 16) outputs, with the inputs the
+    reference computed for them (BF16- and FP32-policy L/R, prescan max, blr).
+    The chain npz files also hold the tfs_bf16 path's three-layer logits.
 """
 import hashlib
 import json
@@ -39,6 +44,11 @@ import gatb200 as G  # noqa: E402
 REF = Path(os.environ.get("REF", "/root/reference"))
 OUT = Path(__file__).resolve().parent
 DUMP = ROOT / "oracle" / "_ref" / "ref_dump"
+
+
+# Boundary shapes (D, K, d) kept for the TFS fixtures: the layer shapes of the
+# configs (128->8x32, 256->8x32, 256->1x47) and three odd ones.
+TFS_CASES = [(17, 1, 7), (33, 2, 40), (128, 8, 32), (256, 8, 32), (256, 1, 47), (128, 4, 47)]
 
 
 def sha256(path) -> str:
@@ -76,6 +86,7 @@ def chain_npz(d: Path, n: int, classes: int) -> dict:
     out["ref_logits"] = load(d, "ref_l3_out.f32").reshape(n, classes)
     out["b0bf16_logits"] = load(d, "b0bf16_out.f32").reshape(n, classes)
     out["b0fp32_logits"] = load(d, "b0fp32_out.f32").reshape(n, classes)
+    out["tfsbf16_logits"] = load(d, "tfsbf16_out.f32").reshape(n, classes)
     return out
 
 
@@ -129,6 +140,22 @@ def main():
                                                  load(d, f"bnd_{key}_al.f32").astype(np.float64).sum(),
                                                  load(d, f"bnd_{key}_ar.f32").astype(np.float64).sum()])
         np.savez_compressed(OUT / "boundary.npz", **b)
+
+        # TFS family (ref_dump tfs), a subset of the boundary shapes
+        d = tmp / "tfs"
+        d.mkdir()
+        subprocess.run([str(DUMP), "tfs", str(d)], check=True)
+        t = {}
+        for D, K, dd in TFS_CASES:
+            key = f"{D}_{K}_{dd}"
+            pre = f"tfs_{key}_"
+            for name in ("lbf", "rbf", "l32", "r32", "max", "b1_den", "online16_den", "online16_max",
+                         "block32_den", "block32_max", "hybrid32_den", "hybrid32_max"):
+                t[f"{name}_{key}"] = load(d, pre + name + ".f32").reshape(35, K)
+            t[f"blr_{key}"] = load(d, pre + "blr.f32").reshape(D, 2 * K)
+            for name in ("b1_out", "online16_out", "block32_out", "hybrid32_out"):
+                t[f"{name}_{key}"] = load(d, pre + name + ".f32").reshape(35, K * dd)
+        np.savez_compressed(OUT / "tfs.npz", **t)
     (OUT / "MANIFEST.json").write_text(json.dumps(manifest, indent=1, sort_keys=True) + "\n")
     print(json.dumps(manifest, indent=1))
 

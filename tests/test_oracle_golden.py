@@ -145,3 +145,71 @@ def test_b0_chain_matches_reference():
     # so the chained B0 restatement agrees to ~4e-5, not to FP32 precision.
     # For scale: B0 BF16 itself is 2.8e-3 (rel-L2) away from R0 on this input.
     assert e["relative_l2"] <= 2e-4, e
+
+
+TFS_CASES = [(17, 1, 7), (33, 2, 40), (128, 8, 32), (256, 8, 32), (256, 1, 47), (128, 4, 47)]
+
+
+@pytest.mark.parametrize("case", TFS_CASES, ids=lambda c: "_".join(map(str, c)))
+def test_tfs_family_matches_reference(case):
+    """TFS restatements vs the reference's own B1 / icpp_online / icpp_block /
+    icpp_heads_hybrid on the same inputs (L, R, max from the reference).
+
+    The reference accumulates V = sum RNE(.) x W with AMX tdpbf16ps, whose
+    internal summation does not reproduce as sequential FP32 adds: the
+    restatement agrees to ~1e-5 relative, not bit for bit. den (plain FP32
+    sums of the same exp values) is exact."""
+    D, K, d = case
+    key = f"{D}_{K}_{d}"
+    t = np.load(GOLDEN / "tfs.npz")
+    row, col, x = O.boundary_graph(D)
+    w, al, ar = O.boundary_params(D, K, d)
+    xq, wq = O.quantize(x), O.quantize(w)
+    L, R, mx = t["lbf_" + key], t["rbf_" + key], t["max_" + key]
+
+    def close(got, want, rel):
+        scale = max(1e-30, float(np.abs(want).max()))
+        assert np.abs(got - want).max() <= rel * scale, (key, float(np.abs(got - want).max() / scale))
+
+    blr = O.prepare_blr(w, al, ar, K, d)
+    close(blr, t["blr_" + key], 1e-6)
+    l0, r0 = O.lr_reordered(x, t["blr_" + key], K, 0)
+    close(np.concatenate([l0, r0]), np.concatenate([L, R]), 1e-4)  # oneMKL BF16 GEMM order
+    l1, r1 = O.lr_reordered(x, t["blr_" + key], K, 1)
+    close(np.concatenate([l1, r1]), np.concatenate([t["l32_" + key], t["r32_" + key]]), 2e-6)
+    assert np.array_equal(O.max_prescan(row, col, L, R, K), mx)
+
+    out, den, _ = O.tfs_aggregate(row, col, xq, wq, L, R, K, d, mx=mx, rounding=O.TFS_EDGE)
+    close(out, t["b1_out_" + key], 5e-5)
+    assert np.array_equal(den, t["b1_den_" + key])
+    for name, rounding, block, thr in (("online16", O.TFS_EDGE, 16, 1), ("block32", O.TFS_BLOCK, 32, 1),
+                                       ("hybrid32", O.TFS_SPLIT if (K, d) == (8, 32) else O.TFS_BLOCK, 32, 16)):
+        out, den, m = O.tfs_aggregate(row, col, xq, wq, L, R, K, d, rounding=rounding, block=block, threshold=thr)
+        close(out, t[f"{name}_out_{key}"], 2e-4 if name == "hybrid32" else 5e-5)
+        assert np.array_equal(den, t[f"{name}_den_{key}"]), name
+        assert np.array_equal(m, t[f"{name}_max_{key}"]), name
+        # the running maximum ends at the prescan maximum (leaky is monotone)
+        nz = np.diff(row.astype(np.int64)) > 0
+        assert np.array_equal(m[nz], mx[nz])
+
+
+@pytest.mark.parametrize("name", ["smoke1024_seed11", "config1"])
+def test_tfs_chain_matches_reference(name):
+    """Three tfs_layer calls (path tfs_bf16, lr policy bf16) vs the reference."""
+    import configs
+    g = np.load(GOLDEN / f"{name}.npz")
+    if name == "config1":
+        cfg = configs.make("c1")
+        graph, model = cfg.graph, [(p.w, p.al, p.ar, p.heads, p.dim) for p in cfg.model]
+    else:
+        graph, model = smoke1024_graph(), O.random_model(128, 40, 11)
+    inp = graph.x
+    for l, (w, al, ar, h, d) in enumerate(model):
+        inp = O.tfs_layer(graph.row, graph.col, inp, w, al, ar, h, d, l < 2)
+    e = O.errors(g["tfsbf16_logits"], inp)
+    # L/R come from a BF16 GEMM whose summation order differs from oneMKL's;
+    # every layer re-rounds to BF16, so last-bit differences flip some
+    # roundings (as for the B0 chain).
+    assert e["relative_l2"] <= 5e-4, e
+    r0 = O.errors(g["ref_logits"], inp)
+    assert r0["relative_l2"] <= 2e-2, r0  # TFS BF16 vs R0: same order as B0 BF16
