@@ -24,10 +24,18 @@ int projection_tc_launch(const gat_b200_layer* p, uint64_t n, const uint16_t* x,
                          float* z, int ldz, float* left, float* right, cudaStream_t st);
 int projection_tc_check_error();
 int aggregate_check_error();
+int tfs_tc_check_error();
+int lr_reordered_launch(const gat_b200_layer* p, uint64_t n, const void* x, int x_dtype, int ldx, int policy,
+                        uint16_t* xb, int ldb, float* left, float* right, cudaStream_t st);
+int tfs_dispatch(const gat_b200_graph* g, const gat_b200_layer* p, const void* x, int ldx, const float* left,
+                 const float* right, const float* max, const float* fixed_p, const float* fixed_den, int rounding,
+                 int block, int threshold, int norm, int hidden, void* out, int out_bf16, int ldo, float* den,
+                 float* max_out, cudaStream_t st, int* launches);
 int device_check_errors() {
     int rc = projection_tc_check_error();
     int rc2 = aggregate_check_error();
-    return rc ? rc : rc2;
+    int rc3 = tfs_tc_check_error();
+    return rc ? rc : (rc2 ? rc2 : rc3);
 }
 
 namespace {
@@ -74,6 +82,7 @@ struct gat_b200_model {
     void* x2 = nullptr;
     int ld_hidden = 0;
     float* logits = nullptr;    // [n][classes]
+    float* max = nullptr;       // TFS paths: prescan maxima [n][8]
     // Optional per-stage CUDA events: `timing_steps` sets of kStageEvents,
     // one set per forward in a ring (no synchronisation inside forward).
     std::vector<cudaEvent_t> events;
@@ -203,15 +212,16 @@ int gat_b200_layer_create(int in, int heads, int dim, const float* w, const floa
     for (int k = 0; k < in; ++k)
         for (int c = 0; c < width; ++c) wt[size_t(c) * p->kp + k] = gat_b200_rne(w[size_t(k) * width + c]);
     // blr[k][h] = sum_d W[k][h*dim+d] aL[h*dim+d], blr[k][heads+h] likewise with aR
-    // (common.cpp:100-108), accumulated in FP32 in ascending d.
+    // (common.cpp:100-108): one FMA chain in ascending d, as the reference's
+    // FMA-contracted build evaluates it (the TFS path's lr_reordered input).
     std::vector<float> blr(size_t(in) * 2 * heads);
     for (int k = 0; k < in; ++k)
         for (int h = 0; h < heads; ++h) {
             float l = 0, r = 0;
             for (int d = 0; d < dim; ++d) {
-                float wv = w[size_t(k) * width + h * dim + d];
-                l += wv * al[h * dim + d];
-                r += wv * ar[h * dim + d];
+                const float wv = w[size_t(k) * width + h * dim + d];
+                l = std::fma(wv, al[h * dim + d], l);
+                r = std::fma(wv, ar[h * dim + d], r);
             }
             blr[size_t(k) * 2 * heads + h] = l;
             blr[size_t(k) * 2 * heads + heads + h] = r;
@@ -319,8 +329,7 @@ int gat_b200_model_create(const gat_b200_graph* g, const gat_b200_layer* const* 
     if (!out) return fail("model_create: null output handle");
     *out = nullptr;
     if (!g || !layers || !layers[0] || !layers[1] || !layers[2]) return fail("model_create: null handle");
-    if (path != GAT_B200_PATH_STANDARD_BF16 && path != GAT_B200_PATH_STANDARD_FP32)
-        return fail("model_create: bad path");
+    if (path < GAT_B200_PATH_STANDARD_BF16 || path > GAT_B200_PATH_ADAPTIVE_BF16) return fail("model_create: bad path");
     for (int l = 0; l < 2; ++l)
         if (layers[l + 1]->in != layers[l]->width) return fail("model_create: layer widths do not chain");
     gat_b200_model* m = new (std::nothrow) gat_b200_model();
@@ -331,8 +340,9 @@ int gat_b200_model_create(const gat_b200_graph* g, const gat_b200_layer* const* 
     m->din = layers[0]->in;
     m->classes = layers[2]->width;
     const uint64_t n = g->n;
-    const int hd = path == GAT_B200_PATH_STANDARD_BF16 ? GAT_B200_BF16 : GAT_B200_F32;
+    const int hd = path == GAT_B200_PATH_STANDARD_FP32 ? GAT_B200_F32 : GAT_B200_BF16;
     const int es = hd == GAT_B200_BF16 ? 2 : 4;
+    const bool tfs = path == GAT_B200_PATH_TFS_BF16 || path == GAT_B200_PATH_ADAPTIVE_BF16;
     int wmax = 0;
     for (int l = 0; l < 3; ++l) wmax = std::max(wmax, layers[l]->width);
     m->ld0 = gat_b200_padded_ld(m->din, hd);
@@ -348,6 +358,7 @@ int gat_b200_model_create(const gat_b200_graph* g, const gat_b200_layer* const* 
         if ((rc = dmalloc(&m->x1, n * size_t(m->ld_hidden) * es))) break;
         if ((rc = dmalloc(&m->x2, n * size_t(m->ld_hidden) * es))) break;
         if ((rc = dmalloc((void**)&m->logits, n * size_t(m->classes) * 4))) break;
+        if (tfs && (rc = dmalloc((void**)&m->max, n * 8 * 4))) break;
         // Padding columns of every feature buffer start (and stay) zero.
         cudaError_t e;
         if ((e = cudaMemset(m->h, 0, n * size_t(ldh) * es)) ||
@@ -377,6 +388,7 @@ int gat_b200_model_destroy(gat_b200_model* m) {
     cudaFree(m->x1);
     cudaFree(m->x2);
     cudaFree(m->logits);
+    cudaFree(m->max);
     delete m;
     return 0;
 }
@@ -395,12 +407,17 @@ int gat_b200_model_forward(gat_b200_model* m, const float* x, int x_on_host, flo
         xin = m->x_f32;
     }
     mark(m, 1, st);
-    const bool bf16 = m->path == GAT_B200_PATH_STANDARD_BF16;
+    const bool bf16 = m->path != GAT_B200_PATH_STANDARD_FP32;
     const int hd = bf16 ? GAT_B200_BF16 : GAT_B200_F32;
     const void* lin = xin;
     int ldin = m->din;
     int rc;
-    if (bf16) {
+    // Layer l runs TFS (lr_reordered + max_prescan, then TFS aggregation with
+    // finish fused) on the TFS path, and on layer 1 of the adaptive path.
+    auto tfs_layer = [&](int l) {
+        return m->path == GAT_B200_PATH_TFS_BF16 || (m->path == GAT_B200_PATH_ADAPTIVE_BF16 && l == 0);
+    };
+    if (bf16 && !tfs_layer(0)) {
         // Layer-1 input conversion (standard_layer's convert, baseline_standard.cpp:127).
         if ((rc = convert_launch(n, m->din, xin, m->din, static_cast<uint16_t*>(m->x0), m->ld0, st))) return rc;
         ++launches;
@@ -410,18 +427,43 @@ int gat_b200_model_forward(gat_b200_model* m, const float* x, int x_on_host, flo
     void* outs[2] = {m->x1, m->x2};
     for (int l = 0; l < 3; ++l) {
         const gat_b200_layer* p = m->layers[l];
-        const int ldh = gat_b200_padded_ld(p->width, hd);
-        mark(m, 2 + 2 * l, st);
-        if ((rc = projection_dispatch(p, n, lin, ldin, hd, m->h, hd, ldh, m->left, m->right, st))) return rc;
-        mark(m, 3 + 2 * l, st);
         const bool last = l == 2;
         float* dst_logits = (last && !logits_on_host) ? logits : m->logits;
         void* dst = last ? static_cast<void*>(dst_logits) : outs[l];
         const int ldo = last ? p->width : m->ld_hidden;
-        if ((rc = aggregate_dispatch(m->g, p->heads, p->dim, m->h, hd, ldh, m->left, m->right, nullptr, nullptr, 0,
-                                     last ? 0 : 1, dst, (!last && bf16) ? 1 : 0, ldo, nullptr, nullptr, st)))
-            return rc;
-        launches += 2 + (m->g->n_hub ? 1 : 0);
+        mark(m, 2 + 2 * l, st);
+        if (tfs_layer(l)) {
+            // baseline_tfs.cpp:111-117: convert + lr_reordered ("bf16" policy), max_prescan
+            if (l == 0) {
+                if ((rc = lr_reordered_launch(p, n, lin, GAT_B200_F32, ldin, GAT_B200_LR_BF16,
+                                              static_cast<uint16_t*>(m->x0), m->ld0, m->left, m->right, st)))
+                    return rc;
+                lin = m->x0;
+                ldin = m->ld0;
+            } else if ((rc = lr_reordered_launch(p, n, lin, GAT_B200_BF16, ldin, GAT_B200_LR_BF16, nullptr, 0,
+                                                  m->left, m->right, st))) {
+                return rc;
+            }
+            if ((rc = max_prescan_launch(m->g, p->heads, m->left, m->right, m->max, st))) return rc;
+            launches += 2;
+            mark(m, 3 + 2 * l, st);
+            // The TFS path keeps the reference's B1 rounding (per neighbour); the
+            // adaptive path takes heads_hybrid's high/low rounding, one block per row.
+            const int rounding = m->path == GAT_B200_PATH_TFS_BF16 ? GAT_B200_TFS_EDGE : GAT_B200_TFS_SPLIT;
+            int k = 0;
+            if ((rc = tfs_dispatch(m->g, p, lin, ldin, m->left, m->right, m->max, nullptr, nullptr, rounding, 0, 1, 1,
+                                   last ? 0 : 1, dst, last ? 0 : 1, ldo, nullptr, nullptr, st, &k)))
+                return rc;
+            launches += k;
+        } else {
+            const int ldh = gat_b200_padded_ld(p->width, hd);
+            if ((rc = projection_dispatch(p, n, lin, ldin, hd, m->h, hd, ldh, m->left, m->right, st))) return rc;
+            mark(m, 3 + 2 * l, st);
+            if ((rc = aggregate_dispatch(m->g, p->heads, p->dim, m->h, hd, ldh, m->left, m->right, nullptr, nullptr,
+                                         0, last ? 0 : 1, dst, (!last && bf16) ? 1 : 0, ldo, nullptr, nullptr, st)))
+                return rc;
+            launches += 2 + (m->g->n_hub ? 1 : 0);
+        }
         lin = dst;
         ldin = ldo;
     }

@@ -29,7 +29,9 @@ if not LIB_PATH.exists():
 _lib = C.CDLL(str(LIB_PATH))
 
 F32, BF16 = 0, 1
-PATH_STANDARD_BF16, PATH_STANDARD_FP32 = 0, 1
+PATH_STANDARD_BF16, PATH_STANDARD_FP32, PATH_TFS_BF16, PATH_ADAPTIVE_BF16 = 0, 1, 2, 3
+TFS_EDGE, TFS_BLOCK, TFS_SPLIT = 0, 1, 2
+LR_BF16, LR_FP32 = 0, 1
 PATHS = {"standard_bf16": PATH_STANDARD_BF16, "standard_fp32": PATH_STANDARD_FP32}
 OK, EINVAL, ECUDA, EUNSUPPORTED, ETIMEOUT, EIO = range(6)
 
@@ -76,6 +78,11 @@ SIGNATURES = [
     ("gat_b200_aggregate_fused", C.c_int, [_vp, C.c_int, C.c_int, _vp, C.c_int, C.c_int, _vp, _vp, C.c_int, _vp, C.c_int, C.c_int, _vp]),
     ("gat_b200_aggregate_fused_noalloc", C.c_int, [C.c_uint64, C.c_uint64, _vp, _vp, C.c_int, C.c_int, _vp, C.c_int, C.c_int, _vp, _vp, C.c_int, _vp, C.c_int, C.c_int, _vp]),
     ("gat_b200_standard_layer", C.c_int, [_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp, _vp, C.c_int, C.c_int, _vp]),
+    ("gat_b200_lr_reordered", C.c_int, [_vp, C.c_uint64, _vp, C.c_int, C.c_int, C.c_int, _vp, C.c_int, _vp, _vp, _vp]),
+    ("gat_b200_tfs_aggregate", C.c_int, [_vp, _vp, _vp, C.c_int, _vp, _vp, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int,
+                                         _vp, C.c_int, _vp, _vp, _vp]),
+    ("gat_b200_tfs_layer", C.c_int, [_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                     _vp, _vp, _vp, _vp, _vp, _vp, C.c_int, C.c_int, _vp]),
     ("gat_b200_check_device", C.c_int, []),
     ("gat_b200_model_create", C.c_int, [_vp, C.POINTER(_vp), C.c_int, C.POINTER(_vp)]),
     ("gat_b200_model_destroy", C.c_int, [_vp]),
@@ -403,6 +410,28 @@ def standard_layer(g: DeviceGraph, layer: DeviceLayer, x, ldx, path, hidden, h, 
                    stream=None):
     _check(_lib.gat_b200_standard_layer(g.handle, layer.handle, _ptr(x), ldx, path, int(hidden), _ptr(h), _ptr(left),
                                         _ptr(right), _ptr(out), out_dtype, ldo, _stream(stream)))
+
+
+def lr_reordered(layer: DeviceLayer, n, x, x_dtype, ldx, policy, left, right, x_bf16=None, ld_bf16=0, stream=None):
+    """[L|R] = X . (W a) (baseline_standard.cpp:29-43), optionally writing the BF16 copy of X."""
+    _check(_lib.gat_b200_lr_reordered(layer.handle, n, _ptr(x), x_dtype, ldx, policy, _ptr(x_bf16), ld_bf16,
+                                      _ptr(left), _ptr(right), _stream(stream)))
+
+
+def tfs_aggregate(g: DeviceGraph, layer: DeviceLayer, x, ldx, left, right, out, ldo, den, mx=None, rounding=TFS_EDGE,
+                  block=0, threshold=1, fixed_p=None, fixed_den=None, max_out=None, stream=None):
+    """TFS aggregation (baseline_tfs.cpp:16-110 and the icpp_* variants): unnormalized V, den (, max)."""
+    _check(_lib.gat_b200_tfs_aggregate(g.handle, layer.handle, _ptr(x), ldx, _ptr(left), _ptr(right), _ptr(mx),
+                                       _ptr(fixed_p), _ptr(fixed_den), rounding, block, threshold, _ptr(out), ldo,
+                                       _ptr(den), _ptr(max_out), _stream(stream)))
+
+
+def tfs_layer(g: DeviceGraph, layer: DeviceLayer, x, x_dtype, ldx, hidden, x_bf16, left, right, mx, den, out,
+              out_dtype, ldo, policy=LR_BF16, rounding=TFS_EDGE, block=0, threshold=1, stream=None):
+    """One TFS layer (baseline_tfs.cpp:111-117 / icpp_*::layer)."""
+    _check(_lib.gat_b200_tfs_layer(g.handle, layer.handle, _ptr(x), x_dtype, ldx, int(hidden), policy, rounding, block,
+                                   threshold, _ptr(x_bf16), _ptr(left), _ptr(right), _ptr(mx), _ptr(den), _ptr(out),
+                                   out_dtype, ldo, _stream(stream)))
 
 
 class DeviceModel:

@@ -43,6 +43,21 @@ extern "C" {
  * (baseline/bench/main.cpp:30, baseline/src/common.cpp:126-134). */
 #define GAT_B200_PATH_STANDARD_BF16 0 /* B0: BF16 X/W on tcgen05, FP32 softmax state */
 #define GAT_B200_PATH_STANDARD_FP32 1 /* B0 FP32 projection, FP32 features         */
+#define GAT_B200_PATH_TFS_BF16 2      /* tfs_bf16: B1 TFS layers (baseline_tfs.cpp:111-117) */
+/* No --path of that name in the reference: layer 1 through TFS aggregation
+ * (tensor cores, heads_hybrid rounding with one block per row), layers 2-3 as
+ * STANDARD_BF16 -- the per-layer choice of the reference's adaptive driver
+ * (baseline/tfs_online/adaptive_main.cpp:86-101), where TFS wins on layer 1. */
+#define GAT_B200_PATH_ADAPTIVE_BF16 3
+
+/* TFS rounding variants (gat_b200_tfs_aggregate). */
+#define GAT_B200_TFS_EDGE 0  /* V += RNE(p x) . W per neighbour: B1, icpp_online  */
+#define GAT_B200_TFS_BLOCK 1 /* V += RNE(sum_B p x) . W per block: icpp_block     */
+#define GAT_B200_TFS_SPLIT 2 /* as BLOCK, sum from BF16 high/low p: heads_hybrid */
+
+/* lr_reordered policies (baseline_standard.cpp:29-43). */
+#define GAT_B200_LR_BF16 0 /* BF16 X times RNE(W a)  ("bf16") */
+#define GAT_B200_LR_FP32 1 /* FP32 X times W a        ("fp32") */
 
 /* Message of this thread's last failure ("" if none). */
 const char* gat_b200_last_error(void);
@@ -238,6 +253,56 @@ int gat_b200_aggregate_fused_noalloc(uint64_t n, uint64_t e, const uint64_t* row
 int gat_b200_standard_layer(const gat_b200_graph* g, const gat_b200_layer* p, const void* x,
                             int ldx, int path, int hidden, void* h, float* left, float* right,
                             void* out, int out_dtype, int ldo, void* stream);
+
+/* ---- TFS path (aggregate the layer input first, then project) ---------- */
+
+/* [L|R] = X . blr with blr[k][h] = sum_d W[k][h*dim+d] aL[h*dim+d] (and aR),
+ * computed once at layer_create (prepare, baseline/src/common.cpp:100-106).
+ * Replaces gat::lr_reordered (baseline/src/baseline_standard.cpp:29-43) for
+ * policy GAT_B200_LR_BF16 ("bf16") or GAT_B200_LR_FP32 ("fp32"); x is FP32 or
+ * BF16 [n][ldx]. If x_bf16 is not NULL the BF16 RNE copy of x (the TFS
+ * gather table, convert() of common.cpp:85-93) is written there with row
+ * stride ld_bf16 (padding columns zeroed). left/right: FP32 [n][heads]. */
+int gat_b200_lr_reordered(const gat_b200_layer* p, uint64_t n, const void* x, int x_dtype, int ldx,
+                          int policy, void* x_bf16, int ld_bf16, float* left, float* right,
+                          void* stream);
+
+/* TFS aggregation writing the UNNORMALIZED out[n][heads*dim] (FP32, stride
+ * ldo) and den[n][heads] (and the final row maximum into max_out if not NULL).
+ * x: BF16 layer input [n][ldx] (the gathered table). Replaces
+ *   rounding EDGE,  max given, block 0: gat::tfs_aggregate (B1,
+ *       baseline/src/baseline_tfs.cpp:16-110; fixed_p/fixed_den as its
+ *       fixed-p mode, baseline/bench/main.cpp:133);
+ *   rounding EDGE,  max NULL, block B: gat::icpp_online::aggregate
+ *       (baseline/tfs_online/icpp_online.hpp:37-39, running max per block);
+ *   rounding BLOCK, max NULL, block B: gat::icpp_block::aggregate
+ *       (baseline/tfs_online/icpp_block.hpp:33-35);
+ *   rounding SPLIT, max NULL, block B, threshold T:
+ *       gat::icpp_heads_hybrid::aggregate (icpp_heads_hybrid.hpp:18-20).
+ * With max given the prescan maximum is used for every block (the online
+ * variants end at that same maximum; only their rescale roundings differ).
+ * block 0 = one block per row, except that with BLOCK/SPLIT rounding a row
+ * longer than the graph's segment length (seg_edges of gat_b200_graph_info)
+ * takes one block per segment. SPLIT with block 0, threshold 1 and max given
+ * runs on the tcgen05 kernel when the layer fits it (in <= 128,
+ * heads*dim <= 256); everything else on the CUDA-core kernel. */
+int gat_b200_tfs_aggregate(const gat_b200_graph* g, const gat_b200_layer* p, const void* x, int ldx,
+                           const float* left, const float* right, const float* max,
+                           const float* fixed_p, const float* fixed_den, int rounding, int block,
+                           int threshold, float* out, int ldo, float* den, float* max_out,
+                           void* stream);
+
+/* One TFS layer: lr_reordered (writing the BF16 copy of x into x_bf16, stride
+ * gat_b200_padded_ld(in, BF16)), max_prescan, TFS aggregation, finish (and
+ * ELU when hidden), output in out_dtype with stride ldo. Replaces
+ * gat::tfs_layer (baseline/src/baseline_tfs.cpp:111-117; rounding EDGE,
+ * block 0) and the layer() functions of icpp_online / icpp_block /
+ * icpp_heads_hybrid (other rounding/block/threshold). Scratch: x_bf16,
+ * left/right/max/den [n][heads]. */
+int gat_b200_tfs_layer(const gat_b200_graph* g, const gat_b200_layer* p, const void* x, int x_dtype,
+                       int ldx, int hidden, int policy, int rounding, int block, int threshold,
+                       void* x_bf16, float* left, float* right, float* max, float* den, void* out,
+                       int out_dtype, int ldo, void* stream);
 
 /* Reports (and clears) a device-side failure recorded by an earlier kernel:
  * GAT_B200_ETIMEOUT if a bounded wait inside a kernel gave up. Synchronizes
