@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default=CONFIG, choices=["c1", "c2", "c4", "c4s"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--path", choices=["standard", "adaptive"], default="standard",
+                    help="standard: B0 on every layer; adaptive: layer 1 through TFS aggregation (tensor cores)")
     return ap.parse_args()
 
 
@@ -236,6 +238,14 @@ def agg_bytes(n, e, heads, dim, out_bytes_per_elem):
     return 8 * (n + 1) + 4 * e + 4 * n * heads + 4 * e * heads + 2 * e * heads * dim + out_bytes_per_elem * n * heads * dim
 
 
+def tfs_bytes(n, e, din, heads, dim):
+    """Algorithmic bytes of one TFS aggregation launch (layer 1 of the adaptive
+    path): rowptr, col, L and the maximum of the row, R of every edge's source,
+    the BF16 input row of every edge's source (16-byte rounded), the BF16 output."""
+    row_bytes = (2 * din + 15) // 16 * 16
+    return 8 * (n + 1) + 4 * e + 8 * n * heads + 4 * e * heads + row_bytes * e + 2 * n * heads * dim
+
+
 def log(msg):
     """Progress line on stderr, tagged with the rank (stdout carries only the JSON line)."""
     print(f"[bench rank {os.environ.get('RANK', '0')}] {msg}", file=sys.stderr, flush=True)
@@ -319,7 +329,7 @@ def main():
         n_loc, e_loc = n, e
         g = G.DeviceGraph(cfg.graph.row, cfg.graph.col, stream)
         layers = [G.DeviceLayer(p) for p in cfg.model]
-        model = G.DeviceModel(g, layers, G.PATH_STANDARD_BF16)
+        model = G.DeviceModel(g, layers, G.PATH_ADAPTIVE_BF16 if args.path == "adaptive" else G.PATH_STANDARD_BF16)
         classes = model.classes
         x_rows = cfg.graph.x
         x_dev = torch.from_numpy(x_rows).cuda()
@@ -374,11 +384,13 @@ def main():
     # roofline of the aggregation kernel (three launches per step, this rank's rows)
     agg_ms = [stage_ms["aggregate_l1"], stage_ms["aggregate_l2"], stage_ms["aggregate_l3"]]
     b = [agg_bytes(n_loc, e_loc, 8, 32, 2), agg_bytes(n_loc, e_loc, 8, 32, 2), agg_bytes(n_loc, e_loc, 1, classes, 4)]
+    if world == 1 and args.path == "adaptive":
+        b[0] = tfs_bytes(n_loc, e_loc, din, 8, 32)
     achieved = sum(b) / (sum(agg_ms) * 1e-3) / 1e9
     peak, peak_kind = peaks()
     traffic = None
     prof = ROOT / "profiles" / "aggregate_c4_traffic.json"
-    if prof.exists() and world == 1 and args.config == "c4":
+    if prof.exists() and world == 1 and args.config == "c4" and args.path == "standard":
         traffic = json.loads(prof.read_text()).get("bytes_per_launch_avg")
 
     # e2e: the same forward with pinned HOST input rows and HOST logits
@@ -414,7 +426,7 @@ def main():
             "config": {"workload": f"{args.config}: products-shaped power-law graph, N={n}, E={e}, "
                                    f"{din}->8x32->8x32->1x{classes}",
                        "nodes": n, "edges": e, "l2": "inputs larger than L2 (H is 1.25 GB per layer)",
-                       "parallelism": parallelism},
+                       "parallelism": parallelism, "path": args.path if world == 1 else "standard"},
             "stage_ms": {k: round(float(v), 4) for k, v in stage_ms.items()},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,

@@ -284,7 +284,7 @@ int gat_b200_lr_reordered(const gat_b200_layer* p, uint64_t n, const void* x, in
  * block 0 = one block per row, except that with BLOCK/SPLIT rounding a row
  * longer than the graph's segment length (seg_edges of gat_b200_graph_info)
  * takes one block per segment. SPLIT with block 0, threshold 1 and max given
- * runs on the tcgen05 kernel when the layer fits it (in <= 128,
+ * runs on the tcgen05 kernel when the layer fits it (in <= 120,
  * heads*dim <= 256); everything else on the CUDA-core kernel. */
 int gat_b200_tfs_aggregate(const gat_b200_graph* g, const gat_b200_layer* p, const void* x, int ldx,
                            const float* left, const float* right, const float* max,

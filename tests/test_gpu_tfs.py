@@ -237,3 +237,32 @@ def test_tfs_model_paths(dev, golden, name):
         inp = O.b0_layer(graph.row, graph.col, inp, p.w, p.al, p.ar, p.heads, p.dim, l < 2, bf16=True,
                          round_z=True)["out"]
     assert rel_l2(inp, got_a) <= 3e-3
+
+
+def test_adaptive_model_tensor_core_layer(dev):
+    """Adaptive path with a layer-1 shape the tcgen05 TFS kernel takes (in=100):
+    power-law degrees with hub rows split into segments, against the oracle
+    (layer 1 TFS with heads_hybrid rounding, one block per row or segment;
+    layers 2-3 B0 BF16 with H rounded to BF16 as the device stores it)."""
+    from test_gpu_parity import _model, _forward
+    n, e = 20000, 420000
+    row, col = G.synth_powerlaw_graph(n, e, 6000, 2.1, 17)
+    x = G.synth_normal((n, 100), 17, 1)
+    params = G.glorot_model(100, 47, 17)
+    graph = G.Graph(n=n, e=e, din=100, classes=47, row=row, col=col, x=x)
+    g, _, m = _model(graph, params, G.PATH_ADAPTIVE_BF16)
+    info = g.info()
+    assert info["n_hub"] > 0
+    got = _forward(m, x)
+    p0 = params[0]
+    blr = O.prepare_blr(p0.w, p0.al, p0.ar, p0.heads, p0.dim)
+    L, R = O.lr_reordered(x, blr, p0.heads, 0)
+    mx = O.max_prescan(row, col, L, R, p0.heads)
+    out, den, _ = O.tfs_aggregate(row, col, O.quantize(x), O.quantize(p0.w), L, R, p0.heads, p0.dim, mx=mx,
+                                  rounding=O.TFS_SPLIT, block=info["seg_edges"])
+    inp = O.finish(out, den, p0.heads, p0.dim, True)
+    for l, p in enumerate(params[1:], 1):
+        inp = O.b0_layer(row, col, inp, p.w, p.al, p.ar, p.heads, p.dim, l < 2, bf16=True, round_z=True)["out"]
+    assert rel_l2(inp, got) <= 3e-3
+    ref = O.ref_chain(row, col, x, [(p.w, p.al, p.ar, p.heads, p.dim) for p in params])[2]["out"]
+    assert rel_l2(ref, got) <= 1e-2
