@@ -89,6 +89,14 @@ struct gat_b200_model {
     int timing_steps = 0;
     uint64_t forwards = 0;
     int launches_last = 0;  // kernels launched by the last forward
+    // Pipelined host-to-host forwards (gat_b200_model_forward_async): two slots
+    // of device input / logits, an upload and a download stream, and the events
+    // that order slot reuse. Created by the first asynchronous call.
+    float* ax[2] = {nullptr, nullptr};
+    float* alog[2] = {nullptr, nullptr};
+    cudaStream_t up = nullptr, down = nullptr;
+    cudaEvent_t ev_up[2] = {}, ev_done[2] = {}, ev_down[2] = {};
+    uint64_t submitted = 0;
 };
 
 namespace {
@@ -389,6 +397,15 @@ int gat_b200_model_destroy(gat_b200_model* m) {
     cudaFree(m->x2);
     cudaFree(m->logits);
     cudaFree(m->max);
+    for (int b = 0; b < 2; ++b) {
+        cudaFree(m->ax[b]);
+        cudaFree(m->alog[b]);
+        if (m->ev_up[b]) cudaEventDestroy(m->ev_up[b]);
+        if (m->ev_done[b]) cudaEventDestroy(m->ev_done[b]);
+        if (m->ev_down[b]) cudaEventDestroy(m->ev_down[b]);
+    }
+    if (m->up) cudaStreamDestroy(m->up);
+    if (m->down) cudaStreamDestroy(m->down);
     delete m;
     return 0;
 }
@@ -507,5 +524,49 @@ int gat_b200_model_stage_times(gat_b200_model* m, float* ms) {
 }
 
 int gat_b200_model_launches(const gat_b200_model* m) { return m ? m->launches_last : 0; }
+
+int gat_b200_model_forward_async(gat_b200_model* m, const float* x, float* logits, void* stream) {
+    clear_error();
+    if (!m || !x || !logits) return fail("model_forward_async: null argument");
+    cudaStream_t st = as_stream(stream);
+    const uint64_t n = m->g->n;
+    const size_t xb = n * size_t(m->din) * 4, lb = n * size_t(m->classes) * 4;
+    if (!m->up) {
+        for (int b = 0; b < 2; ++b) {
+            int rc;
+            if ((rc = dmalloc((void**)&m->ax[b], xb)) || (rc = dmalloc((void**)&m->alog[b], lb))) return rc;
+            GATB_CUDA(cudaEventCreateWithFlags(&m->ev_up[b], cudaEventDisableTiming));
+            GATB_CUDA(cudaEventCreateWithFlags(&m->ev_done[b], cudaEventDisableTiming));
+            GATB_CUDA(cudaEventCreateWithFlags(&m->ev_down[b], cudaEventDisableTiming));
+        }
+        GATB_CUDA(cudaStreamCreateWithFlags(&m->up, cudaStreamNonBlocking));
+        GATB_CUDA(cudaStreamCreateWithFlags(&m->down, cudaStreamNonBlocking));
+    }
+    const int b = int(m->submitted & 1);
+    // upload once the forward that last read this slot is done
+    if (m->submitted >= 2) GATB_CUDA(cudaStreamWaitEvent(m->up, m->ev_done[b], 0));
+    GATB_CUDA(cudaMemcpyAsync(m->ax[b], x, xb, cudaMemcpyHostToDevice, m->up));
+    GATB_CUDA(cudaEventRecord(m->ev_up[b], m->up));
+    // compute once the input is in and the slot's previous logits are downloaded
+    GATB_CUDA(cudaStreamWaitEvent(st, m->ev_up[b], 0));
+    if (m->submitted >= 2) GATB_CUDA(cudaStreamWaitEvent(st, m->ev_down[b], 0));
+    int rc = gat_b200_model_forward(m, m->ax[b], 0, m->alog[b], 0, stream);
+    if (rc) return rc;
+    GATB_CUDA(cudaEventRecord(m->ev_done[b], st));
+    GATB_CUDA(cudaStreamWaitEvent(m->down, m->ev_done[b], 0));
+    GATB_CUDA(cudaMemcpyAsync(logits, m->alog[b], lb, cudaMemcpyDeviceToHost, m->down));
+    GATB_CUDA(cudaEventRecord(m->ev_down[b], m->down));
+    ++m->submitted;
+    return 0;
+}
+
+int gat_b200_model_join(gat_b200_model* m, void* stream) {
+    clear_error();
+    if (!m) return fail("model_join: null argument");
+    if (!m->submitted) return 0;
+    const int b = int((m->submitted - 1) & 1);
+    GATB_CUDA(cudaStreamWaitEvent(as_stream(stream), m->ev_down[b], 0));
+    return 0;
+}
 
 }  // extern "C"

@@ -90,6 +90,8 @@ SIGNATURES = [
     ("gat_b200_model_enable_timing", C.c_int, [_vp, C.c_int]),
     ("gat_b200_model_stage_times", C.c_int, [_vp, _f32p]),
     ("gat_b200_model_launches", C.c_int, [_vp]),
+    ("gat_b200_model_forward_async", C.c_int, [_vp, _vp, _vp, _vp]),
+    ("gat_b200_model_join", C.c_int, [_vp, _vp]),
 ]
 for _name, _res, _args in SIGNATURES:
     _fn = getattr(_lib, _name)
@@ -451,6 +453,14 @@ class DeviceModel:
         """x, logits: torch tensors (pinned host or device) or raw pointers."""
         _check(_lib.gat_b200_model_forward(self.handle, _ptr(x), int(x_on_host), _ptr(logits), int(logits_on_host),
                                            _stream(stream)))
+
+    def forward_async(self, x_host, logits_host, stream=None):
+        """Pipelined host-to-host forward (see gat_b200_model_forward_async); pinned host tensors."""
+        _check(_lib.gat_b200_model_forward_async(self.handle, _ptr(x_host), _ptr(logits_host), _stream(stream)))
+
+    def join(self, stream=None):
+        """Make `stream` wait for every submitted forward_async (no host block)."""
+        _check(_lib.gat_b200_model_join(self.handle, _stream(stream)))
 
     STAGES = ("h2d", "convert", "projection_l1", "aggregate_l1", "projection_l2", "aggregate_l2",
               "projection_l3", "aggregate_l3", "d2h")

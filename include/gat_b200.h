@@ -342,6 +342,18 @@ int gat_b200_model_stage_times(gat_b200_model* m, float* ms);
 /* Number of kernels the last forward launched. */
 int gat_b200_model_launches(const gat_b200_model* m);
 
+/* No counterpart in the reference (its forward runs on host memory in place).
+ * A stream of host-to-host forwards, for a serving loop: uploads x (pinned
+ * FP32 [n][din]), runs the forward on `stream` and downloads the logits into
+ * `logits` (pinned FP32 [n][classes]), returning at once. Two device slots and
+ * the model's own upload / download streams let request k's download and
+ * request k+1's upload overlap compute. The host buffers of a call must stay
+ * untouched until a later gat_b200_model_join has been waited on.
+ * gat_b200_model_join makes `stream` wait (on the device, without blocking the
+ * host) until every submitted forward has finished its download. */
+int gat_b200_model_forward_async(gat_b200_model* m, const float* x, float* logits, void* stream);
+int gat_b200_model_join(gat_b200_model* m, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -344,6 +344,26 @@ def test_model_host_buffers_e2e(dev):
     assert np.array_equal(lh.numpy(), dev_logits)
 
 
+def test_model_forward_async_pipeline(dev):
+    """Pipelined host-to-host forwards (two slots, own copy streams): every
+    request's logits equal the synchronous forward's, bit for bit."""
+    import torch
+    import configs
+    cfg = configs.make("c1")
+    _, _, m = _model(cfg.graph, cfg.model, G.PATH_STANDARD_BF16)
+    xs = [torch.from_numpy((cfg.graph.x * s).astype(np.float32)).pin_memory() for s in (1.0, -0.5, 2.0)]
+    outs = [torch.empty((cfg.graph.n, m.classes), dtype=torch.float32).pin_memory() for _ in xs]
+    st = torch.cuda.current_stream()
+    for x, o in zip(xs, outs):
+        m.forward_async(x, o, st)
+    m.join(st)
+    torch.cuda.synchronize()
+    G.check_device()
+    for x, o in zip(xs, outs):
+        want = _forward(m, x.numpy())
+        assert np.array_equal(o.numpy(), want)
+
+
 @pytest.mark.slow
 def test_config2_model(dev):
     """arxiv-shaped power-law graph (hub rows split into segments)."""
