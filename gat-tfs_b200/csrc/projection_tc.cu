@@ -24,6 +24,7 @@
 
 #include "device.cuh"
 #include "graph.cuh"
+#include "tc.cuh"
 
 namespace gatb {
 
@@ -298,10 +299,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint8_t* sb = stage0 + toggle * kStageBytes;
                 if (lane == 0 && a.store_h) bulk_wait_read<1>();
                 __syncwarp();
-                for (int cc = 0; cc < 4 && g + cc * 16 < NP; ++cc) {
+                // 16 accumulator columns c..c+15 of this row (sub-block cc of the group)
+                auto col16 = [&](int cc, const float* v) {
                     const int c = g + cc * 16;
-                    float v[16];
-                    tmem_ld16(taddr + uint32_t(c), v);
                     if constexpr (ALIGNED16) {
                         float pl = 0.f, pr = 0.f;
 #pragma unroll
@@ -329,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int j = 0; j < 16; ++j)
                             if (c + j < a.width) zr[j] = v[j];
                     }
-                    if (!a.store_h) continue;
+                    if (!a.store_h) return;
                     uint32_t pk[8];
 #pragma unroll
                     for (int j = 0; j < 8; ++j) pk[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
@@ -337,6 +337,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int c0 = (2 * cc) ^ (lane & 7), c1 = (2 * cc + 1) ^ (lane & 7);
                     *reinterpret_cast<uint4*>(sb + lane * 128 + c0 * 16) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                     *reinterpret_cast<uint4*>(sb + lane * 128 + c1 * 16) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                };
+                if (g + 64 <= NP) {
+                    // one TMEM read (and one wait) for the group's 64 columns
+                    float v64[64];
+                    tc::tmem_ld64(taddr + uint32_t(g), v64);
+#pragma unroll
+                    for (int cc = 0; cc < 4; ++cc) col16(cc, v64 + cc * 16);
+                } else {
+                    for (int cc = 0; cc < 4 && g + cc * 16 < NP; ++cc) {
+                        float v[16];
+                        tmem_ld16(taddr + uint32_t(g + cc * 16), v);
+                        col16(cc, v);
+                    }
                 }
                 if (!a.store_h) continue;
                 fence_proxy_async_smem();
