@@ -21,7 +21,14 @@ forward time. Prints ONE JSON line (rank 0).
 workload and prints its line (rank 0 only under torchrun).
 
 Multi-GPU: destination rows are partitioned by edge count; every layer's
-projected features are exchanged with one NCCL all-gather (see DESIGN.md).
+projected features are exchanged with one NCCL all-gather.
+
+--mode micro: the layer-2 micro-benchmark (config c3) on the c2 graph: input H
+169,343 x 256 BF16 ~ N(0,1), W 256 x 256, a_L/a_R ~ U(-0.1, 0.1); the
+reference's micro stages (bench/main.cpp:105-118) and three whole-layer
+variants: transform-first (projection + fused aggregation), fixed-p
+(projection + aggregation with precomputed p, bench/main.cpp:130-133) and TFS
+aggregate-first; one JSON line with ms and HBM GB/s per variant.
 """
 from __future__ import annotations
 
@@ -53,6 +60,7 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default=CONFIG, choices=["c1", "c2", "c4", "c4s"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--mode", choices=["forward", "micro"], default="forward")
     ap.add_argument("--path", choices=["standard", "adaptive"], default="standard",
                     help="standard: B0 on every layer; adaptive: layer 1 through TFS aggregation (tensor cores)")
     return ap.parse_args()
@@ -251,8 +259,126 @@ def log(msg):
     print(f"[bench rank {os.environ.get('RANK', '0')}] {msg}", file=sys.stderr, flush=True)
 
 
+
+def run_micro(args) -> int:
+    """Config c3: layer 2 of the c2 graph with its own seeded input and weights."""
+    import numpy as np
+    import torch
+    import configs
+    import gatb200 as G
+    torch.cuda.set_device(0)
+    stream = torch.cuda.current_stream()
+    g_host = configs.make_graph("c2", features=False)
+    n, e = g_host.n, g_host.e
+    K, d, D = 8, 32, 256
+    W = K * d
+    hx = G.synth_normal((n, D), 303, 1)  # the layer-2 input H ~ N(0,1) (BF16 on device)
+    w = G.synth_uniform((D, W), -np.sqrt(6.0 / (D + W)), np.sqrt(6.0 / (D + W)), 303, 2)
+    al = G.synth_uniform((W,), -0.1, 0.1, 303, 3)
+    ar = G.synth_uniform((W,), -0.1, 0.1, 303, 4)
+    p = G.Param(D, K, d, w, al, ar)
+    g = G.DeviceGraph(g_host.row, g_host.col, stream)
+    layer = G.DeviceLayer(p)
+    ld = G.padded_ld(D, G.BF16)
+    xf = torch.from_numpy(hx).cuda()
+    xb = torch.zeros((n, ld), dtype=torch.int16, device="cuda")
+    h = torch.zeros((n, ld), dtype=torch.int16, device="cuda")
+    f32 = dict(dtype=torch.float32, device="cuda")
+    left, right, mx, den = (torch.empty((n, K), **f32) for _ in range(4))
+    out = torch.empty((n, W), **f32)
+    outb = torch.zeros((n, ld), dtype=torch.int16, device="cuda")
+    G.convert(n, D, xf, D, xb, ld, stream)
+    torch.cuda.synchronize()
+
+    def t_ms(fn, k=None):
+        k = k or max(3, args.steps)
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        times = []
+        for _ in range(k):
+            s0.record(stream)
+            fn()
+            s1.record(stream)
+            torch.cuda.synchronize()
+            times.append(s0.elapsed_time(s1))
+        G.check_device()
+        return statistics.median(times)
+
+    # weights of the fixed-p variant: p = exp(leaky(L+R) - m) from this layer's L/R
+    G.projection(layer, n, xb, ld, G.BF16, h, G.BF16, ld, left, right, stream)
+    G.max_prescan(g, K, left, right, mx, stream)
+    torch.cuda.synchronize()
+    L, R, M = left.cpu().numpy(), right.cpu().numpy(), mx.cpu().numpy()
+    dst = np.repeat(np.arange(n), np.diff(g_host.row.astype(np.int64)))
+    s_ = L[dst] + R[g_host.col]
+    pw = np.exp(np.where(s_ >= 0, s_, np.float32(0.2) * s_) - M[dst]).astype(np.float32)
+    pden = np.zeros((n, K), np.float32)
+    np.add.at(pden, dst, pw)
+    fp, fd = torch.from_numpy(pw).cuda(), torch.from_numpy(pden).cuda()
+
+    stages = {
+        "convert_rne": t_ms(lambda: G.convert(n, D, xf, D, xb, ld, stream)),
+        "projection_bf16": t_ms(lambda: G.projection(layer, n, xb, ld, G.BF16, h, G.BF16, ld, left, right, stream)),
+        "lr_reordered_bf16": t_ms(lambda: G.lr_reordered(layer, n, xb, G.BF16, ld, G.LR_BF16, left, right,
+                                                         stream=stream)),
+        "lr_reordered_fp32": t_ms(lambda: G.lr_reordered(layer, n, xf, G.F32, D, G.LR_FP32, left, right,
+                                                         stream=stream)),
+        "max_prescan": t_ms(lambda: G.max_prescan(g, K, left, right, mx, stream)),
+        "weighted_spmm_score_exp": t_ms(lambda: G.standard_aggregate(g, K, d, h, G.BF16, ld, left, right, out, W, den,
+                                                                     stream=stream)),
+    }
+    G.projection(layer, n, xb, ld, G.BF16, h, G.BF16, ld, left, right, stream)
+
+    def transform_first():
+        G.projection(layer, n, xb, ld, G.BF16, h, G.BF16, ld, left, right, stream)
+        G.aggregate_fused(g, K, d, h, G.BF16, ld, left, right, True, outb, G.BF16, ld, stream)
+
+    def fixed_p():
+        G.projection(layer, n, xb, ld, G.BF16, h, G.BF16, ld, left, right, stream)
+        G.standard_aggregate(g, K, d, h, G.BF16, ld, left, right, out, W, den, fixed_p=fp, fixed_den=fd,
+                             stream=stream)
+        G.finish(n, K, d, den, True, out, W, stream)
+
+    def tfs():
+        G.lr_reordered(layer, n, xb, G.BF16, ld, G.LR_BF16, left, right, stream=stream)
+        G.max_prescan(g, K, left, right, mx, stream)
+        G.tfs_aggregate(g, layer, xb, ld, left, right, out, W, den, mx=mx, rounding=G.TFS_EDGE, stream=stream)
+        G.finish(n, K, d, den, True, out, W, stream)
+
+    gb = 1e9
+    bytes_tf = (2 * n * D + 2 * n * W + 8 * n * K) + (8 * (n + 1) + 4 * e + 4 * n * K + 4 * e * K + 2 * e * W + 2 * n * W)
+    bytes_fp = (2 * n * D + 2 * n * W + 8 * n * K) + (8 * (n + 1) + 4 * e + 4 * e * K + 2 * e * W + 4 * n * W + 4 * n * K) \
+        + 8 * n * W
+    bytes_tfs = (2 * n * D + 8 * n * K) + (8 * (n + 1) + 4 * e + 4 * e * K) + (8 * (n + 1) + 4 * e + 8 * n * K
+                                                                                + 4 * e * K + 2 * e * D + 4 * n * W + 4 * n * K) + 8 * n * W
+    variants = {}
+    for name, fn, b, note in (("transform_first", transform_first, bytes_tf,
+                               "tcgen05 projection + fused edge-softmax aggregation (BF16 out)"),
+                              ("fixed_p", fixed_p, bytes_fp, "projection + aggregation with precomputed p + finish"),
+                              ("tfs_aggregate_first", tfs, bytes_tfs,
+                               "lr_reordered + max prescan + TFS B1 aggregation (CUDA cores: the tensor-core "
+                               "TFS kernel takes inputs of at most 120 features) + finish")):
+        ms = t_ms(fn)
+        variants[name] = {"ms": round(ms, 4), "algorithmic_bytes": int(b), "gbs": round(b / (ms * 1e-3) / gb, 1),
+                          "what": note}
+    peak, peak_kind = peaks()
+    line = {"metric": "layer-2 micro-benchmark (c3) ms", "unit": "ms", "higher_is_better": False,
+            "mode": "micro", "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"c3: layer 2 of c2 (N={n}, E={e}), H {n}x{D} BF16 ~ N(0,1), W {D}x{W}, "
+                                   "a_L/a_R ~ U(-0.1,0.1)"},
+            "stages_ms": {k: round(v, 4) for k, v in stages.items()},
+            "variants": variants, "hbm_peak_gbs": peak, "peak_kind": peak_kind}
+    print(json.dumps(line))
+    layer.close()
+    g.close()
+    return 0
+
 def main():
     args = parse()
+    if args.mode == "micro":
+        return run_micro(args)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

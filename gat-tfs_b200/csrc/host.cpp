@@ -3,6 +3,7 @@
 // and the synthetic-input generators. No GPU is touched here.
 #include "gat_b200_internal.h"
 
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <fstream>
@@ -201,6 +202,78 @@ int gat_b200_synth_powerlaw_rows(uint64_t n, uint64_t e, uint64_t max_degree, do
 int gat_b200_synth_uniform(uint64_t count, double lo, double hi, uint64_t seed, uint64_t stream, float* out) {
     if (!out) return fail("synth: null pointer");
     return synth_uniform(count, lo, hi, seed, stream, out);
+}
+
+// GATFIX1 fixed-p fixture (baseline/src/common.cpp:171-194): magic, u64
+// {n, e, in, heads, dim}, the CSR (to reject a different graph of equal shape),
+// the layer's W/aL/aR (checkpoint), the layer input [n][in], p [e][heads] and
+// den [n][heads].
+int gat_b200_write_fixture(const char* path, uint64_t n, uint64_t e, int in, int heads, int dim,
+                           const uint64_t* row, const uint32_t* col, const float* w, const float* al,
+                           const float* ar, const float* input, const float* p, const float* den) {
+    clear_error();
+    if (!path || !row || !col || !w || !al || !ar || !input || !p || !den) return fail("write_fixture: null argument");
+    if (in <= 0 || heads <= 0 || dim <= 0) return fail("bad fixture sizes");
+    std::ofstream f(path, std::ios::binary);
+    const char magic[8] = "GATFIX1";
+    const uint64_t sizes[5] = {n, e, uint64_t(in), uint64_t(heads), uint64_t(dim)};
+    const uint64_t width = uint64_t(heads) * dim;
+    if (!f || !write_n(f, magic, 8) || !write_n(f, sizes, 5) || !write_n(f, row, n + 1) || !write_n(f, col, e) ||
+        !write_n(f, w, uint64_t(in) * width) || !write_n(f, al, width) || !write_n(f, ar, width) ||
+        !write_n(f, input, n * uint64_t(in)) || !write_n(f, p, e * uint64_t(heads)) ||
+        !write_n(f, den, n * uint64_t(heads)))
+        return fail_code(GAT_B200_EIO, "write failed");
+    return 0;
+}
+
+int gat_b200_read_fixture(const char* path, uint64_t n, uint64_t e, int in, int heads, int dim,
+                          const uint64_t* row, const uint32_t* col, const float* w, const float* al,
+                          const float* ar, float* input, float* p, float* den) {
+    clear_error();
+    if (!path || !row || !col || !w || !al || !ar || !input || !p || !den) return fail("read_fixture: null argument");
+    std::ifstream f(path, std::ios::binary);
+    if (!f) return fail_code(GAT_B200_EIO, "cannot open fixture");
+    char magic[8];
+    if (!read_n(f, magic, 8)) return fail_code(GAT_B200_EIO, "truncated file");
+    if (std::memcmp(magic, "GATFIX1", 7)) return fail("bad fixture magic");
+    uint64_t s[5];
+    if (!read_n(f, s, 5)) return fail_code(GAT_B200_EIO, "truncated file");
+    if (s[0] != n || s[1] != e || s[2] != uint64_t(in) || s[3] != uint64_t(heads) || s[4] != uint64_t(dim))
+        return fail("fixture shape mismatch");
+    const uint64_t width = uint64_t(heads) * dim;
+    std::vector<uint64_t> frow(n + 1);
+    std::vector<uint32_t> fcol(e);
+    if (!read_n(f, frow.data(), n + 1) || !read_n(f, fcol.data(), e)) return fail_code(GAT_B200_EIO, "truncated file");
+    if (std::memcmp(frow.data(), row, (n + 1) * 8) || (e && std::memcmp(fcol.data(), col, e * 4)))
+        return fail("fixture CSR mismatch");
+    const float* masters[3] = {w, al, ar};
+    const uint64_t counts[3] = {uint64_t(in) * width, width, width};
+    for (int k = 0; k < 3; ++k) {
+        std::vector<float> v(counts[k]);
+        if (!read_n(f, v.data(), counts[k])) return fail_code(GAT_B200_EIO, "truncated file");
+        if (std::memcmp(v.data(), masters[k], counts[k] * 4)) return fail("fixture checkpoint mismatch");
+    }
+    if (!read_n(f, input, n * uint64_t(in)) || !read_n(f, p, e * uint64_t(heads)) || !read_n(f, den, n * uint64_t(heads)))
+        return fail_code(GAT_B200_EIO, "truncated file");
+    for (uint64_t i = 0; i < n * uint64_t(in); ++i)
+        if (!std::isfinite(input[i])) return fail("nonfinite fixture input index=" + std::to_string(i));
+    for (uint64_t i = 0; i < e * uint64_t(heads); ++i)
+        if (!std::isfinite(p[i])) return fail("nonfinite fixture p index=" + std::to_string(i));
+    for (uint64_t i = 0; i < n * uint64_t(heads); ++i)
+        if (!std::isfinite(den[i])) return fail("nonfinite fixture denominator index=" + std::to_string(i));
+    for (uint64_t i = 0; i < n; ++i)
+        for (int h = 0; h < heads; ++h) {
+            float sum = 0.f;
+            for (uint64_t k = row[i]; k < row[i + 1]; ++k) {
+                const float x = p[k * heads + h];
+                if (x < 0.f || x > 1.f) return fail("fixture p outside [0,1]");
+                sum += x;
+            }
+            const float d = den[i * heads + h];
+            if (std::fabs(sum - d) > 1e-5f * std::max(1.f, sum) || (row[i] != row[i + 1] && d <= 0.f))
+                return fail("fixture denominator mismatch");
+        }
+    return 0;
 }
 
 }  // extern "C"

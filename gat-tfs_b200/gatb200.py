@@ -55,6 +55,10 @@ SIGNATURES = [
     ("gat_b200_write_graph", C.c_int, [C.c_char_p, C.c_uint64, C.c_uint64, C.c_uint32, C.c_uint32, _u64p, _u32p, _f32p]),
     ("gat_b200_read_weights", C.c_int, [C.c_char_p, C.c_int, C.c_int, C.POINTER(_f32p), C.POINTER(_f32p), C.POINTER(_f32p)]),
     ("gat_b200_write_weights", C.c_int, [C.c_char_p, C.c_int, C.c_int, C.POINTER(_f32p), C.POINTER(_f32p), C.POINTER(_f32p)]),
+    ("gat_b200_write_fixture", C.c_int, [C.c_char_p, C.c_uint64, C.c_uint64, C.c_int, C.c_int, C.c_int, _u64p, _u32p,
+                                         _f32p, _f32p, _f32p, _f32p, _f32p, _f32p]),
+    ("gat_b200_read_fixture", C.c_int, [C.c_char_p, C.c_uint64, C.c_uint64, C.c_int, C.c_int, C.c_int, _u64p, _u32p,
+                                        _f32p, _f32p, _f32p, _f32p, _f32p, _f32p]),
     ("gat_b200_random_model", C.c_int, [C.c_int, C.c_int, C.c_int, C.POINTER(_f32p), C.POINTER(_f32p), C.POINTER(_f32p)]),
     ("gat_b200_synth_uniform_graph", C.c_int, [C.c_uint64, C.c_uint32, C.c_uint64, _u64p, _u32p]),
     ("gat_b200_synth_powerlaw_graph", C.c_int, [C.c_uint64, C.c_uint64, C.c_uint64, C.c_double, C.c_uint64, _u64p, _u32p]),
@@ -249,6 +253,33 @@ def synth_uniform_graph(n: int, sources: int, seed: int):
     col = np.empty(n * (sources + 1), np.uint32)
     _check(_lib.gat_b200_synth_uniform_graph(n, sources, seed, _p(row, _u64p), _p(col, _u32p)))
     return row, col
+
+
+def write_fixture(path, row, col, p: "Param", x, pw, den):
+    """GATFIX1 fixed-p fixture (common.cpp:171-194): layer input x [n][in], p [e][heads], den [n][heads]."""
+    row = np.ascontiguousarray(row, np.uint64)
+    col = np.ascontiguousarray(col, np.uint32)
+    n, e = len(row) - 1, len(col)
+    f = lambda a: np.ascontiguousarray(a, np.float32)
+    x, pw, den = f(x), f(pw), f(den)
+    _check(_lib.gat_b200_write_fixture(str(path).encode(), n, e, p.in_, p.heads, p.dim, _p(row, _u64p),
+                                       _p(col, _u32p), _p(f(p.w), _f32p), _p(f(p.al), _f32p), _p(f(p.ar), _f32p),
+                                       _p(x, _f32p), _p(pw, _f32p), _p(den, _f32p)))
+
+
+def read_fixture(path, row, col, p: "Param"):
+    """Reads and validates a GATFIX1 fixture for this graph and layer: (x, p, den)."""
+    row = np.ascontiguousarray(row, np.uint64)
+    col = np.ascontiguousarray(col, np.uint32)
+    n, e = len(row) - 1, len(col)
+    x = np.empty((n, p.in_), np.float32)
+    pw = np.empty((e, p.heads), np.float32)
+    den = np.empty((n, p.heads), np.float32)
+    f = lambda a: np.ascontiguousarray(a, np.float32)
+    _check(_lib.gat_b200_read_fixture(str(path).encode(), n, e, p.in_, p.heads, p.dim, _p(row, _u64p),
+                                      _p(col, _u32p), _p(f(p.w), _f32p), _p(f(p.al), _f32p), _p(f(p.ar), _f32p),
+                                      _p(x, _f32p), _p(pw, _f32p), _p(den, _f32p)))
+    return x, pw, den
 
 
 def synth_powerlaw_graph(n: int, e: int, max_degree: int, gamma: float, seed: int):

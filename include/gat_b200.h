@@ -130,6 +130,20 @@ int gat_b200_synth_powerlaw_rows(uint64_t n, uint64_t e, uint64_t max_degree, do
 int gat_b200_synth_uniform(uint64_t count, double lo, double hi, uint64_t seed, uint64_t stream,
                            float* out);
 
+/* GATFIX1 fixed-p fixture of one layer: the graph's CSR, the layer's W/aL/aR,
+ * its input [n][in] and the attention weights p [e][heads] with their sums
+ * den [n][heads]. Replaces gat::save_fixture / gat::load_fixture
+ * (baseline/src/common.cpp:171-194); read_fixture rejects a file whose shape,
+ * CSR or checkpoint differ from the given ones, non-finite values, p outside
+ * [0,1] and den that is not the sum of its row's p (the reference's checks and
+ * messages). */
+int gat_b200_write_fixture(const char* path, uint64_t n, uint64_t e, int in, int heads, int dim,
+                           const uint64_t* row, const uint32_t* col, const float* w, const float* al,
+                           const float* ar, const float* input, const float* p, const float* den);
+int gat_b200_read_fixture(const char* path, uint64_t n, uint64_t e, int in, int heads, int dim,
+                          const uint64_t* row, const uint32_t* col, const float* w, const float* al,
+                          const float* ar, float* input, float* p, float* den);
+
 /* ======================================================================== *
  *  Device: graph and degree schedule                                       *
  * ======================================================================== */

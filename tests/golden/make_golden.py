@@ -24,6 +24,10 @@ sources in place by oracle/Makefile; nothing here is hand-written):
     icpp_heads_hybrid (block 32, threshold 16) outputs, with the inputs the
     reference computed for them (BF16- and FP32-policy L/R, prescan max, blr).
     The chain npz files also hold the tfs_bf16 path's three-layer logits.
+  * fixture_small_l1.gatfix (+ fixture_small.gatbin): a GATFIX1 fixed-p
+    fixture written by the reference's own export-fixture mode
+    (bench/main.cpp:103-116) for layer 1 of random_model(seed 11) on a small
+    seeded uniform graph from this repository's generator.
 """
 import hashlib
 import json
@@ -49,6 +53,14 @@ DUMP = ROOT / "oracle" / "_ref" / "ref_dump"
 # Boundary shapes (D, K, d) kept for the TFS fixtures: the layer shapes of the
 # configs (128->8x32, 256->8x32, 256->1x47) and three odd ones.
 TFS_CASES = [(17, 1, 7), (33, 2, 40), (128, 8, 32), (256, 8, 32), (256, 1, 47), (128, 4, 47)]
+
+
+def small_fixture_graph():
+    """200 rows, 7 uniform sources + self loop, 24 features, 5 classes (seed 21)."""
+    n, din, classes = 200, 24, 5
+    row, col = G.synth_uniform_graph(n, 7, 21)
+    x = G.synth_normal((n, din), 21, 1)
+    return G.Graph(n=n, e=len(col), din=din, classes=classes, row=row, col=col, x=x)
 
 
 def sha256(path) -> str:
@@ -156,6 +168,16 @@ def main():
             for name in ("b1_out", "online16_out", "block32_out", "hybrid32_out"):
                 t[f"{name}_{key}"] = load(d, pre + name + ".f32").reshape(35, K * dd)
         np.savez_compressed(OUT / "tfs.npz", **t)
+
+        # GATFIX1 fixture from the reference's export-fixture mode
+        sg = small_fixture_graph()
+        G.save_graph(sg, OUT / "fixture_small.gatbin")
+        baseline = ROOT / "oracle" / "_ref" / "gat_baseline"
+        subprocess.run([str(baseline), "--graph", str(OUT / "fixture_small.gatbin"), "--seed", "11", "--mode",
+                        "export-fixture", "--layer", "1", "--fixture", str(OUT / "fixture_small_l1.gatfix"),
+                        "--threads", "4"], check=True, stdout=subprocess.DEVNULL)
+        manifest["fixture_small_gatbin_sha256"] = sha256(OUT / "fixture_small.gatbin")
+        manifest["fixture_small_l1_gatfix_sha256"] = sha256(OUT / "fixture_small_l1.gatfix")
     (OUT / "MANIFEST.json").write_text(json.dumps(manifest, indent=1, sort_keys=True) + "\n")
     print(json.dumps(manifest, indent=1))
 

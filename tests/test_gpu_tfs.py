@@ -266,3 +266,43 @@ def test_adaptive_model_tensor_core_layer(dev):
     assert rel_l2(inp, got) <= 3e-3
     ref = O.ref_chain(row, col, x, [(p.w, p.al, p.ar, p.heads, p.dim) for p in params])[2]["out"]
     assert rel_l2(ref, got) <= 1e-2
+
+
+def test_reference_fixture_fixed_p(dev, golden):
+    """Fixed-p mode on the reference's own GATFIX1 fixture (bench/main.cpp:127-138):
+    the standard path (BF16 projection, aggregation with the fixture's p and den,
+    finish) and the TFS B1 path with the same weights."""
+    import torch
+    g_host = G.load_graph(golden / "fixture_small.gatbin")
+    params = G.random_model(g_host.din, g_host.classes, 11)
+    p = params[0]
+    x, pw, den = G.read_fixture(golden / "fixture_small_l1.gatfix", g_host.row, g_host.col, p)
+    n, K, d, W = g_host.n, p.heads, p.dim, p.width
+    g = G.DeviceGraph(g_host.row, g_host.col)
+    layer = G.DeviceLayer(p)
+    ld = G.padded_ld(p.in_, G.BF16)
+    xb = T(_bf16_table(x, ld).view(np.int16))
+    f32 = dict(dtype=torch.float32, device="cuda")
+    # standard fixed-p
+    ldh = G.padded_ld(W, G.BF16)
+    h = torch.zeros((n, ldh), dtype=torch.int16, device="cuda")
+    lft, rgt = torch.empty((n, K), **f32), torch.empty((n, K), **f32)
+    G.projection(layer, n, xb, ld, G.BF16, h, G.BF16, ldh, lft, rgt)
+    out = torch.empty((n, W), **f32)
+    dn = torch.empty((n, K), **f32)
+    G.standard_aggregate(g, K, d, h, G.BF16, ldh, lft, rgt, out, W, dn, fixed_p=T(pw), fixed_den=T(den))
+    G.finish(n, K, d, dn, False, out, W)
+    z = O.quantize(O.quantize(x) @ O.quantize(p.w))  # BF16 X . BF16 W, H stored in BF16
+    so, sd = O.standard_aggregate(g_host.row, g_host.col, z, None, None, None, K, d, fixed_p=pw, fixed_den=den)
+    want = O.finish(so, sd, K, d, False)
+    assert np.array_equal(host(dn), den)
+    assert rel_l2(want, host(out)) <= 1e-3
+    # TFS B1 fixed-p: same weights, same arithmetic order as the oracle -> bit-exact
+    out2, den2, _ = _run_tfs(g, layer, _bf16_table(x, ld), ld, None, None, n, K, d, fixed_p=pw, fixed_den=den)
+    oo, od, _ = O.tfs_aggregate(g_host.row, g_host.col, O.quantize(x), O.quantize(p.w), None, None, K, d,
+                                fixed_p=pw, fixed_den=den)
+    assert np.array_equal(out2, oo) and np.array_equal(den2, den)
+    # and the two paths agree as the reference's fixed-p control reports (extra pX rounding only)
+    assert rel_l2(O.finish(oo, od, K, d, False), host(out)) <= 1e-2
+    layer.close()
+    g.close()

@@ -213,3 +213,61 @@ def test_tfs_chain_matches_reference(name):
     assert e["relative_l2"] <= 5e-4, e
     r0 = O.errors(g["ref_logits"], inp)
     assert r0["relative_l2"] <= 2e-2, r0  # TFS BF16 vs R0: same order as B0 BF16
+
+
+def _fixture_inputs():
+    import gatb200 as G
+    g = G.load_graph(GOLDEN / "fixture_small.gatbin")
+    assert hashlib.sha256((GOLDEN / "fixture_small.gatbin").read_bytes()).hexdigest() == MANIFEST[
+        "fixture_small_gatbin_sha256"]
+    return g, G.random_model(g.din, g.classes, 11)
+
+
+def test_reference_fixture_round_trip(tmp_path):
+    """The reference's export-fixture file (GATFIX1, common.cpp:171-194) reads and
+    validates, holds the R0 weights of layer 1, and our writer reproduces it byte
+    for byte."""
+    import gatb200 as G
+    g, model = _fixture_inputs()
+    p = model[0]
+    path = GOLDEN / "fixture_small_l1.gatfix"
+    x, pw, den = G.read_fixture(path, g.row, g.col, p)
+    assert np.array_equal(x, g.x)  # layer 1 input is the graph's features
+    o = O.ref_layer(g.row, g.col, x, p.w, p.al, p.ar, p.heads, p.dim, False, want_p=True)
+    assert np.abs(pw - o["p"]).max() <= 1e-6 and np.abs(den - o["den"]).max() <= 1e-5 * np.abs(den).max()
+    G.write_fixture(tmp_path / "again.gatfix", g.row, g.col, p, x, pw, den)
+    assert (tmp_path / "again.gatfix").read_bytes() == path.read_bytes()
+
+
+def test_fixture_validation_messages(tmp_path):
+    """load_fixture's checks (common.cpp:181-193) with the reference's messages."""
+    import gatb200 as G
+    g, model = _fixture_inputs()
+    p = model[0]
+    x, pw, den = G.read_fixture(GOLDEN / "fixture_small_l1.gatfix", g.row, g.col, p)
+
+    def expect(msg, path, row=g.row, col=g.col, layer=p):
+        with pytest.raises(RuntimeError, match=msg):
+            G.read_fixture(path, row, col, layer)
+
+    bad = tmp_path / "bad.gatfix"
+    raw = bytearray((GOLDEN / "fixture_small_l1.gatfix").read_bytes())
+    raw[0] = ord("X")
+    bad.write_bytes(bytes(raw))
+    expect("bad fixture magic", bad)
+    expect("fixture shape mismatch", GOLDEN / "fixture_small_l1.gatfix", layer=model[1])
+    col2 = g.col.copy()
+    col2[5] = (col2[5] + 1) % g.n
+    expect("fixture CSR mismatch", GOLDEN / "fixture_small_l1.gatfix", col=col2)
+    w2 = p.w.copy()
+    w2[0, 0] += 1.0
+    expect("fixture checkpoint mismatch", GOLDEN / "fixture_small_l1.gatfix",
+           layer=G.Param(p.in_, p.heads, p.dim, w2, p.al, p.ar))
+    p2 = pw.copy()
+    p2[3, 0] = 1.5
+    G.write_fixture(bad, g.row, g.col, p, x, p2, den)
+    expect("fixture p outside", bad)
+    d2 = den.copy()
+    d2[4, 1] *= 1.01
+    G.write_fixture(bad, g.row, g.col, p, x, pw, d2)
+    expect("fixture denominator mismatch", bad)
