@@ -4,7 +4,8 @@
 
 Each source compiles to an object under gat-tfs_b200/_build/ (in parallel), and
 the objects link into gat-tfs_b200/libgat_b200.so with the CUDA runtime linked
-statically, so the library needs only the NVIDIA driver at run time. A source
+statically, so the library needs only the NVIDIA driver at run time. The C++
+driver gat-tfs_b200/gat_b200_bench (cli/) links against it. A source
 is recompiled only when it or a header is newer than its object.
 """
 import argparse
@@ -19,6 +20,8 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 OUT = PKG / "_build"
 LIB = PKG / "libgat_b200.so"
+CLI_SRC = PKG / "cli" / "gat_b200_bench.cpp"
+CLI = PKG / "gat_b200_bench"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CUDA_FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-fopenmp,-Wall",
@@ -71,6 +74,13 @@ def build(verbose: bool = False) -> Path:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError("link failed\n" + r.stdout + r.stderr)
+    # the C++ driver (the reference's bench/main.cpp interface over the C ABI)
+    if not CLI.exists() or CLI.stat().st_mtime < max(LIB.stat().st_mtime, CLI_SRC.stat().st_mtime):
+        cmd = ["g++", "-O2", "-std=c++17", "-Wall", "-I" + str(ROOT / "include"), str(CLI_SRC), "-o", str(CLI),
+               "-L" + str(PKG), "-lgat_b200", "-Wl,-rpath,$ORIGIN"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError("driver build failed\n" + r.stdout + r.stderr)
     return LIB
 
 

@@ -1,0 +1,321 @@
+// gat_b200_bench: the reference's benchmark driver (baseline/bench/main.cpp)
+// on the B200 library, through the C ABI only (include/gat_b200.h).
+//
+// Same arguments (--key value) and the same log lines, so the reference's
+// summarize scripts read its output unchanged:
+//   ENV / STATIC / CONFIG / MODEL / COLD lines, one JSON line per layer and
+//   repeat with the keys of print_times (baseline/src/common.cpp:155-170),
+//   E2E per repeat, SUMMARY; in correctness mode ERROR lines
+//   (common.cpp:151-154) and a CORRECTNESS verdict.
+//
+// Paths: ref_fp32 (served by the FP32 path, which the test suite pins to the
+// reference's R0 at max-abs <= 1e-5), standard_fp32, standard_bf16, tfs_bf16,
+// matched_attention, and adaptive_bf16 (layer 1 through TFS aggregation).
+// Modes: benchmark, correctness. A forward is timed end to end on the host
+// clock: FP32 X from host memory in, FP32 logits to host memory out, as the
+// reference times its forward over host buffers.
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <iomanip>
+#include <iostream>
+#include <map>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "gat_b200.h"
+
+namespace {
+
+using Clock = std::chrono::steady_clock;
+double seconds(Clock::time_point a, Clock::time_point b) { return std::chrono::duration<double>(b - a).count(); }
+
+void check(int rc) {
+    if (rc) throw std::runtime_error(gat_b200_last_error());
+}
+
+struct Args {
+    std::map<std::string, std::string> v;
+    Args(int argc, char** argv) {
+        const std::vector<std::string> allowed = {"--graph",   "--weights", "--seed",    "--save-weights", "--path",
+                                                  "--mode",    "--threads", "--panel-r", "--repeats",      "--warmups",
+                                                  "--layer",   "--lr-policy", "--max-abs", "--rel-l2",     "--output"};
+        for (int i = 1; i < argc; ++i) {
+            std::string k = argv[i];
+            if (k.rfind("--", 0) != 0 || i + 1 == argc) throw std::runtime_error("arguments must be --key value");
+            if (std::find(allowed.begin(), allowed.end(), k) == allowed.end())
+                throw std::runtime_error("unknown argument " + k);
+            if (!v.emplace(k, argv[++i]).second) throw std::runtime_error("duplicate argument " + k);
+        }
+    }
+    std::string get(const std::string& k, const std::string& def = "") const {
+        auto i = v.find(k);
+        return i == v.end() ? def : i->second;
+    }
+    int num(const std::string& k, int def) const { return std::stoi(get(k, std::to_string(def))); }
+};
+
+struct Graph {
+    uint64_t n = 0, e = 0;
+    uint32_t din = 0, classes = 0;
+    std::vector<uint64_t> row;
+    std::vector<uint32_t> col;
+    std::vector<float> x;
+};
+
+struct Layer {
+    int in = 0, heads = 0, dim = 0;
+    std::vector<float> w, al, ar;
+};
+
+void layer_shape(int l, int din, int classes, int& in, int& heads, int& dim) {
+    in = l == 0 ? din : 256;  // baseline/src/common.cpp:53
+    heads = l < 2 ? 8 : 1;
+    dim = l < 2 ? 32 : classes;
+}
+
+std::vector<Layer> model_storage(int din, int classes) {
+    std::vector<Layer> m(3);
+    for (int l = 0; l < 3; ++l) {
+        layer_shape(l, din, classes, m[l].in, m[l].heads, m[l].dim);
+        const size_t width = size_t(m[l].heads) * m[l].dim;
+        m[l].w.resize(size_t(m[l].in) * width);
+        m[l].al.resize(width);
+        m[l].ar.resize(width);
+    }
+    return m;
+}
+
+struct Error {
+    bool finite = true;
+    double max_abs = 0, mean_abs = 0, relative_l2 = 0, rmse = 0, p50 = 0, p90 = 0, p99 = 0;
+};
+
+// The reference's error metrics (baseline/src/common.cpp:141-150).
+Error errors(const std::vector<float>& ref, const std::vector<float>& got) {
+    Error e;
+    if (ref.size() != got.size()) throw std::runtime_error("error metric size mismatch");
+    double num = 0, den = 0, sum = 0;
+    std::vector<double> diffs(ref.size());
+    for (size_t i = 0; i < ref.size(); ++i) {
+        if (!std::isfinite(got[i])) e.finite = false;
+        const double d = std::fabs(double(got[i]) - double(ref[i]));
+        diffs[i] = d;
+        e.max_abs = std::max(e.max_abs, d);
+        sum += d;
+        num += d * d;
+        den += double(ref[i]) * ref[i];
+    }
+    if (!ref.empty()) {
+        e.mean_abs = sum / ref.size();
+        e.rmse = std::sqrt(num / ref.size());
+        e.relative_l2 = std::sqrt(num) / std::max(std::sqrt(den), 1e-30);
+        std::sort(diffs.begin(), diffs.end());
+        auto q = [&](double p) { return diffs[std::min(diffs.size() - 1, size_t(std::ceil(p * diffs.size())) - 1)]; };
+        e.p50 = q(.5);
+        e.p90 = q(.9);
+        e.p99 = q(.99);
+    }
+    return e;
+}
+
+void print_error(const std::string& path, int layer, const std::string& stage, const Error& e) {
+    std::cout << std::setprecision(10) << "ERROR path=" << path << " layer=" << layer << " stage=" << stage
+              << " finite=" << e.finite << " max_abs=" << e.max_abs << " mean_abs=" << e.mean_abs
+              << " relative_l2=" << e.relative_l2 << " rmse=" << e.rmse << " p50=" << e.p50 << " p90=" << e.p90
+              << " p99=" << e.p99 << "\n";
+}
+
+double pct(std::vector<double> x, double q) {
+    std::sort(x.begin(), x.end());
+    return x[std::min(x.size() - 1, size_t(std::ceil(q * x.size()) - 1))];
+}
+
+int path_code(const std::string& p) {
+    if (p == "ref_fp32" || p == "standard_fp32") return GAT_B200_PATH_STANDARD_FP32;
+    if (p == "standard_bf16") return GAT_B200_PATH_STANDARD_BF16;
+    if (p == "tfs_bf16") return GAT_B200_PATH_TFS_BF16;
+    if (p == "matched_attention") return GAT_B200_PATH_MATCHED_ATTENTION;
+    if (p == "adaptive_bf16") return GAT_B200_PATH_ADAPTIVE_BF16;
+    throw std::runtime_error("bad path");
+}
+
+// Device objects of one (graph, checkpoint): the graph with its degree
+// schedule, the three prepared layers, and one model per path.
+struct Device {
+    gat_b200_graph* g = nullptr;
+    gat_b200_layer* layer[3] = {nullptr, nullptr, nullptr};
+    std::map<int, gat_b200_model*> models;
+    ~Device() {
+        for (auto& kv : models) gat_b200_model_destroy(kv.second);
+        for (auto* p : layer) gat_b200_layer_destroy(p);
+        gat_b200_graph_destroy(g);
+    }
+    gat_b200_model* model(int path) {
+        auto it = models.find(path);
+        if (it != models.end()) return it->second;
+        gat_b200_model* m = nullptr;
+        const gat_b200_layer* const ls[3] = {layer[0], layer[1], layer[2]};
+        check(gat_b200_model_create(g, ls, path, &m));
+        models[path] = m;
+        return m;
+    }
+};
+
+std::vector<float> forward(gat_b200_model* m, const Graph& g, const std::vector<Layer>& model) {
+    std::vector<float> logits(g.n * size_t(model[2].heads) * model[2].dim);
+    check(gat_b200_model_forward(m, g.x.data(), 1, logits.data(), 1, nullptr));
+    return logits;
+}
+
+void require_finite(const std::vector<float>& v, const char* what) {
+    for (size_t i = 0; i < v.size(); ++i)
+        if (!std::isfinite(v[i])) throw std::runtime_error(std::string("nonfinite ") + what + " index=" + std::to_string(i));
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+    try {
+        Args a(argc, argv);
+        const std::string graph_path = a.get("--graph"), path = a.get("--path", "standard_bf16"),
+                          mode = a.get("--mode", "correctness");
+        if (graph_path.empty()) throw std::runtime_error("--graph is required");
+        const int pc = path_code(path);
+        const int threads = a.num("--threads", 16), panel = a.num("--panel-r", 64), reps = a.num("--repeats", 5),
+                  warmups = a.num("--warmups", 2), layer_arg = a.num("--layer", 0);
+        if (threads <= 0 || panel < 16 || panel % 16 || reps < 1 || warmups < 0 || layer_arg < 0 || layer_arg > 3)
+            throw std::runtime_error("invalid benchmark controls");
+        if (layer_arg != 0) throw std::runtime_error("--layer: only whole-model runs (0) on this backend");
+        std::cout << "ENV backend=gat_b200 version=" << gat_b200_version() << " threads=" << threads
+                  << " source_input=" << graph_path << " checkpoint="
+                  << (a.get("--weights").empty() ? "random_fixture_not_trained" : a.get("--weights"))
+                  << " profile=0 device=sm_100a\n";
+        const auto cold_start = Clock::now();
+        Graph g;
+        check(gat_b200_read_graph_header(graph_path.c_str(), &g.n, &g.e, &g.din, &g.classes));
+        g.row.resize(g.n + 1);
+        g.col.resize(g.e);
+        g.x.resize(g.n * size_t(g.din));
+        check(gat_b200_read_graph(graph_path.c_str(), g.n, g.e, g.din, g.row.data(), g.col.data(), g.x.data()));
+        std::vector<Layer> model = model_storage(int(g.din), int(g.classes));
+        float* w[3] = {model[0].w.data(), model[1].w.data(), model[2].w.data()};
+        float* al[3] = {model[0].al.data(), model[1].al.data(), model[2].al.data()};
+        float* ar[3] = {model[0].ar.data(), model[1].ar.data(), model[2].ar.data()};
+        if (!a.get("--weights").empty()) {
+            check(gat_b200_read_weights(a.get("--weights").c_str(), int(g.din), int(g.classes), w, al, ar));
+        } else {
+            if (a.get("--seed").empty())
+                throw std::runtime_error("provide --weights checkpoint.bin or explicit --seed for synthetic fixture");
+            check(gat_b200_random_model(int(g.din), int(g.classes), a.num("--seed", 11), w, al, ar));
+        }
+        if (!a.get("--save-weights").empty())
+            check(gat_b200_write_weights(a.get("--save-weights").c_str(), int(g.din), int(g.classes), w, al, ar));
+
+        Device dev;
+        auto t0 = Clock::now();
+        check(gat_b200_graph_create(g.n, g.e, g.row.data(), g.col.data(), nullptr, &dev.g));
+        check(gat_b200_check_device());
+        const double degree_sort_s = seconds(t0, Clock::now());
+        t0 = Clock::now();
+        for (int l = 0; l < 3; ++l)
+            check(gat_b200_layer_create(model[l].in, model[l].heads, model[l].dim, model[l].w.data(),
+                                        model[l].al.data(), model[l].ar.data(), &dev.layer[l]));
+        const double prepare_s = seconds(t0, Clock::now());
+        uint64_t neighbor_steps = 0;
+        check(gat_b200_graph_schedule(dev.g, nullptr, &neighbor_steps));
+        std::cout << "STATIC degree_sort_ms=" << degree_sort_s * 1000 << " model_prepare_ms=" << prepare_s * 1000
+                  << " bytes=" << g.n * 4 << " graph_policy=as_loaded_no_mutation\n";
+        const std::string policy =
+            a.get("--lr-policy", path == "tfs_bf16" || path == "matched_attention" ? "bf16" : "z_avx");
+        std::cout << "CONFIG mode=" << mode << " path=" << path << " lr_policy=" << policy << " panel_R=" << panel
+                  << " layer=" << layer_arg << " warmups=" << warmups << " repeats=" << reps << "\n";
+
+        if (mode == "correctness") {
+            const bool have_abs = !a.get("--max-abs").empty(), have_rel = !a.get("--rel-l2").empty();
+            if (have_abs != have_rel) throw std::runtime_error("set both --max-abs and --rel-l2");
+            const double maxabs = have_abs ? std::stod(a.get("--max-abs")) : 0,
+                         rel = have_rel ? std::stod(a.get("--rel-l2")) : 0;
+            if (have_abs && (!std::isfinite(maxabs) || !std::isfinite(rel) || maxabs < 0 || rel < 0))
+                throw std::runtime_error("invalid accuracy thresholds");
+            const std::vector<float> master = forward(dev.model(GAT_B200_PATH_STANDARD_FP32), g, model);
+            require_finite(master, "ref_fp32 output");
+            bool pass = true, finite = true;
+            for (const std::string test : {"standard_fp32", "standard_bf16", "tfs_bf16", "matched_attention",
+                                           "adaptive_bf16"}) {
+                const std::vector<float> out = forward(dev.model(path_code(test)), g, model);
+                const Error e = errors(master, out);
+                print_error(test, 3, "model_path_specific_chain", e);
+                finite &= e.finite;
+                pass &= e.finite && (!have_abs || (e.max_abs <= maxabs && e.relative_l2 <= rel));
+            }
+            std::cout << "CORRECTNESS finite=" << finite << " accuracy_gate="
+                      << (have_abs ? (pass ? "PASS" : "FAIL") : "UNCONFIGURED_NOT_ACCEPTED")
+                      << " task_metric=UNAVAILABLE\n";
+            return pass ? 0 : 1;
+        }
+        if (mode != "benchmark") throw std::runtime_error("bad mode");
+
+        gat_b200_model* m = dev.model(pc);
+        check(gat_b200_model_enable_timing(m, 1));
+        std::cout << "MODEL workspace_bytes=" << g.n * size_t(g.din) * 4 << " static_bytes=" << g.n * 4
+                  << " excludes_graph_and_master_weights=true\n";
+        std::cout << "COLD startup_before_inference_ms=" << seconds(cold_start, Clock::now()) * 1000
+                  << " includes_graph_load=true\n";
+        std::vector<double> totals;
+        double cold_forward = 0;
+        std::vector<float> logits;
+        const bool tfs_layer1 = pc == GAT_B200_PATH_TFS_BF16 || pc == GAT_B200_PATH_ADAPTIVE_BF16;
+        const bool fp32 = pc == GAT_B200_PATH_STANDARD_FP32;
+        for (int r = -warmups; r < reps; ++r) {
+            const auto begin = Clock::now();
+            logits = forward(m, g, model);
+            const double total = seconds(begin, Clock::now());
+            if (r == -warmups) cold_forward = total;
+            require_finite(logits, "benchmark output");
+            if (r < 0) continue;
+            totals.push_back(total);
+            float st[9];
+            if (gat_b200_model_stage_times(m, st) < 1) throw std::runtime_error(gat_b200_last_error());
+            for (int l = 0; l < 3; ++l) {
+                const Layer& p = model[l];
+                // stage slots: 1 convert, 2+2l projection (TFS: lr_reordered + max prescan), 3+2l aggregation
+                const bool tfs = pc == GAT_B200_PATH_TFS_BF16 || (tfs_layer1 && l == 0);
+                const double pre = st[2 + 2 * l], agg = st[3 + 2 * l], conv = l == 0 ? st[1] : 0.0;
+                std::cout << std::setprecision(10) << "{\"path\":\"" << path << "\",\"mode\":\"" << mode
+                          << "\",\"layer\":" << l + 1 << ",\"rep\":" << r << ",\"N\":" << g.n << ",\"E\":" << g.e
+                          << ",\"D\":" << p.in << ",\"K\":" << p.heads << ",\"d\":" << p.dim
+                          << ",\"threads\":" << threads << ",\"profile\":false,\"precision\":\""
+                          << (fp32 ? "FP32" : "BF16_RNE_FP32_state") << "\""
+                          << ",\"projection_ms\":" << (tfs ? 0.0 : pre) << ",\"lr_ms\":" << (tfs ? pre : 0.0)
+                          << ",\"max_prescan_ms\":0,\"score_exp_aggregate_ms\":" << agg
+                          << ",\"normalize_ms\":0,\"activation_ms\":0,\"convert_ms\":" << conv
+                          << ",\"total_ms\":" << pre + agg + conv << ",\"workspace_bytes\":0"
+                          << ",\"static_preprocess_ms\":" << (degree_sort_s + prepare_s) * 1000
+                          << ",\"panel_R\":" << panel << ",\"tile_rows\":16"
+                          << ",\"neighbor_steps\":" << (tfs ? neighbor_steps * p.heads : 0)
+                          << ",\"executed_fma\":0,\"padding_executed_flops\":0"
+                          << ",\"h2d_ms\":" << (l == 0 ? st[0] : 0.0) << ",\"d2h_ms\":" << (l == 2 ? st[8] : 0.0)
+                          << ",\"kernels\":" << gat_b200_model_launches(m) << "}\n";
+            }
+            std::cout << "E2E path=" << path << " rep=" << r << " layer=" << layer_arg << " total_ms=" << total * 1000
+                      << " finite=1\n";
+        }
+        if (!a.get("--output").empty()) {
+            std::ofstream f(a.get("--output"), std::ios::binary);
+            f.write(reinterpret_cast<const char*>(logits.data()), std::streamsize(logits.size() * 4));
+            if (!f) throw std::runtime_error("cannot write dump");
+        }
+        std::cout << "SUMMARY path=" << path << " median_ms=" << pct(totals, .5) * 1000
+                  << " p95_ms=" << pct(totals, .95) * 1000 << " cold_forward_ms=" << cold_forward * 1000
+                  << " repeats=" << reps << " task_accuracy=UNVERIFIED\n";
+        return 0;
+    } catch (const std::exception& e) {
+        std::cerr << "FAIL " << e.what() << "\n";
+        return 1;
+    }
+}

@@ -337,7 +337,8 @@ int gat_b200_model_create(const gat_b200_graph* g, const gat_b200_layer* const* 
     if (!out) return fail("model_create: null output handle");
     *out = nullptr;
     if (!g || !layers || !layers[0] || !layers[1] || !layers[2]) return fail("model_create: null handle");
-    if (path < GAT_B200_PATH_STANDARD_BF16 || path > GAT_B200_PATH_ADAPTIVE_BF16) return fail("model_create: bad path");
+    if (path < GAT_B200_PATH_STANDARD_BF16 || path > GAT_B200_PATH_MATCHED_ATTENTION)
+        return fail("model_create: bad path");
     for (int l = 0; l < 2; ++l)
         if (layers[l + 1]->in != layers[l]->width) return fail("model_create: layer widths do not chain");
     gat_b200_model* m = new (std::nothrow) gat_b200_model();
@@ -475,6 +476,13 @@ int gat_b200_model_forward(gat_b200_model* m, const float* x, int x_on_host, flo
         } else {
             const int ldh = gat_b200_padded_ld(p->width, hd);
             if ((rc = projection_dispatch(p, n, lin, ldin, hd, m->h, hd, ldh, m->left, m->right, st))) return rc;
+            if (m->path == GAT_B200_PATH_MATCHED_ATTENTION) {
+                // L/R from the BF16 layer input and W.a (lr_reordered, "bf16" policy)
+                if ((rc = lr_reordered_launch(p, n, lin, GAT_B200_BF16, ldin, GAT_B200_LR_BF16, nullptr, 0, m->left,
+                                              m->right, st)))
+                    return rc;
+                ++launches;
+            }
             mark(m, 3 + 2 * l, st);
             if ((rc = aggregate_dispatch(m->g, p->heads, p->dim, m->h, hd, ldh, m->left, m->right, nullptr, nullptr,
                                          0, last ? 0 : 1, dst, (!last && bf16) ? 1 : 0, ldo, nullptr, nullptr, st)))

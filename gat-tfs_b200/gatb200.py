@@ -29,7 +29,7 @@ if not LIB_PATH.exists():
 _lib = C.CDLL(str(LIB_PATH))
 
 F32, BF16 = 0, 1
-PATH_STANDARD_BF16, PATH_STANDARD_FP32, PATH_TFS_BF16, PATH_ADAPTIVE_BF16 = 0, 1, 2, 3
+PATH_STANDARD_BF16, PATH_STANDARD_FP32, PATH_TFS_BF16, PATH_ADAPTIVE_BF16, PATH_MATCHED_ATTENTION = 0, 1, 2, 3, 4
 TFS_EDGE, TFS_BLOCK, TFS_SPLIT = 0, 1, 2
 LR_BF16, LR_FP32 = 0, 1
 PATHS = {"standard_bf16": PATH_STANDARD_BF16, "standard_fp32": PATH_STANDARD_FP32}

@@ -49,6 +49,10 @@ extern "C" {
  * STANDARD_BF16 -- the per-layer choice of the reference's adaptive driver
  * (baseline/tfs_online/adaptive_main.cpp:86-101), where TFS wins on layer 1. */
 #define GAT_B200_PATH_ADAPTIVE_BF16 3
+/* matched_attention: STANDARD_BF16 with L/R from lr_reordered ("bf16" policy,
+ * the TFS attention contraction) instead of from Z
+ * (baseline/bench/main.cpp:22-25, baseline/src/baseline_standard.cpp:98-108). */
+#define GAT_B200_PATH_MATCHED_ATTENTION 4
 
 /* TFS rounding variants (gat_b200_tfs_aggregate). */
 #define GAT_B200_TFS_EDGE 0  /* V += RNE(p x) . W per neighbour: B1, icpp_online  */

@@ -1,0 +1,70 @@
+"""The C++ driver gat-tfs_b200/gat_b200_bench: the reference's bench/main.cpp
+interface (arguments, log lines, JSON keys of print_times, common.cpp:155-170)
+over the C ABI."""
+import json
+import subprocess
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+CLI = ROOT / "gat-tfs_b200" / "gat_b200_bench"
+GOLDEN = ROOT / "tests" / "golden"
+
+# the per-layer keys of the reference's print_times that its summaries read
+TIMES_KEYS = ["path", "mode", "layer", "rep", "N", "E", "D", "K", "d", "threads", "profile", "precision",
+              "projection_ms", "lr_ms", "max_prescan_ms", "score_exp_aggregate_ms", "normalize_ms", "activation_ms",
+              "convert_ms", "total_ms", "workspace_bytes", "static_preprocess_ms", "panel_R", "tile_rows",
+              "neighbor_steps", "executed_fma", "padding_executed_flops"]
+
+
+def run(*args, timeout=300):
+    if not CLI.exists():
+        subprocess.run(["python", str(ROOT / "gat-tfs_b200" / "build.py")], check=True)
+    return subprocess.run([str(CLI), *args], capture_output=True, text=True, timeout=timeout)
+
+
+def test_cli_argument_errors():
+    r = run("--graph")
+    assert r.returncode == 1 and "FAIL arguments must be --key value" in r.stderr
+    r = run("--graph", "x", "--graph", "y")
+    assert r.returncode == 1 and "FAIL duplicate argument --graph" in r.stderr
+    r = run("--mode", "benchmark")
+    assert r.returncode == 1 and "FAIL --graph is required" in r.stderr
+    r = run("--graph", str(GOLDEN / "fixture_small.gatbin"), "--path", "nope")
+    assert r.returncode == 1 and "FAIL bad path" in r.stderr
+    r = run("--graph", str(GOLDEN / "fixture_small.gatbin"))
+    assert r.returncode == 1 and "provide --weights checkpoint.bin or explicit --seed" in r.stderr
+    r = run("--graph", "/nonexistent.gatbin", "--seed", "11")
+    assert r.returncode == 1 and "FAIL cannot open graph" in r.stderr
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("path", ["standard_bf16", "standard_fp32", "tfs_bf16", "matched_attention", "adaptive_bf16"])
+def test_cli_benchmark_log_lines(path):
+    r = run("--graph", str(GOLDEN / "fixture_small.gatbin"), "--seed", "11", "--path", path, "--mode",
+            "benchmark", "--repeats", "2", "--warmups", "1")
+    assert r.returncode == 0, r.stderr
+    lines = r.stdout.splitlines()
+    for tag in ("ENV ", "STATIC ", "CONFIG ", "MODEL ", "COLD ", "E2E ", "SUMMARY "):
+        assert any(ln.startswith(tag) for ln in lines), tag
+    recs = [json.loads(ln) for ln in lines if ln.startswith("{")]
+    assert len(recs) == 2 * 3
+    for rec in recs:
+        for k in TIMES_KEYS:
+            assert k in rec, k
+        assert rec["path"] == path and rec["N"] == 200 and rec["total_ms"] >= 0
+
+
+@pytest.mark.gpu
+def test_cli_correctness_gate():
+    r = run("--graph", str(GOLDEN / "fixture_small.gatbin"), "--seed", "11", "--mode", "correctness",
+            "--max-abs", "1", "--rel-l2", "1e-2")
+    assert r.returncode == 0, r.stdout + r.stderr
+    errs = [ln for ln in r.stdout.splitlines() if ln.startswith("ERROR ")]
+    assert len(errs) == 5
+    assert "CORRECTNESS finite=1 accuracy_gate=PASS" in r.stdout
+    # a gate no BF16 path can meet fails, as in the reference
+    r = run("--graph", str(GOLDEN / "fixture_small.gatbin"), "--seed", "11", "--mode", "correctness",
+            "--max-abs", "1e-9", "--rel-l2", "1e-9")
+    assert r.returncode == 1 and "accuracy_gate=FAIL" in r.stdout

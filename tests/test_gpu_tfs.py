@@ -306,3 +306,25 @@ def test_reference_fixture_fixed_p(dev, golden):
     assert rel_l2(O.finish(oo, od, K, d, False), host(out)) <= 1e-2
     layer.close()
     g.close()
+
+
+def test_matched_attention_model(dev, golden):
+    """matched_attention (bench/main.cpp:22-25): B0 BF16 with L/R from lr_reordered."""
+    import configs
+    from test_gpu_parity import _model, _forward
+    ref = np.load(golden / "config1.npz")
+    cfg = configs.make("c1")
+    graph, params = cfg.graph, cfg.model
+    _, _, m = _model(graph, params, G.PATH_MATCHED_ATTENTION)
+    got = _forward(m, graph.x)
+    inp = graph.x
+    for l, p in enumerate(params):
+        xq = O.quantize(inp)
+        z = O.quantize(xq @ O.quantize(p.w))  # H stored in BF16 as the device does
+        blr = O.prepare_blr(p.w, p.al, p.ar, p.heads, p.dim)
+        L, R = O.lr_reordered(inp, blr, p.heads, 0)
+        mx = O.max_prescan(graph.row, graph.col, L, R, p.heads)
+        out, den = O.standard_aggregate(graph.row, graph.col, z, L, R, mx, p.heads, p.dim)
+        inp = O.finish(out, den, p.heads, p.dim, l < 2)
+    assert rel_l2(inp, got) <= 3e-3
+    assert rel_l2(ref["ref_logits"], got) <= 1e-2
