@@ -9,15 +9,25 @@ of all their sources, so each layer is
   2. one all-gather of H (and of R) into every rank's feature table;
   3. edge-softmax aggregation of the rank's own rows from that table.
 
-The all-gather is the only exchange. Ranks own different row counts while
-ncclAllGather moves equal blocks, so every rank's block is padded to the
-largest row count n_max, and the column ids of the rank's CSR slice are
-remapped once into that padded table: source s of rank r's range becomes
-r*n_max + (s - cuts[r]).
+The all-gather is the only exchange. To overlap it with compute, each rank's
+rows are further cut into `chunks` row chunks (balanced by edges, each with its
+own CSR slice and degree schedule). Aggregating chunk c of layer l yields the
+chunk's rows of layer l+1's input; they are projected at once and chunk c's
+all-gather runs on NCCL's stream while chunk c+1 is aggregated. Only layer
+l+1's aggregation waits for all chunks. Layers alternate between two feature
+tables, so a layer's exchange never overwrites rows the previous layer's
+aggregation still reads.
+
+The feature table is chunk-major: ncclAllGather moves equal blocks, so chunk c
+of every rank is padded to the largest chunk (chunk_max rows) and the table
+holds, for c = 0..chunks-1, the chunk-c blocks of ranks 0..G-1 one after the
+other. Source s, owned by rank r at local chunk c and offset i, sits at table
+row (c*G + r)*chunk_max + i; every CSR slice's source ids are remapped to
+those rows once.
 """
 from __future__ import annotations
 
-from typing import List, Optional, Sequence
+from typing import Optional, Sequence
 
 import numpy as np
 
@@ -35,47 +45,79 @@ def partition(row: np.ndarray, world: int) -> np.ndarray:
     return np.maximum.accumulate(cuts)
 
 
-def slice_local(row: np.ndarray, col_rows: np.ndarray, cuts: np.ndarray, rank: int):
-    """CSR slice of `rank` from the global row pointers and the sources of the
-    rank's own rows (col[row[lo]:row[hi]]), with the source ids remapped into
-    the padded feature table. Returns (row_loc u64[n_loc+1], col_loc u32, n_max)."""
-    row = np.asarray(row, np.uint64)
-    n_max = int(np.diff(cuts).max())
-    lo, hi = int(cuts[rank]), int(cuts[rank + 1])
-    b = int(row[lo])
-    if len(col_rows) != int(row[hi]) - b:
-        raise ValueError("col_rows must hold the sources of the rank's rows")
-    row_loc = (row[lo:hi + 1] - np.uint64(b)).astype(np.uint64)
-    src = np.asarray(col_rows).astype(np.int64)
-    owner = np.searchsorted(cuts, src, side="right") - 1
-    col_loc = (owner * n_max + (src - cuts[owner])).astype(np.uint32)
-    return row_loc, col_loc, n_max
+class Layout:
+    """Rank cuts, per-rank chunk cuts and the chunk-major feature table."""
 
+    def __init__(self, row: np.ndarray, world: int, chunks: int, cuts: Optional[np.ndarray] = None):
+        row = np.asarray(row, np.uint64)
+        self.world, self.chunks = world, chunks
+        self.cuts = partition(row, world) if cuts is None else np.asarray(cuts, np.int64)
+        cc = np.empty((world, chunks + 1), np.int64)
+        for r in range(world):
+            lo, hi = int(self.cuts[r]), int(self.cuts[r + 1])
+            sub = row[lo:hi + 1]
+            e0, e1 = int(sub[0]), int(sub[-1])
+            targets = np.asarray([e0 + (k * (e1 - e0)) // chunks for k in range(1, chunks)], np.uint64)
+            inner = lo + np.searchsorted(sub, targets, side="left").astype(np.int64)
+            cc[r] = np.maximum.accumulate(np.concatenate([[lo], np.clip(inner, lo, hi), [hi]]))
+        self.ccuts = cc  # global row boundaries [world, chunks+1]
+        self.chunk_max = max(1, int(np.diff(cc, axis=1).max()))
+        self.n_table = chunks * world * self.chunk_max
+        self._starts = cc[:, :-1].reshape(-1)  # ascending: ranks' ranges are contiguous
 
-def slice_graph(row: np.ndarray, col: np.ndarray, cuts: np.ndarray, rank: int):
-    """slice_local from the whole column array."""
-    lo, hi = int(cuts[rank]), int(cuts[rank + 1])
-    return slice_local(row, np.asarray(col)[int(row[lo]):int(row[hi])], cuts, rank)
+    def slots(self, src: np.ndarray) -> np.ndarray:
+        """Table rows of global source ids."""
+        src = np.asarray(src).astype(np.int64)
+        k = np.searchsorted(self._starts, src, side="right") - 1  # rank*chunks + chunk (empty chunks skipped)
+        r, c = k // self.chunks, k % self.chunks
+        return ((c * self.world + r) * self.chunk_max + (src - self._starts[k])).astype(np.uint32)
+
+    def chunk_rows(self, rank: int, c: int):
+        """(first, end) local row of chunk c of `rank`."""
+        lo = int(self.cuts[rank])
+        return int(self.ccuts[rank, c]) - lo, int(self.ccuts[rank, c + 1]) - lo
+
+    def slice_chunk(self, row: np.ndarray, col_rows: np.ndarray, rank: int, c: int):
+        """CSR slice of chunk c of `rank` with sources remapped to table rows.
+        col_rows: the sources of all of the rank's rows (col[row[lo]:row[hi]])."""
+        row = np.asarray(row, np.uint64)
+        lo = int(self.cuts[rank])
+        a, b = int(self.ccuts[rank, c]), int(self.ccuts[rank, c + 1])
+        base = int(row[lo])
+        row_loc = (row[a:b + 1] - row[a]).astype(np.uint64)
+        src = np.asarray(col_rows)[int(row[a]) - base:int(row[b]) - base]
+        return row_loc, self.slots(src)
 
 
 class PartitionedModel:
-    """Three-layer BF16 forward of this rank's rows (bench/main.cpp:171-172 per rank)."""
+    """Three-layer BF16 forward of this rank's rows (bench/main.cpp:171-172 per
+    rank), each layer's all-gather overlapped with the previous layer's
+    aggregation chunk by chunk."""
 
     def __init__(self, row: np.ndarray, col_rows: np.ndarray, params: Sequence[G.Param], rank: int, world: int,
-                 stream=None, dist_module=None, cuts: Optional[np.ndarray] = None):
+                 stream=None, dist_module=None, cuts: Optional[np.ndarray] = None, chunks: int = 4):
         """row: all n+1 row pointers; col_rows: the sources of this rank's rows
         (col[row[cuts[rank]]:row[cuts[rank+1]]]); cuts: partition(row, world)."""
         import torch
         self.torch = torch
         self.dist = dist_module
         self.rank, self.world = rank, world
-        self.cuts = partition(row, world) if cuts is None else cuts
-        row_loc, col_loc, n_max = slice_local(row, col_rows, self.cuts, rank)
-        self.n_loc = len(row_loc) - 1
-        self.e_loc = len(col_loc)
-        self.n_max = n_max
+        self.lay = Layout(row, world, chunks, cuts)
+        self.cuts = self.lay.cuts
+        lo, hi = int(self.cuts[rank]), int(self.cuts[rank + 1])
+        if len(col_rows) != int(row[hi]) - int(row[lo]):
+            raise ValueError("col_rows must hold the sources of the rank's rows")
+        self.n_loc = hi - lo
+        self.e_loc = len(col_rows)
         self.stream = stream
-        self.g = G.DeviceGraph(row_loc, col_loc, stream, n_src=world * n_max)
+        self.chunks = []  # (first local row, end local row, DeviceGraph or None)
+        for c in range(chunks):
+            a, b = self.lay.chunk_rows(rank, c)
+            g = None
+            if b > a:
+                rl, cl = self.lay.slice_chunk(row, col_rows, rank, c)
+                g = G.DeviceGraph(rl, cl, stream, n_src=self.lay.n_table)
+            self.chunks.append((a, b, g))
         self.layers = [G.DeviceLayer(p) for p in params]
         self.din = params[0].in_
         self.classes = params[2].width
@@ -84,33 +126,63 @@ class PartitionedModel:
         ldh_max = G.padded_ld(wmax, G.BF16)
         self.ld0 = G.padded_ld(self.din, G.BF16)
         self.ld_hidden = G.padded_ld(max(params[0].width, params[1].width), G.BF16)
-        n = self.n_loc
+        n, cm, P = self.n_loc, self.lay.chunk_max, chunks
         i16 = torch.int16
         self.x_f32 = torch.empty((n, self.din), dtype=torch.float32, device=dev)
         self.x0 = torch.zeros((n, self.ld0), dtype=i16, device=dev)
-        self.h_send = torch.zeros((n_max * ldh_max,), dtype=i16, device=dev)
-        self.h_full = torch.zeros((world * n_max * ldh_max,), dtype=i16, device=dev)
-        self.r_send = torch.zeros((n_max * 8,), dtype=torch.float32, device=dev)
-        self.r_full = torch.zeros((world * n_max * 8,), dtype=torch.float32, device=dev)
-        self.left = torch.zeros((n * 8,), dtype=torch.float32, device=dev)
+        # one send block per chunk; two tables, alternating by layer
+        self.h_send = torch.zeros((P, cm * ldh_max), dtype=i16, device=dev)
+        self.r_send = torch.zeros((P, cm * 8), dtype=torch.float32, device=dev)
+        self.h_full = [torch.zeros((self.lay.n_table * ldh_max,), dtype=i16, device=dev) for _ in range(2)]
+        self.r_full = [torch.zeros((self.lay.n_table * 8,), dtype=torch.float32, device=dev) for _ in range(2)]
+        # L [n][heads] of a layer, alternating by layer like the tables
+        self.left = [torch.zeros((n * 8,), dtype=torch.float32, device=dev) for _ in range(2)]
         self.xs = [torch.zeros((n, self.ld_hidden), dtype=i16, device=dev) for _ in range(2)]
         self.logits = torch.empty((n, self.classes), dtype=torch.float32, device=dev)
         self.events = None
+        self.pending = []
 
     def enable_timing(self, on: bool):
         torch = self.torch
-        self.events = [torch.cuda.Event(enable_timing=True) for _ in range(12)] if on else None
-        self.stage_ms: List[np.ndarray] = []
+        self.events = [torch.cuda.Event(enable_timing=True) for _ in range(7)] if on else None
 
     def _mark(self, i):
-        # events 0 start, 1 after the input copy, 2+3l / 3+3l / 4+3l before the
-        # projection / all-gather / aggregation of layer l, 11 end
+        # 0 start, 1 after the input copy, 2 after layer 1's projections,
+        # 3+l once layer l's exchange is waited for, 6 end
         if self.events is not None:
             self.events[i].record(self.torch.cuda.current_stream())
 
+    def _project(self, l: int, c: int, x, ldx):
+        """Projection of chunk c's rows for layer l, then its all-gather (asynchronous)."""
+        torch = self.torch
+        p = self.layers[l]
+        a, b, _ = self.chunks[c]
+        cm, W, K = self.lay.chunk_max, self.world, p.heads
+        ldh = G.padded_ld(p.width, G.BF16)
+        hs = self.h_send[c, : cm * ldh]
+        rs = self.r_send[c, : cm * K]
+        if b > a:
+            G.projection(p, b - a, x[a:b], ldx, G.BF16, hs, G.BF16, ldh, self.left[l & 1][a * K:b * K], rs,
+                         self.stream)
+        hf = self.h_full[l & 1][c * W * cm * ldh:(c + 1) * W * cm * ldh]
+        rf = self.r_full[l & 1][c * W * cm * K:(c + 1) * W * cm * K]
+        if self.world > 1:
+            # the feature tables hold BF16 bit patterns in int16 storage; NCCL has no
+            # 16-bit integer type, so the exchange goes through a bfloat16 view
+            self.pending.append(self.dist.all_gather_into_tensor(hf.view(torch.bfloat16), hs.view(torch.bfloat16),
+                                                                  async_op=True))
+            self.pending.append(self.dist.all_gather_into_tensor(rf, rs, async_op=True))
+        else:
+            hf.copy_(hs)
+            rf.copy_(rs)
+
+    def _wait(self):
+        for w in self.pending:
+            w.wait()  # the current stream waits for NCCL's
+        self.pending = []
+
     def forward(self, x, logits, x_on_host: bool, logits_on_host: bool):
         """x: this rank's FP32 input rows [n_loc, din]; logits: [n_loc, classes]."""
-        torch = self.torch
         n = self.n_loc
         self._mark(0)
         xin = x
@@ -119,54 +191,44 @@ class PartitionedModel:
             xin = self.x_f32
         self._mark(1)
         G.convert(n, self.din, xin, self.din, self.x0, self.ld0, self.stream)
-        lin, ldin = self.x0, self.ld0
+        for c in range(len(self.chunks)):
+            self._project(0, c, self.x0, self.ld0)
+        self._mark(2)
+        dst_logits = logits if not logits_on_host else self.logits
         for l, p in enumerate(self.layers):
-            ldh = G.padded_ld(p.width, G.BF16)
-            K = p.heads
-            hs = self.h_send[: self.n_max * ldh]
-            hf = self.h_full[: self.world * self.n_max * ldh]
-            rs = self.r_send[: self.n_max * K]
-            rf = self.r_full[: self.world * self.n_max * K]
-            self._mark(2 + 3 * l)
-            G.projection(p, n, lin, ldin, G.BF16, hs, G.BF16, ldh, self.left, rs, self.stream)
-            self._mark(3 + 3 * l)
-            if self.world > 1:
-                # the feature tables hold BF16 bit patterns in int16 storage; NCCL
-                # has no 16-bit integer type, so the exchange goes through a
-                # bfloat16 view of the same bytes
-                self.dist.all_gather_into_tensor(hf.view(torch.bfloat16), hs.view(torch.bfloat16))
-                self.dist.all_gather_into_tensor(rf, rs)
-            else:
-                hf, rf = hs, rs
-            self._mark(4 + 3 * l)
-            last = l == 2
-            if last:
-                dst = logits if not logits_on_host else self.logits
-                G.aggregate_fused(self.g, K, p.dim, hf, G.BF16, ldh, self.left, rf, False, dst, G.F32, p.width,
-                                  self.stream)
-            else:
-                dst = self.xs[l]
-                G.aggregate_fused(self.g, K, p.dim, hf, G.BF16, ldh, self.left, rf, True, dst, G.BF16,
-                                  self.ld_hidden, self.stream)
-                lin, ldin = dst, self.ld_hidden
-        self._mark(11)
+            self._wait()
+            self._mark(3 + l)
+            K, ldh, last = p.heads, G.padded_ld(p.width, G.BF16), l == 2
+            hf, rf, left = self.h_full[l & 1], self.r_full[l & 1], self.left[l & 1]
+            for c, (a, b, g) in enumerate(self.chunks):
+                if g is not None:
+                    if last:
+                        G.aggregate_fused(g, K, p.dim, hf, G.BF16, ldh, left[a * K:b * K], rf, False,
+                                          dst_logits[a:b], G.F32, p.width, self.stream)
+                    else:
+                        G.aggregate_fused(g, K, p.dim, hf, G.BF16, ldh, left[a * K:b * K], rf, True,
+                                          self.xs[l][a:b], G.BF16, self.ld_hidden, self.stream)
+                if not last:
+                    self._project(l + 1, c, self.xs[l], self.ld_hidden)
+        self._mark(6)
         if logits_on_host:
             logits.copy_(self.logits, non_blocking=True)
 
     def stage_times(self) -> dict:
-        """ms of the last forward: projection, all-gather and aggregation per layer."""
+        """ms of the last forward: layer 1's projection, then per layer the time
+        from the wait for its exchange to the next layer's (its aggregation, the
+        next layer's projections and whatever exchange was not overlapped)."""
         torch = self.torch
         torch.cuda.synchronize()
         ev = self.events
-        out = {}
+        out = {"projection_l1": ev[1].elapsed_time(ev[2]), "wait_l1": ev[2].elapsed_time(ev[3])}
         for l in range(3):
-            out[f"projection_l{l + 1}"] = ev[2 + 3 * l].elapsed_time(ev[3 + 3 * l])
-            out[f"allgather_l{l + 1}"] = ev[3 + 3 * l].elapsed_time(ev[4 + 3 * l])
-            nxt = ev[5 + 3 * l] if l < 2 else ev[11]
-            out[f"aggregate_l{l + 1}"] = ev[4 + 3 * l].elapsed_time(nxt)
+            out[f"layer{l + 1}"] = ev[3 + l].elapsed_time(ev[4 + l] if l < 2 else ev[6])
         return out
 
     def close(self):
         for l in self.layers:
             l.close()
-        self.g.close()
+        for _, _, g in self.chunks:
+            if g is not None:
+                g.close()

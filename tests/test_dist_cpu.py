@@ -1,7 +1,7 @@
 """Host logic of the row-partitioned multi-GPU forward, on CPU with gloo.
 
 Each of two ranks builds its slice exactly as the GPU path does
-(dist.partition / slice_local / configs.make_part), runs the three layers with
+(dist.Layout / slice_chunk / configs.make_part), runs the three layers with
 the CPU oracle on its own rows, exchanges the projected features and R with a
 gloo all-gather into the padded table, and the gathered logits must equal the
 single-process oracle bit for bit: every row sees the same sources in the same
@@ -28,30 +28,46 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, name, q):
+def _rank_main(rank, world, port, name, q, chunks=4):
+    """Rank `rank` of the pipelined partitioned forward, with the oracle as the
+    arithmetic: chunk-major feature table, one all-gather per chunk."""
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     tdist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         part = configs.make_part(name, rank, world)
-        row_loc, col_loc, n_max = gdist.slice_local(part.row, part.col_rows, part.cuts, rank)
-        n_loc = len(row_loc) - 1
+        lay = gdist.Layout(part.row, world, chunks, part.cuts)
+        cm = lay.chunk_max
+        slices = [lay.slice_chunk(part.row, part.col_rows, rank, c) for c in range(chunks)]
+        bounds = [lay.chunk_rows(rank, c) for c in range(chunks)]
+        n_loc = part.hi - part.lo
         x = part.x_rows
         for l, p in enumerate(part.model):
             K, d, W = p.heads, p.dim, p.width
             o = O.ref_layer(np.zeros(n_loc + 1, np.uint64), np.zeros(0, np.uint32), x, p.w, p.al, p.ar, K, d, False)
-            z_pad = np.zeros((n_max, W), np.float32)
-            r_pad = np.zeros((n_max, K), np.float32)
-            z_pad[:n_loc] = o["z"]
-            r_pad[:n_loc] = o["right"]
-            zs = [torch.zeros((n_max, W)) for _ in range(world)]
-            rs = [torch.zeros((n_max, K)) for _ in range(world)]
-            tdist.all_gather(zs, torch.from_numpy(z_pad))
-            tdist.all_gather(rs, torch.from_numpy(r_pad))
-            z_full = torch.cat(zs).numpy()
-            r_full = torch.cat(rs).numpy()
-            mx = O.max_prescan(row_loc, col_loc, o["left"], r_full, K)
-            out, den = O.standard_aggregate(row_loc, col_loc, z_full, o["left"], r_full, mx, K, d)
-            x = O.finish(out, den, K, d, l < 2)
+            z_tab = np.zeros((lay.n_table, W), np.float32)
+            r_tab = np.zeros((lay.n_table, K), np.float32)
+            for c, (a_, b_) in enumerate(bounds):
+                zb = np.zeros((cm, W), np.float32)
+                rb = np.zeros((cm, K), np.float32)
+                zb[: b_ - a_] = o["z"][a_:b_]
+                rb[: b_ - a_] = o["right"][a_:b_]
+                zs = [torch.zeros((cm, W)) for _ in range(world)]
+                rs = [torch.zeros((cm, K)) for _ in range(world)]
+                tdist.all_gather(zs, torch.from_numpy(zb))
+                tdist.all_gather(rs, torch.from_numpy(rb))
+                z_tab[c * world * cm:(c + 1) * world * cm] = torch.cat(zs).numpy()
+                r_tab[c * world * cm:(c + 1) * world * cm] = torch.cat(rs).numpy()
+            nxt = np.zeros((n_loc, W), np.float32)
+            for c, (a_, b_) in enumerate(bounds):
+                if b_ == a_:
+                    continue
+                rl, cl = slices[c]
+                left = o["left"][a_:b_]
+                mx = O.max_prescan(rl, cl, left, r_tab, K)
+                out, den = O.standard_aggregate(rl, cl, z_tab, left, r_tab, mx, K, d)
+                nxt[a_:b_] = O.finish(out, den, K, d, l < 2)
+            x = nxt
+        n_max = int(np.diff(part.cuts).max())
         pad = np.zeros((n_max, x.shape[1]), np.float32)
         pad[:n_loc] = x
         outs = [torch.zeros_like(torch.from_numpy(pad)) for _ in range(world)]
@@ -84,20 +100,29 @@ def test_partition_balances_edges():
         assert edges.max() <= g.e / world + 13162  # at most one row over the even share
 
 
-def test_slice_remaps_sources_into_padded_table():
+def test_layout_slots_round_trip():
+    """Every source's table row maps back to it; chunk slices cover every edge once."""
     g = configs.make_graph("c2", features=False)
-    world = 4
-    cuts = gdist.partition(g.row, world)
-    n_max = int(np.diff(cuts).max())
-    for rank in range(world):
-        row_loc, col_loc, nm = gdist.slice_graph(g.row, g.col, cuts, rank)
-        assert nm == n_max
-        lo, hi = cuts[rank], cuts[rank + 1]
-        src = g.col[int(g.row[lo]):int(g.row[hi])].astype(np.int64)
-        owner = col_loc.astype(np.int64) // n_max
-        back = cuts[owner] + col_loc.astype(np.int64) % n_max
-        assert np.array_equal(back, src)
-        assert np.all(col_loc.astype(np.int64) % n_max < np.diff(cuts)[owner])
+    for world in (2, 4, 8):
+        for chunks in (1, 4):
+            lay = gdist.Layout(g.row, world, chunks)
+            src = np.arange(g.n)
+            slots = lay.slots(src).astype(np.int64)
+            assert len(np.unique(slots)) == g.n and slots.max() < lay.n_table
+            blk, i = slots // lay.chunk_max, slots % lay.chunk_max
+            c, r = blk // world, blk % world
+            assert np.array_equal(lay.ccuts[r, c] + i, src)
+            assert np.all(lay.ccuts[r, c] + i < lay.ccuts[r, c + 1])
+            for rank in range(world):
+                lo, hi = int(lay.cuts[rank]), int(lay.cuts[rank + 1])
+                col_rows = g.col[int(g.row[lo]):int(g.row[hi])]
+                got = []
+                for ch in range(chunks):
+                    rl, cl = lay.slice_chunk(g.row, col_rows, rank, ch)
+                    a, b = lay.chunk_rows(rank, ch)
+                    assert len(rl) == b - a + 1 and int(rl[-1]) == len(cl)
+                    got.append(cl)
+                assert np.array_equal(np.concatenate(got), lay.slots(col_rows))
 
 
 def test_make_part_matches_whole_graph():

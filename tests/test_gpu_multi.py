@@ -37,7 +37,7 @@ def _rank_main(rank, world, port, name, q):
         for _ in range(2):
             pm.forward(x, logits, False, False)
         torch.cuda.synchronize()
-        n_max = pm.n_max
+        n_max = int(np.diff(part.cuts).max())
         pad = torch.zeros((n_max, pm.classes), dtype=torch.float32, device="cuda")
         pad[: pm.n_loc] = logits
         full = torch.empty((world * n_max, pm.classes), dtype=torch.float32, device="cuda")
