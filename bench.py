@@ -63,6 +63,11 @@ def parse():
     ap.add_argument("--mode", choices=["forward", "micro"], default="forward")
     ap.add_argument("--path", choices=["standard", "adaptive"], default="standard",
                     help="standard: B0 on every layer; adaptive: layer 1 through TFS aggregation (tensor cores)")
+    ap.add_argument("--chunks", type=int, default=1,
+                    help="N>1: row chunks per rank, each projected and exchanged as soon as it is aggregated")
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="N>1: p2p = the projection kernel stores H/R into every rank's table over NVLink; "
+                         "nccl = NCCL all-gather per chunk")
     return ap.parse_args()
 
 
@@ -483,7 +488,8 @@ def main():
         part = configs.make_part(args.config, rank, world)
         log(f"rows [{part.lo}, {part.hi}) of {len(part.row) - 1}")
         n, e, din = len(part.row) - 1, part.e, part.din
-        pm = gdist.PartitionedModel(part.row, part.col_rows, part.model, rank, world, stream, dist, part.cuts)
+        pm = gdist.PartitionedModel(part.row, part.col_rows, part.model, rank, world, stream, dist, part.cuts,
+                                    chunks=args.chunks, exchange=args.exchange)
         log("device model ready")
         n_loc, e_loc = pm.n_loc, pm.e_loc
         classes = pm.classes
@@ -504,10 +510,14 @@ def main():
         G.check_device()
         stage_ms = pm.stage_times()  # last timed step
         pm.enable_timing(False)
-        # convert, then per layer and chunk a projection and an aggregation (+ hub merge)
-        launches = 1 + sum(3 * (2 + (1 if g.info()["n_hub"] else 0)) for _, _, g in pm.chunks if g is not None)
-        parallelism = (f"rows{world}: destination rows split by edge count, {len(pm.chunks)} row chunks per rank; "
-                       "each chunk's NCCL all-gather of H and R overlaps the next chunk's aggregation")
+        launches = pm.launches()
+        if args.exchange == "p2p":
+            how = ("the projection kernel stores each H/R tile into every rank's table over NVLink (CUDA IPC "
+                   "peer memory), then a cross-GPU flag barrier per layer")
+        else:
+            how = "each chunk's NCCL all-gather of H and R overlaps the next chunk's aggregation"
+        parallelism = (f"rows{world}: destination rows split by edge count, {len(pm.chunks)} row chunk(s) per "
+                       f"rank; {how}")
 
     # roofline of the aggregation kernel (three launches per step, this rank's rows). Under
     # the multi-GPU pipeline a layer's time also holds the next layer's projections and any

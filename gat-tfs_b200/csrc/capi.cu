@@ -21,8 +21,10 @@ int finish_launch(uint64_t n, int heads, int dim, const float* den, int hidden, 
 int projection_simt_launch(const gat_b200_layer* p, uint64_t n, const void* x, int x_bf16, int ldx, void* h,
                            int h_bf16, int ldh, float* left, float* right, cudaStream_t st);
 int projection_tc_launch(const gat_b200_layer* p, uint64_t n, const uint16_t* x, int ldx, uint16_t* h, int ldh,
-                         float* z, int ldz, float* left, float* right, cudaStream_t st);
+                         float* z, int ldz, float* left, float* right, cudaStream_t st, int npeer = 0,
+                         uint16_t* const* h_peer = nullptr, float* const* r_peer = nullptr);
 int projection_tc_check_error();
+int peer_check_error();
 int aggregate_check_error();
 int tfs_tc_check_error();
 int lr_reordered_launch(const gat_b200_layer* p, uint64_t n, const void* x, int x_dtype, int ldx, int policy,
@@ -35,7 +37,8 @@ int device_check_errors() {
     int rc = projection_tc_check_error();
     int rc2 = aggregate_check_error();
     int rc3 = tfs_tc_check_error();
-    return rc ? rc : (rc2 ? rc2 : rc3);
+    int rc4 = peer_check_error();
+    return rc ? rc : (rc2 ? rc2 : (rc3 ? rc3 : rc4));
 }
 
 namespace {
@@ -279,6 +282,22 @@ int gat_b200_projection(const gat_b200_layer* p, uint64_t n, const void* x, int 
                         int h_dtype, int ldh, float* left, float* right, void* stream) {
     clear_error();
     return projection_dispatch(p, n, x, ldx, precision, h, h_dtype, ldh, left, right, as_stream(stream));
+}
+
+int gat_b200_projection_scatter(const gat_b200_layer* p, uint64_t n, const void* x, int ldx, void* h, int ldh,
+                                float* left, float* right, int npeer, void* const* h_peer, float* const* r_peer,
+                                void* stream) {
+    clear_error();
+    if (!p || !x || !h || !right) return fail("projection_scatter: null argument");
+    if (ldx < p->in) return fail("projection_scatter: X row stride smaller than the input width");
+    if (npeer < 0 || npeer > 7) return fail("projection_scatter: npeer must be 0..7");
+    if (npeer && (!h_peer || !r_peer)) return fail("projection_scatter: null peer table");
+    int rc = projection_tc_launch(p, n, static_cast<const uint16_t*>(x), ldx, static_cast<uint16_t*>(h), ldh,
+                                  nullptr, 0, left, right, as_stream(stream), npeer,
+                                  reinterpret_cast<uint16_t* const*>(h_peer), r_peer);
+    if (rc == GAT_B200_EUNSUPPORTED)
+        return fail_code(rc, "projection_scatter: layer outside the tensor-core kernel (input or width > 256)");
+    return rc;
 }
 
 int gat_b200_max_prescan(const gat_b200_graph* g, int heads, const float* left, const float* right, float* max,

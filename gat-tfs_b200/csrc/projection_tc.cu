@@ -38,6 +38,7 @@ constexpr int kABytes = kTileM * kKBlock * 2;     // 16 KB per A stage
 constexpr int kStageRows = 32;                    // epilogue store box rows (one warp)
 constexpr int kStageBytes = kStageRows * 128;     // 4 KB
 constexpr int kThreads = 192;
+constexpr int kMaxPeers = 7;
 
 struct ProjArgs {
     uint64_t n;
@@ -52,6 +53,13 @@ struct ProjArgs {
     int store_h;    // 1: BF16 H through TMA stores (0: only z / left / right)
     const float* al;
     const float* ar;
+    // Extra destinations (other GPUs' tables, mapped peer memory): every H row
+    // and R row is also stored to hp[i] / rp[i], i < npeer, with the same row
+    // index and row stride ldh (R: heads floats per row).
+    int npeer;
+    int ldh;
+    uint16_t* hp[kMaxPeers];
+    float* rp[kMaxPeers];
 };
 
 // ---- PTX wrappers ----------------------------------------------------------
@@ -358,6 +366,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tma_store_2d(&tm_h, sb, g, int(t * kTileM) + q * 32);
                     bulk_commit();
                 }
+                if (a.npeer) {
+                    // the same 32 x 64 box to every peer table: 16-byte stores,
+                    // lanes 8 at a time along a 128-byte row segment
+                    const uint64_t r0 = t * kTileM + uint64_t(q) * 32;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int rr = i * 4 + (lane >> 3), ch = lane & 7;
+                        const int col = g + ch * 8;
+                        if (r0 + rr < a.n && col < a.ldh) {
+                            const uint4 v = *reinterpret_cast<const uint4*>(sb + rr * 128 + ((ch ^ (rr & 7)) * 16));
+                            const uint64_t off = (r0 + rr) * uint64_t(a.ldh) + col;
+#pragma unroll
+                            for (int pi = 0; pi < kMaxPeers; ++pi)
+                                if (pi < a.npeer) *reinterpret_cast<uint4*>(a.hp[pi] + off) = v;
+                        }
+                    }
+                }
                 toggle ^= 1u;
             }
             tc_fence_before();
@@ -367,14 +392,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (a.lr_vec) {
                     float4* lp = reinterpret_cast<float4*>(a.left + row * 8);
                     float4* rp = reinterpret_cast<float4*>(a.right + row * 8);
+                    const float4 r0 = make_float4(R[0], R[1], R[2], R[3]), r1 = make_float4(R[4], R[5], R[6], R[7]);
                     if (a.left) { lp[0] = make_float4(L[0], L[1], L[2], L[3]); lp[1] = make_float4(L[4], L[5], L[6], L[7]); }
-                    if (a.right) { rp[0] = make_float4(R[0], R[1], R[2], R[3]); rp[1] = make_float4(R[4], R[5], R[6], R[7]); }
+                    if (a.right) { rp[0] = r0; rp[1] = r1; }
+#pragma unroll
+                    for (int pi = 0; pi < kMaxPeers; ++pi)
+                        if (pi < a.npeer) {
+                            float4* pp = reinterpret_cast<float4*>(a.rp[pi] + row * 8);
+                            pp[0] = r0;
+                            pp[1] = r1;
+                        }
                 } else {
 #pragma unroll
                     for (int h = 0; h < 8; ++h)
                         if (h < a.heads) {
                             if (a.left) a.left[row * a.heads + h] = L[h];
                             if (a.right) a.right[row * a.heads + h] = R[h];
+#pragma unroll
+                            for (int pi = 0; pi < kMaxPeers; ++pi)
+                                if (pi < a.npeer) a.rp[pi][row * a.heads + h] = R[h];
                         }
                 }
             }
@@ -428,7 +464,8 @@ int make_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uin
 // Returns GAT_B200_EUNSUPPORTED when the shape is outside the kernel (the
 // caller then uses the CUDA-core projection).
 int projection_tc_launch(const gat_b200_layer* p, uint64_t n, const uint16_t* x, int ldx, uint16_t* h, int ldh,
-                         float* z, int ldz, float* left, float* right, cudaStream_t st) {
+                         float* z, int ldz, float* left, float* right, cudaStream_t st, int npeer,
+                         uint16_t* const* h_peer, float* const* r_peer) {
     if (p->np > 256 || p->kp > 256) return GAT_B200_EUNSUPPORTED;
     if (n == 0) return 0;
     if (n > uint64_t(INT32_MAX)) return fail("projection: too many rows");
@@ -452,6 +489,17 @@ int projection_tc_launch(const gat_b200_layer* p, uint64_t n, const uint16_t* x,
     a.store_h = h != nullptr;
     a.lr_vec = p->heads == 8 && (reinterpret_cast<uintptr_t>(left) & 15) == 0 &&
                (reinterpret_cast<uintptr_t>(right) & 15) == 0;
+    if (npeer < 0 || npeer > kMaxPeers) return fail("projection: at most 7 peer destinations");
+    if (npeer && (!h || !right)) return fail("projection: peer destinations need H and R");
+    a.npeer = npeer;
+    a.ldh = ldh;
+    for (int i = 0; i < npeer; ++i) {
+        if (!h_peer[i] || !r_peer[i]) return fail("projection: null peer destination");
+        if (reinterpret_cast<uintptr_t>(h_peer[i]) & 15) return fail("projection: peer H rows must be 16-byte aligned");
+        if (reinterpret_cast<uintptr_t>(r_peer[i]) & 15) a.lr_vec = 0;  // R rows then go out as scalars
+        a.hp[i] = h_peer[i];
+        a.rp[i] = r_peer[i];
+    }
     uint32_t cols = 32;
     while (cols < uint32_t(2 * p->np)) cols <<= 1;
     a.tmem_cols = cols;

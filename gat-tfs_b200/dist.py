@@ -9,14 +9,25 @@ of all their sources, so each layer is
   2. one all-gather of H (and of R) into every rank's feature table;
   3. edge-softmax aggregation of the rank's own rows from that table.
 
-The all-gather is the only exchange. To overlap it with compute, each rank's
-rows are further cut into `chunks` row chunks (balanced by edges, each with its
-own CSR slice and degree schedule). Aggregating chunk c of layer l yields the
-chunk's rows of layer l+1's input; they are projected at once and chunk c's
-all-gather runs on NCCL's stream while chunk c+1 is aggregated. Only layer
-l+1's aggregation waits for all chunks. Layers alternate between two feature
-tables, so a layer's exchange never overwrites rows the previous layer's
-aggregation still reads.
+The all-gather is the only exchange. Two ways to do it:
+
+  exchange="p2p" (default): the feature tables are device allocations every
+    rank maps (CUDA IPC over NVLink). The projection kernel stores each H and R
+    tile into the local table and into every peer's table itself
+    (gat_b200_projection_scatter), so the exchange runs inside the projection,
+    tile by tile; a cross-GPU flag barrier (gat_b200_peer_barrier) then orders
+    those stores before any rank's aggregation.
+  exchange="nccl": the projection writes a send block and NCCL's all-gather
+    moves it; each chunk's all-gather runs on NCCL's stream while the next
+    chunk is aggregated.
+
+Rows of a rank may be cut into `chunks` row chunks (balanced by edges, each
+with its own CSR slice and degree schedule): aggregating chunk c of layer l
+yields the chunk's rows of layer l+1's input, which are projected (and
+exchanged) at once. Each layer has its own table, so a layer's exchange never
+overwrites rows that another layer's aggregation, on any rank, may still read:
+a rank writes layer l's table of step s+1 only after the barrier of layer
+l+1 of step s, which every rank reaches after its layer-l aggregation.
 
 The feature table is chunk-major: ncclAllGather moves equal blocks, so chunk c
 of every rank is padded to the largest chunk (chunk_max rows) and the table
@@ -61,7 +72,8 @@ class Layout:
             inner = lo + np.searchsorted(sub, targets, side="left").astype(np.int64)
             cc[r] = np.maximum.accumulate(np.concatenate([[lo], np.clip(inner, lo, hi), [hi]]))
         self.ccuts = cc  # global row boundaries [world, chunks+1]
-        self.chunk_max = max(1, int(np.diff(cc, axis=1).max()))
+        # padded to 4 rows so every block of an FP32 table starts 16-byte aligned
+        self.chunk_max = (max(1, int(np.diff(cc, axis=1).max())) + 3) // 4 * 4
         self.n_table = chunks * world * self.chunk_max
         self._starts = cc[:, :-1].reshape(-1)  # ascending: ranks' ranges are contiguous
 
@@ -91,16 +103,22 @@ class Layout:
 
 class PartitionedModel:
     """Three-layer BF16 forward of this rank's rows (bench/main.cpp:171-172 per
-    rank), each layer's all-gather overlapped with the previous layer's
-    aggregation chunk by chunk."""
+    rank) with the exchange of each layer's H and R done by peer stores from
+    the projection kernel ("p2p") or by NCCL all-gathers ("nccl")."""
 
     def __init__(self, row: np.ndarray, col_rows: np.ndarray, params: Sequence[G.Param], rank: int, world: int,
-                 stream=None, dist_module=None, cuts: Optional[np.ndarray] = None, chunks: int = 4):
+                 stream=None, dist_module=None, cuts: Optional[np.ndarray] = None, chunks: int = 1,
+                 exchange: str = "p2p"):
         """row: all n+1 row pointers; col_rows: the sources of this rank's rows
         (col[row[cuts[rank]]:row[cuts[rank+1]]]); cuts: partition(row, world)."""
         import torch
+        if exchange not in ("p2p", "nccl"):
+            raise ValueError("exchange must be 'p2p' or 'nccl'")
+        if exchange == "p2p" and world > 8:
+            raise ValueError("p2p exchange supports up to 8 ranks (one NVLink node)")
         self.torch = torch
         self.dist = dist_module
+        self.exchange = exchange
         self.rank, self.world = rank, world
         self.lay = Layout(row, world, chunks, cuts)
         self.cuts = self.lay.cuts
@@ -121,26 +139,68 @@ class PartitionedModel:
         self.layers = [G.DeviceLayer(p) for p in params]
         self.din = params[0].in_
         self.classes = params[2].width
+        self.ldh = [G.padded_ld(p.width, G.BF16) for p in params]
+        self.heads = [p.heads for p in params]
         dev = torch.device("cuda", torch.cuda.current_device())
-        wmax = max(p.width for p in params)
-        ldh_max = G.padded_ld(wmax, G.BF16)
         self.ld0 = G.padded_ld(self.din, G.BF16)
         self.ld_hidden = G.padded_ld(max(params[0].width, params[1].width), G.BF16)
-        n, cm, P = self.n_loc, self.lay.chunk_max, chunks
+        n, cm, P, nt = self.n_loc, self.lay.chunk_max, chunks, self.lay.n_table
         i16 = torch.int16
         self.x_f32 = torch.empty((n, self.din), dtype=torch.float32, device=dev)
         self.x0 = torch.zeros((n, self.ld0), dtype=i16, device=dev)
-        # one send block per chunk; two tables, alternating by layer
-        self.h_send = torch.zeros((P, cm * ldh_max), dtype=i16, device=dev)
-        self.r_send = torch.zeros((P, cm * 8), dtype=torch.float32, device=dev)
-        self.h_full = [torch.zeros((self.lay.n_table * ldh_max,), dtype=i16, device=dev) for _ in range(2)]
-        self.r_full = [torch.zeros((self.lay.n_table * 8,), dtype=torch.float32, device=dev) for _ in range(2)]
-        # L [n][heads] of a layer, alternating by layer like the tables
         self.left = [torch.zeros((n * 8,), dtype=torch.float32, device=dev) for _ in range(2)]
         self.xs = [torch.zeros((n, self.ld_hidden), dtype=i16, device=dev) for _ in range(2)]
         self.logits = torch.empty((n, self.classes), dtype=torch.float32, device=dev)
+        self._owned, self._mapped = [], []
+        if exchange == "p2p":
+            # h_tab[l][j] / r_tab[l][j]: device pointer of rank j's layer-l table in this process
+            own, handles = [], []
+            for l in range(3):
+                for nbytes in (nt * self.ldh[l] * 2, nt * self.heads[l] * 4):
+                    ptr, h = G.peer_alloc(nbytes)
+                    self._owned.append(ptr)
+                    own.append(ptr)
+                    handles.append(h)
+            fptr, fh = G.peer_alloc(64)
+            self._owned.append(fptr)
+            own.append(fptr)
+            handles.append(fh)
+            allh = self._all_gather_bytes(b"".join(handles), dev)
+            hb = G.PEER_HANDLE_BYTES
+            ptrs = []  # [rank][7]
+            for j in range(world):
+                if j == rank:
+                    ptrs.append(own)
+                    continue
+                row_ptrs = []
+                for k in range(len(own)):
+                    p_ = G.peer_open(allh[j][k * hb:(k + 1) * hb])
+                    self._mapped.append(p_)
+                    row_ptrs.append(p_)
+                ptrs.append(row_ptrs)
+            self.h_tab = [[ptrs[j][2 * l] for j in range(world)] for l in range(3)]
+            self.r_tab = [[ptrs[j][2 * l + 1] for j in range(world)] for l in range(3)]
+            self.flags = [ptrs[j][6] for j in range(world)]
+            self.epoch = 0
+        else:
+            ldh_max = max(self.ldh)
+            self.h_send = torch.zeros((P, cm * ldh_max), dtype=i16, device=dev)
+            self.r_send = torch.zeros((P, cm * 8), dtype=torch.float32, device=dev)
+            self.h_full = [torch.zeros((nt * self.ldh[l],), dtype=i16, device=dev) for l in range(3)]
+            self.r_full = [torch.zeros((nt * self.heads[l],), dtype=torch.float32, device=dev) for l in range(3)]
         self.events = None
         self.pending = []
+
+    def _all_gather_bytes(self, blob: bytes, dev):
+        """Every rank's `blob` (same length on all ranks), as a list of bytes."""
+        torch = self.torch
+        if self.world == 1:
+            return [blob]
+        t = torch.frombuffer(bytearray(blob), dtype=torch.uint8).to(dev)
+        out = torch.empty((self.world * len(blob),), dtype=torch.uint8, device=dev)
+        self.dist.all_gather_into_tensor(out, t)
+        a = out.cpu().numpy().reshape(self.world, len(blob))
+        return [a[j].tobytes() for j in range(self.world)]
 
     def enable_timing(self, on: bool):
         torch = self.torch
@@ -148,25 +208,34 @@ class PartitionedModel:
 
     def _mark(self, i):
         # 0 start, 1 after the input copy, 2 after layer 1's projections,
-        # 3+l once layer l's exchange is waited for, 6 end
+        # 3+l once layer l's exchange is complete, 6 end
         if self.events is not None:
             self.events[i].record(self.torch.cuda.current_stream())
 
     def _project(self, l: int, c: int, x, ldx):
-        """Projection of chunk c's rows for layer l, then its all-gather (asynchronous)."""
-        torch = self.torch
+        """Projection of chunk c's rows for layer l and their exchange."""
         p = self.layers[l]
         a, b, _ = self.chunks[c]
-        cm, W, K = self.lay.chunk_max, self.world, p.heads
-        ldh = G.padded_ld(p.width, G.BF16)
+        cm, W, K, ldh = self.lay.chunk_max, self.world, p.heads, self.ldh[l]
+        left = self.left[l & 1][a * K:b * K]
+        if self.exchange == "p2p":
+            if b <= a:
+                return
+            row0 = (c * W + self.rank) * cm  # first table row of this block
+            hs = [self.h_tab[l][j] + row0 * ldh * 2 for j in range(W)]
+            rs = [self.r_tab[l][j] + row0 * K * 4 for j in range(W)]
+            peers = [j for j in range(W) if j != self.rank]
+            G.projection_scatter(p, b - a, x[a:b], ldx, hs[self.rank], ldh, left, rs[self.rank],
+                                 [hs[j] for j in peers], [rs[j] for j in peers], self.stream)
+            return
+        torch = self.torch
         hs = self.h_send[c, : cm * ldh]
         rs = self.r_send[c, : cm * K]
         if b > a:
-            G.projection(p, b - a, x[a:b], ldx, G.BF16, hs, G.BF16, ldh, self.left[l & 1][a * K:b * K], rs,
-                         self.stream)
-        hf = self.h_full[l & 1][c * W * cm * ldh:(c + 1) * W * cm * ldh]
-        rf = self.r_full[l & 1][c * W * cm * K:(c + 1) * W * cm * K]
-        if self.world > 1:
+            G.projection(p, b - a, x[a:b], ldx, G.BF16, hs, G.BF16, ldh, left, rs, self.stream)
+        hf = self.h_full[l][c * W * cm * ldh:(c + 1) * W * cm * ldh]
+        rf = self.r_full[l][c * W * cm * K:(c + 1) * W * cm * K]
+        if W > 1:
             # the feature tables hold BF16 bit patterns in int16 storage; NCCL has no
             # 16-bit integer type, so the exchange goes through a bfloat16 view
             self.pending.append(self.dist.all_gather_into_tensor(hf.view(torch.bfloat16), hs.view(torch.bfloat16),
@@ -176,10 +245,21 @@ class PartitionedModel:
             hf.copy_(hs)
             rf.copy_(rs)
 
-    def _wait(self):
+    def _complete(self):
+        """Every rank's projections of the current layer are in this rank's table."""
+        if self.exchange == "p2p":
+            if self.world > 1:
+                self.epoch += 1
+                G.peer_barrier(self.flags, self.rank, self.epoch, self.stream)
+            return
         for w in self.pending:
             w.wait()  # the current stream waits for NCCL's
         self.pending = []
+
+    def _tables(self, l):
+        if self.exchange == "p2p":
+            return self.h_tab[l][self.rank], self.r_tab[l][self.rank]
+        return self.h_full[l], self.r_full[l]
 
     def forward(self, x, logits, x_on_host: bool, logits_on_host: bool):
         """x: this rank's FP32 input rows [n_loc, din]; logits: [n_loc, classes]."""
@@ -196,10 +276,11 @@ class PartitionedModel:
         self._mark(2)
         dst_logits = logits if not logits_on_host else self.logits
         for l, p in enumerate(self.layers):
-            self._wait()
+            self._complete()
             self._mark(3 + l)
-            K, ldh, last = p.heads, G.padded_ld(p.width, G.BF16), l == 2
-            hf, rf, left = self.h_full[l & 1], self.r_full[l & 1], self.left[l & 1]
+            K, ldh, last = p.heads, self.ldh[l], l == 2
+            hf, rf = self._tables(l)
+            left = self.left[l & 1]
             for c, (a, b, g) in enumerate(self.chunks):
                 if g is not None:
                     if last:
@@ -214,10 +295,18 @@ class PartitionedModel:
         if logits_on_host:
             logits.copy_(self.logits, non_blocking=True)
 
+    def launches(self) -> int:
+        """Kernels one forward launches: the input conversion, per layer and
+        chunk a projection and an aggregation (+ the hub merge of split rows),
+        and one barrier per layer under the p2p exchange."""
+        per_chunk = sum(2 + (1 if g.info()["n_hub"] else 0) for _, _, g in self.chunks if g is not None)
+        barriers = 3 if self.exchange == "p2p" and self.world > 1 else 0
+        return 1 + 3 * per_chunk + barriers
+
     def stage_times(self) -> dict:
         """ms of the last forward: layer 1's projection, then per layer the time
-        from the wait for its exchange to the next layer's (its aggregation, the
-        next layer's projections and whatever exchange was not overlapped)."""
+        from the completion of its exchange to the next one's (its aggregation,
+        the next layer's projections and whatever exchange was not overlapped)."""
         torch = self.torch
         torch.cuda.synchronize()
         ev = self.events
@@ -227,6 +316,19 @@ class PartitionedModel:
         return out
 
     def close(self):
+        """Frees the device state. Under the p2p exchange every rank must call
+        it: peers may still store into this rank's tables until all ranks have
+        finished their last forward."""
+        torch = self.torch
+        torch.cuda.synchronize()
+        if self._owned and self.world > 1 and self.dist is not None:
+            self.dist.barrier()
+            torch.cuda.synchronize()
+        for p_ in self._mapped:
+            G.peer_close(p_)
+        for p_ in self._owned:
+            G.peer_free(p_)
+        self._mapped, self._owned = [], []
         for l in self.layers:
             l.close()
         for _, _, g in self.chunks:

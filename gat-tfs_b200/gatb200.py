@@ -96,6 +96,13 @@ SIGNATURES = [
     ("gat_b200_model_launches", C.c_int, [_vp]),
     ("gat_b200_model_forward_async", C.c_int, [_vp, _vp, _vp, _vp]),
     ("gat_b200_model_join", C.c_int, [_vp, _vp]),
+    ("gat_b200_peer_alloc", C.c_int, [C.c_uint64, C.POINTER(_vp), _vp]),
+    ("gat_b200_peer_open", C.c_int, [_vp, C.POINTER(_vp)]),
+    ("gat_b200_peer_close", C.c_int, [_vp]),
+    ("gat_b200_peer_free", C.c_int, [_vp]),
+    ("gat_b200_projection_scatter", C.c_int, [_vp, C.c_uint64, _vp, C.c_int, _vp, C.c_int, _vp, _vp, C.c_int,
+                                              C.POINTER(_vp), C.POINTER(_vp), _vp]),
+    ("gat_b200_peer_barrier", C.c_int, [C.POINTER(_vp), C.c_int, C.c_int, C.c_uint32, _vp]),
 ]
 for _name, _res, _args in SIGNATURES:
     _fn = getattr(_lib, _name)
@@ -408,6 +415,52 @@ def projection(layer: DeviceLayer, n, x, ldx, precision, h=None, h_dtype=BF16, l
                stream=None):
     _check(_lib.gat_b200_projection(layer.handle, n, _ptr(x), ldx, precision, _ptr(h), h_dtype, ldh, _ptr(left),
                                     _ptr(right), _stream(stream)))
+
+
+PEER_HANDLE_BYTES = 64
+
+
+def peer_alloc(nbytes: int):
+    """(device pointer, IPC handle bytes) of a zero-filled allocation other
+    processes of the node can map with peer_open."""
+    ptr = C.c_void_p()
+    h = C.create_string_buffer(PEER_HANDLE_BYTES)
+    _check(_lib.gat_b200_peer_alloc(int(nbytes), C.byref(ptr), h))
+    return int(ptr.value), bytes(h.raw)
+
+
+def peer_open(handle: bytes) -> int:
+    if len(handle) != PEER_HANDLE_BYTES:
+        raise ValueError("peer handle must be 64 bytes")
+    ptr = C.c_void_p()
+    _check(_lib.gat_b200_peer_open(C.create_string_buffer(handle, PEER_HANDLE_BYTES), C.byref(ptr)))
+    return int(ptr.value)
+
+
+def peer_close(ptr: int):
+    _check(_lib.gat_b200_peer_close(ptr))
+
+
+def peer_free(ptr: int):
+    _check(_lib.gat_b200_peer_free(ptr))
+
+
+def projection_scatter(layer: DeviceLayer, n, x, ldx, h, ldh, left, right, h_peer, r_peer, stream=None):
+    """BF16 projection of n rows storing H and R locally and into every peer
+    table of h_peer / r_peer (device pointers, already offset to row 0)."""
+    k = len(h_peer)
+    if len(r_peer) != k:
+        raise ValueError("h_peer and r_peer must have the same length")
+    hp = (_vp * max(k, 1))(*[int(v) for v in h_peer])
+    rp = (_vp * max(k, 1))(*[int(v) for v in r_peer])
+    _check(_lib.gat_b200_projection_scatter(layer.handle, n, _ptr(x), ldx, _ptr(h), ldh, _ptr(left), _ptr(right),
+                                            k, hp, rp, _stream(stream)))
+
+
+def peer_barrier(flags, rank: int, epoch: int, stream=None):
+    """Cross-GPU barrier on `stream`; flags[j] = rank j's flag array."""
+    arr = (_vp * len(flags))(*[int(v) for v in flags])
+    _check(_lib.gat_b200_peer_barrier(arr, len(flags), rank, epoch & 0xFFFFFFFF, _stream(stream)))
 
 
 def max_prescan(g: DeviceGraph, heads, left, right, mx, stream=None):

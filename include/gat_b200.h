@@ -372,6 +372,47 @@ int gat_b200_model_launches(const gat_b200_model* m);
 int gat_b200_model_forward_async(gat_b200_model* m, const float* x, float* logits, void* stream);
 int gat_b200_model_join(gat_b200_model* m, void* stream);
 
+/* ======================================================================== *
+ *  Multi-GPU exchange (one process per GPU on one NVLink/NVSwitch node)    *
+ * ======================================================================== *
+ * No counterpart in the reference, whose forward runs in one CPU process
+ * (baseline/bench/main.cpp:171-172). With destination rows partitioned over
+ * ranks, every layer's projected features H and right scores R of a rank's
+ * rows must reach every rank's feature table before that layer's aggregation.
+ * These calls do it without a separate collective: the projection kernel
+ * stores its output tiles into the other ranks' tables over NVLink. */
+
+#define GAT_B200_PEER_HANDLE_BYTES 64
+
+/* Device allocation (zero-filled) that other processes of the node can map:
+ * *ptr receives the local pointer, handle (GAT_B200_PEER_HANDLE_BYTES bytes)
+ * the token to pass to gat_b200_peer_open in the other processes. */
+int gat_b200_peer_alloc(uint64_t bytes, void** ptr, void* handle);
+/* Maps another process's gat_b200_peer_alloc allocation into this one. */
+int gat_b200_peer_open(const void* handle, void** ptr);
+/* Unmaps what gat_b200_peer_open mapped / frees what gat_b200_peer_alloc
+ * allocated. NULL is a no-op. */
+int gat_b200_peer_close(void* ptr);
+int gat_b200_peer_free(void* ptr);
+
+/* gat_b200_projection (precision BF16, BF16 H on the tensor-core kernel) that
+ * also stores every H row into h_peer[i] and every R row into r_peer[i],
+ * i < npeer (<= 7): the other ranks' tables, mapped with gat_b200_peer_open,
+ * each pointer already offset to this call's first row. h/h_peer rows have
+ * stride ldh; right/r_peer rows hold `heads` floats. Pointers 16-byte aligned. */
+int gat_b200_projection_scatter(const gat_b200_layer* p, uint64_t n, const void* x, int ldx, void* h,
+                                int ldh, float* left, float* right, int npeer, void* const* h_peer,
+                                float* const* r_peer, void* stream);
+
+/* Cross-GPU barrier on `stream`: flags[j] is rank j's flag array (a
+ * gat_b200_peer_alloc allocation of at least world*4 bytes, mapped in this
+ * process; flags[rank] the own one). Every rank calls it with the same epoch,
+ * which must grow by at least one per call. Stores enqueued on `stream` before
+ * the barrier, to local or peer memory, are visible to work enqueued after it
+ * on every rank. A peer that does not arrive within about a second makes the
+ * next gat_b200_check_device return GAT_B200_ETIMEOUT. world <= 8. */
+int gat_b200_peer_barrier(void* const* flags, int world, int rank, uint32_t epoch, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

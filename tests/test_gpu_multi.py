@@ -1,4 +1,6 @@
-"""Row-partitioned forward on 2 GPUs (NCCL all-gather) against the 1-GPU model.
+"""Row-partitioned forward on 2 GPUs against the 1-GPU model, with the
+exchange done by the projection kernel's peer stores (p2p, one and three row
+chunks) and by NCCL all-gathers (four chunks).
 
 Skipped when fewer than two GPUs are visible. Ranks run as child processes
 with NCCL's NVLink SHARP (NVLS) disabled and a short process-group timeout.
@@ -18,7 +20,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, name, q):
+def _rank_main(rank, world, port, name, q, exchange, chunks):
     import datetime
     import torch
     import torch.distributed as tdist
@@ -31,12 +33,14 @@ def _rank_main(rank, world, port, name, q):
     try:
         part = configs.make_part(name, rank, world)
         pm = gdist.PartitionedModel(part.row, part.col_rows, part.model, rank, world,
-                                    torch.cuda.current_stream(), tdist, part.cuts)
+                                    torch.cuda.current_stream(), tdist, part.cuts, chunks=chunks, exchange=exchange)
         x = torch.from_numpy(part.x_rows).cuda()
         logits = torch.empty((pm.n_loc, pm.classes), dtype=torch.float32, device="cuda")
-        for _ in range(2):
+        for _ in range(3):
             pm.forward(x, logits, False, False)
         torch.cuda.synchronize()
+        import gatb200 as G
+        G.check_device()
         n_max = int(np.diff(part.cuts).max())
         pad = torch.zeros((n_max, pm.classes), dtype=torch.float32, device="cuda")
         pad[: pm.n_loc] = logits
@@ -52,7 +56,8 @@ def _rank_main(rank, world, port, name, q):
         tdist.destroy_process_group()
 
 
-def test_two_gpu_partitioned_forward_matches_single_gpu():
+@pytest.mark.parametrize("exchange,chunks", [("p2p", 1), ("p2p", 3), ("nccl", 4)])
+def test_two_gpu_partitioned_forward_matches_single_gpu(exchange, chunks):
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
@@ -71,7 +76,7 @@ def test_two_gpu_partitioned_forward_matches_single_gpu():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, "c2", q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, "c2", q, exchange, chunks)) for r in range(2)]
     for p in procs:
         p.start()
     import queue
