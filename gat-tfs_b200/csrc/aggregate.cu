@@ -35,7 +35,6 @@ constexpr unsigned kFull = 0xffffffffu;
 struct AggArgs {
     const uint64_t* row;
     const uint32_t* col;
-    uint32_t col_mask;       // source id bits of col; the bits above flag a hot source
     const uint32_t* perm;
     uint64_t n;
     uint32_t n_hub, n_seg;
@@ -135,21 +134,10 @@ __device__ unsigned g_agg_error = 0;
 __device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g, uint32_t src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(saddr), "l"(g), "r"(src_bytes) : "memory");
 }
-// The same with an L2 cache policy (the rows of hot sources).
-__device__ __forceinline__ void cp_async16_keep(uint32_t saddr, const void* g, uint32_t src_bytes, uint64_t pol) {
-    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2, %3;" ::"r"(saddr), "l"(g),
-                 "r"(src_bytes), "l"(pol)
-                 : "memory");
-}
-__device__ __forceinline__ float ldg_keep_f32(const float* p, uint64_t pol) {
-    float v;
-    asm volatile("ld.global.nc.L2::cache_hint.f32 %0, [%1], %2;" : "=f"(v) : "l"(p), "l"(pol));
-    return v;
-}
-__device__ __forceinline__ uint64_t keep_policy() {
-    uint64_t pol;
-    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
-    return pol;
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // Packed FP32 pair: sm_100 f32x2 arithmetic, each half rounded like fmaf.
@@ -317,10 +305,6 @@ __global__ void __launch_bounds__(128) agg_kernel(const AggArgs a) {
     const uint64_t row_bytes = uint64_t(a.ldh) * sizeof(HT);
     const char* hbase = reinterpret_cast<const char*>(a.h) + vl * 16;
     const bool fixed = a.fixed_p != nullptr;
-    // Rows of hot sources (flagged in the column indices) are gathered with an
-    // evict_last L2 policy so they stay resident; all others as plain loads.
-    const uint32_t cmask = a.col_mask;
-    const uint64_t pol_keep = keep_policy();
 
     int hv[VPL];
     int hk[VPL][MIXED ? VEC : 1];
@@ -349,12 +333,10 @@ __global__ void __launch_bounds__(128) agg_kernel(const AggArgs a) {
         for (int g = 0; g < NG; ++g) {
             const int e = g * EG + eo;
             const bool ok = (rc.flags & kValid) && e < rc.cnt && hok;
-            if (fixed) {
+            if (fixed)
                 o[g] = ok ? a.fixed_p[(uint64_t(rc.pos) + e) * K + hh] : 0.f;
-            } else {
-                const float* rp = a.right + uint64_t(c[g] & cmask) * K + hh;
-                o[g] = !ok ? 0.f : ((c[g] & ~cmask) ? ldg_keep_f32(rp, pol_keep) : __ldg(rp));
-            }
+            else
+                o[g] = ok ? __ldg(a.right + uint64_t(c[g]) * K + hh) : 0.f;
         }
     };
     auto load_l = [&](const Rec& rc) -> float {
@@ -561,20 +543,14 @@ __global__ void __launch_bounds__(128) agg_kernel(const AggArgs a) {
                 const int i = i0 + u;
                 const int tt = es + i * EPS;
                 const int g = (i * EPS) / EG;  // static: EPS == 1 or NG == 1
-                const uint32_t cf = __shfl_sync(kFull, colS[g], (tt % EG) * HS);
+                const uint32_t c = __shfl_sync(kFull, colS[g], (tt % EG) * HS);
                 const uint32_t nb = tt < S.cnt ? 16u : 0u;
-                const char* src = hbase + uint64_t(cf & cmask) * row_bytes;
-                const bool keep = (cf & ~cmask) != 0;
+                const char* src = hbase + uint64_t(c) * row_bytes;
 #pragma unroll
                 for (int j = 0; j < VPL; ++j) {
                     const int v = vl + j * LPE;
-                    if (NVC != 0 || v < nvec) {
-                        const uint32_t d = bs + uint32_t(tt * RV + j * LPE) * 16;
-                        if (keep)
-                            cp_async16_keep(d, src + j * LPE * 16, nb, pol_keep);
-                        else
-                            cp_async16(d, src + j * LPE * 16, nb);
-                    }
+                    if (NVC != 0 || v < nvec)
+                        cp_async16(bs + uint32_t(tt * RV + j * LPE) * 16, src + j * LPE * 16, nb);
                 }
             }
         }
@@ -698,8 +674,7 @@ int aggregate_dispatch(const gat_b200_graph* g, int heads, int dim, const void* 
     if (g->e >= (1ull << 32) - 64) return fail_code(GAT_B200_EUNSUPPORTED, "aggregate: more than 2^32 edges");
     AggArgs a{};
     a.row = g->row;
-    a.col = g->col_hint ? g->col_hint : g->col;
-    a.col_mask = g->col_hint ? 0x7fffffffu : 0xffffffffu;
+    a.col = g->col;
     a.perm = g->perm;
     a.n = g->n;
     a.n_hub = g->n_hub;

@@ -193,14 +193,6 @@ int gat_b200_graph_info(const gat_b200_graph* g, uint64_t* n, uint64_t* e, uint3
     return 0;
 }
 
-int gat_b200_graph_set_hot_rows(gat_b200_graph* g, uint64_t rows, uint64_t* flagged, void* stream) {
-    clear_error();
-    if (!g) return fail("graph_set_hot_rows: null graph");
-    int rc = graph_set_hot(g, rows, as_stream(stream));
-    if (flagged) *flagged = g->hot_count;
-    return rc;
-}
-
 int gat_b200_layer_create(int in, int heads, int dim, const float* w, const float* al, const float* ar,
                           gat_b200_layer** out) {
     clear_error();

@@ -14,8 +14,6 @@
 // 17k-edge hub cannot become the tail of the kernel.
 #include <cub/device/device_radix_sort.cuh>
 
-#include <algorithm>
-#include <functional>
 #include <vector>
 
 #include "device.cuh"
@@ -110,69 +108,7 @@ __global__ void build_segments(const uint64_t* __restrict__ row, const uint32_t*
     }
 }
 
-__global__ void in_degree(const uint32_t* __restrict__ col, uint64_t e, uint32_t* __restrict__ cnt) {
-    uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
-    for (uint64_t k = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; k < e; k += stride) atomicAdd(cnt + col[k], 1u);
-}
-
-__global__ void flag_hot(const uint32_t* __restrict__ col, uint64_t e, const uint32_t* __restrict__ cnt,
-                         uint32_t threshold, uint32_t* __restrict__ out) {
-    uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
-    for (uint64_t k = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; k < e; k += stride) {
-        const uint32_t c = col[k];
-        out[k] = c | (cnt[c] >= threshold ? 0x80000000u : 0u);
-    }
-}
-
 }  // namespace
-
-// Flags the edges whose source is among the `hot_rows` sources of highest
-// in-degree (ties at the threshold are included while the set stays within
-// 5/4 of hot_rows). hot_rows = 0 removes the hints.
-int graph_set_hot(gat_b200_graph* g, uint64_t hot_rows, cudaStream_t st) {
-    const uint64_t ns = g->n_src ? g->n_src : g->n;
-    cudaFree(g->col_hint);
-    g->col_hint = nullptr;
-    g->hot_rows = 0;
-    g->hot_count = 0;
-    if (hot_rows == 0 || g->e == 0 || ns == 0) return 0;
-    if (ns >= (uint64_t(1) << 31)) return 0;  // no spare bit in the source ids
-    uint32_t* cnt = nullptr;
-    int rc = 0;
-    do {
-        if ((rc = dalloc((void**)&cnt, ns * sizeof(uint32_t), "cudaMalloc in-degree"))) break;
-        cudaMemsetAsync(cnt, 0, ns * sizeof(uint32_t), st);
-        in_degree<<<1184, 256, 0, st>>>(g->col, g->e, cnt);
-        std::vector<uint32_t> h(ns);
-        cudaMemcpyAsync(h.data(), cnt, ns * sizeof(uint32_t), cudaMemcpyDeviceToHost, st);
-        cudaError_t ce = cudaStreamSynchronize(st);
-        if (ce != cudaSuccess) { rc = cuda_fail(ce, "in-degree"); break; }
-        uint32_t threshold = 1;
-        if (hot_rows < ns) {
-            std::vector<uint32_t> v(h);
-            std::nth_element(v.begin(), v.begin() + (hot_rows - 1), v.end(), std::greater<uint32_t>());
-            threshold = v[hot_rows - 1];
-            uint64_t at_least = 0;
-            for (uint32_t x : h) at_least += x >= threshold;
-            if (at_least > hot_rows + hot_rows / 4) ++threshold;
-        }
-        if (threshold < 1) threshold = 1;
-        uint64_t count = 0;
-        for (uint32_t x : h) count += x >= threshold;
-        if ((rc = dalloc((void**)&g->col_hint, g->e * sizeof(uint32_t), "cudaMalloc hinted columns"))) break;
-        flag_hot<<<1184, 256, 0, st>>>(g->col, g->e, cnt, threshold, g->col_hint);
-        ce = cudaStreamSynchronize(st);
-        if (ce != cudaSuccess) { rc = cuda_fail(ce, "hot sources"); break; }
-        g->hot_rows = hot_rows;
-        g->hot_count = count;
-    } while (0);
-    cudaFree(cnt);
-    if (rc) {
-        cudaFree(g->col_hint);
-        g->col_hint = nullptr;
-    }
-    return rc;
-}
 
 int graph_build(gat_b200_graph* g, const uint64_t* row_h, const uint32_t* col_h, cudaStream_t st) {
     const uint64_t n = g->n, e = g->e;
@@ -266,7 +202,6 @@ int graph_build(gat_b200_graph* g, const uint64_t* row_h, const uint32_t* col_h,
             ce = cudaStreamSynchronize(st);
             if (ce != cudaSuccess) { rc = cuda_fail(ce, "segment table"); break; }
         }
-        if ((rc = graph_set_hot(g, kDefaultHotRows, st))) break;
     } while (0);
     cleanup();
     return rc;
@@ -279,8 +214,6 @@ void graph_release(gat_b200_graph* g) {
     cudaFree(g->segs);
     cudaFree(g->hub_seg_offset);
     cudaFree(g->seg_state);
-    cudaFree(g->col_hint);
-    g->col_hint = nullptr;
     g->seg_state = nullptr;
     g->row = nullptr;
     g->col = nullptr;

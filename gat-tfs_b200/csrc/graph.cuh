@@ -24,12 +24,6 @@ struct gat_b200_graph {
     uint64_t* row = nullptr;  // device [n+1]
     uint32_t* col = nullptr;  // device [e]
     uint32_t* perm = nullptr; // device [n], (degree, id) ascending
-    // col with bit 31 set on edges whose source is among the hot_rows sources of
-    // highest in-degree (built when n_src < 2^31); the aggregation keeps those
-    // feature rows in L2 (evict_last) and streams the others (evict_first).
-    uint32_t* col_hint = nullptr;  // device [e] or null
-    uint64_t hot_rows = 0;
-    uint64_t hot_count = 0;        // sources actually flagged
     uint64_t neighbor_steps = 0;
     uint32_t max_degree = 0;
     // Rows with degree > seg_edges are hubs; they are perm[n-1-k], k < n_hub,
@@ -56,9 +50,6 @@ struct gat_b200_layer {
 
 namespace gatb {
 int graph_build(gat_b200_graph* g, const uint64_t* row_h, const uint32_t* col_h, cudaStream_t st);
-int graph_set_hot(gat_b200_graph* g, uint64_t hot_rows, cudaStream_t st);
-// Default hot set: 64 MB of 512-byte rows (8 heads x 32 BF16), about half of L2.
-constexpr uint64_t kDefaultHotRows = 131072;
 void graph_release(gat_b200_graph* g);
 constexpr int kSegStateFloats = 8 * 64 + 2 * 8;
 }  // namespace gatb

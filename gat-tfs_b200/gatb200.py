@@ -72,7 +72,6 @@ SIGNATURES = [
     ("gat_b200_graph_schedule", C.c_int, [_vp, _u32p, _u64p]),
     ("gat_b200_graph_device_csr", C.c_int, [_vp, C.POINTER(_vp), C.POINTER(_vp)]),
     ("gat_b200_graph_info", C.c_int, [_vp, _u64p, _u64p, _u32p, _u32p, _u32p, _u32p]),
-    ("gat_b200_graph_set_hot_rows", C.c_int, [_vp, C.c_uint64, _u64p, _vp]),
     ("gat_b200_layer_create", C.c_int, [C.c_int, C.c_int, C.c_int, _f32p, _f32p, _f32p, C.POINTER(_vp)]),
     ("gat_b200_layer_destroy", C.c_int, [_vp]),
     ("gat_b200_convert", C.c_int, [C.c_uint64, C.c_int, _vp, C.c_int, _vp, C.c_int, _vp]),
@@ -366,12 +365,6 @@ class DeviceGraph:
                                         C.byref(ns), C.byref(se)))
         return dict(n=n.value, e=e.value, max_degree=md.value, n_hub=nh.value, n_seg=ns.value,
                     seg_edges=se.value)
-
-    def set_hot_rows(self, rows: int, stream=None) -> int:
-        """Sources kept in L2 by the aggregation (0 = no hint); returns how many were flagged."""
-        f = C.c_uint64()
-        _check(_lib.gat_b200_graph_set_hot_rows(self.handle, int(rows), C.byref(f), _stream(stream)))
-        return f.value
 
     def close(self):
         if getattr(self, "handle", None):

@@ -179,13 +179,6 @@ int gat_b200_graph_device_csr(const gat_b200_graph* g, const uint64_t** row, con
  * segments of at most seg_edges edges (n_hub), and those segments (n_seg). */
 int gat_b200_graph_info(const gat_b200_graph* g, uint64_t* n, uint64_t* e, uint32_t* max_degree,
                         uint32_t* n_hub, uint32_t* n_seg, uint32_t* seg_edges);
-/* No counterpart in the reference (an L2 cache policy of the aggregation).
- * The aggregation keeps the feature rows of the `rows` sources of highest
- * in-degree in L2 (evict_last) and streams the others (evict_first); the
- * graph's default is 131072 rows (64 MB of 512-byte rows), 0 turns the hint
- * off. *flagged (may be NULL) receives the number of sources marked (ties at
- * the threshold may add up to a quarter). Results do not depend on it. */
-int gat_b200_graph_set_hot_rows(gat_b200_graph* g, uint64_t rows, uint64_t* flagged, void* stream);
 
 /* ======================================================================== *
  *  Device: prepared layer parameters                                       *

@@ -379,25 +379,3 @@ def test_config2_model(dev):
     got32 = _forward(m32, cfg.graph.x)
     e = O.errors(ref, got32)
     assert e["max_abs"] <= 1e-5, e
-
-
-def test_hot_source_hint_keeps_results_bit_exact(dev):
-    """The L2 hint on the highest in-degree sources changes only cache policy:
-    logits with the default hot set, a tiny one, every source and none must be
-    identical bit for bit, and the flagged count must honour the budget."""
-    import configs
-    cfg = configs.make("c2")
-    g, _, m16 = _model(cfg.graph, cfg.model, G.PATH_STANDARD_BF16)
-    want = _forward(m16, cfg.graph.x)
-    indeg = np.bincount(cfg.graph.col, minlength=cfg.graph.n)
-    for rows in (0, 100, 5000, cfg.graph.n):
-        flagged = g.set_hot_rows(rows)
-        if rows == 0:
-            assert flagged == 0
-        elif rows >= cfg.graph.n:
-            assert flagged == int((indeg >= 1).sum())
-        else:
-            assert 1 <= flagged <= rows + rows // 4, (rows, flagged)
-            # the flagged set is a top set by in-degree: every source at or above some threshold
-            assert flagged in {int((indeg >= t).sum()) for t in np.unique(indeg[indeg > 0])}, flagged
-        assert np.array_equal(_forward(m16, cfg.graph.x), want), rows
