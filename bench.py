@@ -550,23 +550,29 @@ def main():
     e2e_sync_ms = timed(e2e_step, max(1, min(args.steps, 5)))
     # Throughput: a stream of requests through gat_b200_model_forward_async, where request
     # k's download and request k+1's upload overlap compute (one GPU only).
-    e2e_ms, e2e_mode = e2e_sync_ms, "synchronous: upload, forward, download per step"
+    k_pipe = max(2, min(args.steps, 10))
     if world == 1:
-        k_pipe = max(2, min(args.steps, 10))
-        for i in range(2):
-            model.forward_async(x_host, l_host[i & 1], stream)
-        model.join(stream)
-        torch.cuda.synchronize()
+        submit = lambda i: model.forward_async(x_host, l_host[i & 1], stream)
+        join = lambda: model.join(stream)
+        api = "gat_b200_model_forward_async"
+    else:
+        submit = lambda i: pm.forward_async(x_host, l_host[i & 1])
+        join = pm.join
+        api = "PartitionedModel.forward_async on every rank (its rows of X up, its logits down)"
+    for i in range(2):
+        submit(i)
+    join()
+    torch.cuda.synchronize()
 
-        def pipe_steps():
-            for i in range(k_pipe):
-                model.forward_async(x_host, l_host[i & 1], stream)
-            model.join(stream)
+    def pipe_steps():
+        for i in range(k_pipe):
+            submit(i)
+        join()
 
-        e2e_ms = timed(pipe_steps, 1) / k_pipe
-        G.check_device()
-        e2e_mode = (f"pipelined: {k_pipe} requests through gat_b200_model_forward_async, each uploading X and "
-                    "downloading logits (pinned host buffers); request k's download and k+1's upload overlap compute")
+    e2e_ms = timed(pipe_steps, 1) / k_pipe
+    G.check_device()
+    e2e_mode = (f"pipelined: {k_pipe} requests through {api}, each uploading X and downloading logits "
+                "(pinned host buffers); request k's download and k+1's upload overlap compute")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -190,6 +190,7 @@ class PartitionedModel:
             self.r_full = [torch.zeros((nt * self.heads[l],), dtype=torch.float32, device=dev) for l in range(3)]
         self.events = None
         self.pending = []
+        self._pipe = None
 
     def _all_gather_bytes(self, blob: bytes, dev):
         """Every rank's `blob` (same length on all ranks), as a list of bytes."""
@@ -294,6 +295,58 @@ class PartitionedModel:
         self._mark(6)
         if logits_on_host:
             logits.copy_(self.logits, non_blocking=True)
+
+    def forward_async(self, x_host, logits_host):
+        """Host-to-host forward for a stream of requests (the multi-GPU
+        counterpart of gat_b200_model_forward_async): uploads this rank's rows
+        of x_host (pinned FP32 [n_loc, din]) on an upload stream, runs the
+        forward on the current stream (which must be the model's stream) and
+        downloads the logits into logits_host (pinned) on a download stream,
+        returning at once. Two device slots let request k's download and
+        request k+1's upload overlap the compute. Host buffers must stay
+        untouched until join() has been waited on."""
+        torch = self.torch
+        if self._pipe is None:
+            dev = self.x0.device
+            self._pipe = {
+                "x": [torch.empty((self.n_loc, self.din), dtype=torch.float32, device=dev) for _ in range(2)],
+                "y": [torch.empty((self.n_loc, self.classes), dtype=torch.float32, device=dev) for _ in range(2)],
+                "up": torch.cuda.Stream(device=dev), "down": torch.cuda.Stream(device=dev),
+                "uploaded": [torch.cuda.Event() for _ in range(2)],
+                "computed": [torch.cuda.Event() for _ in range(2)],
+                "downloaded": [torch.cuda.Event() for _ in range(2)],
+                "used": [False, False], "k": 0,
+            }
+        P = self._pipe
+        s = P["k"] & 1
+        comp = torch.cuda.current_stream()
+        if P["used"][s]:
+            # slot s still serves request k-2: its X is free once that compute is
+            # done, its logits once their download is
+            P["up"].wait_event(P["computed"][s])
+            comp.wait_event(P["downloaded"][s])
+        with torch.cuda.stream(P["up"]):
+            P["x"][s].copy_(x_host, non_blocking=True)
+            P["uploaded"][s].record(P["up"])
+        comp.wait_event(P["uploaded"][s])
+        self.forward(P["x"][s], P["y"][s], False, False)
+        P["computed"][s].record(comp)
+        P["down"].wait_event(P["computed"][s])
+        with torch.cuda.stream(P["down"]):
+            logits_host.copy_(P["y"][s], non_blocking=True)
+            P["downloaded"][s].record(P["down"])
+        P["used"][s] = True
+        P["k"] += 1
+
+    def join(self):
+        """The current stream waits (on the device) for every submitted
+        forward_async request, downloads included."""
+        if self._pipe is None:
+            return
+        comp = self.torch.cuda.current_stream()
+        for s in range(2):
+            if self._pipe["used"][s]:
+                comp.wait_event(self._pipe["downloaded"][s])
 
     def launches(self) -> int:
         """Kernels one forward launches: the input conversion, per layer and

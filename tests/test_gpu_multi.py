@@ -41,6 +41,17 @@ def _rank_main(rank, world, port, name, q, exchange, chunks):
         torch.cuda.synchronize()
         import gatb200 as G
         G.check_device()
+        # pipelined host-to-host requests (three: one slot is reused) give the same logits
+        xh = torch.from_numpy(part.x_rows).pin_memory()
+        outs = [torch.empty((pm.n_loc, pm.classes), dtype=torch.float32).pin_memory() for _ in range(3)]
+        for o in outs:
+            pm.forward_async(xh, o)
+        pm.join()
+        torch.cuda.synchronize()
+        G.check_device()
+        ref = logits.cpu()
+        for o in outs:
+            assert torch.equal(o, ref), "forward_async differs from forward"
         n_max = int(np.diff(part.cuts).max())
         pad = torch.zeros((n_max, pm.classes), dtype=torch.float32, device="cuda")
         pad[: pm.n_loc] = logits
