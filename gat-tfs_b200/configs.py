@@ -14,6 +14,11 @@ counts, degree tails, feature widths, classes) with seeded generators
   c4  products-like: 2,449,029 nodes, 126,167,053 edges incl. self loops,
       power-law degrees (gamma 2.1, max 17,482), X ~ N(0,1) x100, classes 47.
   c4s c4 scaled down 4x (profiler captures only).
+  c5  RMAT stress: RMAT(a=.57, b=.19, c=.19, d=.05) over 2^24 nodes with
+      2^29 edge draws, self loops, duplicates merged (destination-row CSR),
+      X ~ N(0,1) x256, 256 -> 8x32 -> 8x32 -> 1x64. Generated on the GPU
+      (gat_b200_synth_rmat).
+  c5s c5 scaled down 16x (2^20 nodes, 2^25 draws) for tests and profiles.
 """
 from __future__ import annotations
 
@@ -30,7 +35,13 @@ SPECS = {
     # c4 scaled down 4x in nodes and edges (same mean degree and model) for
     # profiler captures: its features (0.3 GB per layer) still exceed L2.
     "c4s": dict(kind="powerlaw", n=612_257, e=31_541_763, max_degree=8_000, gamma=2.1, din=100, classes=47, seed=4),
+    "c5": dict(kind="rmat", log2n=24, draws=1 << 29, a=0.57, b=0.19, c=0.19, din=256, classes=64, seed=5),
+    "c5s": dict(kind="rmat", log2n=20, draws=1 << 25, a=0.57, b=0.19, c=0.19, din=256, classes=64, seed=5),
 }
+
+
+def _rmat(s, r_lo=0, r_hi=None, cols=True):
+    return G.synth_rmat(s["log2n"], s["draws"], s["a"], s["b"], s["c"], s["seed"], r_lo, r_hi, cols)
 
 
 @dataclass
@@ -44,10 +55,13 @@ def make_graph(name: str, features: bool = True) -> G.Graph:
     s = SPECS[name]
     if s["kind"] == "uniform":
         row, col = G.synth_uniform_graph(s["n"], s["sources"], s["seed"])
+    elif s["kind"] == "rmat":
+        row, col = _rmat(s)
     else:
         row, col = G.synth_powerlaw_graph(s["n"], s["e"], s["max_degree"], s["gamma"], s["seed"])
-    x = G.synth_normal((s["n"], s["din"]), s["seed"], 1) if features else np.zeros((0, s["din"]), np.float32)
-    return G.Graph(s["n"], len(col), s["din"], s["classes"], row, col, x)
+    n = len(row) - 1
+    x = G.synth_normal((n, s["din"]), s["seed"], 1) if features else np.zeros((0, s["din"]), np.float32)
+    return G.Graph(n, len(col), s["din"], s["classes"], row, col, x)
 
 
 def make(name: str, features: bool = True) -> Config:
@@ -75,12 +89,18 @@ def make_part(name: str, rank: int, world: int) -> Part:
     row pointers, then the sources and features of its own rows."""
     import dist
     s = SPECS[name]
-    if s["kind"] != "powerlaw":
-        raise ValueError("make_part needs a power-law configuration")
-    row = G.synth_powerlaw_rowptr(s["n"], s["e"], s["max_degree"], s["gamma"], s["seed"])
+    if s["kind"] == "powerlaw":
+        row = G.synth_powerlaw_rowptr(s["n"], s["e"], s["max_degree"], s["gamma"], s["seed"])
+    elif s["kind"] == "rmat":
+        row, _ = _rmat(s, cols=False)  # generated on this rank's GPU
+    else:
+        raise ValueError("make_part needs a power-law or RMAT configuration")
     cuts = dist.partition(row, world)
     lo, hi = int(cuts[rank]), int(cuts[rank + 1])
-    col = G.synth_powerlaw_cols(s["n"], s["e"], s["max_degree"], s["gamma"], s["seed"], row, lo, hi)
+    if s["kind"] == "rmat":
+        _, col = _rmat(s, lo, hi)
+    else:
+        col = G.synth_powerlaw_cols(s["n"], s["e"], s["max_degree"], s["gamma"], s["seed"], row, lo, hi)
     x = G.synth_normal_range(lo * s["din"], (hi - lo, s["din"]), s["seed"], 1)
     return Part(name, row, col, x, cuts, lo, hi, int(row[-1]), s["din"],
                 G.glorot_model(s["din"], s["classes"], s["seed"]))

@@ -66,6 +66,8 @@ SIGNATURES = [
     ("gat_b200_synth_normal_range", C.c_int, [C.c_uint64, C.c_uint64, C.c_double, C.c_uint64, C.c_uint64, _f32p]),
     ("gat_b200_synth_powerlaw_rows", C.c_int, [C.c_uint64, C.c_uint64, C.c_uint64, C.c_double, C.c_uint64, C.c_uint64, C.c_uint64, _u64p, _u32p]),
     ("gat_b200_synth_uniform", C.c_int, [C.c_uint64, C.c_double, C.c_double, C.c_uint64, C.c_uint64, _f32p]),
+    ("gat_b200_synth_rmat", C.c_int, [C.c_int, C.c_uint64, C.c_double, C.c_double, C.c_double, C.c_uint64,
+                                      C.c_uint64, C.c_uint64, _u64p, _u32p, _u64p]),
     ("gat_b200_graph_create", C.c_int, [C.c_uint64, C.c_uint64, _u64p, _u32p, _vp, C.POINTER(_vp)]),
     ("gat_b200_graph_create_part", C.c_int, [C.c_uint64, C.c_uint64, C.c_uint64, _u64p, _u32p, _vp, C.POINTER(_vp)]),
     ("gat_b200_graph_destroy", C.c_int, [_vp]),
@@ -311,6 +313,23 @@ def synth_powerlaw_cols(n: int, e: int, max_degree: int, gamma: float, seed: int
     _check(_lib.gat_b200_synth_powerlaw_rows(n, e, max_degree, gamma, seed, r_lo, r_hi, _p(row, _u64p),
                                              _p(col, _u32p)))
     return col
+
+
+def synth_rmat(log2_nodes: int, edges: int, a: float, b: float, c: float, seed: int, r_lo: int = 0,
+               r_hi: Optional[int] = None, cols: bool = True):
+    """RMAT graph generated on the current CUDA device: (row pointers of all
+    rows, sources of rows [r_lo, r_hi) or None)."""
+    n = 1 << log2_nodes
+    r_hi = n if r_hi is None else r_hi
+    row = np.empty(n + 1, np.uint64)
+    e = C.c_uint64()
+    _check(_lib.gat_b200_synth_rmat(log2_nodes, edges, a, b, c, seed, 0, 0, _p(row, _u64p), None, C.byref(e)))
+    if not cols:
+        return row, None
+    col = np.empty(int(row[r_hi] - row[r_lo]), np.uint32)
+    _check(_lib.gat_b200_synth_rmat(log2_nodes, edges, a, b, c, seed, r_lo, r_hi, _p(row, _u64p), _p(col, _u32p),
+                                    C.byref(e)))
+    return row, col
 
 
 def synth_normal_range(offset: int, shape, seed: int, stream: int, scale: float = 1.0) -> np.ndarray:

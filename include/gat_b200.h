@@ -133,6 +133,16 @@ int gat_b200_synth_powerlaw_rows(uint64_t n, uint64_t e, uint64_t max_degree, do
                                  uint32_t* col);
 int gat_b200_synth_uniform(uint64_t count, double lo, double hi, uint64_t seed, uint64_t stream,
                            float* out);
+/* RMAT stress graph (configuration c5), generated on the current CUDA device:
+ * 2^log2_nodes nodes, `edges` draws with quadrant probabilities (a, b, c,
+ * 1-a-b-c) per level (source bit first), one self loop per node, duplicate
+ * (destination, source) pairs kept once, destination-row CSR with sources
+ * ascending. Writes all 2^log2_nodes + 1 row pointers to row (host) and the
+ * sources of rows [r_lo, r_hi) to col (host, may be NULL), and the edge count
+ * to *e_total (may be NULL). Identical on every device (counter-based draws).
+ * edges + 2^log2_nodes < 2^31. */
+int gat_b200_synth_rmat(int log2_nodes, uint64_t edges, double a, double b, double c, uint64_t seed,
+                        uint64_t r_lo, uint64_t r_hi, uint64_t* row, uint32_t* col, uint64_t* e_total);
 
 /* GATFIX1 fixed-p fixture of one layer: the graph's CSR, the layer's W/aL/aR,
  * its input [n][in] and the attention weights p [e][heads] with their sums
