@@ -6,15 +6,19 @@
 //   left[i][h] = Z_ih . aL_h,  right[i][h] = Z_ih . aR_h   (from the FP32 Z)
 //   H = BF16 RNE(Z)        (the gathered feature rows of the aggregation)
 //
-// Persistent kernel, one CTA per SM, 6 warps with fixed roles:
+// Persistent kernel, one CTA per SM, 10 warps with fixed roles:
 //   warp 0  TMA producer: W^T once (resident in shared memory for the whole
 //           kernel), then 128-row x 64-column tiles of X through an S-stage ring.
 //   warp 1  TMEM owner and MMA issuer: 128 x NP x 16 tcgen05.mma (kind::f16,
 //           BF16 x BF16 -> FP32) into one of two TMEM accumulators, so the
 //           epilogue of tile t overlaps the MMAs of tile t+1.
-//   warps 2-5 epilogue: tcgen05.ld 16 columns at a time (thread = row),
-//           L/R dot products in FP32, BF16 pack into a 128B-swizzled staging
-//           buffer, TMA store of 32 x 64 boxes.
+//   warps 2-9 epilogue, two sets of four: set b drains accumulator b (the
+//           CTA's even / odd tiles), so two tiles' epilogues run at once and
+//           every SM sub-partition holds two epilogue warps. tcgen05.ld of 64
+//           columns at a time (thread = row), L/R dot products in FP32, BF16
+//           pack into a 128B-swizzled staging buffer, TMA store of 32 x 64
+//           boxes (two staging buffers per warp where shared memory allows,
+//           else one).
 // No cluster launch, no multicast: every CTA loads its own tiles.
 //
 // Every mbarrier wait is bounded: after ~1 s without progress the CTA records
@@ -37,7 +41,8 @@ constexpr int kKBlock = 64;                       // BF16 elements per 128-byte 
 constexpr int kABytes = kTileM * kKBlock * 2;     // 16 KB per A stage
 constexpr int kStageRows = 32;                    // epilogue store box rows (one warp)
 constexpr int kStageBytes = kStageRows * 128;     // 4 KB
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
+constexpr int kEpiWarps = 8;
 constexpr int kMaxPeers = 7;
 
 struct ProjArgs {
@@ -51,6 +56,7 @@ struct ProjArgs {
     int ldz;
     int lr_vec;     // left/right allow float4 stores (heads == 8, aligned)
     int store_h;    // 1: BF16 H through TMA stores (0: only z / left / right)
+    int sb;         // staging buffers per epilogue warp (1 or 2)
     const float* al;
     const float* ar;
     // Extra destinations (other GPUs' tables, mapped peer memory): every H row
@@ -182,8 +188,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int S = a.stages, NP = a.np, KB = a.kb;
     uint8_t* w_s = smem;                                         // KB x [NP x 128 B]
     uint8_t* a_s = w_s + size_t(KB) * NP * 128;                   // S x 16 KB
-    uint8_t* st_s = a_s + size_t(S) * kABytes;                    // 4 warps x 2 x 4 KB
-    float* al_s = reinterpret_cast<float*>(st_s + 8 * kStageBytes);  // [NP]
+    uint8_t* st_s = a_s + size_t(S) * kABytes;                    // 8 warps x sb x 4 KB
+    float* al_s = reinterpret_cast<float*>(st_s + size_t(kEpiWarps) * a.sb * kStageBytes);  // [NP]
     float* ar_s = al_s + NP;                                      // [NP]
     uint64_t* bars = reinterpret_cast<uint64_t*>(ar_s + NP);
     uint64_t* full = bars;              // [S]
@@ -288,14 +294,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_wait(mma_done, 0, abort_flag);
         }
     } else {
-        // ---- epilogue: warps 2..5, TMEM lane quarter = warp % 4 ----
+        // ---- epilogue: warps 2..9, TMEM lane quarter = warp % 4; set b = (warp-2)/4
+        // takes the CTA's tiles of parity b, i.e. accumulator b ----
         const int q = warp & 3;
         const int ew = warp - 2;  // staging slot
-        uint8_t* stage0 = st_s + size_t(ew) * 2 * kStageBytes;
+        const uint32_t buf = uint32_t(ew >> 2);
+        uint8_t* stage0 = st_s + size_t(ew) * a.sb * kStageBytes;
         uint32_t toggle = 0;
-        uint32_t t_local = 0;
-        for (uint64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++t_local) {
-            const uint32_t buf = t_local & 1u, use = t_local >> 1;
+        uint32_t use = 0;
+        for (uint64_t t = blockIdx.x + buf * gridDim.x; t < ntiles; t += 2ull * gridDim.x, ++use) {
             if (!mbar_wait(acc_full + buf, use & 1u, abort_flag)) break;
             tc_fence_after();
             const uint64_t row = t * kTileM + uint64_t(q) * 32 + lane;
@@ -305,7 +312,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int h = 0; h < 8; ++h) { L[h] = 0.f; R[h] = 0.f; }
             for (int g = 0; g < NP; g += 64) {
                 uint8_t* sb = stage0 + toggle * kStageBytes;
-                if (lane == 0 && a.store_h) bulk_wait_read<1>();
+                if (lane == 0 && a.store_h) {
+                    if (a.sb == 2)
+                        bulk_wait_read<1>();  // the store that last used this buffer has read it
+                    else
+                        bulk_wait_read<0>();
+                }
                 __syncwarp();
                 // 16 accumulator columns c..c+15 of this row (sub-block cc of the group)
                 auto col16 = [&](int cc, const float* v) {
@@ -383,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                 }
-                toggle ^= 1u;
+                if (a.sb == 2) toggle ^= 1u;
             }
             tc_fence_before();
             __syncwarp();
@@ -503,11 +515,20 @@ int projection_tc_launch(const gat_b200_layer* p, uint64_t n, const uint16_t* x,
     uint32_t cols = 32;
     while (cols < uint32_t(2 * p->np)) cols <<= 1;
     a.tmem_cols = cols;
-    const size_t fixed = size_t(a.kb) * p->np * 128 + 8 * kStageBytes + 2 * size_t(p->np) * 4 + 512 + 1024;
+    // Two staging buffers per epilogue warp unless that leaves fewer than 4
+    // stages for X (layers with a 256-row W^T), then one.
     const size_t limit = 227 * 1024;
-    int S = int((limit - fixed) / kABytes);
+    int S = 0;
+    for (a.sb = 2; a.sb >= 1; --a.sb) {
+        const size_t fixed_sb = size_t(a.kb) * p->np * 128 + size_t(kEpiWarps) * a.sb * kStageBytes +
+                                2 * size_t(p->np) * 4 + 512 + 1024;
+        S = fixed_sb < limit ? int((limit - fixed_sb) / kABytes) : 0;
+        if (S >= 4 || a.sb == 1) break;
+    }
     S = S > 8 ? 8 : S;
     if (S < 2) return GAT_B200_EUNSUPPORTED;
+    const size_t fixed = size_t(a.kb) * p->np * 128 + size_t(kEpiWarps) * a.sb * kStageBytes +
+                         2 * size_t(p->np) * 4 + 512 + 1024;
     a.stages = S;
     size_t smem = fixed + size_t(S) * kABytes;
     // 512 TMEM columns are only safe with one CTA per SM: make the shared
@@ -529,7 +550,9 @@ int projection_tc_launch(const gat_b200_layer* p, uint64_t n, const uint16_t* x,
     GATB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const uint64_t ntiles = (n + kTileM - 1) / kTileM;
     const unsigned grid = unsigned(ntiles < uint64_t(sms) ? ntiles : uint64_t(sms));
-    if (p->dim % 16 == 0) {
+    // Heads aligned to 16 columns (or a single head, whose columns past the
+    // width carry zero coefficients): one head per 16-column block.
+    if (p->dim % 16 == 0 || p->heads == 1) {
         auto k = proj_tc_kernel<true>;
         GATB_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
         k<<<grid, kThreads, smem, st>>>(tm_x, tm_w, tm_h, a);
