@@ -21,7 +21,11 @@ forward time. Prints ONE JSON line (rank 0).
 workload and prints its line (rank 0 only under torchrun).
 
 Multi-GPU: destination rows are partitioned by edge count; every layer's
-projected features are exchanged with one NCCL all-gather.
+projected features reach every rank's feature table through the projection
+kernel's own stores over NVLink (CUDA IPC peer memory) and a cross-GPU flag
+barrier (--exchange p2p, default), or through NCCL all-gathers (--exchange
+nccl). NCCL otherwise only exchanges the IPC handles and runs host barriers,
+so NVLink SHARP is left off (NCCL_NVLS_ENABLE=0 unless set).
 
 --mode micro: the layer-2 micro-benchmark (config c3) on the c2 graph: input H
 169,343 x 256 BF16 ~ N(0,1), W 256 x 256, a_L/a_R ~ U(-0.1, 0.1); the
@@ -76,9 +80,10 @@ def parse():
                     help="standard: B0 on every layer; adaptive: layer 1 through TFS aggregation (tensor cores)")
     ap.add_argument("--chunks", type=int, default=1,
                     help="N>1: row chunks per rank, each projected and exchanged as soon as it is aggregated")
-    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+    ap.add_argument("--exchange", choices=["p2p", "dma", "nccl"], default="p2p",
                     help="N>1: p2p = the projection kernel stores H/R into every rank's table over NVLink; "
-                         "nccl = NCCL all-gather per chunk")
+                         "dma = copy engines push each projected chunk to the peers while the next chunk "
+                         "is aggregated; nccl = NCCL all-gather per chunk")
     return ap.parse_args()
 
 
@@ -440,6 +445,7 @@ def main():
     if world > 1:
         import datetime
         import torch.distributed as dist
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
         log("process group ready")
     stream = torch.cuda.current_stream()
@@ -531,6 +537,9 @@ def main():
         if args.exchange == "p2p":
             how = ("the projection kernel stores each H/R tile into every rank's table over NVLink (CUDA IPC "
                    "peer memory), then a cross-GPU flag barrier per layer")
+        elif args.exchange == "dma":
+            how = ("copy engines push each projected chunk into every peer's table (CUDA IPC peer memory) while "
+                   "the next chunk is aggregated, then a cross-GPU flag barrier per layer")
         else:
             how = "each chunk's NCCL all-gather of H and R overlaps the next chunk's aggregation"
         parallelism = (f"rows{world}: destination rows split by edge count, {len(pm.chunks)} row chunk(s) per "

@@ -139,6 +139,17 @@ int gat_b200_peer_free(void* ptr) {
     return 0;
 }
 
+int gat_b200_copy_to_peers(const void* src, void* const* dst, int ndst, uint64_t bytes, void* const* streams) {
+    gatb::clear_error();
+    if (ndst < 0 || ndst > 7) return gatb::fail("copy_to_peers: ndst must be 0..7");
+    if (ndst && (!src || !dst || !streams)) return gatb::fail("copy_to_peers: null argument");
+    for (int j = 0; j < ndst; ++j) {
+        if (!dst[j]) return gatb::fail("copy_to_peers: null destination");
+        GATB_CUDA(cudaMemcpyAsync(dst[j], src, bytes, cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(streams[j])));
+    }
+    return 0;
+}
+
 int gat_b200_peer_barrier(void* const* flags, int world, int rank, uint32_t epoch, void* stream) {
     gatb::clear_error();
     return gatb::peer_barrier_launch(flags, world, rank, epoch, static_cast<cudaStream_t>(stream));

@@ -17,6 +17,11 @@ The all-gather is the only exchange. Two ways to do it:
     (gat_b200_projection_scatter), so the exchange runs inside the projection,
     tile by tile; a cross-GPU flag barrier (gat_b200_peer_barrier) then orders
     those stores before any rank's aggregation.
+  exchange="dma": the projection writes the local table only and the copy
+    engines push each chunk's block to every peer (one cudaMemcpyAsync per
+    peer on its own stream) while the next chunk is aggregated; the same
+    barrier follows. The copies take no SMs, so with several chunks the
+    exchange overlaps the aggregation.
   exchange="nccl": the projection writes a send block and NCCL's all-gather
     moves it; each chunk's all-gather runs on NCCL's stream while the next
     chunk is aggregated.
@@ -112,10 +117,10 @@ class PartitionedModel:
         """row: all n+1 row pointers; col_rows: the sources of this rank's rows
         (col[row[cuts[rank]]:row[cuts[rank+1]]]); cuts: partition(row, world)."""
         import torch
-        if exchange not in ("p2p", "nccl"):
-            raise ValueError("exchange must be 'p2p' or 'nccl'")
-        if exchange == "p2p" and world > 8:
-            raise ValueError("p2p exchange supports up to 8 ranks (one NVLink node)")
+        if exchange not in ("p2p", "dma", "nccl"):
+            raise ValueError("exchange must be 'p2p', 'dma' or 'nccl'")
+        if exchange != "nccl" and world > 8:
+            raise ValueError("peer-memory exchanges support up to 8 ranks (one NVLink node)")
         self.torch = torch
         self.dist = dist_module
         self.exchange = exchange
@@ -152,7 +157,7 @@ class PartitionedModel:
         self.xs = [torch.zeros((n, self.ld_hidden), dtype=i16, device=dev) for _ in range(2)]
         self.logits = torch.empty((n, self.classes), dtype=torch.float32, device=dev)
         self._owned, self._mapped = [], []
-        if exchange == "p2p":
+        if exchange in ("p2p", "dma"):
             # h_tab[l][j] / r_tab[l][j]: device pointer of rank j's layer-l table in this process
             own, handles = [], []
             for l in range(3):
@@ -182,6 +187,9 @@ class PartitionedModel:
             self.r_tab = [[ptrs[j][2 * l + 1] for j in range(world)] for l in range(3)]
             self.flags = [ptrs[j][6] for j in range(world)]
             self.epoch = 0
+            self.peers = [j for j in range(world) if j != rank]
+            # dma: one copy stream per peer (copy engines, no SMs)
+            self.copy_streams = [torch.cuda.Stream(device=dev) for _ in self.peers] if exchange == "dma" else []
         else:
             ldh_max = max(self.ldh)
             self.h_send = torch.zeros((P, cm * ldh_max), dtype=i16, device=dev)
@@ -219,6 +227,24 @@ class PartitionedModel:
         a, b, _ = self.chunks[c]
         cm, W, K, ldh = self.lay.chunk_max, self.world, p.heads, self.ldh[l]
         left = self.left[l & 1][a * K:b * K]
+        if self.exchange == "dma":
+            if b <= a:
+                return
+            torch = self.torch
+            row0 = (c * W + self.rank) * cm
+            h_own = self.h_tab[l][self.rank] + row0 * ldh * 2
+            r_own = self.r_tab[l][self.rank] + row0 * K * 4
+            G.projection(p, b - a, x[a:b], ldx, G.BF16, h_own, G.BF16, ldh, left, r_own, self.stream)
+            if self.peers:
+                ev = torch.cuda.Event()
+                ev.record(torch.cuda.current_stream())
+                for cs in self.copy_streams:
+                    cs.wait_event(ev)
+                G.copy_to_peers(h_own, [self.h_tab[l][j] + row0 * ldh * 2 for j in self.peers], (b - a) * ldh * 2,
+                                self.copy_streams)
+                G.copy_to_peers(r_own, [self.r_tab[l][j] + row0 * K * 4 for j in self.peers], (b - a) * K * 4,
+                                self.copy_streams)
+            return
         if self.exchange == "p2p":
             if b <= a:
                 return
@@ -248,8 +274,13 @@ class PartitionedModel:
 
     def _complete(self):
         """Every rank's projections of the current layer are in this rank's table."""
-        if self.exchange == "p2p":
+        if self.exchange in ("p2p", "dma"):
             if self.world > 1:
+                comp = self.torch.cuda.current_stream()
+                for cs in self.copy_streams:  # dma: this rank's pushes have landed
+                    ev = self.torch.cuda.Event()
+                    ev.record(cs)
+                    comp.wait_event(ev)
                 self.epoch += 1
                 G.peer_barrier(self.flags, self.rank, self.epoch, self.stream)
             return
@@ -258,7 +289,7 @@ class PartitionedModel:
         self.pending = []
 
     def _tables(self, l):
-        if self.exchange == "p2p":
+        if self.exchange in ("p2p", "dma"):
             return self.h_tab[l][self.rank], self.r_tab[l][self.rank]
         return self.h_full[l], self.r_full[l]
 
@@ -353,7 +384,7 @@ class PartitionedModel:
         chunk a projection and an aggregation (+ the hub merge of split rows),
         and one barrier per layer under the p2p exchange."""
         per_chunk = sum(2 + (1 if g.info()["n_hub"] else 0) for _, _, g in self.chunks if g is not None)
-        barriers = 3 if self.exchange == "p2p" and self.world > 1 else 0
+        barriers = 3 if self.exchange != "nccl" and self.world > 1 else 0
         return 1 + 3 * per_chunk + barriers
 
     def stage_times(self) -> dict:

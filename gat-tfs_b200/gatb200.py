@@ -105,6 +105,7 @@ SIGNATURES = [
     ("gat_b200_projection_scatter", C.c_int, [_vp, C.c_uint64, _vp, C.c_int, _vp, C.c_int, _vp, _vp, C.c_int,
                                               C.POINTER(_vp), C.POINTER(_vp), _vp]),
     ("gat_b200_peer_barrier", C.c_int, [C.POINTER(_vp), C.c_int, C.c_int, C.c_uint32, _vp]),
+    ("gat_b200_copy_to_peers", C.c_int, [_vp, C.POINTER(_vp), C.c_int, C.c_uint64, C.POINTER(_vp)]),
 ]
 for _name, _res, _args in SIGNATURES:
     _fn = getattr(_lib, _name)
@@ -474,6 +475,14 @@ def projection_scatter(layer: DeviceLayer, n, x, ldx, h, ldh, left, right, h_pee
     rp = (_vp * max(k, 1))(*[int(v) for v in r_peer])
     _check(_lib.gat_b200_projection_scatter(layer.handle, n, _ptr(x), ldx, _ptr(h), ldh, _ptr(left), _ptr(right),
                                             k, hp, rp, _stream(stream)))
+
+
+def copy_to_peers(src: int, dsts, nbytes: int, streams):
+    """dsts[j] <- src (nbytes) on streams[j] (copy engines)."""
+    k = len(dsts)
+    d = (_vp * max(k, 1))(*[int(v) for v in dsts])
+    st = (_vp * max(k, 1))(*[_stream(v) for v in streams])
+    _check(_lib.gat_b200_copy_to_peers(int(src), d, k, int(nbytes), st))
 
 
 def peer_barrier(flags, rank: int, epoch: int, stream=None):

@@ -414,6 +414,11 @@ int gat_b200_projection_scatter(const gat_b200_layer* p, uint64_t n, const void*
                                 int ldh, float* left, float* right, int npeer, void* const* h_peer,
                                 float* const* r_peer, void* stream);
 
+/* Copy-engine push of one block to up to 7 peers: dst[j] <- src (`bytes`
+ * bytes) as one cudaMemcpyAsync on streams[j] each, so the copies use no SMs
+ * and run beside kernels on other streams. */
+int gat_b200_copy_to_peers(const void* src, void* const* dst, int ndst, uint64_t bytes, void* const* streams);
+
 /* Cross-GPU barrier on `stream`: flags[j] is rank j's flag array (a
  * gat_b200_peer_alloc allocation of at least world*4 bytes, mapped in this
  * process; flags[rank] the own one). Every rank calls it with the same epoch,

@@ -1,6 +1,7 @@
 """Row-partitioned forward on 2 GPUs against the 1-GPU model, with the
-exchange done by the projection kernel's peer stores (p2p, one and three row
-chunks) and by NCCL all-gathers (four chunks).
+exchange done by the projection kernel's peer stores (p2p), by copy-engine
+pushes (dma; one and three row chunks each) and by NCCL all-gathers (four
+chunks).
 
 Skipped when fewer than two GPUs are visible. Ranks run as child processes
 with NCCL's NVLink SHARP (NVLS) disabled and a short process-group timeout.
@@ -67,7 +68,7 @@ def _rank_main(rank, world, port, name, q, exchange, chunks):
         tdist.destroy_process_group()
 
 
-@pytest.mark.parametrize("exchange,chunks", [("p2p", 1), ("p2p", 3), ("nccl", 4)])
+@pytest.mark.parametrize("exchange,chunks", [("p2p", 1), ("p2p", 3), ("dma", 1), ("dma", 3), ("nccl", 4)])
 def test_two_gpu_partitioned_forward_matches_single_gpu(exchange, chunks):
     import torch
     import torch.multiprocessing as mp
