@@ -1,7 +1,8 @@
 """Regenerates the golden fixtures in tests/golden/ from the reference itself.
 
-Run in a container where the reference tree exists (REF, default
-/root/reference) after `make -C oracle all ref`:
+Run where the reference source tree exists (its location in the REF
+environment variable, or the default in REF below) after
+`make -C oracle all ref`:
 
     python tests/golden/make_golden.py
 
