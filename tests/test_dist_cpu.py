@@ -148,3 +148,14 @@ def test_two_rank_forward_equals_single_process():
         assert p.exitcode == 0
     want = _single_process_reference("c2")
     assert np.array_equal(got, want)
+
+
+def test_partitioned_model_argument_checks():
+    g = configs.make_graph("c1", features=False)
+    params = G.glorot_model(128, 40, 1)
+    with pytest.raises(ValueError, match="exchange"):
+        gdist.PartitionedModel(g.row, g.col, params, 0, 1, exchange="mpi")
+    with pytest.raises(ValueError, match="up to 8 ranks"):
+        gdist.PartitionedModel(g.row, g.col, params, 0, 9, exchange="p2p")
+    with pytest.raises(ValueError, match="up to 8 ranks"):
+        gdist.PartitionedModel(g.row, g.col, params, 0, 9, exchange="dma")

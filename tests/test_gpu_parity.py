@@ -379,3 +379,22 @@ def test_config2_model(dev):
     got32 = _forward(m32, cfg.graph.x)
     e = O.errors(ref, got32)
     assert e["max_abs"] <= 1e-5, e
+
+
+@pytest.mark.parametrize("n,width,ld_in", [(1000, 100, 100), (333, 47, 48), (257, 13, 13), (64, 256, 260)])
+def test_convert_bit_exact(dev, n, width, ld_in):
+    """gat_b200_convert (16-byte path when rows allow it, else the pairwise one) equals the
+    host RNE bit for bit, padding columns zero; ties, subnormals, infinities and NaN included."""
+    import torch
+    rng = np.random.default_rng(n + width)
+    x = rng.standard_normal((n, ld_in)).astype(np.float32)
+    specials = np.array([np.inf, -np.inf, np.nan, 1.0 + 2.0 ** -8, 1.0 + 3 * 2.0 ** -8, -0.0, 1e-40, 3.4e38],
+                        np.float32)
+    x.reshape(-1)[: len(specials)] = specials
+    ld_out = G.padded_ld(width, G.BF16)
+    out = torch.full((n, ld_out), -1, dtype=torch.int16, device="cuda")
+    G.convert(n, width, T(x), ld_in, out, ld_out)
+    got = host(out)
+    want = G.rne(np.ascontiguousarray(x[:, :width]))
+    assert np.array_equal(got[:, :width], want)
+    assert not got[:, width:].any()
