@@ -26,6 +26,11 @@ The all-gather is the only exchange. Two ways to do it:
     moves it; each chunk's all-gather runs on NCCL's stream while the next
     chunk is aggregated.
 
+Under p2p and dma, layer 1 exchanges its BF16 input rows (din padded, 208 bytes
+per row on c4) rather than H (512 bytes): the copy engines push each rank's
+converted rows into every peer's input table and every rank then projects the
+whole table itself, which costs less than moving H.
+
 Rows of a rank may be cut into `chunks` row chunks (balanced by edges, each
 with its own CSR slice and degree schedule): aggregating chunk c of layer l
 yields the chunk's rows of layer l+1's input, which are projected (and
@@ -157,6 +162,7 @@ class PartitionedModel:
         self.xs = [torch.zeros((n, self.ld_hidden), dtype=i16, device=dev) for _ in range(2)]
         self.logits = torch.empty((n, self.classes), dtype=torch.float32, device=dev)
         self._owned, self._mapped = [], []
+        self.x_exchange = False
         if exchange in ("p2p", "dma"):
             # h_tab[l][j] / r_tab[l][j]: device pointer of rank j's layer-l table in this process
             own, handles = [], []
@@ -170,6 +176,13 @@ class PartitionedModel:
             self._owned.append(fptr)
             own.append(fptr)
             handles.append(fh)
+            # layer 1 exchanges its BF16 input rows instead of H when they are narrower
+            self.x_exchange = world > 1 and self.ld0 < self.ldh[0]
+            if self.x_exchange:
+                xptr, xh = G.peer_alloc(nt * self.ld0 * 2)
+                self._owned.append(xptr)
+                own.append(xptr)
+                handles.append(xh)
             allh = self._all_gather_bytes(b"".join(handles), dev)
             hb = G.PEER_HANDLE_BYTES
             ptrs = []  # [rank][7]
@@ -188,8 +201,13 @@ class PartitionedModel:
             self.flags = [ptrs[j][6] for j in range(world)]
             self.epoch = 0
             self.peers = [j for j in range(world) if j != rank]
-            # dma: one copy stream per peer (copy engines, no SMs)
-            self.copy_streams = [torch.cuda.Stream(device=dev) for _ in self.peers] if exchange == "dma" else []
+            # one copy stream per peer (copy engines, no SMs): dma pushes and the
+            # layer-1 input exchange
+            need_copies = exchange == "dma" or self.x_exchange
+            self.copy_streams = [torch.cuda.Stream(device=dev) for _ in self.peers] if need_copies else []
+            if self.x_exchange:
+                self.x_tab = [ptrs[j][7] for j in range(world)]
+                self.left0 = torch.zeros((nt * self.heads[0],), dtype=torch.float32, device=dev)
         else:
             ldh_max = max(self.ldh)
             self.h_send = torch.zeros((P, cm * ldh_max), dtype=i16, device=dev)
@@ -272,6 +290,40 @@ class PartitionedModel:
             hf.copy_(hs)
             rf.copy_(rs)
 
+    def _exchange_input(self, xin):
+        """Layer 1 with the input exchanged: each rank converts its rows into its
+        blocks of the BF16 input table, the copy engines push them to every
+        peer, and after the barrier every rank projects the whole table itself
+        (H, L and R of all rows, locally). Same kernels on the same inputs, so
+        the tables equal those of the H exchange bit for bit."""
+        torch = self.torch
+        cm, W, ld0 = self.lay.chunk_max, self.world, self.ld0
+        comp = torch.cuda.current_stream()
+        for c, (a, b, _) in enumerate(self.chunks):
+            if b <= a:
+                continue
+            row0 = (c * W + self.rank) * cm
+            dst = self.x_tab[self.rank] + row0 * ld0 * 2
+            G.convert(b - a, self.din, xin[a:b], self.din, dst, ld0, self.stream)
+            ev = torch.cuda.Event()
+            ev.record(comp)
+            for cs in self.copy_streams:
+                cs.wait_event(ev)
+            G.copy_to_peers(dst, [self.x_tab[j] + row0 * ld0 * 2 for j in self.peers], (b - a) * ld0 * 2,
+                            self.copy_streams)
+        self._complete()
+        p = self.layers[0]
+        G.projection(p, self.lay.n_table, self.x_tab[self.rank], ld0, G.BF16, self.h_tab[0][self.rank], G.BF16,
+                     self.ldh[0], self.left0, self.r_tab[0][self.rank], self.stream)
+
+    def _left(self, l, c, a, b):
+        """L rows of chunk c (local rows [a, b)) for layer l."""
+        K = self.heads[l]
+        if l == 0 and self.x_exchange:
+            row0 = (c * self.world + self.rank) * self.lay.chunk_max
+            return self.left0[row0 * K:(row0 + b - a) * K]
+        return self.left[l & 1][a * K:b * K]
+
     def _complete(self):
         """Every rank's projections of the current layer are in this rank's table."""
         if self.exchange in ("p2p", "dma"):
@@ -302,24 +354,28 @@ class PartitionedModel:
             self.x_f32.copy_(x, non_blocking=True)
             xin = self.x_f32
         self._mark(1)
-        G.convert(n, self.din, xin, self.din, self.x0, self.ld0, self.stream)
-        for c in range(len(self.chunks)):
-            self._project(0, c, self.x0, self.ld0)
+        if self.x_exchange:
+            self._exchange_input(xin)
+        else:
+            G.convert(n, self.din, xin, self.din, self.x0, self.ld0, self.stream)
+            for c in range(len(self.chunks)):
+                self._project(0, c, self.x0, self.ld0)
         self._mark(2)
         dst_logits = logits if not logits_on_host else self.logits
         for l, p in enumerate(self.layers):
-            self._complete()
+            if not (l == 0 and self.x_exchange):  # layer 1's tables are local then
+                self._complete()
             self._mark(3 + l)
             K, ldh, last = p.heads, self.ldh[l], l == 2
             hf, rf = self._tables(l)
-            left = self.left[l & 1]
             for c, (a, b, g) in enumerate(self.chunks):
                 if g is not None:
+                    left = self._left(l, c, a, b)
                     if last:
-                        G.aggregate_fused(g, K, p.dim, hf, G.BF16, ldh, left[a * K:b * K], rf, False,
+                        G.aggregate_fused(g, K, p.dim, hf, G.BF16, ldh, left, rf, False,
                                           dst_logits[a:b], G.F32, p.width, self.stream)
                     else:
-                        G.aggregate_fused(g, K, p.dim, hf, G.BF16, ldh, left[a * K:b * K], rf, True,
+                        G.aggregate_fused(g, K, p.dim, hf, G.BF16, ldh, left, rf, True,
                                           self.xs[l][a:b], G.BF16, self.ld_hidden, self.stream)
                 if not last:
                     self._project(l + 1, c, self.xs[l], self.ld_hidden)
@@ -383,9 +439,14 @@ class PartitionedModel:
         """Kernels one forward launches: the input conversion, per layer and
         chunk a projection and an aggregation (+ the hub merge of split rows),
         and one barrier per layer under the p2p exchange."""
-        per_chunk = sum(2 + (1 if g.info()["n_hub"] else 0) for _, _, g in self.chunks if g is not None)
+        live = [g for _, _, g in self.chunks if g is not None]
+        hub = sum(1 for g in live if g.info()["n_hub"])
         barriers = 3 if self.exchange != "nccl" and self.world > 1 else 0
-        return 1 + 3 * per_chunk + barriers
+        if self.x_exchange:
+            # per chunk: convert; one whole-table projection; aggregations of 3 layers
+            # (+ hub merges) and projections of layers 2-3 per chunk
+            return len(live) + 1 + 3 * (len(live) + hub) + 2 * len(live) + barriers
+        return 1 + 3 * (2 * len(live) + hub) + barriers
 
     def stage_times(self) -> dict:
         """ms of the last forward: layer 1's projection, then per layer the time
