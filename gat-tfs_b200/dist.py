@@ -113,8 +113,10 @@ class Layout:
 
 class PartitionedModel:
     """Three-layer BF16 forward of this rank's rows (bench/main.cpp:171-172 per
-    rank) with the exchange of each layer's H and R done by peer stores from
-    the projection kernel ("p2p") or by NCCL all-gathers ("nccl")."""
+    rank). Each layer's H and R reach every rank's table through peer stores
+    from the projection kernel ("p2p"), copy-engine pushes ("dma") or NCCL
+    all-gathers ("nccl"); under p2p and dma layer 1 moves its BF16 input rows
+    instead of H when they are narrower."""
 
     def __init__(self, row: np.ndarray, col_rows: np.ndarray, params: Sequence[G.Param], rank: int, world: int,
                  stream=None, dist_module=None, cuts: Optional[np.ndarray] = None, chunks: int = 1,
@@ -185,7 +187,7 @@ class PartitionedModel:
                 handles.append(xh)
             allh = self._all_gather_bytes(b"".join(handles), dev)
             hb = G.PEER_HANDLE_BYTES
-            ptrs = []  # [rank][7]
+            ptrs = []  # [rank][table]: H/R of layers 1-3, flags, (layer-1 input)
             for j in range(world):
                 if j == rank:
                     ptrs.append(own)
