@@ -141,3 +141,33 @@ def test_device_calls_fail_cleanly_without_gpu():
     with pytest.raises(G.GatError) as e:
         G.DeviceGraph(row, col)
     assert e.value.code == G.ECUDA
+
+
+def test_multi_gpu_and_rmat_entry_points_validate_arguments():
+    """Argument checks of the peer-memory, scatter and RMAT entry points happen
+    before any CUDA call (status GAT_B200_EINVAL = 1 and the message)."""
+    lib = G._lib
+    vp = C.c_void_p
+    flags = (vp * 9)(*([1] * 9))
+    assert lib.gat_b200_peer_barrier(flags, 9, 0, 1, None) == 1
+    assert "world size must be 1..8" in lib.gat_b200_last_error().decode()
+    assert lib.gat_b200_peer_barrier(flags, 2, 2, 1, None) == 1
+    assert "rank outside the world" in lib.gat_b200_last_error().decode()
+    assert lib.gat_b200_peer_barrier(None, 2, 0, 1, None) == 1
+    assert lib.gat_b200_peer_barrier(flags, 1, 0, 1, None) == 0  # one rank: nothing to wait for
+    assert lib.gat_b200_copy_to_peers(vp(1), flags, 8, 16, flags) == 1
+    assert "ndst must be 0..7" in lib.gat_b200_last_error().decode()
+    assert lib.gat_b200_copy_to_peers(None, flags, 0, 16, flags) == 0  # no destinations
+    assert lib.gat_b200_projection_scatter(None, 10, vp(1), 16, vp(1), 16, None, vp(1), 0, None, None, None) == 1
+    assert "null argument" in lib.gat_b200_last_error().decode()
+    assert lib.gat_b200_peer_alloc(16, None, None) == 1
+    assert lib.gat_b200_peer_open(None, None) == 1
+    assert lib.gat_b200_peer_close(None) == 0 and lib.gat_b200_peer_free(None) == 0
+    row = np.zeros(5, np.uint64)
+    rp = row.ctypes.data_as(C.POINTER(C.c_uint64))
+    assert lib.gat_b200_synth_rmat(2, 10, 0.5, 0.3, 0.3, 1, 0, 0, rp, None, None) == 1
+    assert "a+b+c < 1" in lib.gat_b200_last_error().decode()
+    assert lib.gat_b200_synth_rmat(0, 10, 0.57, 0.19, 0.19, 1, 0, 0, rp, None, None) == 1
+    assert lib.gat_b200_synth_rmat(2, 10, 0.57, 0.19, 0.19, 1, 3, 2, rp, None, None) == 1
+    assert "bad row range" in lib.gat_b200_last_error().decode()
+    assert lib.gat_b200_synth_rmat(30, 1 << 31, 0.57, 0.19, 0.19, 1, 0, 0, rp, None, None) == 1
