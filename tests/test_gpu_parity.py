@@ -398,3 +398,51 @@ def test_convert_bit_exact(dev, n, width, ld_in):
     want = G.rne(np.ascontiguousarray(x[:, :width]))
     assert np.array_equal(got[:, :width], want)
     assert not got[:, width:].any()
+
+
+@pytest.mark.parametrize("scenario", range(5))
+@pytest.mark.parametrize("dtype", [G.F32, G.BF16])
+def test_adversarial_scores(dev, scenario, dtype):
+    """The reference's adversarial score cases (baseline/tests/boundaries.cpp:45-51) on its
+    17-feature boundary graph with 8 heads of 32: equal scores, a late +1000 peak after -1000
+    sources, increasing scores, and common offsets of +10000 / -10000. Outputs finite, the
+    max bit-exact, den >= 1 on non-empty rows and 0 on empty ones, and the online-softmax
+    kernels equal to the oracle."""
+    import torch
+    row, col, _ = O.boundary_graph(17)
+    n, K, d = len(row) - 1, 8, 32
+    W = K * d
+    i = np.arange(n, dtype=np.float32)[:, None]
+    h = np.arange(K, dtype=np.float32)[None, :]
+    left = np.broadcast_to({3: np.float32(10000), 4: np.float32(-10000)}.get(scenario, h - 4), (n, K))
+    right = [np.zeros((n, K)), np.where(i == n - 1, 1000.0, -1000.0) + 0 * h, (i - 17) + 0 * h,
+             np.sin(i + h) * 8, np.sin(i + h) * 8][scenario]
+    left = np.ascontiguousarray(left, np.float32)
+    right = np.ascontiguousarray(right, np.float32)
+    z = ((np.arange(n * W) % 9) * np.float32(0.1)).astype(np.float32).reshape(n, W)
+    ld = G.padded_ld(W, dtype)
+    if dtype == G.BF16:
+        z = O.quantize(z)
+        hz = dev_bf16(z, ld)
+    else:
+        hz = T(z)
+    g = G.DeviceGraph(row, col)
+    out = torch.empty((n, W), dtype=torch.float32, device="cuda")
+    den = torch.empty((n, K), dtype=torch.float32, device="cuda")
+    mx = torch.empty((n, K), dtype=torch.float32, device="cuda")
+    G.standard_aggregate(g, K, d, hz, dtype, ld, T(left), T(right), out, W, den, mx)
+    omax = O.max_prescan(row, col, left, right, K)
+    oout, oden = O.standard_aggregate(row, col, z, left, right, omax, K, d)
+    got_out, got_den = host(out), host(den)
+    assert np.all(np.isfinite(got_out)) and np.all(np.isfinite(got_den))
+    assert np.array_equal(host(mx), omax)
+    empty = np.diff(row.astype(np.int64)) == 0
+    assert np.all(got_den[empty] == 0) and np.all(got_den[~empty] >= 1)
+    assert np.abs(got_den - oden).max() <= 1e-5 * max(1, np.abs(oden).max())
+    assert np.abs(got_out - oout).max() <= 1e-5 * max(1, np.abs(oout).max())
+    fused = torch.empty((n, W), dtype=torch.float32, device="cuda")
+    G.aggregate_fused(g, K, d, hz, dtype, ld, T(left), T(right), False, fused, G.F32, W)
+    fin = O.finish(oout, oden, K, d, False)
+    assert np.all(np.isfinite(host(fused)))
+    assert np.abs(host(fused) - fin).max() <= 1e-5 * max(1, np.abs(fin).max())
+    g.close()
