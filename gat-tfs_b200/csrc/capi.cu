@@ -181,6 +181,43 @@ int gat_b200_graph_device_csr(const gat_b200_graph* g, const uint64_t** row, con
     return 0;
 }
 
+int gat_b200_device_alloc(uint64_t bytes, void** ptr) {
+    clear_error();
+    if (!ptr) return fail("device_alloc: null output");
+    *ptr = nullptr;
+    void* p = nullptr;
+    GATB_CUDA(cudaMalloc(&p, bytes ? bytes : 16));
+    cudaError_t e = cudaMemset(p, 0, bytes ? bytes : 16);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return cuda_fail(e, "device_alloc");
+    }
+    *ptr = p;
+    return 0;
+}
+
+int gat_b200_device_free(void* ptr) {
+    clear_error();
+    if (ptr) GATB_CUDA(cudaFree(ptr));
+    return 0;
+}
+
+int gat_b200_copy_to_device(void* dst, const void* src, uint64_t bytes) {
+    clear_error();
+    if (!bytes) return 0;
+    if (!dst || !src) return fail("copy_to_device: null pointer");
+    GATB_CUDA(cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice));
+    return 0;
+}
+
+int gat_b200_copy_to_host(void* dst, const void* src, uint64_t bytes) {
+    clear_error();
+    if (!bytes) return 0;
+    if (!dst || !src) return fail("copy_to_host: null pointer");
+    GATB_CUDA(cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
 int gat_b200_graph_info(const gat_b200_graph* g, uint64_t* n, uint64_t* e, uint32_t* max_degree,
                         uint32_t* n_hub, uint32_t* n_seg, uint32_t* seg_edges) {
     if (!g) return fail("graph_info: null graph");

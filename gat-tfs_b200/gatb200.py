@@ -90,6 +90,10 @@ SIGNATURES = [
     ("gat_b200_tfs_layer", C.c_int, [_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                      _vp, _vp, _vp, _vp, _vp, _vp, C.c_int, C.c_int, _vp]),
     ("gat_b200_check_device", C.c_int, []),
+    ("gat_b200_device_alloc", C.c_int, [C.c_uint64, C.POINTER(_vp)]),
+    ("gat_b200_device_free", C.c_int, [_vp]),
+    ("gat_b200_copy_to_device", C.c_int, [_vp, _vp, C.c_uint64]),
+    ("gat_b200_copy_to_host", C.c_int, [_vp, _vp, C.c_uint64]),
     ("gat_b200_model_create", C.c_int, [_vp, C.POINTER(_vp), C.c_int, C.POINTER(_vp)]),
     ("gat_b200_model_destroy", C.c_int, [_vp]),
     ("gat_b200_model_forward", C.c_int, [_vp, _vp, C.c_int, _vp, C.c_int, _vp]),

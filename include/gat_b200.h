@@ -332,6 +332,15 @@ int gat_b200_tfs_layer(const gat_b200_graph* g, const gat_b200_layer* p, const v
                        void* x_bf16, float* left, float* right, float* max, float* den, void* out,
                        int out_dtype, int ldo, void* stream);
 
+/* Device memory for callers that hold no CUDA runtime of their own (the C++
+ * mirror of the reference API, include/gat_b200.hpp): a zero-filled
+ * allocation on the current device, its release, and synchronous copies
+ * between host and device memory. */
+int gat_b200_device_alloc(uint64_t bytes, void** ptr);
+int gat_b200_device_free(void* ptr);
+int gat_b200_copy_to_device(void* dst, const void* src, uint64_t bytes);
+int gat_b200_copy_to_host(void* dst, const void* src, uint64_t bytes);
+
 /* Reports (and clears) a device-side failure recorded by an earlier kernel:
  * GAT_B200_ETIMEOUT if a bounded wait inside a kernel gave up. Synchronizes
  * with the device. */
