@@ -35,7 +35,7 @@ PER_FILE_FLAGS = {"refrng.cpp": ["-mfma"]}
 
 
 def _headers():
-    return list(CSRC.glob("*.h")) + list(CSRC.glob("*.cuh")) + list((ROOT / "include").glob("*.h"))
+    return list(CSRC.glob("*.h")) + list(CSRC.glob("*.cuh")) + list((ROOT / "include").glob("*.h")) + list((ROOT / "include").glob("*.hpp"))
 
 
 def _stale(src: Path, obj: Path) -> bool:

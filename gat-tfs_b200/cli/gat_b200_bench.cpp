@@ -27,16 +27,15 @@
 #include <string>
 #include <vector>
 
-#include "gat_b200.h"
+#include "gat_b200.hpp"
+
+namespace gat = gat_b200;
 
 namespace {
 
-using Clock = std::chrono::steady_clock;
-double seconds(Clock::time_point a, Clock::time_point b) { return std::chrono::duration<double>(b - a).count(); }
-
-void check(int rc) {
-    if (rc) throw std::runtime_error(gat_b200_last_error());
-}
+using gat::check;
+using gat::Clock;
+using gat::seconds;
 
 struct Args {
     std::map<std::string, std::string> v;
@@ -58,77 +57,6 @@ struct Args {
     }
     int num(const std::string& k, int def) const { return std::stoi(get(k, std::to_string(def))); }
 };
-
-struct Graph {
-    uint64_t n = 0, e = 0;
-    uint32_t din = 0, classes = 0;
-    std::vector<uint64_t> row;
-    std::vector<uint32_t> col;
-    std::vector<float> x;
-};
-
-struct Layer {
-    int in = 0, heads = 0, dim = 0;
-    std::vector<float> w, al, ar;
-};
-
-void layer_shape(int l, int din, int classes, int& in, int& heads, int& dim) {
-    in = l == 0 ? din : 256;  // baseline/src/common.cpp:53
-    heads = l < 2 ? 8 : 1;
-    dim = l < 2 ? 32 : classes;
-}
-
-std::vector<Layer> model_storage(int din, int classes) {
-    std::vector<Layer> m(3);
-    for (int l = 0; l < 3; ++l) {
-        layer_shape(l, din, classes, m[l].in, m[l].heads, m[l].dim);
-        const size_t width = size_t(m[l].heads) * m[l].dim;
-        m[l].w.resize(size_t(m[l].in) * width);
-        m[l].al.resize(width);
-        m[l].ar.resize(width);
-    }
-    return m;
-}
-
-struct Error {
-    bool finite = true;
-    double max_abs = 0, mean_abs = 0, relative_l2 = 0, rmse = 0, p50 = 0, p90 = 0, p99 = 0;
-};
-
-// The reference's error metrics (baseline/src/common.cpp:141-150).
-Error errors(const std::vector<float>& ref, const std::vector<float>& got) {
-    Error e;
-    if (ref.size() != got.size()) throw std::runtime_error("error metric size mismatch");
-    double num = 0, den = 0, sum = 0;
-    std::vector<double> diffs(ref.size());
-    for (size_t i = 0; i < ref.size(); ++i) {
-        if (!std::isfinite(got[i])) e.finite = false;
-        const double d = std::fabs(double(got[i]) - double(ref[i]));
-        diffs[i] = d;
-        e.max_abs = std::max(e.max_abs, d);
-        sum += d;
-        num += d * d;
-        den += double(ref[i]) * ref[i];
-    }
-    if (!ref.empty()) {
-        e.mean_abs = sum / ref.size();
-        e.rmse = std::sqrt(num / ref.size());
-        e.relative_l2 = std::sqrt(num) / std::max(std::sqrt(den), 1e-30);
-        std::sort(diffs.begin(), diffs.end());
-        auto q = [&](double p) { return diffs[std::min(diffs.size() - 1, size_t(std::ceil(p * diffs.size())) - 1)]; };
-        e.p50 = q(.5);
-        e.p90 = q(.9);
-        e.p99 = q(.99);
-    }
-    return e;
-}
-
-void print_error(const std::string& path, int layer, const std::string& stage, const Error& e) {
-    std::cout << std::setprecision(10) << "ERROR path=" << path << " layer=" << layer << " stage=" << stage
-              << " finite=" << e.finite << " max_abs=" << e.max_abs << " mean_abs=" << e.mean_abs
-              << " relative_l2=" << e.relative_l2 << " rmse=" << e.rmse << " p50=" << e.p50 << " p90=" << e.p90
-              << " p99=" << e.p99 << "\n";
-}
 
 double pct(std::vector<double> x, double q) {
     std::sort(x.begin(), x.end());
@@ -166,15 +94,10 @@ struct Device {
     }
 };
 
-std::vector<float> forward(gat_b200_model* m, const Graph& g, const std::vector<Layer>& model) {
-    std::vector<float> logits(g.n * size_t(model[2].heads) * model[2].dim);
+std::vector<float> forward(gat_b200_model* m, const gat::Graph& g, const gat::Model& model) {
+    std::vector<float> logits(g.n * size_t(model[2].width()));
     check(gat_b200_model_forward(m, g.x.data(), 1, logits.data(), 1, nullptr));
     return logits;
-}
-
-void require_finite(const std::vector<float>& v, const char* what) {
-    for (size_t i = 0; i < v.size(); ++i)
-        if (!std::isfinite(v[i])) throw std::runtime_error(std::string("nonfinite ") + what + " index=" + std::to_string(i));
 }
 
 }  // namespace
@@ -196,25 +119,16 @@ int main(int argc, char** argv) {
                   << (a.get("--weights").empty() ? "random_fixture_not_trained" : a.get("--weights"))
                   << " profile=0 device=sm_100a\n";
         const auto cold_start = Clock::now();
-        Graph g;
-        check(gat_b200_read_graph_header(graph_path.c_str(), &g.n, &g.e, &g.din, &g.classes));
-        g.row.resize(g.n + 1);
-        g.col.resize(g.e);
-        g.x.resize(g.n * size_t(g.din));
-        check(gat_b200_read_graph(graph_path.c_str(), g.n, g.e, g.din, g.row.data(), g.col.data(), g.x.data()));
-        std::vector<Layer> model = model_storage(int(g.din), int(g.classes));
-        float* w[3] = {model[0].w.data(), model[1].w.data(), model[2].w.data()};
-        float* al[3] = {model[0].al.data(), model[1].al.data(), model[2].al.data()};
-        float* ar[3] = {model[0].ar.data(), model[1].ar.data(), model[2].ar.data()};
+        const gat::Graph g = gat::load_graph(graph_path);
+        gat::Model model;
         if (!a.get("--weights").empty()) {
-            check(gat_b200_read_weights(a.get("--weights").c_str(), int(g.din), int(g.classes), w, al, ar));
+            model = gat::load_model(a.get("--weights"), g.din, g.classes);
         } else {
             if (a.get("--seed").empty())
                 throw std::runtime_error("provide --weights checkpoint.bin or explicit --seed for synthetic fixture");
-            check(gat_b200_random_model(int(g.din), int(g.classes), a.num("--seed", 11), w, al, ar));
+            model = gat::random_model(g.din, g.classes, a.num("--seed", 11));
         }
-        if (!a.get("--save-weights").empty())
-            check(gat_b200_write_weights(a.get("--save-weights").c_str(), int(g.din), int(g.classes), w, al, ar));
+        if (!a.get("--save-weights").empty()) gat::save_model(model, a.get("--save-weights"));
 
         Device dev;
         auto t0 = Clock::now();
@@ -243,13 +157,13 @@ int main(int argc, char** argv) {
             if (have_abs && (!std::isfinite(maxabs) || !std::isfinite(rel) || maxabs < 0 || rel < 0))
                 throw std::runtime_error("invalid accuracy thresholds");
             const std::vector<float> master = forward(dev.model(GAT_B200_PATH_STANDARD_FP32), g, model);
-            require_finite(master, "ref_fp32 output");
+            gat::require_finite(master, "ref_fp32 output");
             bool pass = true, finite = true;
             for (const std::string test : {"standard_fp32", "standard_bf16", "tfs_bf16", "matched_attention",
                                            "adaptive_bf16"}) {
                 const std::vector<float> out = forward(dev.model(path_code(test)), g, model);
-                const Error e = errors(master, out);
-                print_error(test, 3, "model_path_specific_chain", e);
+                const gat::Error e = gat::errors(master, out);
+                gat::print_error(test, 3, "model_path_specific_chain", e);
                 finite &= e.finite;
                 pass &= e.finite && (!have_abs || (e.max_abs <= maxabs && e.relative_l2 <= rel));
             }
@@ -276,13 +190,13 @@ int main(int argc, char** argv) {
             logits = forward(m, g, model);
             const double total = seconds(begin, Clock::now());
             if (r == -warmups) cold_forward = total;
-            require_finite(logits, "benchmark output");
+            gat::require_finite(logits, "benchmark output");
             if (r < 0) continue;
             totals.push_back(total);
             float st[9];
             if (gat_b200_model_stage_times(m, st) < 1) throw std::runtime_error(gat_b200_last_error());
             for (int l = 0; l < 3; ++l) {
-                const Layer& p = model[l];
+                const gat::Param& p = model[l];
                 // stage slots: 1 convert, 2+2l projection (TFS: lr_reordered + max prescan), 3+2l aggregation
                 const bool tfs = pc == GAT_B200_PATH_TFS_BF16 || (tfs_layer1 && l == 0);
                 const double pre = st[2 + 2 * l], agg = st[3 + 2 * l], conv = l == 0 ? st[1] : 0.0;
