@@ -190,9 +190,58 @@ void gpu_checks() {
                 gat::tfs_layer(g, p, q, s, g.x, wt, true, 16, t, "bf16");
                 const auto et = gat::errors(want16, wt.out);
                 expect(et.finite && et.relative_l2 < 3e-2, "tfs_layer vs FP64");
+                // fixed-p operators (boundaries.cpp:36-42): the same p and den into the
+                // standard and the TFS aggregation; TFS against the scalar BF16
+                // emulation of its edge projection, at the reference's 2e-4 gate
+                std::vector<float> fp(size_t(g.e) * K), fd(size_t(g.n) * K, 0.f);
+                for (uint64_t i = 0; i < g.n; ++i)
+                    for (uint64_t ed = g.row[i]; ed < g.row[i + 1]; ++ed)
+                        for (int h = 0; h < K; ++h) {
+                            fp[ed * K + h] = 0.5f + 0.45f * std::sin(float(ed * K + h));
+                            fd[i * K + h] += fp[ed * K + h];
+                        }
+                gat::Workspace wf;
+                wf.allocate(g, p, "standard_bf16");
+                gat::projection(g, p, q, g.x, wf, true);
+                gat::standard_aggregate(g, p, wf, fp.data(), fd.data());
+                gat::finish(g, p, wf, false, t);
+                std::vector<float> emu_std(wf.out.size(), 0.f);
+                const int W = p.width();
+                for (uint64_t i = 0; i < g.n; ++i)
+                    for (int h = 0; h < K; ++h)
+                        for (int c = 0; c < d; ++c) {
+                            double acc = 0;
+                            for (uint64_t ed = g.row[i]; ed < g.row[i + 1]; ++ed)
+                                acc += double(fp[ed * K + h]) * wf.z[size_t(g.col[ed]) * W + h * d + c];
+                            emu_std[i * W + h * d + c] = fd[i * K + h] > 0 ? float(acc / fd[i * K + h]) : 0.f;
+                        }
+                const auto es = gat::errors(emu_std, wf.out);
+                expect(es.finite && es.max_abs < 1e-5 && es.relative_l2 < 1e-5, "fixed-p standard aggregate");
+                gat::Workspace wt2;
+                wt2.allocate(g, p, "tfs_bf16");
+                gat::lr_reordered(g, p, q, g.x, wt2, "bf16");  // fills the BF16 copy of X
+                gat::tfs_aggregate(g, p, q, s, wt2, 64, t, fp.data(), fd.data());
+                gat::finish(g, p, wt2, false, t);
+                std::vector<float> emu(wt2.out.size(), 0.f);
+                for (uint64_t i = 0; i < g.n; ++i)
+                    for (int h = 0; h < K; ++h) {
+                        for (uint64_t ed = g.row[i]; ed < g.row[i + 1]; ++ed)
+                            for (int k = 0; k < p.in; ++k) {
+                                const float v = gat::expand(gat::rne(
+                                    fp[ed * K + h] * gat::expand(gat::rne(g.x[size_t(g.col[ed]) * p.in + k]))));
+                                for (int c = 0; c < d; ++c)
+                                    emu[i * W + h * d + c] += v * gat::expand(gat::rne(p.w[size_t(k) * W + h * d + c]));
+                            }
+                        for (int c = 0; c < d; ++c)
+                            emu[i * W + h * d + c] = fd[i * K + h] > 0 ? emu[i * W + h * d + c] / fd[i * K + h] : 0.f;
+                    }
+                const auto ef = gat::errors(emu, wt2.out);
+                expect(ef.finite && ef.max_abs < 2e-4 && ef.relative_l2 < 2e-4,
+                       "fixed-p TFS edge projection versus emulator");
                 ++cases;
                 std::cout << "MIRROR PASS D=" << D << " K=" << K << " d=" << d << " fp32_rel=" << e.relative_l2
-                          << " bf16_rel=" << eb.relative_l2 << " tfs_rel=" << et.relative_l2 << "\n";
+                          << " bf16_rel=" << eb.relative_l2 << " tfs_rel=" << et.relative_l2
+                          << " fixed_p_tfs_rel=" << ef.relative_l2 << "\n";
             }
     // degree schedule: a permutation, degrees ascending, ties by id
     gat::Graph g = boundary_graph(17);
