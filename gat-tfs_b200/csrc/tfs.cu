@@ -275,7 +275,107 @@ __global__ void __launch_bounds__(32 * kGenWarps) tfs_generic_kernel(const TfsAr
     }
 }
 
+// icpp_online's exact counters (baseline/tfs_online/icpp_online.cpp:50-116,
+// 146-164, 229-233, 330-346): one warp per (batch of 16 consecutive rows of the
+// degree order, head); lane k < 16 follows row perm[16*batch + k] through
+// neighbour blocks of `block` up to the batch's largest degree, exactly as the
+// reference's tile does: block maximum of leaky(L + R) (same FP32 sum and
+// leaky), a strict raise of the running maximum is a max update, an update
+// after the row's first block (den > 0) a rescale; a batch block with any
+// rescale is one rescale event (warp ballot).
+__global__ void online_counters_kernel(const uint64_t* __restrict__ row, const uint32_t* __restrict__ col,
+                                       const uint32_t* __restrict__ perm, uint64_t n, int heads,
+                                       const float* __restrict__ left, const float* __restrict__ right, int block,
+                                       unsigned long long* row_blocks, unsigned long long* row_updates,
+                                       unsigned long long* row_rescales, unsigned long long* totals) {
+    const uint64_t batches = (n + 15) / 16;
+    const uint64_t warp = (blockIdx.x * uint64_t(blockDim.x) + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= batches * uint64_t(heads)) return;
+    const int h = int(warp / batches);
+    const uint64_t base = (warp % batches) * 16;
+    const bool live = lane < 16 && base + lane < n;
+    uint32_t r = 0;
+    uint64_t beg = 0, deg = 0;
+    float l = 0.f;
+    if (live) {
+        r = perm[base + lane];
+        beg = row[r];
+        deg = row[r + 1] - beg;
+        l = left[uint64_t(r) * heads + h];
+    }
+    uint64_t maxdeg = deg;
+    for (int o = 16; o > 0; o >>= 1) {
+        const uint64_t v = __shfl_xor_sync(0xffffffffu, maxdeg, o);
+        maxdeg = v > maxdeg ? v : maxdeg;
+    }
+    float run = -INFINITY;
+    bool seen = false;
+    unsigned long long nb = 0, nu = 0, nr = 0, events = 0;
+    for (uint64_t b0 = 0; b0 < maxdeg; b0 += uint64_t(block)) {
+        bool rescale = false;
+        if (live && b0 < deg) {
+            const uint64_t end = b0 + uint64_t(block) < deg ? b0 + uint64_t(block) : deg;
+            float bm = -INFINITY;
+            for (uint64_t s = b0; s < end; ++s) {
+                const float sc = leaky(l + right[uint64_t(col[beg + s]) * heads + h]);
+                bm = sc > bm ? sc : bm;
+            }
+            const float prev = run;
+            run = bm > run ? bm : run;
+            const bool update = run > prev;
+            rescale = update && seen;
+            seen = true;
+            ++nb;
+            nu += update ? 1u : 0u;
+            nr += rescale ? 1u : 0u;
+        }
+        if (__ballot_sync(0xffffffffu, rescale)) ++events;
+    }
+    if (live) {
+        const uint64_t idx = uint64_t(r) * heads + h;
+        if (row_blocks) row_blocks[idx] = nb;
+        if (row_updates) row_updates[idx] = nu;
+        if (row_rescales) row_rescales[idx] = nr;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        nb += __shfl_xor_sync(0xffffffffu, nb, o);
+        nu += __shfl_xor_sync(0xffffffffu, nu, o);
+        nr += __shfl_xor_sync(0xffffffffu, nr, o);
+    }
+    if (lane == 0) {
+        atomicAdd(totals + 0, nb);
+        atomicAdd(totals + 1, nu);
+        atomicAdd(totals + 2, nr);
+        atomicAdd(totals + 3, events);
+        atomicAdd(totals + 4, (unsigned long long)maxdeg);
+    }
+}
+
 }  // namespace
+
+int online_counters_launch(const gat_b200_graph* g, int heads, const float* left, const float* right, int block,
+                           uint64_t* row_blocks, uint64_t* row_updates, uint64_t* row_rescales, uint64_t* totals,
+                           cudaStream_t st) {
+    if (!g || !left || !right || !totals) return fail("tfs_online_counters: null argument");
+    if (heads < 1 || heads > 8) return fail("invalid parameter shape (heads <=8, head_dim <=64)");
+    if (block < 1) return fail("tfs_online_counters: block must be positive");
+    unsigned long long* d = nullptr;
+    GATB_CUDA(cudaMalloc(&d, 5 * sizeof(unsigned long long)));
+    cudaError_t e = cudaMemsetAsync(d, 0, 5 * sizeof(unsigned long long), st);
+    const uint64_t warps = (g->n + 15) / 16 * uint64_t(heads);
+    if (e == cudaSuccess && warps) {
+        online_counters_kernel<<<unsigned((warps + 7) / 8), 256, 0, st>>>(
+            g->row, g->col, g->perm, g->n, heads, left, right, block,
+            reinterpret_cast<unsigned long long*>(row_blocks), reinterpret_cast<unsigned long long*>(row_updates),
+            reinterpret_cast<unsigned long long*>(row_rescales), d);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(totals, d, 5 * sizeof(unsigned long long), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    cudaFree(d);
+    return e == cudaSuccess ? 0 : cuda_fail(e, "tfs_online_counters");
+}
 
 int lr_reordered_launch(const gat_b200_layer* p, uint64_t n, const void* x, int x_dtype, int ldx, int policy,
                         uint16_t* xb, int ldb, float* left, float* right, cudaStream_t st) {
@@ -393,6 +493,14 @@ int gat_b200_lr_reordered(const gat_b200_layer* p, uint64_t n, const void* x, in
     clear_error();
     return lr_reordered_launch(p, n, x, x_dtype, ldx, policy, static_cast<uint16_t*>(x_bf16), ld_bf16, left, right,
                                as_stream(stream));
+}
+
+int gat_b200_tfs_online_counters(const gat_b200_graph* g, int heads, const float* left, const float* right,
+                                 int block, uint64_t* row_blocks, uint64_t* row_updates, uint64_t* row_rescales,
+                                 uint64_t* totals, void* stream) {
+    clear_error();
+    return online_counters_launch(g, heads, left, right, block, row_blocks, row_updates, row_rescales, totals,
+                                  as_stream(stream));
 }
 
 int gat_b200_tfs_aggregate(const gat_b200_graph* g, const gat_b200_layer* p, const void* x, int ldx,

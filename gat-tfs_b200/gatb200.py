@@ -89,6 +89,7 @@ SIGNATURES = [
                                          _vp, C.c_int, _vp, _vp, _vp]),
     ("gat_b200_tfs_layer", C.c_int, [_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                      _vp, _vp, _vp, _vp, _vp, _vp, C.c_int, C.c_int, _vp]),
+    ("gat_b200_tfs_online_counters", C.c_int, [_vp, C.c_int, _vp, _vp, C.c_int, _vp, _vp, _vp, _u64p, _vp]),
     ("gat_b200_check_device", C.c_int, []),
     ("gat_b200_device_alloc", C.c_int, [C.c_uint64, C.POINTER(_vp)]),
     ("gat_b200_device_free", C.c_int, [_vp]),
@@ -493,6 +494,18 @@ def peer_barrier(flags, rank: int, epoch: int, stream=None):
     """Cross-GPU barrier on `stream`; flags[j] = rank j's flag array."""
     arr = (_vp * len(flags))(*[int(v) for v in flags])
     _check(_lib.gat_b200_peer_barrier(arr, len(flags), rank, epoch & 0xFFFFFFFF, _stream(stream)))
+
+
+def tfs_online_counters(g: DeviceGraph, heads, left, right, block, row_blocks=None, row_updates=None,
+                        row_rescales=None, stream=None):
+    """icpp_online's exact counters: totals (blocks, max_updates, rescales,
+    rescale_events, neighbor_steps); per (row, head) arrays written to the
+    given device uint64 buffers."""
+    tot = np.zeros(5, np.uint64)
+    _check(_lib.gat_b200_tfs_online_counters(g.handle, heads, _ptr(left), _ptr(right), block, _ptr(row_blocks),
+                                             _ptr(row_updates), _ptr(row_rescales), _p(tot, _u64p),
+                                             _stream(stream)))
+    return tot
 
 
 def max_prescan(g: DeviceGraph, heads, left, right, mx, stream=None):

@@ -341,6 +341,21 @@ int gat_b200_device_free(void* ptr);
 int gat_b200_copy_to_device(void* dst, const void* src, uint64_t bytes);
 int gat_b200_copy_to_host(void* dst, const void* src, uint64_t bytes);
 
+/* icpp_online's exact counters (baseline/tfs_online/icpp_online.hpp:18-22) for
+ * the online TFS variant with neighbour blocks of `block`, from the layer's
+ * left/right ([n][heads], device): per (row, head) the blocks taken, the max
+ * updates and the rescales (row_* device [n][heads] uint64, each may be NULL),
+ * and totals (host, 5 values) = {blocks, max_updates, rescales,
+ * rescale_events, neighbor_steps}, rows batched 16 at a time in the degree
+ * order as the reference does. The reference's other counters follow:
+ * amx_calls = neighbor_steps * padded_in/32 * ceil(dim/16), executed_fma =
+ * neighbor_steps * 16 * padded_in * ceil(dim/16) * 16, rescaled feature
+ * elements = rescales * dim, spill/reload bytes = rescale_events *
+ * ceil(dim/16) * 1024. Synchronizes with `stream`. */
+int gat_b200_tfs_online_counters(const gat_b200_graph* g, int heads, const float* left, const float* right,
+                                 int block, uint64_t* row_blocks, uint64_t* row_updates, uint64_t* row_rescales,
+                                 uint64_t* totals, void* stream);
+
 /* Reports (and clears) a device-side failure recorded by an earlier kernel:
  * GAT_B200_ETIMEOUT if a bounded wait inside a kernel gave up. Synchronizes
  * with the device. */

@@ -202,6 +202,66 @@ void oracle_fp64_layer(uint64_t n, const uint64_t* row, const uint32_t* col,
     free(z); free(l); free(r);
 }
 
+void oracle_online_counters(uint64_t n, const uint64_t* row, const uint32_t* col, const uint32_t* perm,
+                            int heads, const float* left, const float* right, int block,
+                            uint64_t* row_blocks, uint64_t* row_updates, uint64_t* row_rescales,
+                            uint64_t* totals) {
+    uint64_t t_blocks = 0, t_updates = 0, t_rescales = 0, t_events = 0, t_steps = 0;
+    for (int h = 0; h < heads; ++h)
+        for (uint64_t base = 0; base < n; base += 16) {
+            const int batch = (int)(n - base < 16 ? n - base : 16);
+            uint32_t rows[16];
+            uint64_t deg[16], maxdeg = 0;
+            float run[16];
+            int seen[16];
+            for (int k = 0; k < batch; ++k) {
+                rows[k] = perm[base + k];
+                deg[k] = row[rows[k] + 1] - row[rows[k]];
+                maxdeg = deg[k] > maxdeg ? deg[k] : maxdeg;
+                run[k] = -INFINITY;
+                seen[k] = 0;
+                const size_t idx = (size_t)rows[k] * heads + h;
+                if (row_blocks) row_blocks[idx] = 0;
+                if (row_updates) row_updates[idx] = 0;
+                if (row_rescales) row_rescales[idx] = 0;
+            }
+            t_steps += maxdeg;
+            for (uint64_t begin = 0; begin < maxdeg; begin += (uint64_t)block) {
+                int changed = 0;
+                for (int k = 0; k < batch; ++k) {
+                    if (begin >= deg[k]) continue;
+                    const size_t idx = (size_t)rows[k] * heads + h;
+                    const float l = left[idx];
+                    uint64_t end = begin + (uint64_t)block;
+                    end = end < deg[k] ? end : deg[k];
+                    float bm = -INFINITY;
+                    for (uint64_t s = begin; s < end; ++s) {
+                        const float sc = leak(l + right[(size_t)col[row[rows[k]] + s] * heads + h]);
+                        bm = sc > bm ? sc : bm;
+                    }
+                    const float prev = run[k];
+                    run[k] = bm > run[k] ? bm : run[k];
+                    const int update = run[k] > prev;
+                    const int rescale = update && seen[k];  /* den > 0 once a block was taken */
+                    seen[k] = 1;
+                    ++t_blocks;
+                    t_updates += (uint64_t)update;
+                    t_rescales += (uint64_t)rescale;
+                    changed |= rescale;
+                    if (row_blocks) ++row_blocks[idx];
+                    if (row_updates) row_updates[idx] += (uint64_t)update;
+                    if (row_rescales) row_rescales[idx] += (uint64_t)rescale;
+                }
+                t_events += (uint64_t)changed;
+            }
+        }
+    totals[0] = t_blocks;
+    totals[1] = t_updates;
+    totals[2] = t_rescales;
+    totals[3] = t_events;
+    totals[4] = t_steps;  /* summed over heads, as the reference counts them */
+}
+
 void oracle_max_prescan(uint64_t n, const uint64_t* row, const uint32_t* col, int heads,
                         const float* left, const float* right, float* max) {
     /* baseline_standard.cpp:44-51: m = leaky(L + max_j R_j); 0 for empty rows. */

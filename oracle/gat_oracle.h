@@ -59,6 +59,21 @@ void oracle_b0_layer(uint64_t n, const uint64_t* row, const uint32_t* col,
                      float* z, float* left, float* right, float* max, float* den,
                      float* out);
 
+/* icpp_online's exact counters (baseline/tfs_online/icpp_online.cpp:50-116,
+ * 146-164, 229-233, 330-346). Rows go in batches of 16 consecutive entries of
+ * the degree order (perm), per head; a batch walks neighbour blocks of `block`
+ * up to its largest degree. For each row with degree above the block start:
+ * one block; the block maximum of leaky(L_i + R_j) raising the running maximum
+ * (strictly) is a max update; an update after the row's first block (den > 0)
+ * is a rescale. A batch block with any rescale is one rescale event; each
+ * neighbour step of a batch (its largest degree) is one neighbor step.
+ * row_blocks / row_updates / row_rescales ([n][heads]) may be NULL;
+ * totals = {blocks, max_updates, rescales, rescale_events, neighbor_steps}. */
+void oracle_online_counters(uint64_t n, const uint64_t* row, const uint32_t* col, const uint32_t* perm,
+                            int heads, const float* left, const float* right, int block,
+                            uint64_t* row_blocks, uint64_t* row_updates, uint64_t* row_rescales,
+                            uint64_t* totals);
+
 /* baseline/src/baseline_standard.cpp:44-51 (max_prescan). */
 void oracle_max_prescan(uint64_t n, const uint64_t* row, const uint32_t* col, int heads,
                         const float* left, const float* right, float* max);

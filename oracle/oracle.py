@@ -124,6 +124,27 @@ def b0_layer(row, col, x, w, al, ar, heads, dim, hidden, bf16=True, round_z=Fals
     return o
 
 
+_lib.oracle_online_counters.restype = None
+_lib.oracle_online_counters.argtypes = [C.c_uint64, _u64p, _u32p, _u32p, C.c_int, _f32p, _f32p, C.c_int, _u64p,
+                                        _u64p, _u64p, _u64p]
+
+
+def online_counters(row, col, perm, left, right, heads, block):
+    """icpp_online's exact counters (icpp_online.hpp:18-22): per (row, head)
+    blocks / max updates / rescales [n][heads] and the totals
+    (blocks, max_updates, rescales, rescale_events, neighbor_steps)."""
+    row = np.ascontiguousarray(row, np.uint64)
+    col = np.ascontiguousarray(col, np.uint32)
+    perm = np.ascontiguousarray(perm, np.uint32)
+    n = len(row) - 1
+    rb, ru, rr = (np.zeros((n, heads), np.uint64) for _ in range(3))
+    tot = np.zeros(5, np.uint64)
+    _lib.oracle_online_counters(n, _p(row, _u64p), _p(col, _u32p), _p(perm, _u32p), heads, _p(_f(left), _f32p),
+                                _p(_f(right), _f32p), block, _p(rb, _u64p), _p(ru, _u64p), _p(rr, _u64p),
+                                _p(tot, _u64p))
+    return rb, ru, rr, tot
+
+
 def max_prescan(row, col, left, right, heads):
     row = np.ascontiguousarray(row, np.uint64)
     col = np.ascontiguousarray(col, np.uint32)

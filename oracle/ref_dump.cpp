@@ -6,6 +6,7 @@
 //   ref_dump boundary OUTDIR          64 D/K/d cases of baseline/tests/boundaries.cpp
 //   ref_dump chain GRAPH WEIGHTS OUTDIR   three-layer chains on a GATBIN1 graph;
 //                                     WEIGHTS = GATWGT1 path or "seed:N" (random_model)
+//   ref_dump counters GRAPH OUTDIR    icpp_online's exact counters (blocks 4/16/64)
 //   ref_dump tfs OUTDIR               TFS aggregation variants (B1, icpp_online,
 //                                     icpp_block, icpp_heads_hybrid) on the
 //                                     boundary graphs, with their inputs
@@ -130,13 +131,22 @@ static int tfs(const std::string& out) {
                 dumpv(pre + "_b1_den.f32", w.den);
                 {
                     icpp_online::Workspace o;
-                    o.allocate(g, p);
+                    o.allocate(g, p, true);  // with the exact counters (icpp_online.hpp:18-22)
                     o.base.xbf = w.xbf; o.base.left = lbf; o.base.right = rbf;
                     icpp_online::Stats st;
-                    icpp_online::aggregate(g, p, q, s, o, 16, 16, st);
+                    icpp_online::aggregate(g, p, q, s, o, 16, 16, st, 0, true);
                     dumpv(pre + "_online16_out.f32", o.base.out);
                     dumpv(pre + "_online16_den.f32", o.base.den);
                     dumpv(pre + "_online16_max.f32", o.base.max);
+                    dumpv(pre + "_online16_rowblocks.u64", o.row_blocks);
+                    dumpv(pre + "_online16_rowupdates.u64", o.row_max_updates);
+                    dumpv(pre + "_online16_rowrescales.u64", o.row_rescales);
+                    const std::vector<uint64_t> totals = {st.blocks, st.max_updates, st.rescales, st.rescale_events,
+                                                          st.neighbor_steps, st.amx_calls, st.executed_fma,
+                                                          st.rescaled_feature_elements,
+                                                          st.rescaled_padded_feature_elements, st.spill_bytes,
+                                                          st.reload_bytes};
+                    dumpv(pre + "_online16_counters.u64", totals);
                 }
                 {
                     icpp_block::Workspace b;
@@ -163,6 +173,46 @@ static int tfs(const std::string& out) {
                 ++cases;
             }
     std::cout << "TFS_DUMP cases=" << cases << "\n";
+    return 0;
+}
+
+// icpp_online's exact counters (icpp_online.hpp:18-22) on a real graph, with
+// attention scores that rise with the source id so later neighbour blocks
+// raise the running maximum (the boundary graph's periodic sources never do).
+static int counters(const std::string& graph, const std::string& out) {
+    Graph g = load_graph(graph);
+    const int K = 8, d = 32;
+    Param p = boundary_params(g.din, K, d);
+    Prepared q = prepare(p, true, true, true);
+    Schedule s = degree_schedule(g);
+    std::vector<float> left(g.n * K), right(g.n * K);
+    for (uint64_t i = 0; i < g.n; ++i)
+        for (int h = 0; h < K; ++h) {
+            left[i * K + h] = std::sin(0.1f * float(i) + float(h));
+            right[i * K + h] = 0.004f * float(i) * float(h + 1) + std::sin(0.7f * float(i) + float(h));
+        }
+    dumpv(out + "/counters_left.f32", left);
+    dumpv(out + "/counters_right.f32", right);
+    for (int block : {4, 16, 64}) {
+        icpp_online::Workspace o;
+        o.allocate(g, p, true);
+        o.base.xbf.resize(g.x.size());
+        convert(g.x.data(), o.base.xbf.data(), g.x.size());
+        o.base.left = left;
+        o.base.right = right;
+        icpp_online::Stats st;
+        icpp_online::aggregate(g, p, q, s, o, block, 16, st, 0, true);
+        const std::string pre = out + "/counters_b" + std::to_string(block);
+        dumpv(pre + "_rowblocks.u64", o.row_blocks);
+        dumpv(pre + "_rowupdates.u64", o.row_max_updates);
+        dumpv(pre + "_rowrescales.u64", o.row_rescales);
+        const std::vector<uint64_t> totals = {st.blocks, st.max_updates, st.rescales, st.rescale_events,
+                                              st.neighbor_steps, st.amx_calls, st.executed_fma,
+                                              st.rescaled_feature_elements, st.rescaled_padded_feature_elements,
+                                              st.spill_bytes, st.reload_bytes};
+        dumpv(pre + "_totals.u64", totals);
+    }
+    std::cout << "COUNTERS_DUMP n=" << g.n << " e=" << g.e << "\n";
     return 0;
 }
 
@@ -232,7 +282,9 @@ int main(int argc, char** argv) {
         if (mode == "boundary" && argc == 3) return boundary(argv[2]);
         if (mode == "chain" && argc == 5) return chain(argv[2], argv[3], argv[4]);
         if (mode == "tfs" && argc == 3) return tfs(argv[2]);
-        std::cerr << "usage: ref_dump boundary OUTDIR | ref_dump chain GRAPH WEIGHTS OUTDIR | ref_dump tfs OUTDIR\n";
+        if (mode == "counters" && argc == 4) return counters(argv[2], argv[3]);
+        std::cerr << "usage: ref_dump boundary OUTDIR | ref_dump chain GRAPH WEIGHTS OUTDIR | ref_dump tfs OUTDIR | "
+                     "ref_dump counters GRAPH OUTDIR\n";
         return 2;
     } catch (const std::exception& e) {
         std::cerr << "FAIL " << e.what() << "\n";

@@ -25,6 +25,10 @@ sources in place by oracle/Makefile; nothing here is hand-written):
     icpp_heads_hybrid (block 32, threshold 16) outputs, with the inputs the
     reference computed for them (BF16- and FP32-policy L/R, prescan max, blr).
     The chain npz files also hold the tfs_bf16 path's three-layer logits.
+  * tfs_counters.npz: icpp_online's exact counters (icpp_online.hpp:18-22) on
+    smoke1024 with attention scores rising with the source id, for neighbour
+    blocks of 4, 16 and 64: per (row, head) blocks / max updates / rescales
+    and the Stats totals, with the L/R the reference used.
   * fixture_small_l1.gatfix (+ fixture_small.gatbin): a GATFIX1 fixed-p
     fixture written by the reference's own export-fixture mode
     (bench/main.cpp:103-116) for layer 1 of random_model(seed 11) on a small
@@ -122,6 +126,18 @@ def main():
         subprocess.run([str(DUMP), "chain", str(smoke), "seed:11", str(d)], check=True)
         manifest["smoke1024_seed11_gatwgt_sha256"] = sha256(d / "weights.gatwgt")
         np.savez_compressed(OUT / "smoke1024_seed11.npz", **chain_npz(d, 1024, 40))
+
+        # icpp_online's exact counters on smoke1024 (ref_dump counters)
+        d = tmp / "counters"
+        d.mkdir()
+        subprocess.run([str(DUMP), "counters", str(smoke), str(d)], check=True)
+        c = {"left": load(d, "counters_left.f32").reshape(1024, 8),
+             "right": load(d, "counters_right.f32").reshape(1024, 8)}
+        for b in (4, 16, 64):
+            for name in ("rowblocks", "rowupdates", "rowrescales"):
+                c[f"{name}_b{b}"] = np.fromfile(d / f"counters_b{b}_{name}.u64", np.uint64).reshape(1024, 8)
+            c[f"totals_b{b}"] = np.fromfile(d / f"counters_b{b}_totals.u64", np.uint64)
+        np.savez_compressed(OUT / "tfs_counters.npz", **c)
 
         # c1 from this repository's generator
         cfg = configs.make("c1")

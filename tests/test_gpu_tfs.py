@@ -328,3 +328,45 @@ def test_matched_attention_model(dev, golden):
         inp = O.finish(out, den, p.heads, p.dim, l < 2)
     assert rel_l2(inp, got) <= 3e-3
     assert rel_l2(ref["ref_logits"], got) <= 1e-2
+
+
+@pytest.mark.parametrize("block", [4, 16, 64])
+def test_online_counters_match_reference(dev, golden, block):
+    """gat_b200_tfs_online_counters against the reference's own icpp_online
+    counters (ref_dump counters on smoke1024; tests/golden/tfs_counters.npz):
+    per (row, head) blocks / max updates / rescales and the totals, bit-exact."""
+    import torch
+    from test_oracle_golden import smoke1024_graph
+    g = smoke1024_graph()
+    c = np.load(golden / "tfs_counters.npz")
+    dg = G.DeviceGraph(g.row, g.col)
+    n = g.n
+    bufs = [torch.zeros((n, 8), dtype=torch.int64, device="cuda") for _ in range(3)]
+    tot = G.tfs_online_counters(dg, 8, T(c["left"]), T(c["right"]), block, *bufs)
+    for buf, name in zip(bufs, ("rowblocks", "rowupdates", "rowrescales")):
+        assert np.array_equal(host(buf).astype(np.uint64), c[f"{name}_b{block}"]), name
+    assert np.array_equal(tot, c[f"totals_b{block}"][:5])
+    dg.close()
+
+
+@pytest.mark.parametrize("block", [3, 32])
+def test_online_counters_match_oracle_on_hubs(dev, block):
+    """Same counters on the hub graph (rows far above the segment length) against
+    the oracle restatement."""
+    import torch
+    row, col = hub_graph()
+    n = len(row) - 1
+    rng = np.random.default_rng(block)
+    K = 4
+    left = rng.standard_normal((n, K)).astype(np.float32)
+    right = (rng.standard_normal((n, K)) + np.arange(n)[:, None] * 1e-3).astype(np.float32)
+    dg = G.DeviceGraph(row, col)
+    bufs = [torch.zeros((n, K), dtype=torch.int64, device="cuda") for _ in range(3)]
+    tot = G.tfs_online_counters(dg, K, T(left), T(right), block, *bufs)
+    perm, _ = O.degree_schedule(row)
+    rb, ru, rr, otot = O.online_counters(row, col, perm, left, right, K, block)
+    for buf, want in zip(bufs, (rb, ru, rr)):
+        assert np.array_equal(host(buf).astype(np.uint64), want)
+    assert np.array_equal(tot, otot)
+    assert otot[2] > 0
+    dg.close()

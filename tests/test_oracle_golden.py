@@ -271,3 +271,28 @@ def test_fixture_validation_messages(tmp_path):
     d2[4, 1] *= 1.01
     G.write_fixture(bad, g.row, g.col, p, x, pw, d2)
     expect("fixture denominator mismatch", bad)
+
+
+@pytest.mark.parametrize("block", [4, 16, 64])
+def test_online_counters_match_reference(golden, block):
+    """icpp_online's exact counters (icpp_online.hpp:18-22) from the reference
+    (ref_dump counters, smoke1024, scores rising with the source id): per (row,
+    head) blocks, max updates and rescales, and the Stats totals, bit-exact.
+    The derived totals follow from them as the reference computes them."""
+    g = smoke1024_graph()
+    c = np.load(golden / "tfs_counters.npz")
+    perm, _ = O.degree_schedule(g.row)
+    rb, ru, rr, tot = O.online_counters(g.row, g.col, perm, c["left"], c["right"], 8, block)
+    assert np.array_equal(rb, c[f"rowblocks_b{block}"])
+    assert np.array_equal(ru, c[f"rowupdates_b{block}"])
+    assert np.array_equal(rr, c[f"rowrescales_b{block}"])
+    want = c[f"totals_b{block}"]
+    assert np.array_equal(tot, want[:5])
+    # amx_calls, executed_fma, rescaled (padded) feature elements, spill/reload bytes
+    dp, obs, d = 128, 2, 32  # padded_in of D=128, output blocks of d=32
+    steps, rescales, events = int(tot[4]), int(tot[2]), int(tot[3])
+    assert int(want[5]) == steps * (dp // 32) * obs
+    assert int(want[6]) == steps * 16 * dp * obs * 16
+    assert int(want[7]) == rescales * d and int(want[8]) == rescales * obs * 16
+    assert int(want[9]) == int(want[10]) == events * obs * 1024
+    assert rescales > 0 and events > 0  # the case exercises rescaling
