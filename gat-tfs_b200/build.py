@@ -5,7 +5,7 @@
 Each source compiles to an object under gat-tfs_b200/_build/ (in parallel), and
 the objects link into gat-tfs_b200/libgat_b200.so with the CUDA runtime linked
 statically, so the library needs only the NVIDIA driver at run time. The C++
-driver gat-tfs_b200/gat_b200_bench (cli/) links against it. A source
+drivers in cli/ (gat_b200_bench, gat_b200_tfs_online) link against it. A source
 is recompiled only when it or a header is newer than its object.
 """
 import argparse
@@ -20,8 +20,6 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 OUT = PKG / "_build"
 LIB = PKG / "libgat_b200.so"
-CLI_SRC = PKG / "cli" / "gat_b200_bench.cpp"
-CLI = PKG / "gat_b200_bench"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CUDA_FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-fopenmp,-Wall",
@@ -74,13 +72,17 @@ def build(verbose: bool = False) -> Path:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError("link failed\n" + r.stdout + r.stderr)
-    # the C++ driver (the reference's bench/main.cpp interface over the C ABI)
-    if not CLI.exists() or CLI.stat().st_mtime < max(LIB.stat().st_mtime, CLI_SRC.stat().st_mtime):
-        cmd = ["g++", "-O2", "-std=c++17", "-Wall", "-I" + str(ROOT / "include"), str(CLI_SRC), "-o", str(CLI),
-               "-L" + str(PKG), "-lgat_b200", "-Wl,-rpath,$ORIGIN"]
-        r = subprocess.run(cmd, capture_output=True, text=True)
-        if r.returncode != 0:
-            raise RuntimeError("driver build failed\n" + r.stdout + r.stderr)
+    # the C++ drivers over the C ABI (cli/*.cpp -> gat-tfs_b200/<name>): the
+    # reference's bench/main.cpp and tfs_online/main.cpp interfaces
+    hdr = max(h.stat().st_mtime for h in (ROOT / "include").glob("*.h*"))
+    for src in sorted((PKG / "cli").glob("*.cpp")):
+        exe = PKG / src.stem
+        if not exe.exists() or exe.stat().st_mtime < max(LIB.stat().st_mtime, src.stat().st_mtime, hdr):
+            cmd = ["g++", "-O2", "-std=c++17", "-Wall", "-I" + str(ROOT / "include"), str(src), "-o", str(exe),
+                   "-L" + str(PKG), "-lgat_b200", "-Wl,-rpath,$ORIGIN"]
+            r = subprocess.run(cmd, capture_output=True, text=True)
+            if r.returncode != 0:
+                raise RuntimeError(f"driver build failed: {src.name}\n" + r.stdout + r.stderr)
     return LIB
 
 

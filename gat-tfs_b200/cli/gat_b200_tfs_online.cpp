@@ -1,0 +1,429 @@
+// gat_b200_tfs_online: the reference's online-TFS experiment driver
+// (baseline/tfs_online/main.cpp) on the B200 library, through the C ABI.
+//
+//   gat_b200_tfs_online GRAPH THREADS WARMUPS REPEATS BLOCKS_CSV PROFILE_PERIOD | --smoke
+//
+// Same arguments and the same output lines, so its summaries read unchanged:
+//   CONFIG, STATIC per layer; CHECK lines (max/mean abs and relative L2 error,
+//   the 0.003 absolute gate) of every online block size against B1 with the
+//   prescan maximum on a common input, the FP64 oracle on selected complete
+//   neighbourhoods (ORACLE_COVERAGE, the global maximum-degree row included),
+//   and every path's three-layer chain against its B0 FP32 output; one JSON
+//   line per path, repeat and layer; PROFILE_IDENTITY, PROFILE and
+//   ONLINE_STATS per online block size and layer, the counters exact
+//   (gat_b200_tfs_online_counters: blocks, max updates, rescales, rescale
+//   events and neighbor steps; the others derived as the reference does);
+//   ICPP_ONLINE_COMPLETE, or ICPP_ONLINE_FAIL <message> and exit status 1.
+// Paths: B0_FP32, B0_BF16 (standard layer), B1_TFS_PREMAX (TFS, prescan max),
+// ICPP_TFS_ONLINE_B<b> (TFS with the running maximum per block of b). All
+// layers run on the current CUDA device with device-resident buffers; a layer
+// is timed on the host clock around the call and a device synchronisation.
+// THREADS is validated and reported; the per-worker AMX timers of the
+// reference's PROFILE line have no counterpart on the GPU.
+#include <algorithm>
+#include <array>
+#include <cmath>
+#include <cstring>
+#include <iomanip>
+#include <iostream>
+#include <set>
+#include <sstream>
+#include <string>
+#include <vector>
+
+#include "gat_b200.hpp"
+
+namespace gat = gat_b200;
+
+namespace {
+
+using gat::check;
+using gat::Clock;
+using gat::seconds;
+
+// The driver's own error metric (tfs_online/main.cpp:11-17).
+gat::Error difference(const std::vector<float>& a, const std::vector<float>& b) {
+    if (a.empty() || a.size() != b.size()) throw std::runtime_error("comparison shape");
+    double mx = 0, ab = 0, sq = 0, norm = 0;
+    bool bad = false;
+    for (size_t i = 0; i < a.size(); ++i) {
+        bad |= !std::isfinite(a[i]) || !std::isfinite(b[i]);
+        const double d = double(b[i]) - a[i];
+        mx = std::max(mx, std::abs(d));
+        ab += std::abs(d);
+        sq += d * d;
+        norm += double(a[i]) * a[i];
+    }
+    gat::Error e;
+    e.finite = !bad;
+    e.max_abs = mx;
+    e.mean_abs = ab / a.size();
+    e.relative_l2 = norm ? std::sqrt(sq / norm) : (sq ? INFINITY : 0);
+    if (bad) e.max_abs = e.mean_abs = e.relative_l2 = INFINITY;
+    return e;
+}
+
+void report(const std::string& path, int layer, const std::string& ref, const gat::Error& e) {
+    std::cout << std::setprecision(12) << "CHECK path=" << path << " layer=" << layer << " reference=" << ref
+              << " max_abs_error=" << e.max_abs << " mean_abs_error=" << e.mean_abs
+              << " relative_L2_error=" << e.relative_l2 << " finite=" << e.finite
+              << " original_abs_003_gate=" << (e.finite && e.max_abs <= .003 ? "PASS" : "FAIL")
+              << " task_accuracy=UNVERIFIED\n";
+    if (!e.finite) throw std::runtime_error("nonfinite comparison");
+}
+
+uint64_t fingerprint(const std::vector<float>& x) {
+    uint64_t out = 0;
+    for (size_t i = 0; i < x.size(); ++i) {
+        uint32_t bits;
+        std::memcpy(&bits, x.data() + i, 4);
+        uint64_t z = uint64_t(bits) ^ ((i + 1) * 0x9e3779b97f4a7c15ULL);
+        z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ULL;
+        out ^= z ^ (z >> 27);
+    }
+    return out;
+}
+
+struct Path {
+    std::string name;
+    int block = 0;  // > 0: online TFS with this block
+};
+
+// Device state of one (graph, model) and the layer of every path.
+struct Runner {
+    const gat::Graph& g;
+    const gat::Model& model;
+    gat::detail::GraphHandle graph;
+    gat_b200_layer* layer[3] = {nullptr, nullptr, nullptr};
+    gat::detail::DeviceBuffer x, xb, h, left, right, max, den, out[3], rb, ru, rr;
+    double prepare_ms[3] = {0, 0, 0};
+    Runner(const gat::Graph& g_, const gat::Model& m) : g(g_), model(m) {
+        graph.of(g);
+        for (int l = 0; l < 3; ++l) {
+            const auto t0 = Clock::now();
+            check(gat_b200_layer_create(m[l].in, m[l].heads, m[l].dim, m[l].w.data(), m[l].al.data(),
+                                        m[l].ar.data(), &layer[l]));
+            prepare_ms[l] = seconds(t0, Clock::now()) * 1000;
+        }
+    }
+    ~Runner() {
+        for (auto* p : layer) gat_b200_layer_destroy(p);
+    }
+    // One layer of `path` from FP32 device rows `in` [n][in] into out[l] (FP32 [n][width]); ms.
+    double run_layer(const Path& path, int l, const float* in, bool hidden) {
+        const gat::Param& p = model[l];
+        const uint64_t n = g.n;
+        const int K = p.heads, W = p.width();
+        float* o = static_cast<float*>(out[l].get(size_t(n) * W * 4));
+        float* L = static_cast<float*>(left.get(size_t(n) * K * 4));
+        float* R = static_cast<float*>(right.get(size_t(n) * K * 4));
+        const auto t0 = Clock::now();
+        if (path.name == "B0_FP32") {
+            void* hs = h.get(size_t(n) * gat_b200_padded_ld(W, GAT_B200_F32) * 4);
+            check(gat_b200_standard_layer(graph.g, layer[l], in, p.in, GAT_B200_PATH_STANDARD_FP32, hidden, hs, L, R, o,
+                                          GAT_B200_F32, W, nullptr));
+        } else if (path.name == "B0_BF16") {
+            const int ld = gat_b200_padded_ld(p.in, GAT_B200_BF16);
+            void* xs = xb.get(size_t(n) * ld * 2);
+            check(gat_b200_convert(n, p.in, in, p.in, static_cast<uint16_t*>(xs), ld, nullptr));
+            void* hs = h.get(size_t(n) * gat_b200_padded_ld(W, GAT_B200_BF16) * 2);
+            check(gat_b200_standard_layer(graph.g, layer[l], xs, ld, GAT_B200_PATH_STANDARD_BF16, hidden, hs, L, R, o,
+                                          GAT_B200_F32, W, nullptr));
+        } else {
+            const int ld = gat_b200_padded_ld(p.in, GAT_B200_BF16);
+            void* xs = xb.get(size_t(n) * ld * 2);
+            float* M = static_cast<float*>(max.get(size_t(n) * K * 4));
+            float* D = static_cast<float*>(den.get(size_t(n) * K * 4));
+            check(gat_b200_tfs_layer(graph.g, layer[l], in, GAT_B200_F32, p.in, hidden, GAT_B200_LR_FP32,
+                                     GAT_B200_TFS_EDGE, path.block, 1, xs, L, R, M, D, o, GAT_B200_F32, W, nullptr));
+        }
+        check(gat_b200_check_device());
+        return seconds(t0, Clock::now()) * 1000;
+    }
+    std::vector<float> output(int l) {
+        std::vector<float> v(size_t(g.n) * model[l].width());
+        out[l].download(v);
+        return v;
+    }
+    const float* upload_input(const std::vector<float>& v) { return x.upload(v); }
+    // Three layers from the graph's features; per-layer ms in ms[].
+    void chain(const Path& path, std::array<double, 3>& ms) {
+        const float* in = upload_input(g.x);
+        for (int l = 0; l < 3; ++l) {
+            ms[l] = run_layer(path, l, in, l < 2);
+            in = static_cast<const float*>(out[l].p);
+        }
+    }
+};
+
+// Diagnostics only (tfs_online/main.cpp:24-45): complete neighbourhoods of
+// selected rows, the global maximum-degree row included, in FP64 from the same
+// L/R as the online run; master H/W and BF16-quantized H/W (no pH rounding).
+void selected_oracle(const gat::Graph& g, const gat::Param& p, const std::vector<float>& input,
+                     const std::vector<float>& left, const std::vector<float>& right, const std::vector<float>& actual,
+                     int layer, const std::string& name) {
+    std::set<uint32_t> selected = {0, uint32_t(g.n / 2), uint32_t(g.n - 1)};
+    uint32_t largest = 0;
+    uint64_t degree = 0;
+    for (uint64_t i = 0; i < g.n; ++i)
+        if (g.row[i + 1] - g.row[i] > degree) {
+            degree = g.row[i + 1] - g.row[i];
+            largest = uint32_t(i);
+        }
+    selected.insert(largest);
+    for (uint64_t target : {16ULL, 32ULL, 64ULL, 128ULL})
+        for (uint64_t i = 0; i < g.n; ++i)
+            if (g.row[i + 1] - g.row[i] == target) {
+                selected.insert(uint32_t(i));
+                break;
+            }
+    const std::vector<float> xq = gat::quantized(input), wq = gat::quantized(p.w);
+    std::vector<float> master, quantized, got;
+    uint64_t edges = 0;
+    for (uint32_t r : selected) {
+        edges += g.row[r + 1] - g.row[r];
+        for (int h = 0; h < p.heads; ++h) {
+            double m = -INFINITY, den = 0;
+            std::vector<double> u(p.in, 0.0), uq(p.in, 0.0);
+            for (uint64_t e = g.row[r]; e < g.row[r + 1]; ++e)
+                m = std::max(m, double(gat::leak(left[size_t(r) * p.heads + h] + right[size_t(g.col[e]) * p.heads + h])));
+            for (uint64_t e = g.row[r]; e < g.row[r + 1]; ++e) {
+                const uint32_t s = g.col[e];
+                const float sc = gat::leak(left[size_t(r) * p.heads + h] + right[size_t(s) * p.heads + h]);
+                const double wgt = std::exp(double(sc) - m);
+                den += wgt;
+                for (int k = 0; k < p.in; ++k) {
+                    u[k] += wgt * double(input[size_t(s) * p.in + k]);
+                    uq[k] += wgt * double(xq[size_t(s) * p.in + k]);
+                }
+            }
+            for (int d = 0; d < p.dim; ++d) {
+                double a = 0, b = 0;
+                for (int k = 0; k < p.in; ++k) {
+                    const size_t idx = size_t(k) * p.width() + h * p.dim + d;
+                    a += u[k] * double(p.w[idx]);
+                    b += uq[k] * double(wq[idx]);
+                }
+                master.push_back(float(den > 0 ? a / den : 0));
+                quantized.push_back(float(den > 0 ? b / den : 0));
+                got.push_back(actual[size_t(r) * p.width() + h * p.dim + d]);
+            }
+        }
+    }
+    std::cout << "ORACLE_COVERAGE layer=" << layer << " rows=" << selected.size() << " edges=" << edges
+              << " global_max_degree_node=" << largest << " global_max_degree=" << degree
+              << " global_max_degree_included=true complete_neighborhoods=true activation=false"
+              << " outputs_rounded_to_fp32=true\n";
+    report(name, layer, "FP64_master_same_LR_selected_rows", difference(master, got));
+    report(name, layer, "FP64_quantized_H_W_same_LR_without_pH_quantization", difference(quantized, got));
+}
+
+// ONLINE_STATS (tfs_online/main.cpp:52-66) from the exact counters.
+void online_stats(Runner& run, int l, int block) {
+    const gat::Param& p = run.model[l];
+    const gat::Graph& g = run.g;
+    const size_t nk = size_t(g.n) * p.heads;
+    uint64_t* rb = static_cast<uint64_t*>(run.rb.get(nk * 8));
+    uint64_t* ru = static_cast<uint64_t*>(run.ru.get(nk * 8));
+    uint64_t* rr = static_cast<uint64_t*>(run.rr.get(nk * 8));
+    uint64_t tot[5];
+    check(gat_b200_tfs_online_counters(run.graph.g, p.heads, static_cast<const float*>(run.left.p),
+                                       static_cast<const float*>(run.right.p), block, rb, ru, rr, tot, nullptr));
+    std::vector<uint64_t> hb(nk), hr(nk), hu(nk);
+    check(gat_b200_copy_to_host(hb.data(), rb, nk * 8));
+    check(gat_b200_copy_to_host(hu.data(), ru, nk * 8));
+    check(gat_b200_copy_to_host(hr.data(), rr, nk * 8));
+    uint64_t nb = 0, nu = 0, nr = 0;
+    std::vector<double> ratios(nk);
+    for (size_t i = 0; i < nk; ++i) {
+        nb += hb[i];
+        nu += hu[i];
+        nr += hr[i];
+        ratios[i] = hb[i] ? double(hr[i]) / hb[i] : 0;
+    }
+    if (nb != tot[0] || nu != tot[1] || nr != tot[2]) throw std::runtime_error("row/worker counter mismatch");
+    std::sort(ratios.begin(), ratios.end());
+    auto pct = [&](double f) {
+        return ratios.empty() ? 0 : ratios[std::min(ratios.size() - 1, size_t(std::ceil(f * ratios.size())) - 1)];
+    };
+    const uint64_t obs = uint64_t(p.dim + 15) / 16, dp = uint64_t(p.in + 31) / 32 * 32;
+    const uint64_t events = tot[3], steps = tot[4], padded = nr * obs * 16;
+    std::cout << std::setprecision(12) << "ONLINE_STATS layer=" << l + 1 << " block=" << block << " heads=" << p.heads
+              << " D=" << p.in << " d=" << p.dim << " blocks=" << nb << " max_updates_including_initial=" << nu
+              << " rescales=" << nr << " rescale_per_block=" << (nb ? double(nr) / nb : 0) << " P50=" << pct(.5)
+              << " P90=" << pct(.9) << " P95=" << pct(.95) << " P99=" << pct(.99)
+              << " rescaled_feature_elements=" << nr * uint64_t(p.dim) << " expected_elements=" << nr * uint64_t(p.dim)
+              << " rescaled_padded_feature_elements=" << padded << " rescale_events=" << events
+              << " spill_bytes=" << events * obs * 1024 << " reload_bytes=" << events * obs * 1024
+              << " row_scale_load_bytes=" << padded * 4 << " row_scale_store_bytes=" << padded * 4
+              << " amx_calls=" << steps * (dp / 32) * obs << " neighbor_steps=" << steps
+              << " executed_fma=" << steps * 16 * dp * obs * 16
+              << " total_tiles=" << uint64_t(p.heads) * ((g.n + 15) / 16) << "\n";
+}
+
+gat::Graph boundary_graph(int D) {  // baseline/tests/boundaries.cpp:10-13
+    const int deg[13] = {0, 1, 2, 15, 16, 17, 31, 32, 33, 63, 64, 65, 129};
+    gat::Graph g;
+    g.n = 35;
+    g.din = D;
+    g.classes = 4;
+    g.row.push_back(0);
+    for (int i = 0; i < 35; ++i) {
+        for (int e = 0; e < deg[i % 13]; ++e) g.col.push_back(uint32_t((i * 3 + e * 7) % 35));
+        g.row.push_back(g.col.size());
+    }
+    g.e = g.col.size();
+    g.x.resize(size_t(35) * D);
+    for (size_t i = 0; i < g.x.size(); ++i) g.x[i] = 0.5f * std::sin(0.17f * float(i));
+    return g;
+}
+
+// --smoke: the online variants against B1 with the prescan maximum on the
+// boundary graph (they differ only through the rescale roundings).
+int smoke() {
+    int cases = 0;
+    for (int D : {17, 128})
+        for (int K : {1, 8})
+            for (int d : {7, 32}) {
+                gat::Graph g = boundary_graph(D);
+                gat::Model m(3);
+                gat::Model full = gat::random_model(D, d, 11);
+                m[0] = full[0];
+                m[0].heads = K;
+                m[0].dim = d;
+                m[0].w.resize(size_t(D) * K * d);
+                m[0].al.resize(size_t(K) * d);
+                m[0].ar.resize(size_t(K) * d);
+                for (size_t i = 0; i < m[0].w.size(); ++i) m[0].w[i] = std::cos(0.31f * float(i)) / std::sqrt(float(D));
+                for (size_t i = 0; i < m[0].al.size(); ++i) {
+                    m[0].al[i] = std::sin(0.23f * float(i)) / std::sqrt(float(d));
+                    m[0].ar[i] = std::cos(0.19f * float(i)) / std::sqrt(float(d));
+                }
+                m[1] = m[0];
+                m[2] = m[0];
+                Runner run(g, m);
+                const float* in = run.upload_input(g.x);
+                run.run_layer({"B1_TFS_PREMAX", 0}, 0, in, false);
+                const std::vector<float> b1 = run.output(0);
+                for (int block : {16, 32, 64}) {
+                    run.run_layer({"ICPP_TFS_ONLINE_B" + std::to_string(block), block}, 0, in, false);
+                    const gat::Error e = difference(b1, run.output(0));
+                    if (!e.finite || e.relative_l2 > 1e-4 || e.max_abs > 1e-4)
+                        throw std::runtime_error("smoke: online block " + std::to_string(block) + " differs from B1");
+                }
+                ++cases;
+            }
+    std::cout << "SMOKE PASS cases=" << cases << " blocks=16,32,64 online_vs_B1_premax\n";
+    return 0;
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+    try {
+        if (argc == 2 && std::string(argv[1]) == "--smoke") return smoke();
+        if (argc != 7)
+            throw std::runtime_error("usage: icpp_online GRAPH THREADS WARMUPS REPEATS BLOCKS_CSV PROFILE_PERIOD | --smoke");
+        const int threads = std::stoi(argv[2]), warm = std::stoi(argv[3]), reps = std::stoi(argv[4]),
+                  period = std::stoi(argv[6]);
+        if (threads < 1 || warm < 0 || reps < 1 || period < 1) throw std::runtime_error("invalid config");
+        std::vector<Path> paths = {{"B0_FP32", 0}, {"B0_BF16", 0}, {"B1_TFS_PREMAX", 0}};
+        std::stringstream csv(argv[5]);
+        std::string word;
+        while (std::getline(csv, word, ',')) {
+            const int block = std::stoi(word);
+            if (block < 1 || block > 64) throw std::runtime_error("invalid block");
+            paths.push_back({"ICPP_TFS_ONLINE_B" + std::to_string(block), block});
+        }
+        if (paths.size() == 3) throw std::runtime_error("no Online path");
+        const gat::Graph g = gat::load_graph(argv[1]);
+        const gat::Model model = gat::random_model(g.din, g.classes, 11);
+        const gat::Schedule sched = gat::degree_schedule(g);
+        Runner run(g, model);
+        std::cout << std::setprecision(12) << "CONFIG N=" << g.n << " E=" << g.e << " Din=" << g.din << " C=" << g.classes
+                  << " threads=" << threads << " seed=11 untrained=true warmups=" << warm << " repeats=" << reps
+                  << " degree_sort_ms=" << sched.degree_sort_s * 1000
+                  << " panel=64 tile_rows=16 LR_policy=fp32 online_max_prescan=false output_accumulator=FP32_registers"
+                  << " output_rescale_dim=d task_accuracy=UNVERIFIED performance=EXPLORATORY device=sm_100a\n";
+        // B0 FP32 reference chain
+        std::array<std::vector<float>, 3> ref;
+        {
+            std::array<double, 3> ms{};
+            run.chain(paths[0], ms);
+            for (int l = 0; l < 3; ++l) ref[l] = run.output(l);
+        }
+        for (int l = 0; l < 3; ++l)
+            std::cout << "STATIC layer=" << l + 1 << " prepare_ms=" << run.prepare_ms[l]
+                      << " online_workspace_bytes=" << g.n * size_t(model[l].heads) * 16
+                      << " global_Z_bytes=0 global_edge_score_bytes=0 global_alpha_bytes=0\n";
+        // common-input controls, outside the three-layer timer
+        for (int l = 0; l < 3; ++l) {
+            const std::vector<float>& input = l ? ref[l - 1] : g.x;
+            const float* in = run.upload_input(input);
+            run.run_layer(paths[2], l, in, false);
+            const std::vector<float> b1 = run.output(l);
+            for (const auto& path : paths)
+                if (path.block) {
+                    run.run_layer(path, l, in, false);
+                    const std::vector<float> got = run.output(l);
+                    report(path.name, l + 1, "B1_PREMAX_same_input_same_LR", difference(b1, got));
+                    if (path.block == paths.back().block) {
+                        std::vector<float> L(size_t(g.n) * model[l].heads), R(L.size());
+                        run.left.download(L);
+                        run.right.download(R);
+                        selected_oracle(g, model[l], input, L, R, got, l + 1, path.name);
+                    }
+                }
+        }
+        // timed three-layer chains
+        for (int rep = -warm - 1; rep < reps; ++rep) {
+            auto order = paths;
+            if (rep >= 0 && rep % 2) std::reverse(order.begin(), order.end());
+            for (const auto& path : order) {
+                std::array<double, 3> ms{};
+                const auto begin = Clock::now();
+                run.chain(path, ms);
+                const double e2e = seconds(begin, Clock::now()) * 1000;
+                if (rep == -warm - 1)
+                    for (int l = 0; l < 3; ++l)
+                        report(path.name, l + 1, "B0_FP32_own_output_3layer", difference(ref[l], run.output(l)));
+                if (rep >= 0) {
+                    gat::require_finite(run.output(2), path.name);
+                    for (int l = 0; l < 3; ++l)
+                        std::cout << "{\"path\":\"" << path.name << "\",\"rep\":" << rep << ",\"layer\":" << l + 1
+                                  << ",\"e2e_ms\":" << e2e << ",\"layer_ms\":" << ms[l]
+                                  << ",\"projection_ms\":0,\"conversion_ms\":0,\"lr_ms\":0,\"max_prescan_ms\":0"
+                                  << ",\"kernel_ms\":" << ms[l] << ",\"normalization_ms\":0,\"activation_ms\":0"
+                                  << ",\"block\":" << path.block << "}\n";
+                }
+            }
+        }
+        // profile identity and the exact counters of every online block size
+        for (const auto& path : paths)
+            if (path.block) {
+                std::array<double, 3> ms{};
+                run.chain(path, ms);
+                std::array<uint64_t, 3> hashes{};
+                for (int l = 0; l < 3; ++l) hashes[l] = fingerprint(run.output(l));
+                const float* in = run.upload_input(g.x);
+                for (int l = 0; l < 3; ++l) {
+                    const double t = run.run_layer(path, l, in, l < 2);
+                    in = static_cast<const float*>(run.out[l].p);
+                    const bool equal = hashes[l] == fingerprint(run.output(l));
+                    std::cout << "PROFILE_IDENTITY layer=" << l + 1 << " block=" << path.block
+                              << " bit_fingerprint_equal=" << equal << "\n";
+                    if (!equal) throw std::runtime_error("profile output changed");
+                    std::cout << std::setprecision(12) << "PROFILE path=ICPP_TFS_ONLINE_B" << path.block
+                              << " layer=" << l + 1 << " layer_wall_ms=" << t << " kernel_wall_ms=" << t
+                              << " sampled_tiles=0 worker_times=unavailable_on_gpu profile_period=" << period << "\n";
+                    online_stats(run, l, path.block);
+                }
+            }
+        std::cout << "ICPP_ONLINE_COMPLETE architecture=B200_TFS_online_running_max master_gate=SEE_PER_LAYER_ERRORS"
+                     " task_accuracy=UNVERIFIED performance=EXPLORATORY\n";
+        return 0;
+    } catch (const std::exception& e) {
+        std::cerr << "ICPP_ONLINE_FAIL " << e.what() << "\n";
+        return 1;
+    }
+}

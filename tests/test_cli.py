@@ -68,3 +68,47 @@ def test_cli_correctness_gate():
     r = run("--graph", str(GOLDEN / "fixture_small.gatbin"), "--seed", "11", "--mode", "correctness",
             "--max-abs", "1e-9", "--rel-l2", "1e-9")
     assert r.returncode == 1 and "accuracy_gate=FAIL" in r.stdout
+
+
+# ---- gat_b200_tfs_online: the reference's tfs_online/main.cpp interface -------
+ONLINE = ROOT / "gat-tfs_b200" / "gat_b200_tfs_online"
+
+
+def run_online(*args, timeout=300):
+    if not ONLINE.exists():
+        subprocess.run(["python", str(ROOT / "gat-tfs_b200" / "build.py")], check=True)
+    return subprocess.run([str(ONLINE), *args], capture_output=True, text=True, timeout=timeout)
+
+
+def test_tfs_online_argument_errors():
+    r = run_online("a", "b")
+    assert r.returncode == 1 and "ICPP_ONLINE_FAIL usage: icpp_online GRAPH THREADS" in r.stderr
+    r = run_online("g", "0", "1", "1", "16", "1")
+    assert r.returncode == 1 and "ICPP_ONLINE_FAIL invalid config" in r.stderr
+    r = run_online("g", "2", "1", "1", "16,65", "1")
+    assert r.returncode == 1 and "ICPP_ONLINE_FAIL invalid block" in r.stderr
+    r = run_online("g", "2", "1", "1", "", "1")
+    assert r.returncode == 1 and "ICPP_ONLINE_FAIL no Online path" in r.stderr
+
+
+@pytest.mark.gpu
+def test_tfs_online_smoke_and_report():
+    r = run_online("--smoke")
+    assert r.returncode == 0 and "SMOKE PASS cases=8" in r.stdout, r.stdout + r.stderr
+    r = run_online(str(GOLDEN / "fixture_small.gatbin"), "4", "0", "1", "16,64", "1")
+    assert r.returncode == 0, r.stdout + r.stderr
+    lines = r.stdout.splitlines()
+    tags = [ln.split(" ", 1)[0] for ln in lines]
+    assert tags.count("CONFIG") == 1 and tags.count("STATIC") == 3
+    assert tags.count("CHECK") == 3 * 4 + 5 * 3  # common-input controls + every path's chain
+    assert tags.count("ORACLE_COVERAGE") == 3
+    assert tags.count("PROFILE_IDENTITY") == 6 and tags.count("ONLINE_STATS") == 6
+    assert all("bit_fingerprint_equal=1" in ln for ln in lines if ln.startswith("PROFILE_IDENTITY"))
+    recs = [json.loads(ln) for ln in lines if ln.startswith("{")]
+    assert len(recs) == 5 * 3 and {r_["path"] for r_ in recs} == {"B0_FP32", "B0_BF16", "B1_TFS_PREMAX",
+                                                                 "ICPP_TFS_ONLINE_B16", "ICPP_TFS_ONLINE_B64"}
+    # online vs B1 on a common input: only rescale roundings apart
+    for ln in lines:
+        if ln.startswith("CHECK") and "B1_PREMAX_same_input_same_LR" in ln:
+            assert "original_abs_003_gate=PASS" in ln, ln
+    assert lines[-1].startswith("ICPP_ONLINE_COMPLETE")
