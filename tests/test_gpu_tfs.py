@@ -370,3 +370,31 @@ def test_online_counters_match_oracle_on_hubs(dev, block):
     assert np.array_equal(tot, otot)
     assert otot[2] > 0
     dg.close()
+
+
+@pytest.mark.parametrize("block", [16, 32, 64])
+def test_online_equals_b1_when_scores_are_equal(dev, block):
+    """The reference's all-equal-scores lifecycle check (tfs_online/checks.cpp:452-520):
+    with every score equal the running maximum never rises after a row's first block, so
+    the online variant takes the same weights as B1 with the prescan maximum, bit for bit;
+    the counters show no rescale."""
+    import torch
+    rng = np.random.default_rng(block)
+    row, col = hub_graph(n=600, hubs=(500, 300), seed=4)
+    n = len(row) - 1
+    K, d, D = 8, 32, 64
+    p = random_layer(rng, D, K, d)
+    layer = G.DeviceLayer(p)
+    g = G.DeviceGraph(row, col)
+    x = rng.standard_normal((n, D)).astype(np.float32)
+    ld = G.padded_ld(D, G.BF16)
+    L = np.full((n, K), 0.25, np.float32)
+    R = np.full((n, K), -0.75, np.float32)
+    mx = O.max_prescan(row, col, L, R, K)
+    b1, b1d, _ = _run_tfs(g, layer, _bf16_table(x, ld), ld, L, R, n, K, d, mx=mx)
+    on, ond, _ = _run_tfs(g, layer, _bf16_table(x, ld), ld, L, R, n, K, d, block=block)
+    assert np.array_equal(on, b1) and np.array_equal(ond, b1d)
+    tot = G.tfs_online_counters(g, K, T(L), T(R), block)
+    assert int(tot[2]) == 0 and int(tot[3]) == 0
+    layer.close()
+    g.close()
