@@ -159,3 +159,35 @@ def test_partitioned_model_argument_checks():
         gdist.PartitionedModel(g.row, g.col, params, 0, 9, exchange="p2p")
     with pytest.raises(ValueError, match="up to 8 ranks"):
         gdist.PartitionedModel(g.row, g.col, params, 0, 9, exchange="dma")
+
+
+def _rank_fails(rank, world, port, q):
+    """Rank 1 dies before the layer exchange (it raises after joining); rank 0
+    must learn of it from the process group's deadline, not hang."""
+    import datetime
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    tdist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        raise RuntimeError("injected rank failure before the exchange")
+    t0 = time.time()
+    try:
+        zs = [torch.zeros(4) for _ in range(world)]
+        tdist.all_gather(zs, torch.ones(4))
+        q.put(("no error", time.time() - t0))
+    except Exception as e:  # the exchange of a dead peer fails within the deadline
+        q.put((type(e).__name__, time.time() - t0))
+
+
+def test_failed_rank_is_detected_by_the_exchange_deadline():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_fails, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    kind, waited = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+    assert kind != "no error" and waited < 60, (kind, waited)
+    assert procs[1].exitcode != 0 and procs[0].exitcode == 0
