@@ -6,6 +6,8 @@
 #include <string>
 #include <vector>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "device.cuh"
 #include "graph.cuh"
 
@@ -106,7 +108,17 @@ namespace {
 // Stage boundaries of one forward: h2d, convert, (projection, aggregation) x 3, d2h.
 constexpr int kStages = 9;
 constexpr int kStageEvents = kStages + 1;
+// Stage boundaries of the forward: per-stage CUDA events when timing is on, and
+// NVTX ranges (host side, one per stage inside a "gat_b200 forward" range) for
+// Nsight timelines; NVTX calls cost nothing without a tool attached.
+constexpr const char* kStageNames[kStages] = {"h2d",          "convert",      "projection L1",
+                                              "aggregation L1", "projection L2", "aggregation L2",
+                                              "projection L3", "aggregation L3", "d2h"};
 inline void mark(gat_b200_model* m, int stage, cudaStream_t st) {
+    if (stage == 0) nvtxRangePushA("gat_b200 forward");
+    if (stage > 0) nvtxRangePop();
+    if (stage < kStages) nvtxRangePushA(kStageNames[stage]);
+    if (stage == kStages) nvtxRangePop();
     if (!m->timing_steps) return;
     const size_t set = size_t(m->forwards % uint64_t(m->timing_steps));
     cudaEventRecord(m->events[set * kStageEvents + stage], st);
