@@ -266,7 +266,10 @@ int gat_b200_aggregate_fused(const gat_b200_graph* g, int heads, int dim, const 
  * looks up the array's device address (cudaGetSymbolAddress) with that device
  * current; make that first call before any stream capture. All calls share the
  * array: calls whose kernels can overlap on the GPU (other streams, other host
- * threads) race on it and must be serialized by the caller. Arguments and
+ * threads) race on it and must be serialized by the caller. The CSR is read as
+ * given: it must be a valid destination-row CSR (row[0] = 0, row[n] = e,
+ * non-decreasing, every source id < n), which gat_b200_validate_csr checks on a
+ * host copy; gat_b200_graph_create validates on the device. Arguments and
  * output as in gat_b200_aggregate_fused. */
 int gat_b200_aggregate_fused_noalloc(uint64_t n, uint64_t e, const uint64_t* row,
                                      const uint32_t* col, int heads, int dim, const void* h,
