@@ -418,6 +418,10 @@ inline void lr_reordered(const Graph& g, const Param& p, const Prepared& q, cons
     w.lr_from_projection = false;
 }
 inline void max_prescan(const Graph& g, const Param& p, Workspace& w) {
+    const size_t nk = checked(g.n, uint64_t(p.heads));
+    detail::need(w.left, nk, "left");
+    detail::need(w.right, nk, "right");
+    detail::need(w.max, nk, "max");
     const float* l = w.d_left->upload(w.left);
     const float* r = w.d_right->upload(w.right);
     float* m = static_cast<float*>(w.d_max->get(w.max.size() * 4));
@@ -429,6 +433,13 @@ inline void max_prescan(const Graph& g, const Param& p, Workspace& w) {
 inline void standard_aggregate(const Graph& g, const Param& p, Workspace& w, const float* fixed_p = nullptr,
                                const float* fixed_den = nullptr, Times* times = nullptr) {
     auto t0 = Clock::now();
+    const size_t nk = checked(g.n, uint64_t(p.heads)), nw = checked(g.n, uint64_t(p.width()));
+    detail::need(w.z, nw, "z");
+    detail::need(w.left, nk, "left");
+    detail::need(w.right, nk, "right");
+    detail::need(w.out, nw, "out");
+    detail::need(w.den, nk, "den");
+    detail::need(w.max, nk, "max");
     const int ldz = detail::padded(p.width(), GAT_B200_F32);
     std::vector<float> zp(size_t(g.n) * ldz, 0.f);
     for (uint64_t i = 0; i < g.n; ++i)
@@ -455,6 +466,8 @@ inline void standard_aggregate(const Graph& g, const Param& p, Workspace& w, con
 }
 inline void finish(const Graph& g, const Param& p, Workspace& w, bool hidden, Times& t) {
     auto t0 = Clock::now();
+    detail::need(w.out, checked(g.n, uint64_t(p.width())), "out");
+    detail::need(w.den, checked(g.n, uint64_t(p.heads)), "den");
     float* o = w.d_out->upload(w.out);
     const float* dn = w.d_den->upload(w.den);
     check(gat_b200_finish(g.n, p.heads, p.dim, dn, hidden, o, p.width(), nullptr));
@@ -468,6 +481,9 @@ inline void standard_layer(const Graph& g, const Param& p, const Prepared& q, co
     (void)lr_policy;
     auto t0 = Clock::now();
     if (input.size() != checked(g.n, uint64_t(p.in))) throw std::runtime_error("layer input size mismatch");
+    detail::need(w.out, checked(g.n, uint64_t(p.width())), "out");
+    detail::need(w.left, checked(g.n, uint64_t(p.heads)), "left");
+    detail::need(w.right, checked(g.n, uint64_t(p.heads)), "right");
     const void* x;
     int ldx = p.in;
     if (fp32)
@@ -496,6 +512,13 @@ inline void ref_layer(const Graph& g, const Param& p, const std::vector<float>& 
 inline void tfs_aggregate(const Graph& g, const Param& p, const Prepared& q, const Schedule&, Workspace& w, int,
                           Times& t, const float* fixed_p = nullptr, const float* fixed_den = nullptr) {
     auto t0 = Clock::now();
+    const size_t nk = checked(g.n, uint64_t(p.heads));
+    if (w.xbf.size() != checked(g.n, uint64_t(p.in))) throw std::runtime_error("workspace xbf has the wrong size");
+    detail::need(w.left, nk, "left");
+    detail::need(w.right, nk, "right");
+    if (!fixed_p) detail::need(w.max, nk, "max");
+    detail::need(w.out, checked(g.n, uint64_t(p.width())), "out");
+    detail::need(w.den, nk, "den");
     const int ldb = detail::padded(p.in, GAT_B200_BF16);
     std::vector<BF16> xp(size_t(g.n) * ldb, 0);
     for (uint64_t i = 0; i < g.n; ++i)

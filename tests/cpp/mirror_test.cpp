@@ -126,6 +126,9 @@ void host_checks(const std::string& dir) {
     rejects("bad_heads", "invalid parameter shape", [&] { auto b = p; b.heads = 9; b.validate(); });
     rejects("error_size_mismatch", "size mismatch", [&] { gat::errors({1}, {1, 2}); });
     rejects("allocation_overflow", "size overflow", [&] { gat::checked(UINT64_MAX, 2); });
+    // a workspace not allocated for the call's graph and path is refused before any device work
+    rejects("workspace_mismatch", "workspace z has the wrong size", [&] { gat::Workspace w; gat::standard_aggregate(g, p, w); });
+    rejects("workspace_mismatch", "workspace out has the wrong size", [&] { gat::Workspace w; gat::Times t; gat::finish(g, p, w, true, t); });
     expect(!gat::errors({1}, {NAN}).finite && !gat::errors({1}, {INFINITY}).finite, "nonfinite comparison passed");
     // RNE ties and tails (boundaries.cpp:25-26)
     expect(gat::rne(1.0f + 1.0f / 256) == 0x3f80, "tie to even (down)");
