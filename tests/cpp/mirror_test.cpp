@@ -5,6 +5,8 @@
 //   mirror_test          host-side checks (no GPU): validation messages, RNE
 //                        ties, error metrics, file round trips
 //   mirror_test --gpu    the layer functions on the current CUDA device
+//   mirror_test --gpu-online  the online TFS variants (icpp_online, icpp_block,
+//                        icpp_heads_hybrid) on the current CUDA device
 // Prints "MIRROR PASS ..." lines; exits 1 with "MIRROR FAIL <what>" otherwise.
 #include <cmath>
 #include <cstdio>
@@ -145,6 +147,41 @@ void host_checks(const std::string& dir) {
     gat::Model m2 = gat::load_model(dir + "/m.gatwgt", 17, 4);
     for (int l = 0; l < 3; ++l) expect(m2[l].w == m[l].w && m2[l].al == m[l].al && m2[l].ar == m[l].ar, "GATWGT round trip");
     rejects("missing_graph", "cannot open graph", [&] { gat::load_graph(dir + "/missing.gatbin"); });
+    // online TFS variants (icpp_online.cpp:265-290, icpp_block.cpp:244-270,
+    // icpp_heads_hybrid.cpp:35-41,296-316): argument checks before device work
+    {
+        gat::Prepared q0;
+        gat::Schedule s0;
+        gat::icpp_online::Workspace wo;
+        gat::icpp_online::Stats so;
+        rejects("online_block", "ICPP Online block must be in [1,64]",
+                [&] { gat::icpp_online::aggregate(g, p, q0, s0, wo, 0, 16, so); });
+        rejects("online_panel", "ICPP Online panel must be a multiple of 16",
+                [&] { gat::icpp_online::aggregate(g, p, q0, s0, wo, 16, 24, so); });
+        rejects("online_period", "ICPP Online profile period must be nonnegative",
+                [&] { gat::icpp_online::aggregate(g, p, q0, s0, wo, 16, 16, so, -1); });
+        rejects("online_unallocated", "ICPP Online workspace or parameter shape mismatch",
+                [&] { gat::icpp_online::aggregate(g, p, q0, s0, wo, 16, 16, so); });
+        gat::icpp_block::Workspace wk;
+        gat::icpp_block::Stats sk;
+        rejects("block_size", "ICPP block size must be in [1,64]",
+                [&] { gat::icpp_block::aggregate(g, p, q0, s0, wk, 65, 16, sk); });
+        gat::icpp_heads_hybrid::Workspace wh;
+        gat::icpp_heads_hybrid::Stats sh;
+        rejects("hybrid_threshold", "ICPP heads hybrid threshold must be in [1,33]",
+                [&] { gat::icpp_heads_hybrid::aggregate(g, p, q0, s0, wh, 16, 16, sh, 0, false, 34); });
+        rejects("hybrid_block", "optimized ICPP heads block must be 16 or 32",
+                [&] { gat::icpp_heads_hybrid::aggregate(g, p, q0, s0, wh, 8, 16, sh); });
+        const gat::Param p2 = params(17, 2, 16, 1);  // not the optimized shape: icpp_block's checks
+        rejects("hybrid_fallback", "ICPP block size must be in [1,64]",
+                [&] { gat::icpp_heads_hybrid::aggregate(g, p2, q0, s0, wh, 0, 16, sh); });
+        // the reference's batches of 16 rows of the schedule: with the identity
+        // order the batches hold degrees up to 129, 129 and 33
+        gat::Schedule id;
+        for (uint32_t i = 0; i < g.n; ++i) id.perm.push_back(i);
+        const auto b16 = gat::detail::batch_steps(g, id, 16);
+        expect(b16.batches == 3 && b16.active == 3 && b16.steps == 291 && b16.blocks == 21, "batch steps");
+    }
     std::cout << "MIRROR PASS host\n";
 }
 
@@ -260,14 +297,111 @@ void gpu_checks() {
     std::cout << "MIRROR PASS gpu cases=" << cases << "\n";
 }
 
+template <class T>
+uint64_t total(const std::vector<T>& v) {
+    uint64_t s = 0;
+    for (const T& x : v) s += uint64_t(x);
+    return s;
+}
+
+// The online TFS variants through their reference entry points: each layer
+// against the FP64 layer on BF16-rounded X and W at the TFS gate, the exact
+// counters against what the CSR and the schedule determine, aggregate() plus
+// finish against layer(), and heads_hybrid's dispatch.
+void online_checks() {
+    int cases = 0;
+    for (int D : {17, 33})
+        for (int K : {2, 8})
+            for (int d : {16, 32}) {
+                gat::Graph g = boundary_graph(D);
+                gat::Param p = params(D, K, d, D + K + d);
+                gat::Prepared q = gat::prepare(p);
+                gat::Schedule s = gat::degree_schedule(g);
+                const auto want16 = fp64_layer(g, p, g.x, true, true);
+                const uint64_t tiles = uint64_t(K) * ((g.n + 15) / 16);
+                for (int block : {16, 32}) {
+                    // per (row, head): ceil(degree / block) blocks; every update
+                    // after a row's first block is a rescale
+                    uint64_t blocks = 0, nonempty = 0;
+                    for (uint64_t i = 0; i < g.n; ++i) {
+                        const uint64_t deg = g.row[i + 1] - g.row[i];
+                        blocks += K * ((deg + block - 1) / block);
+                        nonempty += deg ? K : 0;
+                    }
+                    const auto steps = gat::detail::batch_steps(g, s, block);
+                    gat::icpp_online::Timing t;
+                    gat::icpp_online::Workspace wo;
+                    wo.allocate(g, p, true);
+                    gat::icpp_online::Stats so;
+                    gat::icpp_online::layer(g, p, q, s, g.x, wo, true, block, 64, t, so, 0, true, "fp32");
+                    const auto eo = gat::errors(want16, wo.base.out);
+                    expect(eo.finite && eo.relative_l2 < 3e-2, "icpp_online layer vs FP64");
+                    expect(so.blocks == blocks && total(wo.row_blocks) == blocks, "online blocks");
+                    expect(so.max_updates >= nonempty && so.rescales == so.max_updates - nonempty, "online rescales");
+                    expect(total(wo.row_max_updates) == so.max_updates && total(wo.row_rescales) == so.rescales,
+                           "online row arrays");
+                    expect(so.neighbor_steps == K * steps.steps && so.total_tiles == tiles && so.sampled_tiles == 0,
+                           "online steps and tiles");
+                    // aggregate() on the copies the layer left, then finish
+                    const std::vector<float> layer_out = wo.base.out;
+                    gat::icpp_online::Stats sa;
+                    gat::icpp_online::aggregate(g, p, q, s, wo, block, 64, sa, 4, false);
+                    expect(sa.blocks == 0 && sa.total_tiles == tiles && sa.sampled_tiles == (tiles + 3) / 4,
+                           "online sampled tiles");
+                    gat::Times tf;
+                    gat::finish(g, p, wo.base, true, tf);
+                    const auto ea = gat::errors(layer_out, wo.base.out);
+                    expect(ea.finite && ea.max_abs <= 1e-5, "icpp_online aggregate + finish vs layer");
+                    // icpp_block: the same Online units, one projection per batch block
+                    gat::icpp_block::Workspace wk;
+                    wk.allocate(g, p, true);
+                    gat::icpp_block::Stats sk;
+                    gat::icpp_block::layer(g, p, q, s, g.x, wk, true, block, 64, t, sk, 0, true, "fp32");
+                    const auto ek = gat::errors(want16, wk.original.base.out);
+                    expect(ek.finite && ek.relative_l2 < 3e-2, "icpp_block layer vs FP64");
+                    expect(sk.baseline.blocks == so.blocks && sk.baseline.max_updates == so.max_updates &&
+                               sk.baseline.rescales == so.rescales && sk.baseline.rescale_events == so.rescale_events,
+                           "block units");
+                    expect(sk.block_projection_calls == K * steps.blocks &&
+                               sk.baseline.neighbor_steps == sk.block_projection_calls &&
+                               sk.source_neighbor_steps == so.neighbor_steps &&
+                               sk.actual_input_feature_FMA == uint64_t(K) * g.e * uint64_t(D),
+                           "block calls");
+                    // icpp_heads_hybrid: optimized for heads 8, dim 32, else icpp_block
+                    gat::icpp_heads_hybrid::Workspace wh;
+                    wh.allocate(g, p, true);
+                    gat::icpp_heads_hybrid::Stats sh;
+                    gat::icpp_heads_hybrid::layer(g, p, q, s, g.x, wh, true, block, 64, t, sh, 0, true, "fp32", 16);
+                    const auto eh = gat::errors(want16, wh.fallback.original.base.out);
+                    expect(eh.finite && eh.relative_l2 < 3e-2, "icpp_heads_hybrid layer vs FP64");
+                    const bool optimized = K == 8 && d == 32;
+                    expect(sh.optimized == optimized, "hybrid dispatch");
+                    expect(sh.projection_calls == K * steps.blocks && sh.baseline.blocks == so.blocks &&
+                               sh.baseline.rescales == so.rescales,
+                           "hybrid counts");
+                    if (!optimized) {
+                        const auto ef = gat::errors(wk.original.base.out, wh.fallback.original.base.out);
+                        expect(ef.finite && ef.max_abs <= 1e-5, "hybrid falls back to icpp_block");
+                    }
+                    ++cases;
+                    std::cout << "MIRROR PASS online D=" << D << " K=" << K << " d=" << d << " block=" << block
+                              << " online_rel=" << eo.relative_l2 << " block_rel=" << ek.relative_l2
+                              << " hybrid_rel=" << eh.relative_l2 << " rescales=" << so.rescales << "\n";
+                }
+            }
+    std::cout << "MIRROR PASS online cases=" << cases << "\n";
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {
     try {
-        const bool gpu = argc > 1 && std::string(argv[1]) == "--gpu";
+        const std::string mode = argc > 1 ? argv[1] : "--host";
         const std::string dir = argc > 2 ? argv[2] : ".";
-        if (gpu)
+        if (mode == "--gpu")
             gpu_checks();
+        else if (mode == "--gpu-online")
+            online_checks();
         else
             host_checks(dir);
         return 0;

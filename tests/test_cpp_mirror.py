@@ -24,7 +24,7 @@ def mirror_bin(tmp_path_factory):
 def test_mirror_host_checks(mirror_bin, tmp_path):
     r = subprocess.run([str(mirror_bin), "--host", str(tmp_path)], capture_output=True, text=True, timeout=120)
     assert r.returncode == 0, r.stdout + r.stderr
-    assert "MIRROR PASS host" in r.stdout and r.stdout.count("MIRROR PASS rejects") == 11
+    assert "MIRROR PASS host" in r.stdout and r.stdout.count("MIRROR PASS rejects") == 19
 
 
 @pytest.mark.gpu
