@@ -114,6 +114,21 @@ int main(int argc, char** argv) {
         if (threads <= 0 || panel < 16 || panel % 16 || reps < 1 || warmups < 0 || layer_arg < 0 || layer_arg > 3)
             throw std::runtime_error("invalid benchmark controls");
         if (layer_arg != 0) throw std::runtime_error("--layer: only whole-model runs (0) on this backend");
+        const std::string policy =
+            a.get("--lr-policy", path == "tfs_bf16" || path == "matched_attention" ? "bf16" : "z_avx");
+        // bench/main.cpp:61-63 (checked here before any device work)
+        if (policy != "bf16" && policy != "fp32" && policy != "avx" && policy != "z_avx" && policy != "z_mkl")
+            throw std::runtime_error("bad LR policy");
+        const bool reordered = path == "tfs_bf16" || path == "matched_attention";
+        if (reordered && (policy == "z_avx" || policy == "z_mkl"))
+            throw std::runtime_error("reordered LR path requires bf16/fp32/avx");
+        // The device model takes the reordered L/R of these paths from the BF16
+        // layer input ("bf16"); the standard paths take L/R from Z in the
+        // projection epilogue, which serves every policy there (the reference
+        // runs any policy but z_mkl as z_avx on them, bench/main.cpp:24).
+        if (reordered && policy != "bf16")
+            throw std::runtime_error("LR policy " + policy + " is not available for path " + path +
+                                     " on this backend (bf16 only)");
         std::cout << "ENV backend=gat_b200 version=" << gat_b200_version() << " threads=" << threads
                   << " source_input=" << graph_path << " checkpoint="
                   << (a.get("--weights").empty() ? "random_fixture_not_trained" : a.get("--weights"))
@@ -144,8 +159,6 @@ int main(int argc, char** argv) {
         check(gat_b200_graph_schedule(dev.g, nullptr, &neighbor_steps));
         std::cout << "STATIC degree_sort_ms=" << degree_sort_s * 1000 << " model_prepare_ms=" << prepare_s * 1000
                   << " bytes=" << g.n * 4 << " graph_policy=as_loaded_no_mutation\n";
-        const std::string policy =
-            a.get("--lr-policy", path == "tfs_bf16" || path == "matched_attention" ? "bf16" : "z_avx");
         std::cout << "CONFIG mode=" << mode << " path=" << path << " lr_policy=" << policy << " panel_R=" << panel
                   << " layer=" << layer_arg << " warmups=" << warmups << " repeats=" << reps << "\n";
 

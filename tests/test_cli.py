@@ -37,6 +37,14 @@ def test_cli_argument_errors():
     assert r.returncode == 1 and "provide --weights checkpoint.bin or explicit --seed" in r.stderr
     r = run("--graph", "/nonexistent.gatbin", "--seed", "11")
     assert r.returncode == 1 and "FAIL cannot open graph" in r.stderr
+    # bench/main.cpp:61-63: the LR policy checks
+    g = str(GOLDEN / "fixture_small.gatbin")
+    r = run("--graph", g, "--seed", "11", "--lr-policy", "nope")
+    assert r.returncode == 1 and "FAIL bad LR policy" in r.stderr
+    r = run("--graph", g, "--seed", "11", "--path", "tfs_bf16", "--lr-policy", "z_avx")
+    assert r.returncode == 1 and "FAIL reordered LR path requires bf16/fp32/avx" in r.stderr
+    r = run("--graph", g, "--seed", "11", "--path", "matched_attention", "--lr-policy", "fp32")
+    assert r.returncode == 1 and "not available for path matched_attention" in r.stderr
 
 
 @pytest.mark.gpu
