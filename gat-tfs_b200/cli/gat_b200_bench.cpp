@@ -11,18 +11,24 @@
 // Paths: ref_fp32 (served by the FP32 path, which the test suite pins to the
 // reference's R0 at max-abs <= 1e-5), standard_fp32, standard_bf16, tfs_bf16,
 // matched_attention, and adaptive_bf16 (layer 1 through TFS aggregation).
-// Modes: benchmark, correctness. A forward is timed end to end on the host
-// clock: FP32 X from host memory in, FP32 logits to host memory out, as the
-// reference times its forward over host buffers.
+// Modes: benchmark, correctness (with --dump-prefix), and the operator modes
+// micro, export-fixture and fixed-p on one layer (--layer, default 2). A
+// forward is timed end to end on the host clock: FP32 X from host memory in,
+// FP32 logits to host memory out, as the reference times its forward over host
+// buffers. The operator modes time each operation on device-resident buffers.
+// --init-policy and --diagnostics are accepted: they place the reference's CPU
+// threads and report its NUMA maps, which have no device counterpart.
 #include <algorithm>
 #include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <fstream>
+#include <functional>
 #include <iomanip>
 #include <iostream>
 #include <map>
+#include <sstream>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -40,9 +46,11 @@ using gat::seconds;
 struct Args {
     std::map<std::string, std::string> v;
     Args(int argc, char** argv) {
-        const std::vector<std::string> allowed = {"--graph",   "--weights", "--seed",    "--save-weights", "--path",
-                                                  "--mode",    "--threads", "--panel-r", "--repeats",      "--warmups",
-                                                  "--layer",   "--lr-policy", "--max-abs", "--rel-l2",     "--output"};
+        const std::vector<std::string> allowed = {
+            "--graph",  "--weights",   "--seed",    "--save-weights", "--path",        "--mode",
+            "--threads", "--panel-r",  "--repeats", "--warmups",      "--layer",       "--lr-policy",
+            "--fixture", "--max-abs",  "--rel-l2",  "--dump-prefix",  "--output",      "--init-policy",
+            "--diagnostics"};
         for (int i = 1; i < argc; ++i) {
             std::string k = argv[i];
             if (k.rfind("--", 0) != 0 || i + 1 == argc) throw std::runtime_error("arguments must be --key value");
@@ -70,6 +78,38 @@ int path_code(const std::string& p) {
     if (p == "matched_attention") return GAT_B200_PATH_MATCHED_ATTENTION;
     if (p == "adaptive_bf16") return GAT_B200_PATH_ADAPTIVE_BF16;
     throw std::runtime_error("bad path");
+}
+
+// Stage times (ms) and counts of one layer, the fields of the reference's
+// Times (baseline/include/gat.hpp:68-76).
+struct StageMs {
+    double convert = 0, projection = 0, lr = 0, max_prescan = 0, aggregate = 0, normalize = 0, activation = 0,
+           total = 0;
+    uint64_t neighbor_steps = 0, executed_fma = 0, workspace_bytes = 0;
+};
+
+// One JSON line per layer and repeat with print_times' keys
+// (baseline/src/common.cpp:155-170); `extra` appends keys of this backend.
+void print_times(const std::string& path, const std::string& mode, int layer, int rep, const gat::Graph& g,
+                 const gat::Param& p, int threads, bool fp32, const StageMs& t, double static_ms, int panel,
+                 const std::string& extra = "") {
+    std::cout << std::setprecision(10) << "{\"path\":\"" << path << "\",\"mode\":\"" << mode
+              << "\",\"layer\":" << layer << ",\"rep\":" << rep << ",\"N\":" << g.n << ",\"E\":" << g.e
+              << ",\"D\":" << p.in << ",\"K\":" << p.heads << ",\"d\":" << p.dim << ",\"threads\":" << threads
+              << ",\"profile\":false,\"precision\":\"" << (fp32 ? "FP32" : "BF16_RNE_FP32_state") << "\""
+              << ",\"projection_ms\":" << t.projection << ",\"lr_ms\":" << t.lr
+              << ",\"max_prescan_ms\":" << t.max_prescan << ",\"score_exp_aggregate_ms\":" << t.aggregate
+              << ",\"normalize_ms\":" << t.normalize << ",\"activation_ms\":" << t.activation
+              << ",\"convert_ms\":" << t.convert << ",\"total_ms\":" << t.total
+              << ",\"workspace_bytes\":" << t.workspace_bytes << ",\"static_preprocess_ms\":" << static_ms
+              << ",\"panel_R\":" << panel << ",\"tile_rows\":16,\"neighbor_steps\":" << t.neighbor_steps
+              << ",\"executed_fma\":" << t.executed_fma << ",\"padding_executed_flops\":0" << extra << "}\n";
+}
+
+void dump(const std::string& path, const std::vector<float>& v) {
+    std::ofstream f(path, std::ios::binary);
+    f.write(reinterpret_cast<const char*>(v.data()), std::streamsize(v.size() * 4));
+    if (!f) throw std::runtime_error("cannot write dump");
 }
 
 // Device objects of one (graph, checkpoint): the graph with its degree
@@ -100,6 +140,205 @@ std::vector<float> forward(gat_b200_model* m, const gat::Graph& g, const gat::Mo
     return logits;
 }
 
+// Timing of one operation on the device: host clock around the call and a
+// synchronization (so that a kernel's time lands in its own stage).
+template <class F>
+double timed_ms(F&& f) {
+    const auto t0 = Clock::now();
+    f();
+    check(gat_b200_check_device());
+    return seconds(t0, Clock::now()) * 1000;
+}
+
+// The operator modes of the reference's driver on one layer (bench/main.cpp:103-151):
+//   micro           each stage of the layer timed alone (MICRO lines)
+//   export-fixture  R0's weights p and den of the layer, written as GATFIX1
+//   fixed-p         the standard (BF16 projection + aggregation with the
+//                   fixture's p, den + finish) and TFS B1 (aggregate-first with
+//                   the same p, den + finish) operators, alternated AB/BA, with
+//                   the reference's error controls and FIXED_P summary
+// The layer's input is the R0 chain of the earlier layers; the operators run
+// on device-resident buffers (input conversion shared and untimed, as the
+// reference excludes it).
+int operator_modes(const Args& a, const std::string& mode, const gat::Graph& g, const gat::Model& model,
+                   Device& dev, int layer_arg, int threads, int panel, int reps, int warmups, double static_ms,
+                   uint64_t neighbor_steps) {
+    const int layer = layer_arg ? layer_arg : 2;
+    const gat::Param& p = model[layer - 1];
+    const gat_b200_layer* lp = dev.layer[layer - 1];
+    std::vector<float> input = g.x;
+    for (int l = 0; l < layer - 1; ++l) {
+        gat::Workspace rw;
+        rw.allocate(g, model[l], "standard_fp32");
+        gat::Times t;
+        gat::ref_layer(g, model[l], input, rw, true, t);
+        input = std::move(rw.out);
+    }
+    const uint64_t n = g.n, e = g.e;
+    const int K = p.heads, d = p.dim, W = p.width(), D = p.in;
+    const int ldb = gat_b200_padded_ld(D, GAT_B200_BF16), ldz = gat_b200_padded_ld(W, GAT_B200_F32);
+    gat::detail::DeviceBuffer bx, bxb, bz, bl, br, bm, bo, bd, bo2, bd2, bp, bpd;
+    float* L = static_cast<float*>(bl.get(n * K * 4));
+    float* R = static_cast<float*>(br.get(n * K * 4));
+    float* z = static_cast<float*>(bz.get(n * size_t(ldz) * 4));
+    float* out = static_cast<float*>(bo.get(n * size_t(W) * 4));
+    float* den = static_cast<float*>(bd.get(n * K * 4));
+    uint16_t* xb = static_cast<uint16_t*>(bxb.get(n * size_t(ldb) * 2));
+
+    if (mode == "micro") {
+        // bench/main.cpp:107-118
+        const float* xf = bx.upload(input);
+        float* mx = static_cast<float*>(bm.get(n * K * 4));
+        auto bench = [&](const std::string& name, const std::function<void()>& fn) {
+            std::vector<double> samples;
+            for (int r = -warmups; r < reps; ++r) {
+                const double ms = timed_ms(fn);
+                if (r >= 0) samples.push_back(ms);
+            }
+            std::cout << "MICRO name=" << name << " layer=" << layer << " median_ms=" << pct(samples, .5)
+                      << " p95_ms=" << pct(samples, .95) << "\n";
+        };
+        bench("convert_rne", [&] { check(gat_b200_convert(n, D, xf, D, xb, ldb, nullptr)); });
+        bench("projection_bf16", [&] {
+            check(gat_b200_projection(lp, n, xb, ldb, GAT_B200_BF16, z, GAT_B200_F32, ldz, L, R, nullptr));
+        });
+        // L and R from Z are computed in the projection's epilogue on this backend
+        std::cout << "MICRO name=lr_z_avx layer=" << layer << " fused_into=projection_bf16\n";
+        std::cout << "MICRO name=lr_z_sgemm_static_workspace layer=" << layer << " fused_into=projection_bf16\n";
+        bench("lr_reordered_bf16", [&] {
+            check(gat_b200_lr_reordered(lp, n, xb, GAT_B200_BF16, ldb, GAT_B200_LR_BF16, nullptr, 0, L, R, nullptr));
+        });
+        bench("lr_reordered_fp32", [&] {
+            check(gat_b200_lr_reordered(lp, n, xf, GAT_B200_F32, D, GAT_B200_LR_FP32, nullptr, 0, L, R, nullptr));
+        });
+        // "avx" is the same FP32 product as "fp32" here
+        std::cout << "MICRO name=lr_reordered_avx layer=" << layer << " same_as=lr_reordered_fp32\n";
+        check(gat_b200_projection(lp, n, xb, ldb, GAT_B200_BF16, z, GAT_B200_F32, ldz, L, R, nullptr));
+        bench("max_prescan", [&] { check(gat_b200_max_prescan(dev.g, K, L, R, mx, nullptr)); });
+        bench("weighted_spmm_score_exp", [&] {
+            check(gat_b200_standard_aggregate(dev.g, K, d, z, GAT_B200_F32, ldz, L, R, nullptr, nullptr, out, W, den,
+                                              mx, nullptr));
+        });
+        return 0;
+    }
+
+    gat::Fixture fixture;
+    if (mode == "export-fixture" || a.get("--fixture").empty()) {
+        // R0's p and den (ref_fp32.cpp:3-14): FP32 projection, edge softmax
+        const float* xf = bx.upload(input);
+        check(gat_b200_projection(lp, n, xf, D, GAT_B200_F32, z, GAT_B200_F32, ldz, L, R, nullptr));
+        float* pp = static_cast<float*>(bp.get(e * K * 4));
+        check(gat_b200_edge_softmax(dev.g, K, L, R, nullptr, nullptr, pp, den, nullptr, nullptr));
+        fixture.input = input;
+        fixture.p.resize(e * K);
+        fixture.den.resize(n * K);
+        check(gat_b200_copy_to_host(fixture.p.data(), pp, e * K * 4));
+        check(gat_b200_copy_to_host(fixture.den.data(), den, n * K * 4));
+    } else {
+        fixture = gat::load_fixture(g, p, a.get("--fixture"));
+    }
+    if (mode == "export-fixture") {
+        gat::save_fixture(g, p, fixture, a.get("--fixture"));
+        std::cout << "FIXTURE saved layer=" << layer << "\n";
+        return 0;
+    }
+
+    // fixed-p: both operators on the identical fixture, input converted once
+    input = std::move(fixture.input);
+    const float* xf = bx.upload(input);
+    check(gat_b200_convert(n, D, xf, D, xb, ldb, nullptr));
+    const float* fp = bp.upload(fixture.p);
+    const float* fd = bpd.upload(fixture.den);
+    float* out2 = static_cast<float*>(bo2.get(n * size_t(W) * 4));
+    float* den2 = static_cast<float*>(bd2.get(n * K * 4));
+    auto standard_op = [&](StageMs& t) {
+        t.projection = timed_ms([&] {
+            check(gat_b200_projection(lp, n, xb, ldb, GAT_B200_BF16, z, GAT_B200_F32, ldz, L, R, nullptr));
+        });
+        t.aggregate = timed_ms([&] {
+            check(gat_b200_standard_aggregate(dev.g, K, d, z, GAT_B200_F32, ldz, nullptr, nullptr, fp, fd, out, W,
+                                              den, nullptr, nullptr));
+        });
+        t.normalize = timed_ms([&] { check(gat_b200_finish(n, K, d, den, 0, out, W, nullptr)); });
+        t.total = t.projection + t.aggregate + t.normalize;
+        t.workspace_bytes = n * (uint64_t(ldz) * 4 + uint64_t(W) * 4 + uint64_t(K) * 12 + uint64_t(ldb) * 2);
+    };
+    auto tfs_op = [&](StageMs& t) {
+        t.aggregate = timed_ms([&] {
+            check(gat_b200_tfs_aggregate(dev.g, lp, xb, ldb, nullptr, nullptr, nullptr, fp, fd, GAT_B200_TFS_EDGE, 0,
+                                         1, out2, W, den2, nullptr, nullptr));
+        });
+        t.normalize = timed_ms([&] { check(gat_b200_finish(n, K, d, den2, 0, out2, W, nullptr)); });
+        t.total = t.aggregate + t.normalize;
+        t.workspace_bytes = n * (uint64_t(W) * 4 + uint64_t(K) * 4 + uint64_t(ldb) * 2);
+    };
+    auto host = [&](const float* dptr, size_t count) {
+        std::vector<float> v(count);
+        check(gat_b200_copy_to_host(v.data(), dptr, count * 4));
+        return v;
+    };
+    StageMs st, tt;
+    standard_op(st);
+    tfs_op(tt);
+    const std::vector<float> sw = host(out, n * W), tw = host(out2, n * W);
+    gat::require_finite(sw, "fixed-p standard");
+    gat::require_finite(tw, "fixed-p TFS");
+    gat::print_error("tfs_fixed_p", layer, "vs_standard_bf16_extra_pX_quantization_and_reduction",
+                     gat::errors(sw, tw));
+    // the FP32 fixed-p operator (FP32 projection) as the master: separates the
+    // cost of the pX rounding from that of BF16 X and W
+    check(gat_b200_projection(lp, n, xf, D, GAT_B200_F32, z, GAT_B200_F32, ldz, L, R, nullptr));
+    check(gat_b200_standard_aggregate(dev.g, K, d, z, GAT_B200_F32, ldz, nullptr, nullptr, fp, fd, out, W, den,
+                                      nullptr, nullptr));
+    check(gat_b200_finish(n, K, d, den, 0, out, W, nullptr));
+    const std::vector<float> master = host(out, n * W);
+    gat::print_error("standard_fixed_p", layer, "vs_master_fixed_p", gat::errors(master, sw));
+    gat::print_error("tfs_fixed_p", layer, "vs_master_fixed_p", gat::errors(master, tw));
+    // scalar emulation of the TFS edge projection: BF16(p x) times BF16 W in
+    // neighbour order (bench/main.cpp:132-137), for small layers
+    if (double(e) * K * D * d <= 2e7) {
+        std::vector<float> emulated(n * size_t(W), 0.f);
+        const std::vector<float> xq = gat::quantized(input), wq = gat::quantized(p.w);
+        for (uint64_t i = 0; i < n; ++i)
+            for (int h = 0; h < K; ++h) {
+                float* o = emulated.data() + i * W + h * d;
+                for (uint64_t ed = g.row[i]; ed < g.row[i + 1]; ++ed)
+                    for (int k = 0; k < D; ++k) {
+                        const float v = gat::expand(gat::rne(fixture.p[ed * K + h] * xq[size_t(g.col[ed]) * D + k]));
+                        for (int c = 0; c < d; ++c) o[c] += v * wq[size_t(k) * W + h * d + c];
+                    }
+                const float dn = fixture.den[i * K + h];
+                for (int c = 0; c < d; ++c) o[c] = dn > 0 ? o[c] / dn : 0.f;
+            }
+        gat::print_error("tfs_fixed_p", layer, "vs_pX_bf16_emulation_reduction_only", gat::errors(emulated, tw));
+    } else {
+        std::cout << "CONTROL pX_scalar_emulation=SKIPPED_TOO_LARGE validated_in_boundary_tests=true\n";
+    }
+    std::vector<double> ss, ts;
+    const int dp = (D + 31) / 32 * 32, obs = (d + 15) / 16;
+    for (int r = -warmups; r < reps; ++r) {
+        StageMs s1, t1;
+        if (r % 2 == 0) {
+            standard_op(s1);
+            tfs_op(t1);
+        } else {
+            tfs_op(t1);
+            standard_op(s1);
+        }
+        if (r < 0) continue;
+        ss.push_back(s1.total);
+        ts.push_back(t1.total);
+        t1.neighbor_steps = neighbor_steps * uint64_t(K);
+        t1.executed_fma = t1.neighbor_steps * 16 * uint64_t(dp) * uint64_t(obs) * 16;
+        print_times("standard_bf16", "fixed-p", layer, r, g, p, threads, false, s1, static_ms, panel);
+        print_times("tfs_bf16", "fixed-p", layer, r, g, p, threads, false, t1, static_ms, panel);
+    }
+    std::cout << "FIXED_P median_standard_ms=" << pct(ss, .5) << " median_tfs_ms=" << pct(ts, .5)
+              << " speedup=" << pct(ss, .5) / pct(ts, .5)
+              << " conversion_excluded=true input_preparation=shared policy=AB_BA\n";
+    return 0;
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {
@@ -113,7 +352,18 @@ int main(int argc, char** argv) {
                   warmups = a.num("--warmups", 2), layer_arg = a.num("--layer", 0);
         if (threads <= 0 || panel < 16 || panel % 16 || reps < 1 || warmups < 0 || layer_arg < 0 || layer_arg > 3)
             throw std::runtime_error("invalid benchmark controls");
-        if (layer_arg != 0) throw std::runtime_error("--layer: only whole-model runs (0) on this backend");
+        const bool operator_mode = mode == "export-fixture" || mode == "fixed-p" || mode == "micro";
+        if (mode != "correctness" && mode != "benchmark" && mode != "profile" && !operator_mode)
+            throw std::runtime_error("bad mode");
+        // the profile mode needs the reference's counter build (GAT_PROFILE); this
+        // backend's stage times come from CUDA events in every benchmark run
+        if (mode == "profile") throw std::runtime_error("profile requires profile binary");
+        if (mode == "benchmark" && layer_arg != 0)
+            throw std::runtime_error("--layer: only whole-model runs (0) on this backend");
+        if (mode == "export-fixture" && a.get("--fixture").empty())
+            throw std::runtime_error("--fixture output is required");
+        const std::string init = a.get("--init-policy", "original");
+        if (init != "original" && init != "warm") throw std::runtime_error("bad init policy");
         const std::string policy =
             a.get("--lr-policy", path == "tfs_bf16" || path == "matched_attention" ? "bf16" : "z_avx");
         // bench/main.cpp:61-63 (checked here before any device work)
@@ -171,10 +421,31 @@ int main(int argc, char** argv) {
                 throw std::runtime_error("invalid accuracy thresholds");
             const std::vector<float> master = forward(dev.model(GAT_B200_PATH_STANDARD_FP32), g, model);
             gat::require_finite(master, "ref_fp32 output");
+            // --dump-prefix: R0's per-layer trace and every path's logits as raw
+            // FP32 files with the reference's names (bench/main.cpp:72-75,94-96)
+            const std::string prefix = a.get("--dump-prefix");
+            if (!prefix.empty()) {
+                std::vector<float> input = g.x;
+                for (int l = 0; l < 3; ++l) {
+                    gat::Workspace rw;
+                    rw.allocate(g, model[l], "ref_fp32");
+                    gat::Times t;
+                    gat::ref_layer(g, model[l], input, rw, l < 2, t);
+                    const std::string pre = prefix + "_layer" + std::to_string(l + 1) + "_";
+                    const std::pair<const char*, const std::vector<float>*> items[] = {
+                        {"output", &rw.out}, {"z", &rw.z},     {"left", &rw.left}, {"right", &rw.right},
+                        {"max", &rw.max},    {"den", &rw.den}, {"score", &rw.score}, {"p", &rw.p},
+                        {"alpha", &rw.alpha}};
+                    for (const auto& item : items) dump(pre + item.first + ".f32", *item.second);
+                    input = std::move(rw.out);
+                }
+                dump(prefix + "_model_ref_fp32.f32", master);
+            }
             bool pass = true, finite = true;
             for (const std::string test : {"standard_fp32", "standard_bf16", "tfs_bf16", "matched_attention",
                                            "adaptive_bf16"}) {
                 const std::vector<float> out = forward(dev.model(path_code(test)), g, model);
+                if (!prefix.empty()) dump(prefix + "_model_" + test + ".f32", out);
                 const gat::Error e = gat::errors(master, out);
                 gat::print_error(test, 3, "model_path_specific_chain", e);
                 finite &= e.finite;
@@ -185,7 +456,9 @@ int main(int argc, char** argv) {
                       << " task_metric=UNAVAILABLE\n";
             return pass ? 0 : 1;
         }
-        if (mode != "benchmark") throw std::runtime_error("bad mode");
+        if (operator_mode)
+            return operator_modes(a, mode, g, model, dev, layer_arg, threads, panel, reps, warmups,
+                                  (degree_sort_s + prepare_s) * 1000, neighbor_steps);
 
         gat_b200_model* m = dev.model(pc);
         check(gat_b200_model_enable_timing(m, 1));
@@ -213,30 +486,22 @@ int main(int argc, char** argv) {
                 // stage slots: 1 convert, 2+2l projection (TFS: lr_reordered + max prescan), 3+2l aggregation
                 const bool tfs = pc == GAT_B200_PATH_TFS_BF16 || (tfs_layer1 && l == 0);
                 const double pre = st[2 + 2 * l], agg = st[3 + 2 * l], conv = l == 0 ? st[1] : 0.0;
-                std::cout << std::setprecision(10) << "{\"path\":\"" << path << "\",\"mode\":\"" << mode
-                          << "\",\"layer\":" << l + 1 << ",\"rep\":" << r << ",\"N\":" << g.n << ",\"E\":" << g.e
-                          << ",\"D\":" << p.in << ",\"K\":" << p.heads << ",\"d\":" << p.dim
-                          << ",\"threads\":" << threads << ",\"profile\":false,\"precision\":\""
-                          << (fp32 ? "FP32" : "BF16_RNE_FP32_state") << "\""
-                          << ",\"projection_ms\":" << (tfs ? 0.0 : pre) << ",\"lr_ms\":" << (tfs ? pre : 0.0)
-                          << ",\"max_prescan_ms\":0,\"score_exp_aggregate_ms\":" << agg
-                          << ",\"normalize_ms\":0,\"activation_ms\":0,\"convert_ms\":" << conv
-                          << ",\"total_ms\":" << pre + agg + conv << ",\"workspace_bytes\":0"
-                          << ",\"static_preprocess_ms\":" << (degree_sort_s + prepare_s) * 1000
-                          << ",\"panel_R\":" << panel << ",\"tile_rows\":16"
-                          << ",\"neighbor_steps\":" << (tfs ? neighbor_steps * p.heads : 0)
-                          << ",\"executed_fma\":0,\"padding_executed_flops\":0"
-                          << ",\"h2d_ms\":" << (l == 0 ? st[0] : 0.0) << ",\"d2h_ms\":" << (l == 2 ? st[8] : 0.0)
-                          << ",\"kernels\":" << gat_b200_model_launches(m) << "}\n";
+                StageMs t;
+                (tfs ? t.lr : t.projection) = pre;
+                t.aggregate = agg;
+                t.convert = conv;
+                t.total = pre + agg + conv;
+                t.neighbor_steps = tfs ? neighbor_steps * p.heads : 0;
+                std::ostringstream extra;
+                extra << std::setprecision(10) << ",\"h2d_ms\":" << (l == 0 ? st[0] : 0.0)
+                      << ",\"d2h_ms\":" << (l == 2 ? st[8] : 0.0) << ",\"kernels\":" << gat_b200_model_launches(m);
+                print_times(path, mode, l + 1, r, g, p, threads, fp32, t, (degree_sort_s + prepare_s) * 1000, panel,
+                            extra.str());
             }
             std::cout << "E2E path=" << path << " rep=" << r << " layer=" << layer_arg << " total_ms=" << total * 1000
                       << " finite=1\n";
         }
-        if (!a.get("--output").empty()) {
-            std::ofstream f(a.get("--output"), std::ios::binary);
-            f.write(reinterpret_cast<const char*>(logits.data()), std::streamsize(logits.size() * 4));
-            if (!f) throw std::runtime_error("cannot write dump");
-        }
+        if (!a.get("--output").empty()) dump(a.get("--output"), logits);
         std::cout << "SUMMARY path=" << path << " median_ms=" << pct(totals, .5) * 1000
                   << " p95_ms=" << pct(totals, .95) * 1000 << " cold_forward_ms=" << cold_forward * 1000
                   << " repeats=" << reps << " task_accuracy=UNVERIFIED\n";

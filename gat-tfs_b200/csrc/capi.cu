@@ -20,6 +20,8 @@ int convert_launch(uint64_t n, int width, const float* in, int ld_in, uint16_t* 
 int max_prescan_launch(const gat_b200_graph* g, int heads, const float* left, const float* right, float* max,
                        cudaStream_t st);
 int finish_launch(uint64_t n, int heads, int dim, const float* den, int hidden, float* out, int ldo, cudaStream_t st);
+int edge_softmax_launch(const gat_b200_graph* g, int heads, const float* left, const float* right, float* score,
+                        float* max, float* p, float* den, float* alpha, cudaStream_t st);
 int projection_simt_launch(const gat_b200_layer* p, uint64_t n, const void* x, int x_bf16, int ldx, void* h,
                            int h_bf16, int ldh, float* left, float* right, cudaStream_t st);
 int projection_tc_launch(const gat_b200_layer* p, uint64_t n, const uint16_t* x, int ldx, uint16_t* h, int ldh,
@@ -347,6 +349,12 @@ int gat_b200_projection_scatter(const gat_b200_layer* p, uint64_t n, const void*
     if (rc == GAT_B200_EUNSUPPORTED)
         return fail_code(rc, "projection_scatter: layer outside the tensor-core kernel (input or width > 256)");
     return rc;
+}
+
+int gat_b200_edge_softmax(const gat_b200_graph* g, int heads, const float* left, const float* right, float* score,
+                          float* max, float* p, float* den, float* alpha, void* stream) {
+    clear_error();
+    return edge_softmax_launch(g, heads, left, right, score, max, p, den, alpha, as_stream(stream));
 }
 
 int gat_b200_max_prescan(const gat_b200_graph* g, int heads, const float* left, const float* right, float* max,

@@ -84,6 +84,38 @@ __global__ void max_prescan_kernel(const uint64_t* __restrict__ row, const uint3
     }
 }
 
+// R0's edge softmax (baseline/src/ref_fp32.cpp:7-14), one thread per (row,
+// head) so that the maximum and the FP32 sum of p run over the row's edges in
+// the reference's order: score = leaky(L_ih + R_jh), m = the row maximum (0 for
+// an empty row), p = exp(score - m), den = sum p, alpha = p / den.
+__global__ void edge_softmax_kernel(const uint64_t* __restrict__ row, const uint32_t* __restrict__ col, uint64_t n,
+                                    int heads, const float* __restrict__ left, const float* __restrict__ right,
+                                    float* __restrict__ score, float* __restrict__ max, float* __restrict__ p,
+                                    float* __restrict__ den, float* __restrict__ alpha) {
+    const uint64_t total = n * uint64_t(heads);
+    for (uint64_t t = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; t < total;
+         t += uint64_t(gridDim.x) * blockDim.x) {
+        const uint64_t i = t / uint64_t(heads);
+        const int h = int(t - i * uint64_t(heads));
+        const uint64_t b = row[i], e_end = row[i + 1];
+        const float l = left[t];
+        float m = -INFINITY;
+        for (uint64_t e = b; e < e_end; ++e) m = fmaxf(m, leaky(l + right[uint64_t(col[e]) * heads + h]));
+        float sum = 0.f;
+        for (uint64_t e = b; e < e_end; ++e) {
+            const float sc = leaky(l + right[uint64_t(col[e]) * heads + h]);
+            const float v = expf(sc - m);
+            if (score) score[e * heads + h] = sc;
+            p[e * heads + h] = v;
+            sum += v;
+        }
+        den[t] = sum;
+        if (max) max[t] = b == e_end ? 0.f : m;
+        if (alpha)
+            for (uint64_t e = b; e < e_end; ++e) alpha[e * heads + h] = p[e * heads + h] / sum;
+    }
+}
+
 // baseline/src/baseline_standard.cpp:85-97
 __global__ void finish_kernel(uint64_t n, int heads, int dim, const float* __restrict__ den, int hidden,
                               float* __restrict__ out, int ldo) {
@@ -221,6 +253,17 @@ int max_prescan_launch(const gat_b200_graph* g, int heads, const float* left, co
     if (heads < 1 || heads > 8) return fail("invalid parameter shape (heads <=8, head_dim <=64)");
     max_prescan_kernel<<<grid_for(g->n * 32, 256), 256, 0, st>>>(g->row, g->col, g->n, heads, left, right, max);
     GATB_LAUNCH("max prescan kernel");
+    return 0;
+}
+
+int edge_softmax_launch(const gat_b200_graph* g, int heads, const float* left, const float* right, float* score,
+                        float* max, float* p, float* den, float* alpha, cudaStream_t st) {
+    if (!g || !left || !right || !p || !den) return fail("edge_softmax: null buffer");
+    if (heads < 1 || heads > 8) return fail("invalid parameter shape (heads <=8, head_dim <=64)");
+    if (g->n == 0) return 0;
+    edge_softmax_kernel<<<grid_for(g->n * uint64_t(heads), 256), 256, 0, st>>>(g->row, g->col, g->n, heads, left,
+                                                                               right, score, max, p, den, alpha);
+    GATB_LAUNCH("edge softmax kernel");
     return 0;
 }
 

@@ -79,6 +79,7 @@ SIGNATURES = [
     ("gat_b200_convert", C.c_int, [C.c_uint64, C.c_int, _vp, C.c_int, _vp, C.c_int, _vp]),
     ("gat_b200_projection", C.c_int, [_vp, C.c_uint64, _vp, C.c_int, C.c_int, _vp, C.c_int, C.c_int, _vp, _vp, _vp]),
     ("gat_b200_max_prescan", C.c_int, [_vp, C.c_int, _vp, _vp, _vp, _vp]),
+    ("gat_b200_edge_softmax", C.c_int, [_vp, C.c_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     ("gat_b200_standard_aggregate", C.c_int, [_vp, C.c_int, C.c_int, _vp, C.c_int, C.c_int, _vp, _vp, _vp, _vp, _vp, C.c_int, _vp, _vp, _vp]),
     ("gat_b200_finish", C.c_int, [C.c_uint64, C.c_int, C.c_int, _vp, C.c_int, _vp, C.c_int, _vp]),
     ("gat_b200_aggregate_fused", C.c_int, [_vp, C.c_int, C.c_int, _vp, C.c_int, C.c_int, _vp, _vp, C.c_int, _vp, C.c_int, C.c_int, _vp]),
@@ -510,6 +511,13 @@ def tfs_online_counters(g: DeviceGraph, heads, left, right, block, row_blocks=No
 
 def max_prescan(g: DeviceGraph, heads, left, right, mx, stream=None):
     _check(_lib.gat_b200_max_prescan(g.handle, heads, _ptr(left), _ptr(right), _ptr(mx), _stream(stream)))
+
+
+def edge_softmax(g: DeviceGraph, heads, left, right, p, den, score=None, mx=None, alpha=None, stream=None):
+    """R0's edge softmax trace (ref_fp32.cpp:7-14): p [e][heads], den [n][heads],
+    optionally score, the row maximum and alpha = p / den."""
+    _check(_lib.gat_b200_edge_softmax(g.handle, heads, _ptr(left), _ptr(right), _ptr(score), _ptr(mx), _ptr(p),
+                                      _ptr(den), _ptr(alpha), _stream(stream)))
 
 
 def standard_aggregate(g: DeviceGraph, heads, dim, h, h_dtype, ldh, left, right, out, ldo, den, mx=None,

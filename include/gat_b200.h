@@ -238,6 +238,17 @@ int gat_b200_standard_aggregate(const gat_b200_graph* g, int heads, int dim, con
                                 const float* fixed_p, const float* fixed_den, float* out, int ldo,
                                 float* den, float* max, void* stream);
 
+/* R0's edge softmax trace (baseline/src/ref_fp32.cpp:7-14): per row i and
+ * head h, score[e][h] = leaky(L_ih + R_jh) over the row's edges, the row
+ * maximum m (max[i][h], 0 for an empty row), p[e][h] = exp(score - m),
+ * den[i][h] = the sum of the row's p in edge order, alpha[e][h] = p / den.
+ * One thread per (row, head), so that the FP32 sums run in the reference's
+ * order; exp is the device's expf (within 2 ulp of the host's). The weights of
+ * the reference's fixed-p fixtures (GATFIX1) are p and den. score, max and
+ * alpha may be NULL; left [n][heads], right [sources][heads] (device). */
+int gat_b200_edge_softmax(const gat_b200_graph* g, int heads, const float* left, const float* right,
+                          float* score, float* max, float* p, float* den, float* alpha, void* stream);
+
 /* out *= (den>0 ? 1/den : 0), then ELU if hidden. Replaces gat::finish
  * (baseline/src/baseline_standard.cpp:85-97). FP32 out [n][ldo]. */
 int gat_b200_finish(uint64_t n, int heads, int dim, const float* den, int hidden, float* out,

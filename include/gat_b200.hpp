@@ -309,7 +309,7 @@ inline Schedule degree_schedule(const Graph& g) {
 struct Workspace {
     std::vector<BF16> xbf;
     std::vector<float> z, left, right, max, den, out;
-    std::vector<float> score, p, alpha;  // R0 trace: not produced (the FP32 path serves R0)
+    std::vector<float> score, p, alpha;  // R0 trace [e][heads] (ref_fp32 workspaces)
     // device state
     std::shared_ptr<detail::GraphHandle> graph = std::make_shared<detail::GraphHandle>();
     std::shared_ptr<detail::DeviceBuffer> d_x = std::make_shared<detail::DeviceBuffer>(),
@@ -321,7 +321,8 @@ struct Workspace {
                                           d_den = std::make_shared<detail::DeviceBuffer>(),
                                           d_out = std::make_shared<detail::DeviceBuffer>(),
                                           d_fp = std::make_shared<detail::DeviceBuffer>(),
-                                          d_fd = std::make_shared<detail::DeviceBuffer>();
+                                          d_fd = std::make_shared<detail::DeviceBuffer>(),
+                                          d_trace = std::make_shared<detail::DeviceBuffer>();
     bool lr_from_projection = false;
     // baseline/src/common.cpp:126-134: the buffers of each path
     void allocate(const Graph& g, const Param& p, const std::string& path) {
@@ -336,10 +337,16 @@ struct Workspace {
         den.assign(nk, 0.f);
         out.assign(nw, 0.f);
         xbf.assign(path == "standard_fp32" || path == "ref_fp32" ? 0 : checked(g.n, uint64_t(p.in)), 0);
+        const size_t ek = path == "ref_fp32" ? checked(g.e, uint64_t(p.heads)) : 0;
+        score.assign(ek, 0.f);
+        this->p.assign(ek, 0.f);
+        alpha.assign(ek, 0.f);
         graph->of(g);
     }
     size_t bytes() const {
-        return xbf.size() * 2 + (z.size() + left.size() + right.size() + max.size() + den.size() + out.size()) * 4;
+        return xbf.size() * 2 + (z.size() + left.size() + right.size() + max.size() + den.size() + out.size() +
+                                 score.size() + p.size() + alpha.size()) *
+                                    4;
     }
 };
 
@@ -510,9 +517,38 @@ inline void standard_layer(const Graph& g, const Param& p, const Prepared& q, co
     t.total += seconds(t0, Clock::now());
 }
 // R0 (baseline/src/ref_fp32.cpp:3-26): served by the FP32 path.
+// R0 (baseline/src/ref_fp32.cpp:3-26): out from the FP32 path (FP32 projection,
+// aggregation, finish), and the R0 trace from gat_b200_edge_softmax: z, left,
+// right, and max, den in R0's order, with score, p and alpha when the workspace
+// was allocated for ref_fp32.
 inline void ref_layer(const Graph& g, const Param& p, const std::vector<float>& input, Workspace& w, bool hidden,
                       Times& t) {
-    standard_layer(g, p, prepare(p), input, w, hidden, t, true);
+    const auto begin = Clock::now();
+    auto a = begin;
+    const Prepared q = prepare(p);
+    projection(g, p, q, input, w, false);
+    t.projection += seconds(a, Clock::now());
+    a = Clock::now();
+    standard_aggregate(g, p, w);
+    finish(g, p, w, hidden, t);
+    t.aggregate += seconds(a, Clock::now());
+    const size_t ek = checked(g.e, uint64_t(p.heads)), nk = checked(g.n, uint64_t(p.heads));
+    const bool trace = w.score.size() == ek && w.p.size() == ek && w.alpha.size() == ek;
+    float* buf = static_cast<float*>(w.d_trace->get(((trace ? 3 : 1) * ek + 2 * nk) * 4));
+    float *pp = buf, *dn = buf + ek, *mx = dn + nk;
+    float* sc = trace ? mx + nk : nullptr;
+    float* al = trace ? sc + ek : nullptr;
+    const float* l = w.d_left->upload(w.left);
+    const float* r = w.d_right->upload(w.right);
+    check(gat_b200_edge_softmax(w.graph->of(g), p.heads, l, r, sc, mx, pp, dn, al, nullptr));
+    check(gat_b200_copy_to_host(w.den.data(), dn, nk * 4));
+    check(gat_b200_copy_to_host(w.max.data(), mx, nk * 4));
+    if (trace) {
+        check(gat_b200_copy_to_host(w.score.data(), sc, ek * 4));
+        check(gat_b200_copy_to_host(w.p.data(), pp, ek * 4));
+        check(gat_b200_copy_to_host(w.alpha.data(), al, ek * 4));
+    }
+    t.total += seconds(begin, Clock::now());
 }
 // B1 (baseline/src/baseline_tfs.cpp:16-110) from w.xbf, w.left, w.right, w.max.
 inline void tfs_aggregate(const Graph& g, const Param& p, const Prepared& q, const Schedule&, Workspace& w, int,

@@ -390,6 +390,41 @@ void online_checks() {
                 }
             }
     std::cout << "MIRROR PASS online cases=" << cases << "\n";
+    // R0's trace (ref_fp32.cpp:7-14) from a ref_fp32 workspace: score and the
+    // row maximum bit for bit from the layer's own L/R, p within the ulps of
+    // two exp implementations, den and alpha to FP32 rounding
+    gat::Graph g = boundary_graph(33);
+    gat::Param p = params(33, 8, 32, 5);
+    gat::Workspace w;
+    w.allocate(g, p, "ref_fp32");
+    gat::Times t;
+    gat::ref_layer(g, p, g.x, w, true, t);
+    const int K = p.heads;
+    expect(w.score.size() == g.e * K && w.p.size() == g.e * K && w.alpha.size() == g.e * K, "trace sizes");
+    for (uint64_t i = 0; i < g.n; ++i)
+        for (int h = 0; h < K; ++h) {
+            float m = -INFINITY;
+            double den = 0;
+            for (uint64_t e = g.row[i]; e < g.row[i + 1]; ++e) {
+                float sc = w.left[i * K + h] + w.right[size_t(g.col[e]) * K + h];
+                sc = sc >= 0 ? sc : 0.2f * sc;
+                expect(w.score[e * K + h] == sc, "R0 score");
+                m = std::max(m, sc);
+            }
+            expect(w.max[i * K + h] == (g.row[i] == g.row[i + 1] ? 0.f : m), "R0 row maximum");
+            for (uint64_t e = g.row[i]; e < g.row[i + 1]; ++e) {
+                const float diff = w.score[e * K + h] - m;  // R0 subtracts in FP32
+                const double want = std::exp(double(diff));
+                expect(std::fabs(w.p[e * K + h] - want) <= 1e-6 * want, "R0 p");
+                den += w.p[e * K + h];
+            }
+            expect(std::fabs(w.den[i * K + h] - den) <= 1e-5 * std::max(den, 1e-30), "R0 den");
+            for (uint64_t e = g.row[i]; e < g.row[i + 1]; ++e) {
+                const float want = w.p[e * K + h] / w.den[i * K + h];
+                expect(std::fabs(w.alpha[e * K + h] - want) <= 2.5e-7f * want, "R0 alpha");
+            }
+        }
+    std::cout << "MIRROR PASS r0_trace edges=" << g.e << "\n";
 }
 
 }  // namespace

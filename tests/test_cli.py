@@ -37,6 +37,15 @@ def test_cli_argument_errors():
     assert r.returncode == 1 and "provide --weights checkpoint.bin or explicit --seed" in r.stderr
     r = run("--graph", "/nonexistent.gatbin", "--seed", "11")
     assert r.returncode == 1 and "FAIL cannot open graph" in r.stderr
+    # modes and their checks (bench/main.cpp:33-35,103-121,145-147)
+    g0 = str(GOLDEN / "fixture_small.gatbin")
+    for args, msg in ((("--mode", "nope"), "FAIL bad mode"),
+                      (("--mode", "profile"), "FAIL profile requires profile binary"),
+                      (("--mode", "export-fixture"), "FAIL --fixture output is required"),
+                      (("--init-policy", "cold"), "FAIL bad init policy"),
+                      (("--mode", "benchmark", "--layer", "2"), "FAIL --layer: only whole-model runs")):
+        r = run("--graph", g0, "--seed", "11", *args)
+        assert r.returncode == 1 and msg in r.stderr, (args, r.stderr)
     # bench/main.cpp:61-63: the LR policy checks
     g = str(GOLDEN / "fixture_small.gatbin")
     r = run("--graph", g, "--seed", "11", "--lr-policy", "nope")
