@@ -415,7 +415,7 @@ void online_checks() {
             for (uint64_t e = g.row[i]; e < g.row[i + 1]; ++e) {
                 const float diff = w.score[e * K + h] - m;  // R0 subtracts in FP32
                 const double want = std::exp(double(diff));
-                expect(std::fabs(w.p[e * K + h] - want) <= 1e-6 * want, "R0 p");
+                expect(std::fabs(w.p[e * K + h] - want) <= 1e-6 * want + 1e-37, "R0 p");
                 den += w.p[e * K + h];
             }
             expect(std::fabs(w.den[i * K + h] - den) <= 1e-5 * std::max(den, 1e-30), "R0 den");
