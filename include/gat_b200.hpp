@@ -645,9 +645,9 @@ inline Fixture load_fixture(const Graph& g, const Param& p, const std::string& p
 // With counters=true the exact counts are filled: the Online units (blocks, max
 // updates, rescales, rescale events and the per-row arrays) from
 // gat_b200_tfs_online_counters, and the counts of the reference's fixed CPU
-// schedule (neighbour steps, AMX calls and FMAs, conversions, spills) from the
-// degree order in batches of 16 rows. The sampled seconds stay 0, and so do
-// heads_hybrid's PH counters, which depend on its AVX/AMX split per block.
+// schedule (neighbour steps, AMX calls and FMAs, conversions, spills, and
+// heads_hybrid's PH work by its AVX/AMX split per block) from the CSR and the
+// degree order in batches of 16 rows. The sampled seconds stay 0.
 namespace icpp_online {
 struct Timing {
     double convert = 0, lr = 0, kernel = 0, normalize = 0, activation = 0, total = 0;
@@ -1002,13 +1002,17 @@ inline void validate(const Graph& g, const Param& p, const Prepared& q, const Sc
     if (counters && (o.row_blocks.size() != nk || o.row_max_updates.size() != nk || o.row_rescales.size() != nk))
         throw std::runtime_error("ICPP heads counter arrays not allocated");
 }
-// The counts of the optimized kernel (icpp_heads_hybrid.cpp:100-265): one UW
-// projection per head and neighbour block of a batch, V stored at every head
-// switch and reloaded after the first block.
+// The counts of the optimized kernel (icpp_heads_hybrid.cpp:100-265), as the
+// reference's own work identities state them (tfs_online/adaptive_main.cpp:
+// 44-60): one UW projection per head and neighbour block of a batch, V stored
+// at every head switch and reloaded after the first block; per row and block of
+// `len` neighbours, PH on AMX (high and low halves) when len >= threshold, else
+// on AVX over the FP32 p.
 inline void stats_of(const Graph& g, const Param& p, const Prepared& q, const Schedule& sched, int block,
-                     const uint64_t tot[5], Stats& st) {
+                     int threshold, const uint64_t tot[5], Stats& st) {
     auto& s = st.baseline;
-    const uint64_t dp = uint64_t(q.padded_in), K = uint64_t(p.heads);
+    const uint64_t dp = uint64_t(q.padded_in), K = uint64_t(p.heads), in = uint64_t(p.in);
+    const uint64_t in16 = (in + 15) / 16 * 16;
     const auto b = gat_b200::detail::batch_steps(g, sched, block);
     const uint64_t calls = K * b.blocks;
     gat_b200::detail::online_units(tot, 32, 32, s);
@@ -1018,6 +1022,25 @@ inline void stats_of(const Graph& g, const Param& p, const Prepared& q, const Sc
     st.projection_calls = calls;
     st.head_switch_store_bytes = calls * 2048;
     st.head_switch_reload_bytes = (calls - K * b.active) * 2048;
+    uint64_t amx = 0, avx = 0, avx_edges = 0;
+    for (uint64_t i = 0; i < g.n; ++i) {
+        const uint64_t deg = g.row[i + 1] - g.row[i];
+        for (uint64_t at = 0; at < deg; at += uint64_t(block)) {
+            const uint64_t len = std::min<uint64_t>(uint64_t(block), deg - at);
+            if (len < uint64_t(threshold)) {
+                ++avx;
+                avx_edges += len;
+            } else {
+                ++amx;
+            }
+        }
+    }
+    st.ph_calls = amx * (dp / 16) * 2;
+    st.ph_physical_fma = amx * K * 32 * dp * 2 + avx_edges * K * in16;
+    st.ph_useful_fma = g.e * K * in;
+    st.raw_H_bytes = g.e * in * sizeof(BF16);
+    st.packed_H_bytes = amx * 32 * dp * sizeof(BF16);
+    st.ub_scatter_bytes = amx * K * dp * sizeof(float) + avx * K * in16 * sizeof(float);
 }
 }  // namespace detail
 // icpp_heads_hybrid.hpp:18-20
@@ -1038,7 +1061,7 @@ inline void aggregate(const Graph& g, const Param& p, const Prepared& q, const S
     uint64_t tot[5] = {};
     gat_b200::detail::online_from_host(g, p, q, w.fallback.original, GAT_B200_TFS_SPLIT, block, threshold, counters,
                                        tot);
-    if (counters) detail::stats_of(g, p, q, sched, block, tot, stats);
+    if (counters) detail::stats_of(g, p, q, sched, block, threshold, tot, stats);
     gat_b200::detail::tiles(g, p.heads, profile_period, counters, stats.baseline);
 }
 // icpp_heads_hybrid.hpp:21-24
@@ -1065,7 +1088,7 @@ inline void layer(const Graph& g, const Param& p, const Prepared& q, const Sched
     uint64_t tot[5] = {};
     gat_b200::detail::online_layer(g, p, q, input, w.fallback.original, hidden, policy, GAT_B200_TFS_SPLIT, block,
                                    threshold, counters, t, tot);
-    if (counters) detail::stats_of(g, p, q, sched, block, tot, stats);
+    if (counters) detail::stats_of(g, p, q, sched, block, threshold, tot, stats);
     gat_b200::detail::tiles(g, p.heads, profile_period, counters, stats.baseline);
 }
 }  // namespace icpp_heads_hybrid

@@ -379,6 +379,11 @@ void online_checks() {
                     expect(sh.projection_calls == K * steps.blocks && sh.baseline.blocks == so.blocks &&
                                sh.baseline.rescales == so.rescales,
                            "hybrid counts");
+                    if (optimized)  // the reference's work identities (adaptive_main.cpp:50-53)
+                        expect(sh.ph_useful_fma == uint64_t(K) * g.e * uint64_t(D) &&
+                                   sh.raw_H_bytes == g.e * uint64_t(D) * 2 && sh.baseline.spill_bytes == 0 &&
+                                   sh.head_switch_reload_bytes == (steps.blocks - steps.active) * uint64_t(K) * 2048,
+                               "hybrid work identities");
                     if (!optimized) {
                         const auto ef = gat::errors(wk.original.base.out, wh.fallback.original.base.out);
                         expect(ef.finite && ef.max_abs <= 1e-5, "hybrid falls back to icpp_block");
