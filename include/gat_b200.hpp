@@ -491,7 +491,11 @@ inline void finish(const Graph& g, const Param& p, Workspace& w, bool hidden, Ti
 inline void standard_layer(const Graph& g, const Param& p, const Prepared& q, const std::vector<float>& input,
                            Workspace& w, bool hidden, Times& t, bool fp32 = false,
                            const std::string& lr_policy = "z_avx") {
-    (void)lr_policy;
+    // "z_avx" / "z_mkl": L and R from Z (the projection's epilogue); any other
+    // policy is lr_reordered's (baseline_standard.cpp:103-105), the attention of
+    // the matched_attention path
+    const bool matched = lr_policy != "z_avx" && lr_policy != "z_mkl";
+    const int policy = matched ? detail::lr_policy(lr_policy) : 0;
     auto t0 = Clock::now();
     if (input.size() != checked(g.n, uint64_t(p.in))) throw std::runtime_error("layer input size mismatch");
     detail::need(w.out, checked(g.n, uint64_t(p.width())), "out");
@@ -508,15 +512,30 @@ inline void standard_layer(const Graph& g, const Param& p, const Prepared& q, co
     float* l = static_cast<float*>(w.d_left->get(w.left.size() * 4));
     float* r = static_cast<float*>(w.d_right->get(w.right.size() * 4));
     float* o = static_cast<float*>(w.d_out->get(w.out.size() * 4));
-    check(gat_b200_standard_layer(w.graph->of(g), q.layer->p, x, ldx,
-                                  fp32 ? GAT_B200_PATH_STANDARD_FP32 : GAT_B200_PATH_STANDARD_BF16, hidden, h, l, r,
-                                  o, GAT_B200_F32, p.width(), nullptr));
+    if (!matched) {
+        check(gat_b200_standard_layer(w.graph->of(g), q.layer->p, x, ldx,
+                                      fp32 ? GAT_B200_PATH_STANDARD_FP32 : GAT_B200_PATH_STANDARD_BF16, hidden, h, l,
+                                      r, o, GAT_B200_F32, p.width(), nullptr));
+    } else {
+        const int ldh = detail::padded(p.width(), hd);
+        check(gat_b200_projection(q.layer->p, g.n, x, ldx, hd, h, hd, ldh, l, r, nullptr));
+        // lr_reordered reads the FP32 input ("fp32", "avx") or its BF16 copy ("bf16")
+        const void* xl = w.d_x->p;
+        int xdt = GAT_B200_F32, ldl = p.in;
+        if (policy == GAT_B200_LR_BF16) {
+            xl = fp32 ? detail::upload_bf16(w, input, g.n, p.in, ldl) : x;
+            if (!fp32) ldl = ldx;
+            xdt = GAT_B200_BF16;
+        }
+        check(gat_b200_lr_reordered(q.layer->p, g.n, xl, xdt, ldl, policy, nullptr, 0, l, r, nullptr));
+        check(gat_b200_aggregate_fused(w.graph->of(g), p.heads, p.dim, h, hd, ldh, l, r, hidden, o, GAT_B200_F32,
+                                       p.width(), nullptr));
+    }
     w.d_out->download(w.out);
     w.d_left->download(w.left);
     w.d_right->download(w.right);
     t.total += seconds(t0, Clock::now());
 }
-// R0 (baseline/src/ref_fp32.cpp:3-26): served by the FP32 path.
 // R0 (baseline/src/ref_fp32.cpp:3-26): out from the FP32 path (FP32 projection,
 // aggregation, finish), and the R0 trace from gat_b200_edge_softmax: z, left,
 // right, and max, den in R0's order, with score, p and alpha when the workspace

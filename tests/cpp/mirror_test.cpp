@@ -395,6 +395,26 @@ void online_checks() {
                 }
             }
     std::cout << "MIRROR PASS online cases=" << cases << "\n";
+    // standard_layer with an lr_reordered policy (matched attention,
+    // baseline_standard.cpp:103-105): L and R are lr_reordered's, and the layer
+    // meets the BF16 gate
+    for (int K : {1, 8})
+        for (const std::string policy : {"bf16", "fp32", "avx"}) {
+            gat::Graph g = boundary_graph(33);
+            gat::Param p = params(33, K, 32, 7 + K);
+            gat::Prepared q = gat::prepare(p);
+            gat::Workspace wm, wl;
+            wm.allocate(g, p, "matched_attention");
+            wl.allocate(g, p, "tfs_bf16");
+            gat::Times t;
+            gat::standard_layer(g, p, q, g.x, wm, true, t, false, policy);
+            gat::lr_reordered(g, p, q, g.x, wl, policy);
+            const auto el = gat::errors(wl.left, wm.left), er = gat::errors(wl.right, wm.right);
+            expect(el.finite && er.finite && el.max_abs <= 1e-6 && er.max_abs <= 1e-6, "matched attention L/R");
+            const auto em = gat::errors(fp64_layer(g, p, g.x, true, true), wm.out);
+            expect(em.finite && em.relative_l2 < 1e-2, "matched attention layer vs FP64");
+            std::cout << "MIRROR PASS matched K=" << K << " policy=" << policy << " rel=" << em.relative_l2 << "\n";
+        }
     // R0's trace (ref_fp32.cpp:7-14) from a ref_fp32 workspace: score and the
     // row maximum bit for bit from the layer's own L/R, p within the ulps of
     // two exp implementations, den and alpha to FP32 rounding
