@@ -129,3 +129,16 @@ def test_tfs_online_smoke_and_report():
         if ln.startswith("CHECK") and "B1_PREMAX_same_input_same_LR" in ln:
             assert "original_abs_003_gate=PASS" in ln, ln
     assert lines[-1].startswith("ICPP_ONLINE_COMPLETE")
+
+
+# ---- gat_b200_tfs_adaptive: the reference's tfs_online/adaptive_main.cpp interface ----
+ADAPTIVE = ROOT / "gat-tfs_b200" / "gat_b200_tfs_adaptive"
+
+
+def test_tfs_adaptive_argument_errors():
+    if not ADAPTIVE.exists():
+        subprocess.run(["python", str(ROOT / "gat-tfs_b200" / "build.py")], check=True)
+    r = subprocess.run([str(ADAPTIVE), "a", "b"], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 1 and "ICPP_HEADS_FAIL usage: icpp_heads GRAPH THREADS" in r.stderr
+    r = subprocess.run([str(ADAPTIVE), "g", "0", "1", "1", "1"], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 1 and "ICPP_HEADS_FAIL invalid configuration" in r.stderr

@@ -12,6 +12,8 @@
   the fixture the reference itself exported (tests/golden/fixture_small_l1.gatfix);
 - the driver's operator modes (bench/main.cpp:103-151): export-fixture against
   that same file, fixed-p on it with the reference's error controls, and micro.
+- the adaptive experiment driver (tfs_online/adaptive_main.cpp): its smoke and a
+  full run, whose exact counters pass the reference's own work identities.
 
 The kernels underneath the online variants are checked against the oracle in
 test_gpu_tfs.py. This file is collected late so that a failure here leaves the
@@ -122,3 +124,23 @@ def test_driver_operator_modes(tmp_path):
     names = {f.split("=")[1] for l in out.splitlines() if l.startswith("MICRO ") for f in l.split()[1:2]}
     assert {"convert_rne", "projection_bf16", "lr_reordered_bf16", "lr_reordered_fp32", "max_prescan",
             "weighted_spmm_score_exp"} <= names
+
+
+def test_adaptive_driver():
+    exe = PKG / "gat_b200_tfs_adaptive"
+    r = subprocess.run([str(exe), "--smoke"], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "SMOKE PASS cases=6" in r.stdout, r.stdout + r.stderr
+    r = subprocess.run([str(exe), str(GOLDEN / "fixture_small.gatbin"), "2", "1", "2", "4"], capture_output=True,
+                       text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    out = r.stdout.splitlines()
+    checks = [l for l in out if l.startswith("CHECK ")]
+    assert len(checks) == 3 * 3 + 2 + 1  # chains of 3 paths, 2 layer-2 controls, the layer-3 control
+    assert all(" finite=1 " in l for l in checks)
+    recs = [json.loads(l) for l in out if l.startswith("{")]
+    assert len(recs) == 3 * 2 * 3 and {r["path"] for r in recs} == {"B0_BF16", "HYBRID_T16_B32",
+                                                                        "TFS_L12_B0_L3_MATCHED"}
+    assert sum(l.startswith("PROFILE_IDENTITY ") and l.endswith("bit_fingerprint_equal=1") for l in out) == 3
+    assert sum(l.startswith("ONLINE_STATS ") for l in out) == 3 and sum(l.startswith("HEAD_WORK ") for l in out) == 3
+    assert sum(l.startswith("HYBRID_MIX ") for l in out) == 2  # layers 1-2; layer 3 is icpp_block
+    assert out[-1].startswith("ICPP_HEADS_COMPLETE")
