@@ -5,7 +5,7 @@
 Each source compiles to an object under gat-tfs_b200/_build/ (in parallel), and
 the objects link into gat-tfs_b200/libgat_b200.so with the CUDA runtime linked
 statically, so the library needs only the NVIDIA driver at run time. The C++
-drivers in cli/ (gat_b200_bench, gat_b200_tfs_online) link against it. A source
+drivers in cli/ (gat_b200_bench, gat_b200_tfs_online, gat_b200_tfs_adaptive) link against it. A source
 is recompiled only when it or a header is newer than its object.
 """
 import argparse
