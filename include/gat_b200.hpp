@@ -1,5 +1,6 @@
-// C++ mirror of the reference's host API (baseline/include/gat.hpp) over the
-// C ABI of libgat_b200.so (include/gat_b200.h). A caller of the reference
+// C++ mirror of the reference's host API (baseline/include/gat.hpp, and the
+// online TFS experiments of baseline/tfs_online/icpp_*.hpp) over the C ABI of
+// libgat_b200.so (include/gat_b200.h). A caller of the reference
 // switches by including this header and aliasing the namespace:
 //
 //   #include "gat_b200.hpp"
@@ -14,9 +15,11 @@
 // There is no host arithmetic on the compute path. Differences, by design:
 //   * projection() computes Z together with L and R (one tensor-core kernel);
 //     lr_from_z() checks that they came from the preceding projection();
-//   * ref_layer() (R0) is served by the FP32 path, which the library's tests pin
-//     to R0 at max-abs <= 1e-5;
-//   * standard_layer() runs the fused layer: it writes out, left and right;
+//   * ref_layer() (R0) takes its output from the FP32 path, which the
+//     library's tests pin to R0 at max-abs <= 1e-5, and its trace (max, den,
+//     score, p, alpha) from R0's edge softmax on the device;
+//   * standard_layer() runs the fused layer: it writes out, left and right
+//     (with an lr_reordered policy, the matched-attention layer);
 //   * the panel argument of the TFS calls has no counterpart (the degree
 //     schedule orders and balances the rows); it is accepted and ignored.
 // Header-only; link with -lgat_b200.
