@@ -181,6 +181,30 @@ void host_checks(const std::string& dir) {
         for (uint32_t i = 0; i < g.n; ++i) id.perm.push_back(i);
         const auto b16 = gat::detail::batch_steps(g, id, 16);
         expect(b16.batches == 3 && b16.active == 3 && b16.steps == 291 && b16.blocks == 21, "batch steps");
+        // the work counts of the reference's CPU schedule from the CSR and the
+        // degree order (icpp_block.cpp:100-212; the identities of
+        // adaptive_main.cpp:44-60), against values computed separately from
+        // those formulas for this graph; tot[] holds given Online units
+        const uint64_t tot[5] = {0, 0, 5, 3, 0};
+        gat::Prepared qh;
+        qh.padded_in = 32;
+        qh.output_blocks = 2;
+        gat::icpp_heads_hybrid::Stats sh2;
+        gat::icpp_heads_hybrid::detail::stats_of(g, params(17, 8, 32, 1), qh, id, 32, 16, tot, sh2);
+        expect(sh2.ph_calls == 140 && sh2.ph_physical_fma == 589056 && sh2.packed_H_bytes == 71680 &&
+                   sh2.ub_scatter_bytes == 52224 && sh2.ph_useful_fma == 147288 && sh2.raw_H_bytes == 36822 &&
+                   sh2.projection_calls == 96 && sh2.baseline.amx_calls == 192 &&
+                   sh2.baseline.executed_fma == 1572864 && sh2.head_switch_store_bytes == 96 * 2048 &&
+                   sh2.head_switch_reload_bytes == 72 * 2048 && sh2.baseline.rescaled_feature_elements == 5 * 32,
+               "hybrid work counts");
+        qh.output_blocks = 1;
+        gat::icpp_block::Stats sb2;
+        gat::detail::block_stats(g, params(17, 2, 16, 1), qh, id, 16, tot, sb2);
+        expect(sb2.block_projection_calls == 42 && sb2.baseline.amx_calls == 42 &&
+                   sb2.baseline.executed_fma == 344064 && sb2.conversion_elements == 21504 &&
+                   sb2.actual_input_feature_FMA == 36822 && sb2.padded_input_feature_FMA == 69312 &&
+                   sb2.logical_H_bytes == 73644 && sb2.baseline.spill_bytes == 3 * 1024,
+               "block work counts");
     }
     std::cout << "MIRROR PASS host\n";
 }
