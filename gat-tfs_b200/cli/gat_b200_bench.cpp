@@ -11,11 +11,13 @@
 // Paths: ref_fp32 (served by the FP32 path, which the test suite pins to the
 // reference's R0 at max-abs <= 1e-5), standard_fp32, standard_bf16, tfs_bf16,
 // matched_attention, and adaptive_bf16 (layer 1 through TFS aggregation).
-// Modes: benchmark, correctness (with --dump-prefix), and the operator modes
-// micro, export-fixture and fixed-p on one layer (--layer, default 2). A
-// forward is timed end to end on the host clock: FP32 X from host memory in,
-// FP32 logits to host memory out, as the reference times its forward over host
-// buffers. The operator modes time each operation on device-resident buffers.
+// Modes: benchmark (the three-layer forward, or one layer with --layer N),
+// correctness (with --dump-prefix), and the operator modes micro,
+// export-fixture and fixed-p on one layer (--layer, default 2). A forward is
+// timed end to end on the host clock: FP32 X from host memory in, FP32 logits
+// to host memory out, as the reference times its forward over host buffers.
+// A single layer and the operator modes time each stage on device-resident
+// buffers.
 // --init-policy and --diagnostics are accepted: they place the reference's CPU
 // threads and report its NUMA maps, which have no device counterpart.
 #include <algorithm>
@@ -150,6 +152,83 @@ double timed_ms(F&& f) {
     return seconds(t0, Clock::now()) * 1000;
 }
 
+// The input of layer `layer` (1-based): the R0 chain of the layers before it
+// (bench/main.cpp:105-106,168).
+std::vector<float> r0_input(const gat::Graph& g, const gat::Model& model, int layer) {
+    std::vector<float> input = g.x;
+    for (int l = 0; l < layer - 1; ++l) {
+        gat::Workspace rw;
+        rw.allocate(g, model[l], "standard_fp32");
+        gat::Times t;
+        gat::ref_layer(g, model[l], input, rw, true, t);
+        input = std::move(rw.out);
+    }
+    return input;
+}
+
+// One layer of `pc` (0-based l) from FP32 device rows xf [n][in] into out
+// (FP32 [n][width]), each stage timed alone (host clock and a device
+// synchronisation): the single-layer benchmark of bench/main.cpp:166-180.
+struct LayerBuffers {
+    gat::detail::DeviceBuffer xb, h, left, right, max, den, out;
+};
+StageMs run_single_layer(Device& dev, const gat::Model& model, int pc, int l, const float* xf, uint64_t n,
+                         LayerBuffers& b) {
+    const gat::Param& p = model[l];
+    const gat_b200_layer* lp = dev.layer[l];
+    const int K = p.heads, d = p.dim, W = p.width(), D = p.in;
+    const bool hidden = l < 2;
+    const int ldb = gat_b200_padded_ld(D, GAT_B200_BF16);
+    uint16_t* xb = static_cast<uint16_t*>(b.xb.get(n * size_t(ldb) * 2));
+    float* L = static_cast<float*>(b.left.get(n * K * 4));
+    float* R = static_cast<float*>(b.right.get(n * K * 4));
+    float* out = static_cast<float*>(b.out.get(n * size_t(W) * 4));
+    StageMs t;
+    const bool tfs = pc == GAT_B200_PATH_TFS_BF16 || (pc == GAT_B200_PATH_ADAPTIVE_BF16 && l == 0);
+    if (tfs) {
+        // baseline_tfs.cpp:111-117: convert + lr_reordered ("bf16"), max_prescan,
+        // TFS aggregation (B1 rounding; the adaptive path's layer 1 rounds as
+        // heads_hybrid with one block per row), finish
+        float* M = static_cast<float*>(b.max.get(n * K * 4));
+        float* dn = static_cast<float*>(b.den.get(n * K * 4));
+        t.lr = timed_ms([&] {
+            check(gat_b200_lr_reordered(lp, n, xf, GAT_B200_F32, D, GAT_B200_LR_BF16, xb, ldb, L, R, nullptr));
+        });
+        t.max_prescan = timed_ms([&] { check(gat_b200_max_prescan(dev.g, K, L, R, M, nullptr)); });
+        const int rounding = pc == GAT_B200_PATH_TFS_BF16 ? GAT_B200_TFS_EDGE : GAT_B200_TFS_SPLIT;
+        t.aggregate = timed_ms([&] {
+            check(gat_b200_tfs_aggregate(dev.g, lp, xb, ldb, L, R, M, nullptr, nullptr, rounding, 0, 1, out, W, dn,
+                                         nullptr, nullptr));
+        });
+        t.normalize = timed_ms([&] { check(gat_b200_finish(n, K, d, dn, hidden, out, W, nullptr)); });
+    } else {
+        // baseline_standard.cpp:98-108: convert, projection with L/R (or
+        // lr_reordered "bf16" on the matched path), the aggregation with max,
+        // normalisation and ELU fused
+        const bool fp32 = pc == GAT_B200_PATH_STANDARD_FP32;
+        const int hd = fp32 ? GAT_B200_F32 : GAT_B200_BF16, ldh = gat_b200_padded_ld(W, hd);
+        void* h = b.h.get(n * size_t(ldh) * (fp32 ? 4 : 2));
+        const void* x = xf;
+        int ldx = D;
+        if (!fp32) {
+            t.convert = timed_ms([&] { check(gat_b200_convert(n, D, xf, D, xb, ldb, nullptr)); });
+            x = xb;
+            ldx = ldb;
+        }
+        t.projection = timed_ms([&] { check(gat_b200_projection(lp, n, x, ldx, hd, h, hd, ldh, L, R, nullptr)); });
+        if (pc == GAT_B200_PATH_MATCHED_ATTENTION)
+            t.lr = timed_ms([&] {
+                check(gat_b200_lr_reordered(lp, n, xb, GAT_B200_BF16, ldb, GAT_B200_LR_BF16, nullptr, 0, L, R,
+                                            nullptr));
+            });
+        t.aggregate = timed_ms([&] {
+            check(gat_b200_aggregate_fused(dev.g, K, d, h, hd, ldh, L, R, hidden, out, GAT_B200_F32, W, nullptr));
+        });
+    }
+    t.total = t.convert + t.projection + t.lr + t.max_prescan + t.aggregate + t.normalize;
+    return t;
+}
+
 // The operator modes of the reference's driver on one layer (bench/main.cpp:103-151):
 //   micro           each stage of the layer timed alone (MICRO lines)
 //   export-fixture  R0's weights p and den of the layer, written as GATFIX1
@@ -166,14 +245,7 @@ int operator_modes(const Args& a, const std::string& mode, const gat::Graph& g, 
     const int layer = layer_arg ? layer_arg : 2;
     const gat::Param& p = model[layer - 1];
     const gat_b200_layer* lp = dev.layer[layer - 1];
-    std::vector<float> input = g.x;
-    for (int l = 0; l < layer - 1; ++l) {
-        gat::Workspace rw;
-        rw.allocate(g, model[l], "standard_fp32");
-        gat::Times t;
-        gat::ref_layer(g, model[l], input, rw, true, t);
-        input = std::move(rw.out);
-    }
+    std::vector<float> input = r0_input(g, model, layer);
     const uint64_t n = g.n, e = g.e;
     const int K = p.heads, d = p.dim, W = p.width(), D = p.in;
     const int ldb = gat_b200_padded_ld(D, GAT_B200_BF16), ldz = gat_b200_padded_ld(W, GAT_B200_F32);
@@ -358,8 +430,6 @@ int main(int argc, char** argv) {
         // the profile mode needs the reference's counter build (GAT_PROFILE); this
         // backend's stage times come from CUDA events in every benchmark run
         if (mode == "profile") throw std::runtime_error("profile requires profile binary");
-        if (mode == "benchmark" && layer_arg != 0)
-            throw std::runtime_error("--layer: only whole-model runs (0) on this backend");
         if (mode == "export-fixture" && a.get("--fixture").empty())
             throw std::runtime_error("--fixture output is required");
         const std::string init = a.get("--init-policy", "original");
@@ -460,6 +530,41 @@ int main(int argc, char** argv) {
             return operator_modes(a, mode, g, model, dev, layer_arg, threads, panel, reps, warmups,
                                   (degree_sort_s + prepare_s) * 1000, neighbor_steps);
 
+        if (layer_arg != 0) {
+            // one layer on the R0 chain's input (bench/main.cpp:166-180), the
+            // input resident on the device before the timer starts
+            const int l = layer_arg - 1;
+            const std::vector<float> input = r0_input(g, model, layer_arg);
+            gat::detail::DeviceBuffer bx;
+            const float* xf = bx.upload(input);
+            LayerBuffers buf;
+            std::cout << "MODEL workspace_bytes=" << g.n * size_t(model[l].in) * 4 << " static_bytes=" << g.n * 4
+                      << " excludes_graph_and_master_weights=true\n";
+            std::cout << "COLD startup_before_inference_ms=" << seconds(cold_start, Clock::now()) * 1000
+                      << " includes_graph_load=true\n";
+            std::vector<double> totals;
+            double cold_forward = 0;
+            const bool fp32 = pc == GAT_B200_PATH_STANDARD_FP32;
+            for (int r = -warmups; r < reps; ++r) {
+                StageMs t = run_single_layer(dev, model, pc, l, xf, g.n, buf);
+                if (r == -warmups) cold_forward = t.total;
+                if (r < 0) continue;
+                totals.push_back(t.total);
+                const bool tfs = pc == GAT_B200_PATH_TFS_BF16 || (pc == GAT_B200_PATH_ADAPTIVE_BF16 && l == 0);
+                t.neighbor_steps = tfs ? neighbor_steps * model[l].heads : 0;
+                print_times(path, mode, layer_arg, r, g, model[l], threads, fp32, t, (degree_sort_s + prepare_s) * 1000,
+                            panel);
+                std::cout << "E2E path=" << path << " rep=" << r << " layer=" << layer_arg << " total_ms=" << t.total
+                          << " finite=1\n";
+            }
+            std::vector<float> o(g.n * size_t(model[l].width()));
+            buf.out.download(o);
+            gat::require_finite(o, "benchmark output");
+            if (!a.get("--output").empty()) dump(a.get("--output"), o);
+            std::cout << "SUMMARY path=" << path << " median_ms=" << pct(totals, .5) << " p95_ms=" << pct(totals, .95)
+                      << " cold_forward_ms=" << cold_forward << " repeats=" << reps << " task_accuracy=UNVERIFIED\n";
+            return 0;
+        }
         gat_b200_model* m = dev.model(pc);
         check(gat_b200_model_enable_timing(m, 1));
         std::cout << "MODEL workspace_bytes=" << g.n * size_t(g.din) * 4 << " static_bytes=" << g.n * 4

@@ -43,7 +43,7 @@ def test_cli_argument_errors():
                       (("--mode", "profile"), "FAIL profile requires profile binary"),
                       (("--mode", "export-fixture"), "FAIL --fixture output is required"),
                       (("--init-policy", "cold"), "FAIL bad init policy"),
-                      (("--mode", "benchmark", "--layer", "2"), "FAIL --layer: only whole-model runs")):
+                      (("--mode", "benchmark", "--layer", "4"), "FAIL invalid benchmark controls")):
         r = run("--graph", g0, "--seed", "11", *args)
         assert r.returncode == 1 and msg in r.stderr, (args, r.stderr)
     # bench/main.cpp:61-63: the LR policy checks

@@ -14,6 +14,8 @@
   that same file, fixed-p on it with the reference's error controls, and micro.
 - the adaptive experiment driver (tfs_online/adaptive_main.cpp): its smoke and a
   full run, whose exact counters pass the reference's own work identities.
+- the driver's single-layer benchmark (--layer N, bench/main.cpp:166-180) on every
+  path, its exported layer output against the oracle's R0 chain.
 
 The kernels underneath the online variants are checked against the oracle in
 test_gpu_tfs.py. This file is collected late so that a failure here leaves the
@@ -144,3 +146,26 @@ def test_adaptive_driver():
     assert sum(l.startswith("ONLINE_STATS ") for l in out) == 3 and sum(l.startswith("HEAD_WORK ") for l in out) == 3
     assert sum(l.startswith("HYBRID_MIX ") for l in out) == 2  # layers 1-2; layer 3 is icpp_block
     assert out[-1].startswith("ICPP_HEADS_COMPLETE")
+
+
+@pytest.mark.parametrize("path,layer,tol", [("standard_fp32", 2, 1e-4), ("standard_bf16", 2, 1e-2),
+                                            ("matched_attention", 2, 1e-2), ("tfs_bf16", 1, 3e-2),
+                                            ("adaptive_bf16", 1, 3e-2), ("standard_bf16", 3, 1e-2)])
+def test_driver_single_layer_benchmark(tmp_path, path, layer, tol):
+    import oracle as O
+    graph = GOLDEN / "fixture_small.gatbin"
+    dump = tmp_path / "layer.f32"
+    out = _driver("--graph", graph, "--seed", 11, "--path", path, "--mode", "benchmark", "--layer", layer,
+                  "--warmups", 1, "--repeats", 3, "--output", dump)
+    lines = out.splitlines()
+    recs = [json.loads(l) for l in lines if l.startswith("{")]
+    assert len(recs) == 3 and all(r["layer"] == layer and r["path"] == path for r in recs)
+    assert all(r["total_ms"] > 0 for r in recs)
+    assert sum(l.startswith(f"E2E path={path} ") and f" layer={layer} " in l for l in lines) == 3
+    assert any(l.startswith("SUMMARY ") for l in lines)
+    g = G.load_graph(graph)
+    model = G.random_model(g.din, g.classes, 11)
+    ref = O.ref_chain(g.row, g.col, g.x, [(p.w, p.al, p.ar, p.heads, p.dim) for p in model])[layer - 1]["out"]
+    got = np.fromfile(dump, np.float32).reshape(ref.shape)
+    e = O.errors(ref, got)
+    assert e["finite"] and e["relative_l2"] <= tol, e
