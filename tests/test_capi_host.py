@@ -171,3 +171,15 @@ def test_multi_gpu_and_rmat_entry_points_validate_arguments():
     assert lib.gat_b200_synth_rmat(2, 10, 0.57, 0.19, 0.19, 1, 3, 2, rp, None, None) == 1
     assert "bad row range" in lib.gat_b200_last_error().decode()
     assert lib.gat_b200_synth_rmat(30, 1 << 31, 0.57, 0.19, 0.19, 1, 0, 0, rp, None, None) == 1
+
+
+def test_edge_softmax_validates_arguments():
+    """gat_b200_edge_softmax's checks come before any CUDA call."""
+    lib = G._lib
+    vp = C.c_void_p
+    assert lib.gat_b200_edge_softmax(None, 8, vp(1), vp(1), None, None, vp(1), vp(1), None, None) == 1
+    assert "edge_softmax: null buffer" in lib.gat_b200_last_error().decode()
+    assert lib.gat_b200_edge_softmax(vp(1), 8, vp(1), vp(1), None, None, None, vp(1), None, None) == 1
+    assert "edge_softmax: null buffer" in lib.gat_b200_last_error().decode()
+    assert lib.gat_b200_edge_softmax(vp(1), 9, vp(1), vp(1), None, None, vp(1), vp(1), None, None) == 1
+    assert "invalid parameter shape" in lib.gat_b200_last_error().decode()
