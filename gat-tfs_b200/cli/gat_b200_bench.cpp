@@ -53,13 +53,15 @@ struct Args {
             "--threads", "--panel-r",  "--repeats", "--warmups",      "--layer",       "--lr-policy",
             "--fixture", "--max-abs",  "--rel-l2",  "--dump-prefix",  "--output",      "--init-policy",
             "--diagnostics"};
+        // bench/main.cpp:9-14: pairs first (duplicates rejected), then the names
         for (int i = 1; i < argc; ++i) {
             std::string k = argv[i];
             if (k.rfind("--", 0) != 0 || i + 1 == argc) throw std::runtime_error("arguments must be --key value");
-            if (std::find(allowed.begin(), allowed.end(), k) == allowed.end())
-                throw std::runtime_error("unknown argument " + k);
-            if (!v.emplace(k, argv[++i]).second) throw std::runtime_error("duplicate argument " + k);
+            if (!v.emplace(k, argv[++i]).second) throw std::runtime_error("duplicate argument: " + k);
         }
+        for (const auto& kv : v)
+            if (std::find(allowed.begin(), allowed.end(), kv.first) == allowed.end())
+                throw std::runtime_error("unknown option: " + kv.first);
     }
     std::string get(const std::string& k, const std::string& def = "") const {
         auto i = v.find(k);

@@ -28,7 +28,9 @@ def test_cli_argument_errors():
     r = run("--graph")
     assert r.returncode == 1 and "FAIL arguments must be --key value" in r.stderr
     r = run("--graph", "x", "--graph", "y")
-    assert r.returncode == 1 and "FAIL duplicate argument --graph" in r.stderr
+    assert r.returncode == 1 and "FAIL duplicate argument: --graph" in r.stderr
+    r = run("--graph", "x", "--nope", "1")
+    assert r.returncode == 1 and "FAIL unknown option: --nope" in r.stderr
     r = run("--mode", "benchmark")
     assert r.returncode == 1 and "FAIL --graph is required" in r.stderr
     r = run("--graph", str(GOLDEN / "fixture_small.gatbin"), "--path", "nope")
