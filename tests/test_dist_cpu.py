@@ -7,6 +7,7 @@ gloo all-gather into the padded table, and the gathered logits must equal the
 single-process oracle bit for bit: every row sees the same sources in the same
 order, so the arithmetic is identical.
 """
+import functools
 import os
 import socket
 
@@ -134,20 +135,27 @@ def test_make_part_matches_whole_graph():
         assert np.array_equal(p.x_rows, g.x[p.lo:p.hi])
 
 
+@functools.lru_cache(maxsize=None)
+def _reference_c2():
+    return _single_process_reference("c2")
+
+
 @pytest.mark.slow
-def test_two_rank_forward_equals_single_process():
+@pytest.mark.parametrize("world,chunks", [(2, 4), (8, 2)])
+def test_partitioned_forward_equals_single_process(world, chunks):
+    """The rank-local pipeline at the bench's smallest and largest world sizes:
+    the gathered logits equal the single-process oracle bit for bit."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, "c2", q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, "c2", q, chunks)) for r in range(world)]
     for p in procs:
         p.start()
     got = q.get(timeout=600)
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    want = _single_process_reference("c2")
-    assert np.array_equal(got, want)
+    assert np.array_equal(got, _reference_c2())
 
 
 def test_partitioned_model_argument_checks():
