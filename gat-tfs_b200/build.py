@@ -74,7 +74,7 @@ def build(verbose: bool = False) -> Path:
             raise RuntimeError("link failed\n" + r.stdout + r.stderr)
     # the C++ drivers over the C ABI (cli/*.cpp -> gat-tfs_b200/<name>): the
     # reference's bench/main.cpp and tfs_online/main.cpp interfaces
-    hdr = max(h.stat().st_mtime for h in (ROOT / "include").glob("*.h*"))
+    hdr = max(h.stat().st_mtime for h in list((ROOT / "include").glob("*.h*")) + list((PKG / "cli").glob("*.hpp")))
     for src in sorted((PKG / "cli").glob("*.cpp")):
         exe = PKG / src.stem
         if not exe.exists() or exe.stat().st_mtime < max(LIB.stat().st_mtime, src.stat().st_mtime, hdr):
