@@ -6,7 +6,8 @@
 //   ref_dump boundary OUTDIR          64 D/K/d cases of baseline/tests/boundaries.cpp
 //   ref_dump chain GRAPH WEIGHTS OUTDIR   three-layer chains on a GATBIN1 graph;
 //                                     WEIGHTS = GATWGT1 path or "seed:N" (random_model)
-//   ref_dump counters GRAPH OUTDIR    icpp_online's exact counters (blocks 4/16/64)
+//   ref_dump counters GRAPH OUTDIR    icpp_online's exact counters (blocks 4/16/64),
+//                                     icpp_block's and icpp_heads_hybrid's stats
 //   ref_dump tfs OUTDIR               TFS aggregation variants (B1, icpp_online,
 //                                     icpp_block, icpp_heads_hybrid) on the
 //                                     boundary graphs, with their inputs
@@ -211,6 +212,48 @@ static int counters(const std::string& graph, const std::string& out) {
                                               st.rescaled_feature_elements, st.rescaled_padded_feature_elements,
                                               st.spill_bytes, st.reload_bytes};
         dumpv(pre + "_totals.u64", totals);
+    }
+    // icpp_block's and icpp_heads_hybrid's statistics with exact counters on the
+    // same inputs (icpp_block.hpp:17-26, icpp_heads.hpp:16-27)
+    auto base_fields = [](const icpp_online::Stats& st) {
+        return std::vector<uint64_t>{st.blocks, st.max_updates, st.rescales, st.rescale_events, st.neighbor_steps,
+                                     st.amx_calls, st.executed_fma, st.rescaled_feature_elements,
+                                     st.rescaled_padded_feature_elements, st.spill_bytes, st.reload_bytes,
+                                     st.total_tiles};
+    };
+    for (int block : {16, 32}) {
+        icpp_block::Workspace b;
+        b.allocate(g, p, true);
+        auto& bb = b.original.base;
+        bb.xbf.resize(g.x.size());
+        convert(g.x.data(), bb.xbf.data(), g.x.size());
+        bb.left = left;
+        bb.right = right;
+        icpp_block::Stats st;
+        icpp_block::aggregate(g, p, q, s, b, block, 16, st, 0, true);
+        std::vector<uint64_t> v = base_fields(st.baseline);
+        for (uint64_t x : {st.actual_input_feature_FMA, st.padded_input_feature_FMA, st.useful_projection_FMA,
+                           st.logical_H_bytes, st.block_projection_calls, st.conversion_elements,
+                           st.source_neighbor_steps})
+            v.push_back(x);
+        dumpv(out + "/counters_block" + std::to_string(block) + "_stats.u64", v);
+        for (int threshold : {1, 16, 33}) {
+            icpp_heads_hybrid::Workspace hw;
+            hw.allocate(g, p, true);
+            auto& hb = hw.fallback.original.base;
+            hb.xbf = bb.xbf;
+            hb.left = left;
+            hb.right = right;
+            icpp_heads_hybrid::Stats hs;
+            icpp_heads_hybrid::aggregate(g, p, q, s, hw, block, 16, hs, 0, true, threshold);
+            std::vector<uint64_t> u = base_fields(hs.baseline);
+            for (uint64_t x : {uint64_t(hs.optimized), hs.ph_calls, hs.ph_physical_fma, hs.ph_useful_fma,
+                               hs.raw_H_bytes, hs.packed_H_bytes, hs.projection_calls, hs.head_switch_store_bytes,
+                               hs.head_switch_reload_bytes, hs.ub_scatter_bytes})
+                u.push_back(x);
+            dumpv(out + "/counters_hybrid" + std::to_string(block) + "_t" + std::to_string(threshold) + "_stats.u64",
+                  u);
+        }
     }
     std::cout << "COUNTERS_DUMP n=" << g.n << " e=" << g.e << "\n";
     return 0;

@@ -7,9 +7,12 @@
 //   mirror_test --gpu    the layer functions on the current CUDA device
 //   mirror_test --gpu-online  the online TFS variants (icpp_online, icpp_block,
 //                        icpp_heads_hybrid) on the current CUDA device
+//   mirror_test --stats DIR   the online variants' statistics (host counting)
+//                        for the inputs in DIR
 // Prints "MIRROR PASS ..." lines; exits 1 with "MIRROR FAIL <what>" otherwise.
 #include <cmath>
 #include <cstdio>
+#include <fstream>
 #include <functional>
 #include <iostream>
 #include <string>
@@ -476,6 +479,61 @@ void online_checks() {
     std::cout << "MIRROR PASS r0_trace edges=" << g.e << "\n";
 }
 
+// --stats DIR: the online variants' statistics from the mirror's counting
+// (icpp_block and icpp_heads_hybrid, heads 8, dim 32), for the graph, degree
+// order and Online units written into DIR, one "STATS <case> <values>" line per
+// case in the order of the reference's Stats fields.
+template <class T>
+std::vector<T> read_raw(const std::string& path) {
+    std::ifstream f(path, std::ios::binary | std::ios::ate);
+    if (!f) throw std::runtime_error("cannot open " + path);
+    std::vector<T> v(size_t(f.tellg()) / sizeof(T));
+    f.seekg(0);
+    f.read(reinterpret_cast<char*>(v.data()), std::streamsize(v.size() * sizeof(T)));
+    return v;
+}
+void print_stats(const std::string& name, const gat::icpp_online::Stats& s, const std::vector<uint64_t>& extra) {
+    std::cout << "STATS " << name;
+    for (uint64_t x : {s.blocks, s.max_updates, s.rescales, s.rescale_events, s.neighbor_steps, s.amx_calls,
+                       s.executed_fma, s.rescaled_feature_elements, s.rescaled_padded_feature_elements, s.spill_bytes,
+                       s.reload_bytes, s.total_tiles})
+        std::cout << " " << x;
+    for (uint64_t x : extra) std::cout << " " << x;
+    std::cout << "\n";
+}
+void stats_checks(const std::string& dir) {
+    const gat::Graph g = gat::load_graph(dir + "/graph.gatbin");
+    gat::Schedule s;
+    s.perm = read_raw<uint32_t>(dir + "/perm.u32");
+    gat::Param p;
+    p.in = int(g.din);
+    p.heads = 8;
+    p.dim = 32;
+    gat::Prepared q;
+    q.padded_in = (p.in + 31) / 32 * 32;
+    q.output_blocks = 2;
+    for (int block : {16, 32}) {
+        const std::vector<uint64_t> tot = read_raw<uint64_t>(dir + "/units_b" + std::to_string(block) + ".u64");
+        expect(tot.size() == 5, "units file");
+        gat::icpp_block::Stats bs;
+        gat::detail::block_stats(g, p, q, s, block, tot.data(), bs);
+        gat::detail::tiles(g, p.heads, 0, true, bs.baseline);
+        print_stats("block" + std::to_string(block), bs.baseline,
+                    {bs.actual_input_feature_FMA, bs.padded_input_feature_FMA, bs.useful_projection_FMA,
+                     bs.logical_H_bytes, bs.block_projection_calls, bs.conversion_elements, bs.source_neighbor_steps});
+        for (int threshold : {1, 16, 33}) {
+            gat::icpp_heads_hybrid::Stats hs;
+            hs.optimized = true;
+            gat::icpp_heads_hybrid::detail::stats_of(g, p, q, s, block, threshold, tot.data(), hs);
+            gat::detail::tiles(g, p.heads, 0, true, hs.baseline);
+            print_stats("hybrid" + std::to_string(block) + "_t" + std::to_string(threshold), hs.baseline,
+                        {uint64_t(hs.optimized), hs.ph_calls, hs.ph_physical_fma, hs.ph_useful_fma, hs.raw_H_bytes,
+                         hs.packed_H_bytes, hs.projection_calls, hs.head_switch_store_bytes,
+                         hs.head_switch_reload_bytes, hs.ub_scatter_bytes});
+        }
+    }
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {
@@ -486,6 +544,8 @@ int main(int argc, char** argv) {
             gpu_checks();
         else if (mode == "--gpu-online")
             online_checks();
+        else if (mode == "--stats")
+            stats_checks(dir);
         else
             host_checks(dir);
         return 0;

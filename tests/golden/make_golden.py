@@ -28,7 +28,9 @@ sources in place by oracle/Makefile; nothing here is hand-written):
   * tfs_counters.npz: icpp_online's exact counters (icpp_online.hpp:18-22) on
     smoke1024 with attention scores rising with the source id, for neighbour
     blocks of 4, 16 and 64: per (row, head) blocks / max updates / rescales
-    and the Stats totals, with the L/R the reference used.
+    and the Stats totals, with the L/R the reference used; and on the same
+    inputs icpp_block's statistics (blocks of 16 and 32) and
+    icpp_heads_hybrid's (blocks of 16 and 32, thresholds 1, 16 and 33).
   * fixture_small_l1.gatfix (+ fixture_small.gatbin): a GATFIX1 fixed-p
     fixture written by the reference's own export-fixture mode
     (bench/main.cpp:103-116) for layer 1 of random_model(seed 11) on a small
@@ -137,6 +139,11 @@ def main():
             for name in ("rowblocks", "rowupdates", "rowrescales"):
                 c[f"{name}_b{b}"] = np.fromfile(d / f"counters_b{b}_{name}.u64", np.uint64).reshape(1024, 8)
             c[f"totals_b{b}"] = np.fromfile(d / f"counters_b{b}_totals.u64", np.uint64)
+        # icpp_block's and icpp_heads_hybrid's statistics on the same inputs
+        for b in (16, 32):
+            c[f"blockstats_b{b}"] = np.fromfile(d / f"counters_block{b}_stats.u64", np.uint64)
+            for t in (1, 16, 33):
+                c[f"hybridstats_b{b}_t{t}"] = np.fromfile(d / f"counters_hybrid{b}_t{t}_stats.u64", np.uint64)
         np.savez_compressed(OUT / "tfs_counters.npz", **c)
 
         # c1 from this repository's generator

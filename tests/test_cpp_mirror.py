@@ -32,3 +32,35 @@ def test_mirror_layer_functions_on_gpu(mirror_bin, tmp_path):
     r = subprocess.run([str(mirror_bin), "--gpu", str(tmp_path)], capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "MIRROR PASS gpu cases=12" in r.stdout
+
+
+def test_mirror_online_statistics_match_the_reference(mirror_bin, tmp_path):
+    """The statistics the mirror fills for icpp_block and icpp_heads_hybrid with
+    counters=true, against the Stats the reference's own code produced on
+    smoke1024 (ref_dump counters; tests/golden/tfs_counters.npz): every field,
+    from the Online units (which the oracle's online counters must reproduce
+    for the same block size), the CSR and the degree order."""
+    import numpy as np
+    import gatb200 as G
+    import oracle as O
+    from test_oracle_golden import smoke1024_graph
+    g = smoke1024_graph()
+    z = np.load(ROOT / "tests" / "golden" / "tfs_counters.npz")
+    perm, _ = O.degree_schedule(g.row)
+    G.save_graph(g, tmp_path / "graph.gatbin")
+    perm.astype(np.uint32).tofile(tmp_path / "perm.u32")
+    for b in (16, 32):
+        ref = z[f"blockstats_b{b}"]
+        # blocks, max updates, rescales, rescale events; source neighbour steps
+        units = np.array([ref[0], ref[1], ref[2], ref[3], ref[18]], np.uint64)
+        _, _, _, tot = O.online_counters(g.row, g.col, perm, z["left"], z["right"], 8, b)
+        assert np.array_equal(tot, units), (b, tot, units)
+        units.tofile(tmp_path / f"units_b{b}.u64")
+    r = subprocess.run([str(mirror_bin), "--stats", str(tmp_path)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stdout + r.stderr
+    got = {l.split()[1]: np.array(l.split()[2:], np.uint64) for l in r.stdout.splitlines() if l.startswith("STATS ")}
+    assert len(got) == 8
+    for b in (16, 32):
+        assert np.array_equal(got[f"block{b}"], z[f"blockstats_b{b}"]), b
+        for t in (1, 16, 33):
+            assert np.array_equal(got[f"hybrid{b}_t{t}"], z[f"hybridstats_b{b}_t{t}"]), (b, t)
