@@ -480,7 +480,7 @@ void online_checks() {
 }
 
 // --stats DIR: the online variants' statistics from the mirror's counting
-// (icpp_block and icpp_heads_hybrid, heads 8, dim 32), for the graph, degree
+// (icpp_online, icpp_block and icpp_heads_hybrid, heads 8, dim 32), for the graph, degree
 // order and Online units written into DIR, one "STATS <case> <values>" line per
 // case in the order of the reference's Stats fields.
 template <class T>
@@ -512,6 +512,18 @@ void stats_checks(const std::string& dir) {
     gat::Prepared q;
     q.padded_in = (p.in + 31) / 32 * 32;
     q.output_blocks = 2;
+    for (int block : {4, 16, 64}) {  // icpp_online
+        const std::vector<uint64_t> tot = read_raw<uint64_t>(dir + "/units_b" + std::to_string(block) + ".u64");
+        expect(tot.size() == 5, "units file");
+        gat::icpp_online::Stats os;
+        gat::detail::online_stats(p, q, tot.data(), os);
+        std::cout << "STATS online" << block;
+        for (uint64_t x : {os.blocks, os.max_updates, os.rescales, os.rescale_events, os.neighbor_steps, os.amx_calls,
+                           os.executed_fma, os.rescaled_feature_elements, os.rescaled_padded_feature_elements,
+                           os.spill_bytes, os.reload_bytes})
+            std::cout << " " << x;
+        std::cout << "\n";
+    }
     for (int block : {16, 32}) {
         const std::vector<uint64_t> tot = read_raw<uint64_t>(dir + "/units_b" + std::to_string(block) + ".u64");
         expect(tot.size() == 5, "units file");

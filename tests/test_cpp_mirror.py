@@ -35,8 +35,8 @@ def test_mirror_layer_functions_on_gpu(mirror_bin, tmp_path):
 
 
 def test_mirror_online_statistics_match_the_reference(mirror_bin, tmp_path):
-    """The statistics the mirror fills for icpp_block and icpp_heads_hybrid with
-    counters=true, against the Stats the reference's own code produced on
+    """The statistics the mirror fills for icpp_online, icpp_block and
+    icpp_heads_hybrid with counters=true, against the Stats the reference's own code produced on
     smoke1024 (ref_dump counters; tests/golden/tfs_counters.npz): every field,
     from the Online units (which the oracle's online counters must reproduce
     for the same block size), the CSR and the degree order."""
@@ -49,6 +49,8 @@ def test_mirror_online_statistics_match_the_reference(mirror_bin, tmp_path):
     perm, _ = O.degree_schedule(g.row)
     G.save_graph(g, tmp_path / "graph.gatbin")
     perm.astype(np.uint32).tofile(tmp_path / "perm.u32")
+    for b in (4, 64):
+        z[f"totals_b{b}"][:5].tofile(tmp_path / f"units_b{b}.u64")
     for b in (16, 32):
         ref = z[f"blockstats_b{b}"]
         # blocks, max updates, rescales, rescale events; source neighbour steps
@@ -59,7 +61,9 @@ def test_mirror_online_statistics_match_the_reference(mirror_bin, tmp_path):
     r = subprocess.run([str(mirror_bin), "--stats", str(tmp_path)], capture_output=True, text=True, timeout=120)
     assert r.returncode == 0, r.stdout + r.stderr
     got = {l.split()[1]: np.array(l.split()[2:], np.uint64) for l in r.stdout.splitlines() if l.startswith("STATS ")}
-    assert len(got) == 8
+    assert len(got) == 11
+    for b in (4, 16, 64):
+        assert np.array_equal(got[f"online{b}"], z[f"totals_b{b}"]), b
     for b in (16, 32):
         assert np.array_equal(got[f"block{b}"], z[f"blockstats_b{b}"]), b
         for t in (1, 16, 33):
