@@ -35,7 +35,7 @@
 #include <vector>
 
 #include "driver_common.hpp"
-#include "gat_b200.hpp"
+#include "gat_b200_online.hpp"
 
 namespace gat = gat_b200;
 

@@ -18,7 +18,7 @@
 #include <string>
 #include <vector>
 
-#include "gat_b200.hpp"
+#include "gat_b200_online.hpp"
 
 namespace gat = gat_b200;
 
