@@ -183,3 +183,20 @@ def test_edge_softmax_validates_arguments():
     assert "edge_softmax: null buffer" in lib.gat_b200_last_error().decode()
     assert lib.gat_b200_edge_softmax(vp(1), 9, vp(1), vp(1), None, None, vp(1), vp(1), None, None) == 1
     assert "invalid parameter shape" in lib.gat_b200_last_error().decode()
+
+
+def test_bindings_match_header_arity():
+    """Every ctypes binding in gatb200.py takes as many arguments as the C
+    declaration in include/gat_b200.h, and every declared function is bound."""
+    import re
+    hdr = re.sub(r"/\*.*?\*/", "", (ROOT / "include" / "gat_b200.h").read_text(), flags=re.S)
+    decls = {}
+    for m in re.finditer(r"\b(gat_b200_\w+)\s*\(([^;{]*?)\)\s*;", hdr):
+        args = m.group(2).strip()
+        decls[m.group(1)] = 0 if args in ("", "void") else len(args.split(","))
+    src = (ROOT / "gat-tfs_b200" / "gatb200.py").read_text()
+    bound = {}
+    for m in re.finditer(r'\("(gat_b200_\w+)",\s*[^\[]+?,\s*\[([^\]]*)\]\)', src, flags=re.S):
+        bound[m.group(1)] = len([a for a in m.group(2).split(",") if a.strip()])
+    assert decls and set(decls) == set(bound), sorted(set(decls) ^ set(bound))
+    assert {k: v for k, v in bound.items() if decls[k] != v} == {}
