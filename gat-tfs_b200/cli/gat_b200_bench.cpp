@@ -491,37 +491,106 @@ int main(int argc, char** argv) {
                          rel = have_rel ? std::stod(a.get("--rel-l2")) : 0;
             if (have_abs && (!std::isfinite(maxabs) || !std::isfinite(rel) || maxabs < 0 || rel < 0))
                 throw std::runtime_error("invalid accuracy thresholds");
-            const std::vector<float> master = forward(dev.model(GAT_B200_PATH_STANDARD_FP32), g, model);
-            gat::require_finite(master, "ref_fp32 output");
-            // --dump-prefix: R0's per-layer trace and every path's logits as raw
-            // FP32 files with the reference's names (bench/main.cpp:72-75,94-96)
+            bool pass = true, finite = true;
+            auto check_e = [&](const std::string& name, int layer, const std::string& stage,
+                               const std::vector<float>& r, const std::vector<float>& v, bool gate) {
+                const gat::Error e = gat::errors(r, v);
+                gat::print_error(name, layer, stage, e);
+                pass &= e.finite;
+                finite &= e.finite;
+                if (gate && have_abs) pass &= e.max_abs <= maxabs && e.relative_l2 <= rel;
+            };
+            // Per layer, on R0's input (bench/main.cpp:70-92): R0 with its trace,
+            // R0 on BF16-quantized X and W, every path's stages through the C++
+            // mirror of the reference API, and the FP32 attention-reorder control.
+            // --dump-prefix writes R0's per-layer trace and every path's logits as
+            // raw FP32 files with the reference's names (bench/main.cpp:72-75,94-96).
             const std::string prefix = a.get("--dump-prefix");
-            if (!prefix.empty()) {
-                std::vector<float> input = g.x;
-                for (int l = 0; l < 3; ++l) {
-                    gat::Workspace rw;
-                    rw.allocate(g, model[l], "ref_fp32");
-                    gat::Times t;
-                    gat::ref_layer(g, model[l], input, rw, l < 2, t);
+            const gat::Schedule sched = gat::degree_schedule(g);
+            std::vector<float> master = g.x;
+            for (int l = 0; l < 3; ++l) {
+                const gat::Param& p = model[l];
+                const bool hidden = l < 2;
+                const gat::Prepared q = gat::prepare(p);
+                gat::Workspace rw;
+                rw.allocate(g, p, "ref_fp32");
+                gat::Times rt;
+                gat::ref_layer(g, p, master, rw, hidden, rt);
+                gat::require_finite(rw.out, "output");
+                if (!prefix.empty()) {
                     const std::string pre = prefix + "_layer" + std::to_string(l + 1) + "_";
                     const std::pair<const char*, const std::vector<float>*> items[] = {
                         {"output", &rw.out}, {"z", &rw.z},     {"left", &rw.left}, {"right", &rw.right},
                         {"max", &rw.max},    {"den", &rw.den}, {"score", &rw.score}, {"p", &rw.p},
                         {"alpha", &rw.alpha}};
                     for (const auto& item : items) dump(pre + item.first + ".f32", *item.second);
-                    input = std::move(rw.out);
                 }
-                dump(prefix + "_model_ref_fp32.f32", master);
+                gat::Param qp = p;
+                qp.w = gat::quantized(p.w);
+                gat::Workspace qr;
+                qr.allocate(g, p, "ref_fp32");
+                gat::Times qt;
+                gat::ref_layer(g, qp, gat::quantized(master), qr, hidden, qt);
+                check_e("quantized_XW_fp32_accum", l + 1, "Z", rw.z, qr.z, false);
+                check_e("quantized_XW_fp32_accum", l + 1, "layer", rw.out, qr.out, false);
+                for (const std::string test : {"standard_fp32", "standard_bf16", "tfs_bf16", "matched_attention"}) {
+                    gat::Workspace w;
+                    w.allocate(g, p, test);
+                    gat::Times t;
+                    if (test == "tfs_bf16") {
+                        gat::tfs_layer(g, p, q, sched, master, w, hidden, panel, t, "bf16");
+                    } else {
+                        const auto t0 = Clock::now();
+                        gat::projection(g, p, q, master, w, test != "standard_fp32");
+                        t.projection = seconds(t0, Clock::now());
+                        const auto t1 = Clock::now();
+                        if (test == "matched_attention")
+                            gat::lr_reordered(g, p, q, master, w, "bf16");
+                        else
+                            gat::lr_from_z(g, p, w);
+                        t.lr = seconds(t1, Clock::now());
+                        const auto t2 = Clock::now();
+                        gat::max_prescan(g, p, w);
+                        t.max_prescan = seconds(t2, Clock::now());
+                        gat::standard_aggregate(g, p, w, nullptr, nullptr, &t);
+                        gat::finish(g, p, w, hidden, t);
+                        t.total = t.projection + t.lr + t.max_prescan + t.aggregate + t.normalize;
+                    }
+                    if (!w.z.empty()) {
+                        check_e(test, l + 1, "Z", rw.z, w.z, false);
+                        check_e(test, l + 1, "Z_accum_vs_quantized_fp32", qr.z, w.z, false);
+                    }
+                    check_e(test, l + 1, "L", rw.left, w.left, false);
+                    check_e(test, l + 1, "R", rw.right, w.right, false);
+                    check_e(test, l + 1, "row_max", rw.max, w.max, false);
+                    check_e(test, l + 1, "denominator", rw.den, w.den, false);
+                    check_e(test, l + 1, "layer", rw.out, w.out, true);
+                    StageMs ms;
+                    ms.projection = t.projection * 1000;
+                    ms.lr = t.lr * 1000;
+                    ms.max_prescan = t.max_prescan * 1000;
+                    ms.aggregate = t.aggregate * 1000;
+                    ms.normalize = t.normalize * 1000;
+                    ms.total = t.total * 1000;
+                    ms.workspace_bytes = w.bytes();
+                    print_times(test, "correctness", l + 1, 0, g, p, threads, test == "standard_fp32", ms,
+                                (degree_sort_s + prepare_s) * 1000, panel);
+                }
+                // FP32 contraction control: the attention reorder alone, without BF16
+                gat::Workspace control;
+                control.allocate(g, p, "tfs_bf16");
+                gat::lr_reordered(g, p, q, master, control, "fp32");
+                check_e("attention_reorder_fp32", l + 1, "L", rw.left, control.left, false);
+                check_e("attention_reorder_fp32", l + 1, "R", rw.right, control.right, false);
+                master = std::move(rw.out);
             }
-            bool pass = true, finite = true;
+            if (!prefix.empty()) dump(prefix + "_model_ref_fp32.f32", master);
+            // every path's own three-layer chain against the R0 chain (bench/main.cpp:89-94)
             for (const std::string test : {"standard_fp32", "standard_bf16", "tfs_bf16", "matched_attention",
                                            "adaptive_bf16"}) {
                 const std::vector<float> out = forward(dev.model(path_code(test)), g, model);
                 if (!prefix.empty()) dump(prefix + "_model_" + test + ".f32", out);
-                const gat::Error e = gat::errors(master, out);
-                gat::print_error(test, 3, "model_path_specific_chain", e);
-                finite &= e.finite;
-                pass &= e.finite && (!have_abs || (e.max_abs <= maxabs && e.relative_l2 <= rel));
+                check_e(test, 3, "model_path_specific_chain", master, out, true);
             }
             std::cout << "CORRECTNESS finite=" << finite << " accuracy_gate="
                       << (have_abs ? (pass ? "PASS" : "FAIL") : "UNCONFIGURED_NOT_ACCEPTED")

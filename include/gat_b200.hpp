@@ -606,11 +606,19 @@ inline void tfs_aggregate(const Graph& g, const Param& p, const Prepared& q, con
     w.d_den->download(w.den);
     t.aggregate += seconds(t0, Clock::now());
 }
-// The B1 layer (baseline/src/baseline_tfs.cpp:111-117): out of w.
+// The B1 layer (baseline/src/baseline_tfs.cpp:111-117).
 inline void tfs_layer(const Graph& g, const Param& p, const Prepared& q, const Schedule&,
                       const std::vector<float>& input, Workspace& w, bool hidden, int, Times& t,
                       const std::string& lr_policy) {
     auto t0 = Clock::now();
+    const size_t nk = checked(g.n, uint64_t(p.heads));
+    if (input.size() != checked(g.n, uint64_t(p.in))) throw std::runtime_error("layer input size mismatch");
+    if (w.xbf.size() != checked(g.n, uint64_t(p.in))) throw std::runtime_error("workspace xbf has the wrong size");
+    detail::need(w.left, nk, "left");
+    detail::need(w.right, nk, "right");
+    detail::need(w.max, nk, "max");
+    detail::need(w.den, nk, "den");
+    detail::need(w.out, checked(g.n, uint64_t(p.width())), "out");
     const float* x = w.d_x->upload(input);
     const int ldb = detail::padded(p.in, GAT_B200_BF16);
     void* xb = w.d_xb->get(size_t(g.n) * ldb * 2);
@@ -622,7 +630,17 @@ inline void tfs_layer(const Graph& g, const Param& p, const Prepared& q, const S
     check(gat_b200_tfs_layer(w.graph->of(g), q.layer->p, x, GAT_B200_F32, p.in, hidden,
                              detail::lr_policy(lr_policy), GAT_B200_TFS_EDGE, 0, 1, xb,
                              l, r, m, dn, o, GAT_B200_F32, p.width(), nullptr));
+    // the workspace as the reference's tfs_layer leaves it: xbf, left, right,
+    // max, den and the finished out
     w.d_out->download(w.out);
+    w.d_left->download(w.left);
+    w.d_right->download(w.right);
+    w.d_max->download(w.max);
+    w.d_den->download(w.den);
+    std::vector<BF16> tmp(size_t(g.n) * ldb);
+    check(gat_b200_copy_to_host(tmp.data(), xb, tmp.size() * 2));
+    for (uint64_t i = 0; i < g.n; ++i)
+        std::copy(tmp.begin() + i * ldb, tmp.begin() + i * ldb + p.in, w.xbf.begin() + i * p.in);
     t.total += seconds(t0, Clock::now());
 }
 

@@ -16,6 +16,9 @@
   full run, whose exact counters pass the reference's own work identities.
 - the driver's single-layer benchmark (--layer N, bench/main.cpp:166-180) on every
   path, its exported layer output against the oracle's R0 chain.
+- the driver's correctness mode (bench/main.cpp:64-97): every path's stages per
+  layer against R0 with the quantized and attention-reorder controls, the chains,
+  the accuracy gate, and --dump-prefix.
 
 The kernels underneath the online variants are checked against the oracle in
 test_gpu_tfs.py. This file is collected late so that a failure here leaves the
@@ -169,3 +172,34 @@ def test_driver_single_layer_benchmark(tmp_path, path, layer, tol):
     got = np.fromfile(dump, np.float32).reshape(ref.shape)
     e = O.errors(ref, got)
     assert e["finite"] and e["relative_l2"] <= tol, e
+
+
+def test_driver_correctness_mode(tmp_path):
+    graph = GOLDEN / "fixture_small.gatbin"
+    prefix = tmp_path / "dump"
+    out = _driver("--graph", graph, "--seed", 11, "--mode", "correctness", "--max-abs", 1, "--rel-l2", "1e-2",
+                  "--dump-prefix", prefix)
+    errs = [l for l in out.splitlines() if l.startswith("ERROR ")]
+    # per layer: 2 quantized controls, 7 + 7 + 5 + 7 path stages, 2 reorder controls; 5 chains
+    assert len(errs) == 3 * 30 + 5
+    assert "CORRECTNESS finite=1 accuracy_gate=PASS" in out
+    recs = [json.loads(l) for l in out.splitlines() if l.startswith("{")]
+    assert len(recs) == 12 and {r["mode"] for r in recs} == {"correctness"}
+    # the dumped R0 trace has the reference's names and sizes, and its chain is
+    # the oracle's R0 chain
+    import oracle as O
+    g = G.load_graph(graph)
+    model = G.random_model(g.din, g.classes, 11)
+    chain = O.ref_chain(g.row, g.col, g.x, [(p.w, p.al, p.ar, p.heads, p.dim) for p in model])
+    assert (tmp_path / "dump_layer1_p.f32").stat().st_size == len(g.col) * 8 * 4
+    for layer in (1, 2, 3):
+        got = np.fromfile(tmp_path / f"dump_layer{layer}_output.f32", np.float32)
+        assert np.abs(got - chain[layer - 1]["out"].ravel()).max() <= 1e-4
+    ref = np.fromfile(tmp_path / "dump_model_ref_fp32.f32", np.float32)
+    std = np.fromfile(tmp_path / "dump_model_standard_fp32.f32", np.float32)
+    assert ref.size == g.n * g.classes and np.abs(ref - std).max() <= 1e-5
+    # a gate no BF16 path can meet fails, as in the reference
+    cli = PKG / "gat_b200_bench"
+    r = subprocess.run([str(cli), "--graph", str(graph), "--seed", "11", "--mode", "correctness", "--max-abs", "1e-9",
+                        "--rel-l2", "1e-9"], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 1 and "accuracy_gate=FAIL" in r.stdout
