@@ -1,21 +1,22 @@
 """Reference entry points outside the timed forward, on the GPU:
 
-- the online TFS variants of the C++ mirror (include/gat_b200.hpp): icpp_online,
+- the online TFS variants of the C++ mirror (include/gat_b200_online.hpp): icpp_online,
   icpp_block and icpp_heads_hybrid with the reference's signatures
   (baseline/tfs_online/icpp_online.hpp:37-43, icpp_block.hpp:33-39,
   icpp_heads_hybrid.hpp:18-24), through tests/cpp/mirror_test.cpp --gpu-online:
   every layer against the FP64 layer at the TFS gate, the exact counters against
   what the CSR and the degree schedule determine, aggregate() + finish against
   layer(), heads_hybrid's fallback to icpp_block outside heads 8, dim 32, and
-  ref_layer's R0 trace (score, max, p, den, alpha);
+  ref_layer's R0 trace (score, max, p, den, alpha), and standard_layer with
+  the lr_reordered policies (matched attention);
 - gat_b200_edge_softmax, the R0 edge weights that fixed-p fixtures hold, against
   the fixture the reference itself exported (tests/golden/fixture_small_l1.gatfix);
 - the driver's operator modes (bench/main.cpp:103-151): export-fixture against
-  that same file, fixed-p on it with the reference's error controls, and micro.
+  that same file, fixed-p on it with the reference's error controls, and micro;
 - the adaptive experiment driver (tfs_online/adaptive_main.cpp): its smoke and a
-  full run, whose exact counters pass the reference's own work identities.
+  full run, whose exact counters pass the reference's own work identities;
 - the driver's single-layer benchmark (--layer N, bench/main.cpp:166-180) on every
-  path, its exported layer output against the oracle's R0 chain.
+  path, its exported layer output against the oracle's R0 chain;
 - the driver's correctness mode (bench/main.cpp:64-97): every path's stages per
   layer against R0 with the quantized and attention-reorder controls, the chains,
   the accuracy gate, and --dump-prefix.
