@@ -92,11 +92,13 @@ struct StageMs {
     uint64_t neighbor_steps = 0, executed_fma = 0, workspace_bytes = 0;
 };
 
-// One JSON line per layer and repeat with print_times' keys
-// (baseline/src/common.cpp:155-170); `extra` appends keys of this backend.
+// One JSON line per layer and repeat with print_times' keys, in its order
+// (baseline/src/common.cpp:155-170; the CPU worker sums of its profile build
+// print as 0); `extra` appends keys of this backend.
 void print_times(const std::string& path, const std::string& mode, int layer, int rep, const gat::Graph& g,
                  const gat::Param& p, int threads, bool fp32, const StageMs& t, double static_ms, int panel,
                  const std::string& extra = "") {
+    const uint64_t useful = g.e * uint64_t(p.heads) * uint64_t(p.in) * uint64_t(p.dim);
     std::cout << std::setprecision(10) << "{\"path\":\"" << path << "\",\"mode\":\"" << mode
               << "\",\"layer\":" << layer << ",\"rep\":" << rep << ",\"N\":" << g.n << ",\"E\":" << g.e
               << ",\"D\":" << p.in << ",\"K\":" << p.heads << ",\"d\":" << p.dim << ",\"threads\":" << threads
@@ -106,8 +108,15 @@ void print_times(const std::string& path, const std::string& mode, int layer, in
               << ",\"normalize_ms\":" << t.normalize << ",\"activation_ms\":" << t.activation
               << ",\"convert_ms\":" << t.convert << ",\"total_ms\":" << t.total
               << ",\"workspace_bytes\":" << t.workspace_bytes << ",\"static_preprocess_ms\":" << static_ms
-              << ",\"panel_R\":" << panel << ",\"tile_rows\":16,\"neighbor_steps\":" << t.neighbor_steps
-              << ",\"executed_fma\":" << t.executed_fma << ",\"padding_executed_flops\":0" << extra << "}\n";
+              << ",\"panel_R\":" << panel << ",\"tile_rows\":16";
+    for (const char* k : {"score_exp_worker_ms", "gather_weight_convert_worker_ms", "tile_load_worker_ms",
+                          "gather_load_worker_ms", "p_times_x_convert_worker_ms", "weighted_spmm_worker_ms",
+                          "amx_compute_worker_ms", "tile_store_worker_ms", "tile_config_worker_ms",
+                          "scheduling_worker_ms", "output_write_worker_ms"})
+        std::cout << ",\"" << k << "\":0";
+    std::cout << ",\"neighbor_steps\":" << t.neighbor_steps << ",\"executed_fma\":" << t.executed_fma
+              << ",\"padding_executed_flops\":" << (t.executed_fma ? 2 * (t.executed_fma - useful) : 0) << extra
+              << "}\n";
 }
 
 void dump(const std::string& path, const std::vector<float>& v) {

@@ -181,6 +181,11 @@ inline std::vector<float> quantized(const std::vector<float>& a) {
 struct Times {
     double convert = 0, projection = 0, lr = 0, max_prescan = 0, aggregate = 0, normalize = 0, activation = 0,
            total = 0;
+    // the reference's profile-build worker sums (CPU workers): kept at 0 here
+    double score_exp_worker = 0, gather_weight_convert_worker = 0, tile_load_worker = 0;
+    double gather_load_worker = 0, p_times_x_convert_worker = 0, weighted_spmm_worker = 0;
+    double amx_compute_worker = 0, tile_store_worker = 0, normalize_worker = 0, activation_worker = 0;
+    double tile_config_worker = 0, scheduling_worker = 0, output_write_worker = 0;
     uint64_t neighbor_steps = 0, executed_fma = 0;
 };
 struct Error {
@@ -218,6 +223,36 @@ inline void print_error(const std::string& path, int layer, const std::string& s
               << " finite=" << e.finite << " max_abs=" << e.max_abs << " mean_abs=" << e.mean_abs
               << " relative_l2=" << e.relative_l2 << " rmse=" << e.rmse << " p50=" << e.p50 << " p90=" << e.p90
               << " p99=" << e.p99 << "\n";
+}
+
+// The per-layer JSON line (common.cpp:155-170) with the reference's keys. The
+// reference's OpenMP thread count has no counterpart: `threads` prints 1.
+// (The overload taking the Workspace, as gat.hpp declares it, follows it.)
+inline void print_times(const std::string& path, const std::string& mode, int layer, int rep, const Graph& g,
+                        const Param& p, size_t workspace_bytes, const Times& t, double stat, int panel) {
+    const uint64_t useful = g.e * uint64_t(p.heads) * uint64_t(p.in) * uint64_t(p.dim);
+    std::cout << std::setprecision(10) << "{\"path\":\"" << path << "\",\"mode\":\"" << mode << "\",\"layer\":" << layer
+              << ",\"rep\":" << rep << ",\"N\":" << g.n << ",\"E\":" << g.e << ",\"D\":" << p.in << ",\"K\":" << p.heads
+              << ",\"d\":" << p.dim << ",\"threads\":1,\"profile\":false,\"precision\":\""
+              << (path == "ref_fp32" || path == "standard_fp32" ? "FP32" : "BF16_RNE_FP32_state") << "\""
+              << ",\"projection_ms\":" << t.projection * 1000 << ",\"lr_ms\":" << t.lr * 1000
+              << ",\"max_prescan_ms\":" << t.max_prescan * 1000 << ",\"score_exp_aggregate_ms\":" << t.aggregate * 1000
+              << ",\"normalize_ms\":" << t.normalize * 1000 << ",\"activation_ms\":" << t.activation * 1000
+              << ",\"convert_ms\":" << t.convert * 1000 << ",\"total_ms\":" << t.total * 1000
+              << ",\"workspace_bytes\":" << workspace_bytes << ",\"static_preprocess_ms\":" << stat * 1000
+              << ",\"panel_R\":" << panel << ",\"tile_rows\":16,\"score_exp_worker_ms\":" << t.score_exp_worker * 1000
+              << ",\"gather_weight_convert_worker_ms\":" << t.gather_weight_convert_worker * 1000
+              << ",\"tile_load_worker_ms\":" << t.tile_load_worker * 1000
+              << ",\"gather_load_worker_ms\":" << t.gather_load_worker * 1000
+              << ",\"p_times_x_convert_worker_ms\":" << t.p_times_x_convert_worker * 1000
+              << ",\"weighted_spmm_worker_ms\":" << t.weighted_spmm_worker * 1000
+              << ",\"amx_compute_worker_ms\":" << t.amx_compute_worker * 1000
+              << ",\"tile_store_worker_ms\":" << t.tile_store_worker * 1000
+              << ",\"tile_config_worker_ms\":" << t.tile_config_worker * 1000
+              << ",\"scheduling_worker_ms\":" << t.scheduling_worker * 1000
+              << ",\"output_write_worker_ms\":" << t.output_write_worker * 1000
+              << ",\"neighbor_steps\":" << t.neighbor_steps << ",\"executed_fma\":" << t.executed_fma
+              << ",\"padding_executed_flops\":" << (t.executed_fma ? 2 * (t.executed_fma - useful) : 0) << "}\n";
 }
 
 // ---- device objects ---------------------------------------------------------
@@ -279,6 +314,10 @@ struct LayerHandle {
 // prepare(): the device copy of a layer (BF16 W^T, FP32 W, a, W.a).
 struct Prepared {
     std::shared_ptr<detail::LayerHandle> layer;
+    // The reference's host copies (BF16 W, W a in FP32 / BF16 / transposed, the
+    // AMX packing) live on the device inside `layer`; these vectors stay empty.
+    std::vector<BF16> w, blr_bf16, packed;
+    std::vector<float> blr, blr_dot;
     int padded_in = 0, output_blocks = 0;
     double weight_prepare_s = 0;
 };
@@ -313,6 +352,10 @@ struct Workspace {
     std::vector<BF16> xbf;
     std::vector<float> z, left, right, max, den, out;
     std::vector<float> score, p, alpha;  // R0 trace [e][heads] (ref_fp32 workspaces)
+    // the reference's CPU scratch (L/R staging, per-thread tiles, the L/R SGEMM
+    // operands): no counterpart on the device, kept empty
+    std::vector<float> lr, thread_cbuf, lr_sgemm_weights, lr_sgemm_tmp;
+    std::vector<BF16> thread_hbuf;
     // device state
     std::shared_ptr<detail::GraphHandle> graph = std::make_shared<detail::GraphHandle>();
     std::shared_ptr<detail::DeviceBuffer> d_x = std::make_shared<detail::DeviceBuffer>(),
@@ -346,12 +389,22 @@ struct Workspace {
         alpha.assign(ek, 0.f);
         graph->of(g);
     }
+    // common.cpp:135-138: L/R come from the projection's epilogue on every
+    // policy, so there is no SGEMM operand to prepare
+    void prepare_lr_sgemm(const Graph&, const Param&) {}
     size_t bytes() const {
-        return xbf.size() * 2 + (z.size() + left.size() + right.size() + max.size() + den.size() + out.size() +
-                                 score.size() + p.size() + alpha.size()) *
-                                    4;
+        return (xbf.size() + thread_hbuf.size()) * 2 +
+               (z.size() + left.size() + right.size() + max.size() + den.size() + out.size() + lr.size() +
+                score.size() + p.size() + alpha.size() + thread_cbuf.size() + lr_sgemm_weights.size() +
+                lr_sgemm_tmp.size()) *
+                   4;
     }
 };
+
+inline void print_times(const std::string& path, const std::string& mode, int layer, int rep, const Graph& g,
+                        const Param& p, const Workspace& w, const Times& t, double stat, int panel) {
+    print_times(path, mode, layer, rep, g, p, w.bytes(), t, stat, panel);
+}
 
 namespace detail {
 inline int padded(int width, int dtype) { return gat_b200_padded_ld(width, dtype); }
@@ -414,6 +467,8 @@ inline void projection(const Graph& g, const Param& p, const Prepared& q, const 
 inline void lr_from_z(const Graph&, const Param&, Workspace& w, bool = false) {
     if (!w.lr_from_projection) throw std::runtime_error("lr_from_z: L and R come from projection(); call it first");
 }
+// baseline_standard.cpp:21-28 (the same L and R through an SGEMM)
+inline void lr_from_z_mkl(const Graph& g, const Param& p, Workspace& w) { lr_from_z(g, p, w); }
 inline void lr_reordered(const Graph& g, const Param& p, const Prepared& q, const std::vector<float>& input,
                          Workspace& w, const std::string& policy) {
     const int pol = detail::lr_policy(policy);

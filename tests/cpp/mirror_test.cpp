@@ -150,6 +150,15 @@ void host_checks(const std::string& dir) {
     gat::Model m2 = gat::load_model(dir + "/m.gatwgt", 17, 4);
     for (int l = 0; l < 3; ++l) expect(m2[l].w == m[l].w && m2[l].al == m[l].al && m2[l].ar == m[l].ar, "GATWGT round trip");
     rejects("missing_graph", "cannot open graph", [&] { gat::load_graph(dir + "/missing.gatbin"); });
+    {  // the per-layer JSON line (common.cpp:155-170), parsed by the Python test
+        gat::Times tt;
+        tt.projection = 0.001;
+        tt.aggregate = 0.002;
+        tt.total = 0.003;
+        tt.executed_fma = g.e * uint64_t(p.heads) * uint64_t(p.in) * uint64_t(p.dim) + 8;
+        gat::Workspace ws;
+        gat::print_times("standard_bf16", "benchmark", 2, 0, g, p, ws, tt, 0.5, 64);
+    }
     // online TFS variants (icpp_online.cpp:265-290, icpp_block.cpp:244-270,
     // icpp_heads_hybrid.cpp:35-41,296-316): argument checks before device work
     {

@@ -21,9 +21,24 @@ def mirror_bin(tmp_path_factory):
     return out
 
 
+# print_times' keys, in the reference's order (baseline/src/common.cpp:155-170)
+PRINT_TIMES_KEYS = [
+    "path", "mode", "layer", "rep", "N", "E", "D", "K", "d", "threads", "profile", "precision", "projection_ms",
+    "lr_ms", "max_prescan_ms", "score_exp_aggregate_ms", "normalize_ms", "activation_ms", "convert_ms", "total_ms",
+    "workspace_bytes", "static_preprocess_ms", "panel_R", "tile_rows", "score_exp_worker_ms",
+    "gather_weight_convert_worker_ms", "tile_load_worker_ms", "gather_load_worker_ms",
+    "p_times_x_convert_worker_ms", "weighted_spmm_worker_ms", "amx_compute_worker_ms", "tile_store_worker_ms",
+    "tile_config_worker_ms", "scheduling_worker_ms", "output_write_worker_ms", "neighbor_steps", "executed_fma",
+    "padding_executed_flops"]
+
+
 def test_mirror_host_checks(mirror_bin, tmp_path):
+    import json
     r = subprocess.run([str(mirror_bin), "--host", str(tmp_path)], capture_output=True, text=True, timeout=120)
     assert r.returncode == 0, r.stdout + r.stderr
+    rec = json.loads(next(l for l in r.stdout.splitlines() if l.startswith("{")))
+    assert list(rec) == PRINT_TIMES_KEYS
+    assert rec["projection_ms"] == 1 and rec["total_ms"] == 3 and rec["padding_executed_flops"] == 16
     assert "MIRROR PASS host" in r.stdout and r.stdout.count("MIRROR PASS rejects") == 19
 
 
