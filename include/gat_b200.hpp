@@ -18,8 +18,9 @@
 //   * ref_layer() (R0) takes its output from the FP32 path, which the
 //     library's tests pin to R0 at max-abs <= 1e-5, and its trace (max, den,
 //     score, p, alpha) from R0's edge softmax on the device;
-//   * standard_layer() runs the fused layer: it writes out, left and right
-//     (with an lr_reordered policy, the matched-attention layer);
+//   * standard_layer() runs the stages one by one (one device call each) and
+//     leaves the workspace as the reference does; the timed forward is the
+//     model API;
 //   * the panel argument of the TFS calls has no counterpart (the degree
 //     schedule orders and balances the rows); it is accepted and ignored.
 // Header-only; link with -lgat_b200.
@@ -45,6 +46,9 @@ using Clock = std::chrono::steady_clock;
 inline double seconds(Clock::time_point a, Clock::time_point b) {
     return std::chrono::duration<double>(b - a).count();
 }
+// the reference's profile-build switches (gat.hpp:23-29): a speed build here
+inline Clock::time_point tick() { return {}; }
+inline constexpr bool profiling = false;
 
 inline void check(int rc) {
     if (rc) throw std::runtime_error(gat_b200_last_error());
@@ -314,8 +318,9 @@ struct LayerHandle {
 // prepare(): the device copy of a layer (BF16 W^T, FP32 W, a, W.a).
 struct Prepared {
     std::shared_ptr<detail::LayerHandle> layer;
-    // The reference's host copies (BF16 W, W a in FP32 / BF16 / transposed, the
-    // AMX packing) live on the device inside `layer`; these vectors stay empty.
+    // w: the BF16 RNE copy of W, as the reference keeps it. Its other host
+    // copies (W a in FP32 / BF16 / transposed, the AMX packing) live on the
+    // device inside `layer`; those vectors stay empty.
     std::vector<BF16> w, blr_bf16, packed;
     std::vector<float> blr, blr_dot;
     int padded_in = 0, output_blocks = 0;
@@ -329,6 +334,10 @@ inline Prepared prepare(const Param& p, bool = true, bool = true, bool = true) {
     check(gat_b200_layer_create(p.in, p.heads, p.dim, p.w.data(), p.al.data(), p.ar.data(), &q.layer->p));
     q.padded_in = (p.in + 31) / 32 * 32;
     q.output_blocks = (p.dim + 15) / 16;
+    // the reference's BF16 copy of W (common.cpp:98-99), for callers that emulate
+    // the BF16 arithmetic themselves (boundaries.cpp:44)
+    q.w.resize(p.w.size());
+    check(gat_b200_convert_host(p.w.data(), q.w.data(), p.w.size()));
     q.weight_prepare_s = seconds(t0, Clock::now());
     return q;
 }
@@ -545,54 +554,39 @@ inline void finish(const Graph& g, const Param& p, Workspace& w, bool hidden, Ti
     w.d_out->download(w.out);
     t.normalize += seconds(t0, Clock::now());
 }
-// The fused B0 layer (BF16, or FP32 with fp32): out, left and right of w.
+// The B0 layer (baseline_standard.cpp:98-108), stage by stage as the reference
+// runs it, so that the workspace holds what the reference leaves there: xbf
+// (BF16 path), z (FP32), left and right (from Z, or from lr_reordered with the
+// policies "bf16" / "fp32" / "avx": the matched-attention layer), max, den and
+// the finished out. Each stage is one device call with its copies; the timed
+// forward is the model API.
 inline void standard_layer(const Graph& g, const Param& p, const Prepared& q, const std::vector<float>& input,
                            Workspace& w, bool hidden, Times& t, bool fp32 = false,
                            const std::string& lr_policy = "z_avx") {
-    // "z_avx" / "z_mkl": L and R from Z (the projection's epilogue); any other
-    // policy is lr_reordered's (baseline_standard.cpp:103-105), the attention of
-    // the matched_attention path
     const bool matched = lr_policy != "z_avx" && lr_policy != "z_mkl";
-    const int policy = matched ? detail::lr_policy(lr_policy) : 0;
-    auto t0 = Clock::now();
+    if (matched) detail::lr_policy(lr_policy);  // "unknown LR policy"
     if (input.size() != checked(g.n, uint64_t(p.in))) throw std::runtime_error("layer input size mismatch");
-    detail::need(w.out, checked(g.n, uint64_t(p.width())), "out");
-    detail::need(w.left, checked(g.n, uint64_t(p.heads)), "left");
-    detail::need(w.right, checked(g.n, uint64_t(p.heads)), "right");
-    const void* x;
-    int ldx = p.in;
-    if (fp32)
-        x = w.d_x->upload(input);
+    const auto begin = Clock::now();
+    auto a = begin;
+    if (!fp32 && w.xbf.size() == input.size()) check(gat_b200_convert_host(input.data(), w.xbf.data(), input.size()));
+    t.convert = seconds(a, Clock::now());
+    a = Clock::now();
+    projection(g, p, q, input, w, !fp32);
+    t.projection = seconds(a, Clock::now());
+    a = Clock::now();
+    if (matched)
+        lr_reordered(g, p, q, input, w, lr_policy);
     else
-        x = detail::upload_bf16(w, input, g.n, p.in, ldx);
-    const int hd = fp32 ? GAT_B200_F32 : GAT_B200_BF16;
-    void* h = w.d_z->get(size_t(g.n) * detail::padded(p.width(), hd) * (fp32 ? 4 : 2));
-    float* l = static_cast<float*>(w.d_left->get(w.left.size() * 4));
-    float* r = static_cast<float*>(w.d_right->get(w.right.size() * 4));
-    float* o = static_cast<float*>(w.d_out->get(w.out.size() * 4));
-    if (!matched) {
-        check(gat_b200_standard_layer(w.graph->of(g), q.layer->p, x, ldx,
-                                      fp32 ? GAT_B200_PATH_STANDARD_FP32 : GAT_B200_PATH_STANDARD_BF16, hidden, h, l,
-                                      r, o, GAT_B200_F32, p.width(), nullptr));
-    } else {
-        const int ldh = detail::padded(p.width(), hd);
-        check(gat_b200_projection(q.layer->p, g.n, x, ldx, hd, h, hd, ldh, l, r, nullptr));
-        // lr_reordered reads the FP32 input ("fp32", "avx") or its BF16 copy ("bf16")
-        const void* xl = w.d_x->p;
-        int xdt = GAT_B200_F32, ldl = p.in;
-        if (policy == GAT_B200_LR_BF16) {
-            xl = fp32 ? detail::upload_bf16(w, input, g.n, p.in, ldl) : x;
-            if (!fp32) ldl = ldx;
-            xdt = GAT_B200_BF16;
-        }
-        check(gat_b200_lr_reordered(q.layer->p, g.n, xl, xdt, ldl, policy, nullptr, 0, l, r, nullptr));
-        check(gat_b200_aggregate_fused(w.graph->of(g), p.heads, p.dim, h, hd, ldh, l, r, hidden, o, GAT_B200_F32,
-                                       p.width(), nullptr));
-    }
-    w.d_out->download(w.out);
-    w.d_left->download(w.left);
-    w.d_right->download(w.right);
-    t.total += seconds(t0, Clock::now());
+        lr_from_z(g, p, w);
+    t.lr = seconds(a, Clock::now());
+    a = Clock::now();
+    max_prescan(g, p, w);
+    t.max_prescan = seconds(a, Clock::now());
+    a = Clock::now();
+    standard_aggregate(g, p, w, nullptr, nullptr, &t);
+    t.aggregate = seconds(a, Clock::now());
+    finish(g, p, w, hidden, t);
+    t.total = seconds(begin, Clock::now());
 }
 // R0 (baseline/src/ref_fp32.cpp:3-26): out from the FP32 path (FP32 projection,
 // aggregation, finish), and the R0 trace from gat_b200_edge_softmax: z, left,

@@ -19,7 +19,10 @@
   path, its exported layer output against the oracle's R0 chain;
 - the driver's correctness mode (bench/main.cpp:64-97): every path's stages per
   layer against R0 with the quantized and attention-reorder controls, the chains,
-  the accuracy gate, and --dump-prefix.
+  the accuracy gate, and --dump-prefix;
+- the reference's own boundary test (baseline/tests/boundaries.cpp), compiled
+  unchanged against the C++ mirror (oracle/compat/gat.hpp) and linked with the
+  library: all 64 boundary cases, the adversarial scores and the negative tests.
 
 The kernels underneath the online variants are checked against the oracle in
 test_gpu_tfs.py. This file is collected late so that a failure here leaves the
@@ -204,3 +207,16 @@ def test_driver_correctness_mode(tmp_path):
     r = subprocess.run([str(cli), "--graph", str(graph), "--seed", "11", "--mode", "correctness", "--max-abs", "1e-9",
                         "--rel-l2", "1e-9"], capture_output=True, text=True, timeout=300)
     assert r.returncode == 1 and "accuracy_gate=FAIL" in r.stdout
+
+
+def test_reference_boundary_test_on_the_library():
+    """oracle/_ref/boundaries_on_b200 is built (make -C oracle ref) where the
+    reference tree is present and travels with the build; the test reads no
+    reference file at run time."""
+    exe = ROOT / "oracle" / "_ref" / "boundaries_on_b200"
+    if not exe.exists():
+        pytest.skip("built only where the reference tree was present at build time")
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr
+    assert "TESTS PASS boundary_cases=64" in r.stdout
+    assert r.stdout.count("BOUNDARY PASS ") == 64 and r.stdout.count("NEGATIVE PASS ") == 6
