@@ -83,3 +83,18 @@ def test_mirror_online_statistics_match_the_reference(mirror_bin, tmp_path):
         assert np.array_equal(got[f"block{b}"], z[f"blockstats_b{b}"]), b
         for t in (1, 16, 33):
             assert np.array_equal(got[f"hybrid{b}_t{t}"], z[f"hybridstats_b{b}_t{t}"]), (b, t)
+
+
+def test_reference_sources_compile_against_the_mirror():
+    """The reference's own boundary test compiles unchanged against the C++ mirror
+    with the adapter oracle/compat/gat.hpp, so the mirror keeps every name and
+    signature it uses (where the reference tree is present: the check reads its
+    source, never copies it)."""
+    import os
+    ref = Path(os.environ.get("REF", "/root/reference")) / "baseline"
+    if not (ref / "tests" / "boundaries.cpp").exists():
+        pytest.skip("reference tree absent")
+    cmd = ["g++", "-std=c++17", "-fopenmp", "-fsyntax-only", "-w", "-I", str(ROOT / "oracle" / "compat"),
+           "-I", str(ROOT / "include"), str(ref / "tests" / "boundaries.cpp")]
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-3000:]
