@@ -53,6 +53,10 @@ sys.path.insert(0, str(ROOT / "gat-tfs_b200"))
 TMP = Path(os.environ.get("GAT_B200_TMP", "/tmp"))
 REF_BIN = ROOT / "oracle" / "_ref" / "gat_baseline"
 CONFIG = "c4"
+# (nodes, edges) of the configurations the reference arm runs (the power-law
+# and uniform ones of gat-tfs_b200/configs.py; gat_b200_make_inputs writes them)
+SPECS_SHAPE = {"c1": (1024, 16384), "c2": (169_343, 2_484_941), "c4": (2_449_029, 126_167_053),
+               "c4s": (612_257, 31_541_763)}
 METRIC = "3-layer GAT fwd GEdges/s (2.45M nodes/126M edges, BF16)"
 
 
@@ -75,6 +79,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default=CONFIG, choices=["c1", "c2", "c4", "c4s", "c5", "c5s"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the parity check of the timed forward's logits (printed as \"parity\")")
     ap.add_argument("--mode", choices=["forward", "micro"], default="forward")
     ap.add_argument("--path", choices=["standard", "adaptive"], default="standard",
                     help="standard: B0 on every layer; adaptive: layer 1 through TFS aggregation (tensor cores)")
@@ -218,37 +224,89 @@ def peaks():
 
 
 # ---------------------------------------------------------- reference (CPU)
-def write_reference_inputs(cfg) -> tuple[Path, Path]:
-    import gatb200 as G
-    g = TMP / f"gat_b200_{cfg.name}.gatbin"
-    w = TMP / f"gat_b200_{cfg.name}.gatwgt"
-    want = 32 + 8 * (cfg.graph.n + 1) + 4 * cfg.graph.e + 4 * cfg.graph.n * cfg.graph.din
-    if not g.exists() or g.stat().st_size != want:
-        G.save_graph(cfg.graph, g)
-    G.save_model(cfg.model, w)
+MAKE_INPUTS = ROOT / "gat-tfs_b200" / "gat_b200_make_inputs"
+
+
+def write_reference_inputs(config: str) -> tuple[Path, Path]:
+    """GATBIN1 / GATWGT1 files of `config`, written by gat_b200_make_inputs: a
+    program linked from the library's host sources only, so no process of
+    the reference arm maps libgat_b200.so."""
+    g = TMP / f"gat_b200_{config}.gatbin"
+    w = TMP / f"gat_b200_{config}.gatwgt"
+    r = subprocess.run([str(MAKE_INPUTS), config, str(g), str(w)], capture_output=True, text=True, timeout=900)
+    if r.returncode != 0:
+        raise RuntimeError(f"gat_b200_make_inputs {config} failed: {(r.stderr or r.stdout).strip()[-300:]}")
     return g, w
 
 
-def physical_cores() -> int:
+def socket_placement() -> dict:
+    """One socket's physical cores (the first hardware thread of each core that
+    this process may run on) and that socket's NUMA nodes: the placement of
+    the reference's runs (baseline/scripts/arxiv_payload.sh:36, numactl
+    --interleave over the used nodes, OMP_NUM_THREADS = physical cores)."""
+    allowed = os.sched_getaffinity(0)
+    rows = []
     try:
-        out = subprocess.run(["lscpu", "-p=CORE,SOCKET"], capture_output=True, text=True, timeout=10).stdout
-        cores = {l for l in out.splitlines() if l and not l.startswith("#")}
-        return max(1, len(cores))
+        out = subprocess.run(["lscpu", "-p=CPU,CORE,SOCKET,NODE"], capture_output=True, text=True,
+                             timeout=10).stdout
+        for ln in out.splitlines():
+            if ln and not ln.startswith("#"):
+                f = ln.split(",")
+                rows.append((int(f[0]), int(f[1]), int(f[2] or 0), int(f[3] or 0)))
     except Exception:
-        return os.cpu_count() or 1
+        rows = []
+    rows = [r for r in rows if r[0] in allowed]
+    if not rows:
+        cpus = sorted(allowed)
+        return {"cpus": cpus, "socket": 0, "nodes": [0], "sockets": 1}
+    sockets = sorted({r[2] for r in rows})
+    sock = max(sockets, key=lambda k: (sum(1 for r in rows if r[2] == k), -k))
+    first = {}
+    for cpu, core, sk, node in sorted(rows):
+        if sk == sock and core not in first:
+            first[core] = (cpu, node)
+    cpus = sorted(c for c, _ in first.values())
+    nodes = sorted({nd for _, nd in first.values()})
+    return {"cpus": cpus, "socket": sock, "nodes": nodes, "sockets": len(sockets)}
 
 
-def run_reference(cfg, warmups: int, repeats: int, timeout_s: int = 900) -> dict:
-    """The reference's B0 BF16 path (baseline/bench/main.cpp benchmark mode)."""
+def _pin_and_interleave(cpus, nodes):
+    """preexec_fn of the reference process: CPU affinity to `cpus` and an
+    interleaved memory policy over `nodes` (set_mempolicy(MPOL_INTERLEAVE),
+    what numactl --interleave does; numactl itself is not installed). Both are
+    inherited across exec."""
+    def fn():
+        os.sched_setaffinity(0, cpus)
+        try:
+            import ctypes
+            libc = ctypes.CDLL(None, use_errno=True)
+            mask = (ctypes.c_ulong * 2)()
+            for nd in nodes:
+                mask[nd // 64] |= 1 << (nd % 64)
+            libc.syscall(238, 3, mask, 129)  # SYS_set_mempolicy (x86-64), MPOL_INTERLEAVE
+        except Exception:
+            pass
+    return fn
+
+
+def run_reference(config: str, warmups: int, repeats: int, timeout_s: int = 1800) -> dict:
+    """The reference's B0 BF16 path (baseline/bench/main.cpp benchmark mode),
+    built from its sources into oracle/_ref/gat_baseline, on one socket's
+    physical cores with memory interleaved over that socket's NUMA nodes."""
     if not REF_BIN.exists():
         return {"unavailable": "oracle/_ref/gat_baseline was not built (reference tree absent at build time)"}
-    g, w = write_reference_inputs(cfg)
-    threads = physical_cores()
-    env = dict(os.environ, OMP_NUM_THREADS=str(threads), OMP_PROC_BIND="close", OMP_PLACES="cores")
+    if not MAKE_INPUTS.exists():
+        return {"unavailable": "gat-tfs_b200/gat_b200_make_inputs was not built"}
+    g, w = write_reference_inputs(config)
+    pl = socket_placement()
+    threads = len(pl["cpus"])
+    env = dict(os.environ, OMP_NUM_THREADS=str(threads), MKL_NUM_THREADS=str(threads), OMP_PROC_BIND="close",
+               OMP_PLACES="cores")
     cmd = [str(REF_BIN), "--graph", str(g), "--weights", str(w), "--path", "standard_bf16", "--mode", "benchmark",
            "--threads", str(threads), "--warmups", str(warmups), "--repeats", str(repeats)]
     try:
-        r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=timeout_s)
+        r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=timeout_s,
+                           preexec_fn=_pin_and_interleave(pl["cpus"], pl["nodes"]))
     except subprocess.TimeoutExpired:
         return {"unavailable": f"reference B0 run exceeded {timeout_s} s"}
     if r.returncode != 0:
@@ -257,7 +315,9 @@ def run_reference(cfg, warmups: int, repeats: int, timeout_s: int = 900) -> dict
     if not totals:
         return {"unavailable": "no E2E lines in reference output"}
     med = statistics.median(totals)
-    return {"median_ms": med, "totals_ms": totals, "threads": threads}
+    where = (f"socket {pl['socket']} of {pl['sockets']}: {threads} physical cores, OMP_PLACES=cores, memory "
+             f"interleaved over NUMA node(s) {pl['nodes']}")
+    return {"median_ms": med, "totals_ms": totals, "threads": threads, "placement": where}
 
 
 # ------------------------------------------------------------------ our arm
@@ -267,12 +327,90 @@ def agg_bytes(n, e, heads, dim, out_bytes_per_elem):
     return 8 * (n + 1) + 4 * e + 4 * n * heads + 4 * e * heads + 2 * e * heads * dim + out_bytes_per_elem * n * heads * dim
 
 
-def tfs_bytes(n, e, din, heads, dim):
-    """Algorithmic bytes of one TFS aggregation launch (layer 1 of the adaptive
-    path): rowptr, col, L and the maximum of the row, R of every edge's source,
-    the BF16 input row of every edge's source (16-byte rounded), the BF16 output."""
-    row_bytes = (2 * din + 15) // 16 * 16
-    return 8 * (n + 1) + 4 * e + 8 * n * heads + 4 * e * heads + row_bytes * e + 2 * n * heads * dim
+def _bf16_rows(t, idx, width):
+    """BF16 rows idx of device tensor t (int16 storage) as float64 (host)."""
+    import numpy as np
+    import torch
+    import gatb200 as G
+    sel = t.index_select(0, torch.from_numpy(np.asarray(idx, np.int64)).to(t.device)).cpu().numpy()
+    return G.bf16_to_f32(sel.view(np.uint16)[:, :width]).astype(np.float64)
+
+
+def _fp64_layer(xn, xi, w, al, ar, heads, dim):
+    """Output layer of one destination row in FP64 (R0's semantics,
+    baseline/src/ref_fp32.cpp:3-26, on BF16 inputs and BF16 W)."""
+    import numpy as np
+    z, zi = xn @ w, xi @ w
+    zh = z.reshape(len(xn), heads, dim)
+    L = (zi.reshape(heads, dim) * al.reshape(heads, dim)).sum(1)
+    s = L[None, :] + (zh * ar.reshape(1, heads, dim)).sum(2)
+    s = np.where(s > 0, s, 0.2 * s)
+    p = np.exp(s - s.max(0, keepdims=True))
+    return ((p / p.sum(0, keepdims=True))[:, :, None] * zh).sum(0).reshape(-1)
+
+
+def parity(cfg, got, nsample=48, seed=17) -> dict:
+    """Checks the logits `got` ([n, classes] FP32, host) of the forward just
+    timed. The 1-GPU forward runs layer by layer (gat_b200_standard_layer,
+    BF16) on the same inputs; `got` is compared with its logits over all rows
+    (vs_1gpu), and on sampled rows (random ones, the 50/90/99/99.9/99.99 %
+    degree quantiles and the largest hub) with an FP64 recomputation of layer
+    3 from that forward's layer-3 input rows of every neighbour (vs_fp64)."""
+    import numpy as np
+    import torch
+    import gatb200 as G
+    gr = cfg.graph
+    n = gr.n
+    g = G.DeviceGraph(gr.row, gr.col)
+    layers = [G.DeviceLayer(p) for p in cfg.model]
+    try:
+        ld0 = G.padded_ld(gr.din, G.BF16)
+        x0 = torch.zeros((n, ld0), dtype=torch.int16, device="cuda")
+        for a in range(0, n, 1 << 20):
+            b = min(n, a + (1 << 20))
+            G.convert(b - a, gr.din, torch.from_numpy(gr.x[a:b]).cuda(), gr.din, x0[a:b], ld0)
+        ldx = G.padded_ld(256, G.BF16)
+        h = torch.zeros((n, ldx), dtype=torch.int16, device="cuda")
+        left = torch.zeros((n, 8), dtype=torch.float32, device="cuda")
+        right = torch.zeros((n, 8), dtype=torch.float32, device="cuda")
+        xs = [x0, torch.zeros((n, ldx), dtype=torch.int16, device="cuda"),
+              torch.zeros((n, ldx), dtype=torch.int16, device="cuda")]
+        p3 = cfg.model[2]
+        ref = torch.zeros((n, p3.width), dtype=torch.float32, device="cuda")
+        for l, p in enumerate(cfg.model):
+            hidden = l < 2
+            G.standard_layer(g, layers[l], xs[l], ld0 if l == 0 else ldx, G.PATH_STANDARD_BF16, hidden, h, left,
+                             right, xs[l + 1] if hidden else ref, G.BF16 if hidden else G.F32,
+                             ldx if hidden else p3.width)
+        torch.cuda.synchronize()
+        G.check_device()
+        ref_h = ref.cpu().numpy()
+        got = np.asarray(got, np.float32)
+        d = got.astype(np.float64) - ref_h
+        vs1 = {"relative_l2": float(np.linalg.norm(d) / np.linalg.norm(ref_h)), "max_abs": float(np.abs(d).max()),
+               "rows": int(n)}
+        deg = np.diff(gr.row.astype(np.int64))
+        rng = np.random.default_rng(seed)
+        order = np.argsort(deg, kind="stable")
+        quant = [order[int(q * (n - 1))] for q in (0.5, 0.9, 0.99, 0.999, 0.9999)] + [int(order[-1])]
+        rows = np.unique(np.concatenate([rng.choice(n, nsample, replace=False), quant]))
+        w = G.bf16_to_f32(G.rne(p3.w)).astype(np.float64)
+        al, ar = p3.al.astype(np.float64), p3.ar.astype(np.float64)
+        err, nrm = 0.0, 0.0
+        for i in rows:
+            nb = gr.col[int(gr.row[i]):int(gr.row[i + 1])]
+            want = _fp64_layer(_bf16_rows(xs[2], nb, p3.in_), _bf16_rows(xs[2], [i], p3.in_)[0], w, al, ar,
+                               p3.heads, p3.dim)
+            err += float(((got[i].astype(np.float64) - want) ** 2).sum())
+            nrm += float((want ** 2).sum())
+        vs64 = {"relative_l2": (err / nrm) ** 0.5 if nrm else 0.0, "rows": int(len(rows)),
+                "largest_degree": int(deg.max()), "layer": 3}
+        return {"vs_1gpu": vs1, "vs_fp64": vs64}
+    finally:
+        for lay in layers:
+            lay.close()
+        g.close()
+        torch.cuda.empty_cache()
 
 
 def log(msg):
@@ -403,39 +541,44 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    import configs
 
     if args.impl == "reference":
         # Rank 0 alone times the reference CPU implementation; the others exit.
+        # This process never imports the library: the input files come from
+        # gat_b200_make_inputs (host code only) and the timed forward runs in
+        # the reference's own binary.
         if rank != 0:
             return 0
-        if configs.SPECS[args.config]["kind"] == "rmat":
+        spec = SPECS_SHAPE.get(args.config)
+        if spec is None:
             print(json.dumps({"impl": "reference", "unavailable": "not run on the RMAT stress graph: the "
                               "reference's B0 keeps three FP32 workspaces of it (tens of GB) and takes minutes "
                               "per forward on the host cores"}))
             return 0
-        cfg = configs.make(args.config)
-        w = 3  # the timing rules' minimum of warm-up forwards; the steps stay bounded
-        k = max(1, min(args.steps, 5))
-        res = run_reference(cfg, w, k)
-        e3 = 3 * cfg.graph.e
+        n_, e_ = spec
+        w = max(args.warmup, 3)
+        k = args.steps
+        res = run_reference(args.config, w, k)
+        e3 = 3 * e_
         if "unavailable" in res:
             print(json.dumps({"impl": "reference", "unavailable": res["unavailable"]}))
             return 0
         v = e3 / (res["median_ms"] * 1e-3) / 1e9
         sample = (f"full {args.config} forward per step, median of {len(res['totals_ms'])} timed forwards "
-                  f"after {w} warm-up (bounded)")
-        line = {"impl": "reference", "metric": metric_for(args.config, cfg.graph.n, cfg.graph.e),
+                  f"after {w} warm-up; {res['placement']}")
+        line = {"impl": "reference", "metric": metric_for(args.config, n_, e_),
                 "value": round(v, 5), "unit": "GEdges/s", "n_gpus": 0,
                 "steps": len(res["totals_ms"]), "warmup": w, "ms_per_step": round(res["median_ms"], 3),
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-                "data": "synthetic", "config": {"workload": args.config, "path": "reference B0 standard_bf16 (CPU)"},
+                "data": "synthetic", "config": {"workload": args.config, "path": "reference B0 standard_bf16 (CPU)",
+                                                "placement": res["placement"]},
                 "cpu_baseline": {"value": round(v, 5), "unit": "GEdges/s", "cores": res["threads"],
                                  "kind": "reference", "sample": sample},
                 "e2e": {"value": round(v, 5), "unit": "GEdges/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line))
         return 0
 
+    import configs
     import numpy as np
     import torch
     import gatb200 as G
@@ -545,22 +688,40 @@ def main():
         parallelism = (f"rows{world}: destination rows split by edge count, {len(pm.chunks)} row chunk(s) per "
                        f"rank; {how}")
 
-    # roofline of the aggregation kernel (three launches per step, this rank's rows). Under
-    # the multi-GPU pipeline a layer's time also holds the next layer's projections and any
-    # exchange not overlapped, so the figure is a lower bound there.
-    if world == 1:
-        agg_ms = [stage_ms["aggregate_l1"], stage_ms["aggregate_l2"], stage_ms["aggregate_l3"]]
-    else:
-        agg_ms = [stage_ms["layer1"], stage_ms["layer2"], stage_ms["layer3"]]
-    b = [agg_bytes(n_loc, e_loc, 8, 32, 2), agg_bytes(n_loc, e_loc, 8, 32, 2), agg_bytes(n_loc, e_loc, 1, classes, 4)]
-    if world == 1 and args.path == "adaptive":
-        b[0] = tfs_bytes(n_loc, e_loc, din, 8, 32)
-    achieved = sum(b) / (sum(agg_ms) * 1e-3) / 1e9
+    # roofline of the dominant kernel: the hidden-layer aggregation (agg_kernel,
+    # launches of layers 1 and 2, the same bytes each), averaged over the timed
+    # steps. Layer 3's aggregation and the projections are reported beside it.
+    # Under the multi-GPU pipeline a layer's time also holds the next layer's
+    # projection and any exchange not overlapped, so the figure is a lower
+    # bound there.
     peak, peak_kind = peaks()
+    b_hid = agg_bytes(n_loc, e_loc, 8, 32, 2)
+    b_l3 = agg_bytes(n_loc, e_loc, 1, classes, 4)
+    if world == 1:
+        hid = [stage_ms["aggregate_l2"]] if args.path == "adaptive" else [stage_ms["aggregate_l1"],
+                                                                            stage_ms["aggregate_l2"]]
+        l3_ms = stage_ms["aggregate_l3"]
+    else:
+        hid = [stage_ms["layer1"], stage_ms["layer2"]]
+        l3_ms = stage_ms["layer3"]
+    hid_ms = sum(hid) / len(hid)
+    achieved = b_hid / (hid_ms * 1e-3) / 1e9
     traffic = None
     prof = ROOT / "profiles" / "aggregate_c4_traffic.json"
     if prof.exists() and world == 1 and args.config == "c4" and args.path == "standard":
-        traffic = json.loads(prof.read_text()).get("bytes_per_launch_avg")
+        pl = json.loads(prof.read_text())["per_launch_bytes"]
+        traffic = (pl["layer1"] + pl["layer2"]) / 2
+    others = {"aggregate_l3": {"ms": round(l3_ms, 4), "algorithmic_bytes": int(b_l3),
+                               "achieved_gbs": round(b_l3 / (l3_ms * 1e-3) / 1e9, 1),
+                               "frac": round(b_l3 / (l3_ms * 1e-3) / 1e9 / peak, 4)}}
+    if world == 1:
+        widths = [(din, 8, 32), (256, 8, 32), (256, 1, classes)]
+        for l, (D, K, dd) in enumerate(widths, 1):
+            pb = 2 * n_loc * D + 2 * D * (K * dd + 2 * K) + 2 * n_loc * K * dd + 8 * n_loc * K
+            pms = stage_ms[f"projection_l{l}"]
+            others[f"projection_l{l}"] = {"ms": round(pms, 4), "algorithmic_bytes": int(pb),
+                                          "achieved_gbs": round(pb / (pms * 1e-3) / 1e9, 1),
+                                          "frac": round(pb / (pms * 1e-3) / 1e9 / peak, 4)}
 
     # e2e: the same forward with pinned HOST input rows and HOST logits, through the C ABI.
     # Latency: one synchronous call per step (upload, forward, download, wait).
@@ -602,20 +763,38 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config.startswith("c5"):
-        cpu = {"value": None, "unit": "GEdges/s", "cores": physical_cores(), "kind": "reference",
+        cpu = {"value": None, "unit": "GEdges/s", "cores": len(socket_placement()["cpus"]), "kind": "reference",
                "sample": "not run: the reference's B0 keeps three FP32 workspaces of the RMAT graph "
                          "(tens of GB) and takes minutes per forward on the host cores"}
     elif rank == 0 and world == 1 and not args.no_cpu_baseline:
-        res = run_reference(cfg, 1, 2)
+        res = run_reference(args.config, 1, 2)
         if "unavailable" in res:
-            cpu = {"value": None, "unit": "GEdges/s", "cores": physical_cores(), "kind": "reference",
+            cpu = {"value": None, "unit": "GEdges/s", "cores": len(socket_placement()["cpus"]), "kind": "reference",
                    "sample": res["unavailable"]}
         else:
             cpu = {"value": round(3 * e / (res["median_ms"] * 1e-3) / 1e9, 5), "unit": "GEdges/s",
                    "cores": res["threads"], "kind": "reference",
                    "sample": f"full {args.config} forward, median of {len(res['totals_ms'])} after 1 warm-up "
-                             f"(reference B0 standard_bf16, {res['median_ms']:.1f} ms)"}
+                             f"(reference B0 standard_bf16, {res['median_ms']:.1f} ms; {res['placement']})"}
 
+    # parity of the timed forward's logits (outside every timed region): rank 0
+    # gathers all ranks' rows, then checks them after the process group is gone
+    got = None
+    if world == 1:
+        got = logits.cpu().numpy()
+    else:
+        n_max = int(np.diff(part.cuts).max())
+        pad = torch.zeros((n_max, classes), dtype=torch.float32, device="cuda")
+        pad[:n_loc] = logits
+        full = torch.empty((world * n_max, classes), dtype=torch.float32, device="cuda")
+        dist.all_gather_into_tensor(full, pad)
+        if rank == 0:
+            fh = full.cpu().numpy()
+            got = np.concatenate([fh[k * n_max:k * n_max + int(part.cuts[k + 1] - part.cuts[k])]
+                                  for k in range(world)])
+        del full, pad
+
+    line = None
     if rank == 0:
         value = 3 * e / (ms * 1e-3) / 1e9
         line = {
@@ -631,10 +810,10 @@ def main():
             "stage_ms": {k: round(float(v), 4) for k, v in stage_ms.items()},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
-                         "kernel": "edge-softmax aggregation (3 launches/step" +
-                                   (", rank 0 rows, per-layer time incl. next projection and exposed exchange)"
-                                    if world > 1 else ")"),
-                         "algorithmic_bytes_per_launch": int(sum(b) / 3)},
+                         "kernel": "agg_kernel, hidden layers (" + ("layer 2" if len(hid) == 1 else "layers 1-2") +
+                                   (", rank 0 rows, layer time incl. next projection and exposed exchange)"
+                                    if world > 1 else ", mean launch over the timed steps)"),
+                         "algorithmic_bytes_per_launch": int(b_hid), "others": others},
             "e2e": {"value": round(3 * e / (e2e_ms * 1e-3) / 1e9, 4), "unit": "GEdges/s",
                     "ms_per_step": round(e2e_ms, 3), "mode": e2e_mode,
                     "sync_ms_per_step": round(e2e_sync_ms, 3), "h2d_bytes_per_step": n * din * 4,
@@ -644,12 +823,17 @@ def main():
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
-        print(json.dumps(line))
     if world == 1:
         model.close()
     else:
         pm.close()
         dist.destroy_process_group()
+    if rank == 0:
+        if args.path == "standard" and not args.no_parity:
+            log("parity check")
+            full_cfg = cfg if world == 1 else configs.make(args.config)
+            line["parity"] = parity(full_cfg, got)
+        print(json.dumps(line))
     return 0
 
 

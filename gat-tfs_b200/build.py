@@ -7,6 +7,8 @@ the objects link into gat-tfs_b200/libgat_b200.so with the CUDA runtime linked
 statically, so the library needs only the NVIDIA driver at run time. The C++
 drivers in cli/ (gat_b200_bench, gat_b200_tfs_online, gat_b200_tfs_adaptive) link against it. A source
 is recompiled only when it or a header is newer than its object.
+gat_b200_make_inputs links the host objects only (no CUDA runtime, no
+libgat_b200.so).
 """
 import argparse
 import concurrent.futures as cf
@@ -26,6 +28,10 @@ CUDA_FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-fop
                      "-I" + str(ROOT / "include"), "-Xptxas", "-v"]
 CXX_FLAGS = ["-O3", "-std=c++17", "-fPIC", "-fopenmp", "-Wall", "-I" + str(ROOT / "include"),
              "-I/usr/local/cuda/include"]
+
+# cli programs that need no GPU and must not load the library: the input
+# writer of the CPU reference arm (bench.py --impl reference)
+HOST_ONLY = {"gat_b200_make_inputs"}
 
 # refrng.cpp must round like the reference's sources as oracle/Makefile builds
 # them (g++ -O3 -mfma): std::normal_distribution is inline and contracts to FMA.
@@ -75,11 +81,17 @@ def build(verbose: bool = False) -> Path:
     # the C++ drivers over the C ABI (cli/*.cpp -> gat-tfs_b200/<name>): the
     # reference's bench/main.cpp and tfs_online/main.cpp interfaces
     hdr = max(h.stat().st_mtime for h in list((ROOT / "include").glob("*.h*")) + list((PKG / "cli").glob("*.hpp")))
+    host_objs = [OUT / "host.o", OUT / "synth.o", OUT / "refrng.o"]
     for src in sorted((PKG / "cli").glob("*.cpp")):
         exe = PKG / src.stem
         if not exe.exists() or exe.stat().st_mtime < max(LIB.stat().st_mtime, src.stat().st_mtime, hdr):
-            cmd = ["g++", "-O2", "-std=c++17", "-Wall", "-I" + str(ROOT / "include"), str(src), "-o", str(exe),
-                   "-L" + str(PKG), "-lgat_b200", "-Wl,-rpath,$ORIGIN"]
+            if src.stem in HOST_ONLY:
+                # linked from the host objects alone: no CUDA, no libgat_b200.so
+                cmd = ["g++", "-O2", "-std=c++17", "-Wall", "-I" + str(ROOT / "include"), str(src)] + \
+                      [str(o) for o in host_objs] + ["-fopenmp", "-o", str(exe)]
+            else:
+                cmd = ["g++", "-O2", "-std=c++17", "-Wall", "-I" + str(ROOT / "include"), str(src), "-o", str(exe),
+                       "-L" + str(PKG), "-lgat_b200", "-Wl,-rpath,$ORIGIN"]
             r = subprocess.run(cmd, capture_output=True, text=True)
             if r.returncode != 0:
                 raise RuntimeError(f"driver build failed: {src.name}\n" + r.stdout + r.stderr)

@@ -259,14 +259,15 @@ void profile(Runner& run, const gat::Schedule& sched, const std::string& name, i
               << " rescaled_feature_elements=" << s.rescaled_feature_elements << " rescale_events=" << s.rescale_events
               << " spill_bytes=" << s.spill_bytes << " reload_bytes=" << s.reload_bytes << " UW_calls=" << s.amx_calls
               << " UW_physical_FMA=" << s.executed_fma << " head_tiles=" << s.total_tiles
-              << " projection_groups=" << st.projection_calls << "\n";
+              << " projection_groups=" << st.projection_calls << " cpu_schedule_counters=modelled_not_measured_on_gpu\n";
     std::cout << "HEAD_WORK path=" << name << " layer=" << l + 1 << " optimized=" << opt << " PH_calls=" << st.ph_calls
               << " PH_physical_FMA=" << st.ph_physical_fma << " PH_useful_FMA=" << st.ph_useful_fma
               << " raw_H_bytes=" << st.raw_H_bytes << " packed_H_bytes=" << st.packed_H_bytes
               << " UB_scatter_bytes=" << st.ub_scatter_bytes << " head_switch_store_bytes="
               << st.head_switch_store_bytes << " head_switch_reload_bytes=" << st.head_switch_reload_bytes
               << " sparse_width_amplification=" << double(p.in) / p.dim
-              << " traffic_is_logical_not_DRAM=true no_full_Z_U_e_alpha=true bounded_V_in_local_memory=true\n";
+              << " traffic_is_logical_not_DRAM=true no_full_Z_U_e_alpha=true bounded_V_in_local_memory=true"
+              << " cpu_schedule_counters=modelled_not_measured_on_gpu\n";
 }
 
 

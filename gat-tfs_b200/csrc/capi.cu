@@ -382,6 +382,7 @@ int gat_b200_aggregate_fused(const gat_b200_graph* g, int heads, int dim, const 
                              const float* left, const float* right, int hidden, void* out, int out_dtype, int ldo,
                              void* stream) {
     clear_error();
+    if (out_dtype != GAT_B200_BF16 && out_dtype != GAT_B200_F32) return fail("aggregate_fused: bad output dtype");
     return aggregate_dispatch(g, heads, dim, h, h_dtype, ldh, left, right, nullptr, nullptr, 0, hidden, out,
                               out_dtype == GAT_B200_BF16, ldo, nullptr, nullptr, as_stream(stream));
 }
@@ -395,6 +396,7 @@ int gat_b200_standard_layer(const gat_b200_graph* g, const gat_b200_layer* p, co
     const int hd = path == GAT_B200_PATH_STANDARD_BF16 ? GAT_B200_BF16 : GAT_B200_F32;
     if (path != GAT_B200_PATH_STANDARD_BF16 && path != GAT_B200_PATH_STANDARD_FP32)
         return fail("standard_layer: bad path");
+    if (out_dtype != GAT_B200_BF16 && out_dtype != GAT_B200_F32) return fail("standard_layer: bad output dtype");
     const int ldh = gat_b200_padded_ld(p->width, hd);
     int rc = projection_dispatch(p, g->n, x, ldx, hd, h, hd, ldh, left, right, st);
     if (rc) return rc;

@@ -19,8 +19,6 @@
 // kernels overlap on the GPU (different streams, or several host threads)
 // race on it and must be serialized by the caller. Nothing in it needs to start
 // at zero: every slot a merge reads was written by the same call.
-#include <mutex>
-
 #include "device.cuh"
 #include "graph.cuh"
 
@@ -64,6 +62,9 @@ __device__ __forceinline__ uint64_t lower_bound_rows(const uint64_t* row, uint64
     return lo;
 }
 
+// Normalisation and, for hidden layers, ELU as exp(v) - 1: the activation of
+// the reference's B0 finish (baseline/include/gat.hpp:57-62), which the
+// regular fused kernel also uses.
 __device__ __forceinline__ float na_finalize(const NaArgs& a, int c, float acc, float den) {
     if (c >= a.width) return 0.f;
     float v = acc * (den > 0.f ? 1.f / den : 0.f);
@@ -201,6 +202,9 @@ __global__ void __launch_bounds__(128) na_range_kernel(const NaArgs a) {
                     for (int h = 1; h < 8; ++h) d = hh == h ? den[h] : d;
                     na_store(a, r, c, na_finalize(a, c, acc[j][k], d));
                 }
+            // padding columns beyond the vectors a lane holds (ldo > 512):
+            // zeros, as the merge kernel writes them
+            for (int c = NVP * 32 * VEC + lane; c < a.ldo; c += 32) na_store(a, r, c, 0.f);
         };
         // The row that started before lo and continues into this range.
         if (r0 > 0 && (r0 > a.n || a.row[r0] > lo) && lo < a.e) {
@@ -268,22 +272,16 @@ __global__ void __launch_bounds__(128) na_merge_kernel(const NaArgs a) {
     }
 }
 
-// Device address of the scratch array, looked up once per device.
-std::mutex g_scratch_mu;
-float* g_scratch_ptr[64] = {};
-
+// Device address of the scratch array in the current device's context. It is
+// looked up on every call (a host-side table lookup once the module is loaded),
+// so a context that was reset and reloaded the module never sees a stale
+// address. The first lookup on a device loads the module; that first call must
+// come before any stream capture.
 int scratch_for_current_device(float** out) {
-    int dev = 0;
-    GATB_CUDA(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64) return fail("aggregate_fused_noalloc: device index out of range");
-    std::lock_guard<std::mutex> lock(g_scratch_mu);
-    if (!g_scratch_ptr[dev]) {
-        void* p = nullptr;
-        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
-        g_scratch_ptr[dev] = static_cast<float*>(p);
-    }
-    *out = g_scratch_ptr[dev];
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+    *out = static_cast<float*>(p);
     return 0;
 }
 
@@ -313,6 +311,7 @@ extern "C" int gat_b200_aggregate_fused_noalloc(uint64_t n, uint64_t e, const ui
     if (!row || (e && !col) || !h || !left || !right || !out) return fail("aggregate_fused_noalloc: null buffer");
     if (heads < 1 || heads > 8 || dim < 1 || dim > 64) return fail("invalid parameter shape (heads <=8, head_dim <=64)");
     if (h_dtype != GAT_B200_BF16 && h_dtype != GAT_B200_F32) return fail("aggregate_fused_noalloc: bad feature dtype");
+    if (out_dtype != GAT_B200_BF16 && out_dtype != GAT_B200_F32) return fail("aggregate_fused_noalloc: bad output dtype");
     const int width = heads * dim;
     const int elem = h_dtype == GAT_B200_BF16 ? 2 : 4;
     if (ldh < padded_ld(width, elem) || ldo < width) return fail("aggregate_fused_noalloc: row stride smaller than the width");

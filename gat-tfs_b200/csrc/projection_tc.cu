@@ -68,115 +68,27 @@ struct ProjArgs {
     float* rp[kMaxPeers];
 };
 
-// ---- PTX wrappers ----------------------------------------------------------
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Bounded wait. Returns false (and raises the CTA's abort flag) on timeout or
-// when another role of this CTA has already aborted.
+// ---- PTX wrappers (tc.cuh) -------------------------------------------------
+using tc::bulk_commit;
+using tc::bulk_wait_all;
+using tc::bulk_wait_read;
+using tc::fence_proxy_async_smem;
+using tc::mbar_arrive;
+using tc::mbar_expect_tx;
+using tc::mbar_init;
+using tc::mbar_try;
+using tc::mma_bf16;
+using tc::mma_commit;
+using tc::smem_u32;
+using tc::tma_load_2d;
+using tc::tma_store_2d;
+using tc::tmem_ld16;
+// Bounded wait recording a timeout in this kernel's error flag.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-    if (mbar_try(bar, parity)) return true;
-    const long long start = clock64();
-    for (uint32_t it = 0;; ++it) {
-        if (mbar_try(bar, parity)) return true;
-        if (*abort_flag) return false;
-        if ((it & 63) == 63) {
-            __nanosleep(128);
-            if (clock64() - start > (1ll << 31)) {  // ~1 s at the B200 clock
-                *abort_flag = 1;
-                atomicOr(&g_proj_error, 1u);
-                return false;
-            }
-        }
-    }
+    return tc::mbar_wait(bar, parity, abort_flag, &g_proj_error);
 }
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
-        ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
-        : "memory");
-}
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
-    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
-                 ::"l"(map), "r"(smem_u32(src)), "r"(x), "r"(y)
-                 : "memory");
-}
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void bulk_wait_read() {
-    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
-}
-__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-__device__ __forceinline__ void fence_proxy_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_before() {
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-// K-major operand in the 128-byte swizzle layout: rows of 128 bytes, 8-row
-// groups 1024 bytes apart (SBO = 1024), descriptor version 1 (sm_100).
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-    uint64_t d = 0;
-    d |= uint64_t((saddr >> 4) & 0x3fff);
-    d |= uint64_t(1) << 16;               // LBO (unused for swizzled K-major)
-    d |= uint64_t(1024 >> 4) << 32;       // SBO
-    d |= uint64_t(1) << 46;               // version
-    d |= uint64_t(2) << 61;               // SWIZZLE_128B
-    return d;
-}
-__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                     smem_u32(bar))
-                 : "memory");
-}
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-    uint32_t r[16];
-    // Load and wait in one asm statement: the registers are defined only after
-    // the wait, so no use of them can be scheduled before it.
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
-        "tcgen05.wait::ld.sync.aligned;"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr)
-        : "memory");
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
+// K-major operand in the 128-byte swizzle layout: 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) { return tc::desc_sw128(saddr, 16, 1024); }
 
 template <bool ALIGNED16>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -227,9 +139,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                      "r"(a.tmem_cols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
-    tc_fence_before();
+    tc::fence_before();
     __syncthreads();
-    tc_fence_after();
+    tc::fence_after();
     const uint32_t tmem_base = *tmem_holder;
 
     if (warp == 0) {
@@ -266,18 +178,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                                    | (uint32_t(NP >> 3) << 17)  // N
                                    | (uint32_t(kTileM >> 4) << 24);  // M
             bool ok = mbar_wait(w_full, 0, abort_flag);
-            tc_fence_after();
+            tc::fence_after();
             uint64_t kc = 0;
             uint32_t t_local = 0;
             for (uint64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++t_local) {
                 const uint32_t buf = t_local & 1u, use = t_local >> 1;
                 if (!mbar_wait(acc_empty + buf, (use & 1u) ^ 1u, abort_flag)) { ok = false; break; }
-                tc_fence_after();
+                tc::fence_after();
                 const uint32_t d_tmem = tmem_base + buf * (a.tmem_cols / 2);
                 for (int k = 0; k < KB; ++k, ++kc) {
                     const int s = int(kc % S);
                     if (!mbar_wait(full + s, uint32_t(kc / S) & 1u, abort_flag)) { ok = false; break; }
-                    tc_fence_after();
+                    tc::fence_after();
                     const uint32_t a_addr = smem_u32(a_s + size_t(s) * kABytes);
                     const uint32_t b_addr = smem_u32(w_s + size_t(k) * NP * 128);
 #pragma unroll
@@ -304,7 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t use = 0;
         for (uint64_t t = blockIdx.x + buf * gridDim.x; t < ntiles; t += 2ull * gridDim.x, ++use) {
             if (!mbar_wait(acc_full + buf, use & 1u, abort_flag)) break;
-            tc_fence_after();
+            tc::fence_after();
             const uint64_t row = t * kTileM + uint64_t(q) * 32 + lane;
             const uint32_t taddr = tmem_base + (uint32_t(q * 32) << 16) + buf * (a.tmem_cols / 2);
             float L[8], R[8];
@@ -397,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (a.sb == 2) toggle ^= 1u;
             }
-            tc_fence_before();
+            tc::fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(acc_empty + buf);
             if (row < a.n) {
@@ -430,10 +342,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) bulk_wait_all();
         __syncwarp();
     }
-    tc_fence_before();
+    tc::fence_before();
     __syncthreads();
     if (warp == 1) {
-        tc_fence_after();
+        tc::fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(a.tmem_cols));
     }
 }

@@ -1,6 +1,6 @@
 // sm_100a building blocks for the tensor-core kernels: mbarriers with bounded
-// waits, tcgen05.mma (kind::f16) with shared-memory matrix descriptors, TMEM
-// loads, cp.async with zero fill.
+// waits, TMA tiled loads/stores and bulk groups, tcgen05.mma (kind::f16) with
+// shared-memory matrix descriptors, TMEM loads, cp.async with zero fill.
 //
 // Shared-memory operand layouts (128-byte swizzle, descriptor version 1):
 //   K-major: rows of 128 bytes (64 BF16 along K), 8-row groups SBO bytes apart;
@@ -10,6 +10,8 @@
 //            K SBO bytes apart.
 // In both, the 16-byte chunk c of row r within an atom sits at chunk c ^ (r & 7).
 #pragma once
+#include <cuda.h>
+
 #include <cstdint>
 
 namespace gatb {
@@ -20,6 +22,10 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 }
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
 }
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
@@ -135,6 +141,25 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
 #pragma unroll
     for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
 }
+// TMA tiled 2-D load (completes on `bar` with the byte count) and store
+// (bulk group); no multicast.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+                 ::"l"(map), "r"(smem_u32(src)), "r"(x), "r"(y)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 // 16-byte asynchronous copy global -> shared; src_bytes < 16 zero-fills the rest.
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");

@@ -273,15 +273,17 @@ int gat_b200_aggregate_fused(const gat_b200_graph* g, int heads, int dim, const 
  * its scratch in a 32 MiB array compiled into the library, which every GPU
  * that loads the library's module keeps until the process exits. Limits:
  * at most 7936 * 65536 = 520,093,696 edges (larger graphs get
- * GAT_B200_EUNSUPPORTED), heads <= 8, dim <= 64. The first call on a device
- * looks up the array's device address (cudaGetSymbolAddress) with that device
- * current; make that first call before any stream capture. All calls share the
+ * GAT_B200_EUNSUPPORTED), heads <= 8, dim <= 64. Every call looks up the
+ * array's device address in the current device's context
+ * (cudaGetSymbolAddress); the first call on a device also loads the module
+ * there, so make that first call before any stream capture. All calls share the
  * array: calls whose kernels can overlap on the GPU (other streams, other host
  * threads) race on it and must be serialized by the caller. The CSR is read as
  * given: it must be a valid destination-row CSR (row[0] = 0, row[n] = e,
  * non-decreasing, every source id < n), which gat_b200_validate_csr checks on a
  * host copy; gat_b200_graph_create validates on the device. Arguments and
- * output as in gat_b200_aggregate_fused. */
+ * output as in gat_b200_aggregate_fused; out_dtype must be GAT_B200_BF16 or
+ * GAT_B200_F32, and padding columns [heads*dim, ldo) are written as zeros. */
 int gat_b200_aggregate_fused_noalloc(uint64_t n, uint64_t e, const uint64_t* row,
                                      const uint32_t* col, int heads, int dim, const void* h,
                                      int h_dtype, int ldh, const float* left, const float* right,

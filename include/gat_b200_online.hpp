@@ -44,6 +44,14 @@ namespace icpp_online {
 struct Timing {
     double convert = 0, lr = 0, kernel = 0, normalize = 0, activation = 0, total = 0;
 };
+// Counters of the reference's CPU schedule. blocks, max_updates, rescales,
+// rescale_events and neighbor_steps are the device's exact counts
+// (gat_b200_tfs_online_counters). The AMX call, FMA, tile, spill/reload and
+// rescaled-element counts are MODELLED from those counts with the reference's
+// CPU work identities (AMX tiles of 16 rows, 32-wide K blocks, register
+// spills per rescale event); the GPU kernels do not execute that schedule, so
+// they are not device measurements. The drivers print them with
+// cpu_schedule_counters=modelled_not_measured_on_gpu.
 struct Stats {
     double score_generation = 0, block_max = 0, exp_den = 0;
     double rescale_store = 0, rescale_vector = 0, rescale_reload = 0;

@@ -1,8 +1,8 @@
 """Regenerates the golden fixtures in tests/golden/ from the reference itself.
 
-Run where the reference source tree exists (its location in the REF
-environment variable, or the default in REF below) after
-`make -C oracle all ref`:
+Run where the reference source tree exists (its location in the GAT_B200_REF
+environment variable, or a `reference` directory next to this repository)
+after `make -C oracle all ref`:
 
     python tests/golden/make_golden.py
 
@@ -52,7 +52,7 @@ sys.path.insert(0, str(ROOT / "gat-tfs_b200"))
 import configs  # noqa: E402
 import gatb200 as G  # noqa: E402
 
-REF = Path(os.environ.get("REF", "/root/reference"))
+REF = Path(os.environ.get("GAT_B200_REF") or ROOT.parent / "reference")
 OUT = Path(__file__).resolve().parent
 DUMP = ROOT / "oracle" / "_ref" / "ref_dump"
 

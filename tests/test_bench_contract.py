@@ -37,6 +37,25 @@ def test_reference_arm_line():
     assert cb["kind"] == "reference" and cb["value"] == d["value"] and cb["cores"] >= 1 and cb["sample"]
 
 
+def test_reference_arm_maps_no_repo_library():
+    """The reference arm's process imports no binding and maps no library of
+    this repository: its inputs come from gat_b200_make_inputs (host code,
+    separate program) and the forward runs in the reference's binary."""
+    if not REF_BIN.exists():
+        pytest.skip("the reference's driver is not built (oracle/_ref)")
+    code = ("import sys, runpy; sys.argv = ['bench.py', '--impl', 'reference', '--config', 'c1', '--steps', '1', "
+            "'--warmup', '3']\n"
+            "try:\n    runpy.run_path('bench.py', run_name='__main__')\nexcept SystemExit:\n    pass\n"
+            "maps = open('/proc/self/maps').read()\n"
+            "print('MAPPED', 'libgat_b200' in maps, 'gatb200' in sys.modules, 'configs' in sys.modules)")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert "MAPPED False False False" in r.stdout, r.stdout[-2000:]
+    d = json.loads([ln for ln in r.stdout.splitlines() if ln.startswith("{")][0])
+    assert d["steps"] == 1 and d["warmup"] == 3
+    assert "physical cores" in d["cpu_baseline"]["sample"] and "NUMA" in d["config"]["placement"]
+
+
 def test_reference_arm_unavailable_on_rmat():
     d = _bench("--impl", "reference", "--config", "c5", "--steps", "1", "--warmup", "1")
     assert d["impl"] == "reference" and "not run" in d["unavailable"]

@@ -130,3 +130,23 @@ def test_tfs_adaptive_argument_errors():
     assert r.returncode == 1 and "ICPP_HEADS_FAIL usage: icpp_heads GRAPH THREADS" in r.stderr
     r = subprocess.run([str(ADAPTIVE), "g", "0", "1", "1", "1"], capture_output=True, text=True, timeout=60)
     assert r.returncode == 1 and "ICPP_HEADS_FAIL invalid configuration" in r.stderr
+
+
+@pytest.mark.parametrize("config", ["c1", "c2"])
+def test_make_inputs_equals_binding(config, tmp_path):
+    """gat_b200_make_inputs (host objects only, used by the CPU reference arm)
+    writes the same GATBIN1 / GATWGT1 bytes as configs.make + the binding."""
+    import configs
+    import gatb200 as G
+    exe = ROOT / "gat-tfs_b200" / "gat_b200_make_inputs"
+    r = subprocess.run([str(exe), config, str(tmp_path / "a.gatbin"), str(tmp_path / "a.gatwgt")],
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    assert r.stdout.startswith(f"INPUTS config={config} ")
+    c = configs.make(config)
+    G.save_graph(c.graph, tmp_path / "b.gatbin")
+    G.save_model(c.model, tmp_path / "b.gatwgt")
+    for ext in ("gatbin", "gatwgt"):
+        assert (tmp_path / f"a.{ext}").read_bytes() == (tmp_path / f"b.{ext}").read_bytes(), ext
+    # the RMAT configurations are generated on the GPU only: refused
+    assert subprocess.run([str(exe), "c5", "x", "y"], capture_output=True, text=True).returncode == 1

@@ -91,7 +91,7 @@ def test_reference_sources_compile_against_the_mirror():
     signature it uses (where the reference tree is present: the check reads its
     source, never copies it)."""
     import os
-    ref = Path(os.environ.get("REF", "/root/reference")) / "baseline"
+    ref = Path(os.environ.get("GAT_B200_REF") or ROOT.parent / "reference") / "baseline"
     if not (ref / "tests" / "boundaries.cpp").exists():
         pytest.skip("reference tree absent")
     cmd = ["g++", "-std=c++17", "-fopenmp", "-fsyntax-only", "-w", "-I", str(ROOT / "oracle" / "compat"),

@@ -29,20 +29,33 @@ def _graph(kind):
         return np.array(row, np.uint64), np.array(col, np.uint32)
     if kind == "powerlaw":
         return G.synth_powerlaw_graph(20000, 400000, 9000, 2.1, 5)
+    if kind == "large":
+        # more than 7936 * 1024 edges: the range count is capped and every
+        # range grows beyond 1024 edges, as on the benchmark graphs
+        return G.synth_powerlaw_graph(300_000, 9_000_000, 20_000, 2.1, 7)
     return G.synth_uniform_graph(1024, 15, 1)
 
 
-@pytest.mark.parametrize("kind", ["hubs", "powerlaw", "uniform"])
-@pytest.mark.parametrize("K,d,out_dtype", [(8, 32, G.BF16), (1, 47, G.F32), (4, 40, G.BF16)])
-def test_noalloc_matches_regular_entry_point(dev, kind, K, d, out_dtype):
+@pytest.mark.parametrize("kind,K,d,out_dtype,h_dtype", [
+    (kind, K, d, o, G.BF16) for kind in ("hubs", "powerlaw", "uniform")
+    for K, d, o in ((8, 32, G.BF16), (1, 47, G.F32), (4, 40, G.BF16))
+] + [("hubs", 8, 32, G.F32, G.F32), ("powerlaw", 1, 47, G.F32, G.F32), ("large", 8, 32, G.BF16, G.BF16),
+     ("large", 1, 47, G.F32, G.BF16)])
+def test_noalloc_matches_regular_entry_point(dev, kind, K, d, out_dtype, h_dtype):
     import torch
     row, col = _graph(kind)
     n, e, W = len(row) - 1, len(col), K * d
     rng = np.random.default_rng(K * 1000 + d)
-    ldh = G.padded_ld(W, G.BF16)
-    hz = np.zeros((n, ldh), np.uint16)
-    hz[:, :W] = G.rne(rng.standard_normal((n, W)).astype(np.float32))
-    h = torch.from_numpy(hz.view(np.int16)).cuda()
+    ldh = G.padded_ld(W, h_dtype)
+    hf = rng.standard_normal((n, W)).astype(np.float32)
+    if h_dtype == G.BF16:
+        hz = np.zeros((n, ldh), np.uint16)
+        hz[:, :W] = G.rne(hf)
+        h = torch.from_numpy(hz.view(np.int16)).cuda()
+    else:
+        hz = np.zeros((n, ldh), np.float32)
+        hz[:, :W] = hf
+        h = torch.from_numpy(hz).cuda()
     left = torch.from_numpy(rng.standard_normal((n, K)).astype(np.float32)).cuda()
     right = torch.from_numpy(rng.standard_normal((n, K)).astype(np.float32)).cuda()
     ldo = G.padded_ld(W, out_dtype)
@@ -50,13 +63,13 @@ def test_noalloc_matches_regular_entry_point(dev, kind, K, d, out_dtype):
 
     g = G.DeviceGraph(row, col)
     ref = torch.zeros((n, ldo), dtype=odt, device="cuda")
-    G.aggregate_fused(g, K, d, h, G.BF16, ldh, left, right, True, ref, out_dtype, ldo)
+    G.aggregate_fused(g, K, d, h, h_dtype, ldh, left, right, True, ref, out_dtype, ldo)
 
     row_d = torch.from_numpy(row.view(np.int64)).cuda()
     col_d = torch.from_numpy(col.view(np.int32)).cuda()
     for call in range(2):  # the second call reuses the scratch left by the first
         out = torch.full((n, ldo), 3, dtype=odt, device="cuda")
-        G.aggregate_fused_noalloc(n, e, row_d, col_d, K, d, h, G.BF16, ldh, left, right, True, out, out_dtype, ldo)
+        G.aggregate_fused_noalloc(n, e, row_d, col_d, K, d, h, h_dtype, ldh, left, right, True, out, out_dtype, ldo)
         torch.cuda.synchronize()
         G.check_device()
         a, b = ref.cpu().numpy(), out.cpu().numpy()
@@ -81,6 +94,8 @@ def test_noalloc_rejects_bad_arguments(dev):
     out = torch.zeros((n, 256), dtype=torch.int16, device="cuda")
     with pytest.raises(G.GatError, match="heads <=8"):
         G.aggregate_fused_noalloc(n, e, row_d, col_d, 9, 32, h, G.BF16, 256, lr, lr, True, out, G.BF16, 256)
+    with pytest.raises(G.GatError, match="bad output dtype"):
+        G.aggregate_fused_noalloc(n, e, row_d, col_d, 8, 32, h, G.BF16, 256, lr, lr, True, out, 7, 256)
     with pytest.raises(G.GatError, match="exceed the maximum"):
         G.aggregate_fused_noalloc(n, 600_000_000, row_d, col_d, 8, 32, h, G.BF16, 256, lr, lr, True, out, G.BF16,
                                   256)
