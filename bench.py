@@ -813,7 +813,11 @@ def main():
                          "kernel": "agg_kernel, hidden layers (" + ("layer 2" if len(hid) == 1 else "layers 1-2") +
                                    (", rank 0 rows, layer time incl. next projection and exposed exchange)"
                                     if world > 1 else ", mean launch over the timed steps)"),
-                         "algorithmic_bytes_per_launch": int(b_hid), "others": others},
+                         "algorithmic_bytes_per_launch": int(b_hid), "others": others,
+                         "dram_frac": (round(traffic / (hid_ms * 1e-3) / 1e9 / peak, 4) if traffic else None),
+                         "note": "frac counts every edge's row gather as HBM traffic (the L2 serves repeat "
+                                 "gathers of popular sources, so it can exceed 1); dram_frac uses the ncu DRAM "
+                                 "bytes of the same launch (profiles/aggregate_c4_traffic.json)"},
             "e2e": {"value": round(3 * e / (e2e_ms * 1e-3) / 1e9, 4), "unit": "GEdges/s",
                     "ms_per_step": round(e2e_ms, 3), "mode": e2e_mode,
                     "sync_ms_per_step": round(e2e_sync_ms, 3), "h2d_bytes_per_step": n * din * 4,

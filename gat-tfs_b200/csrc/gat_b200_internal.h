@@ -32,4 +32,12 @@ int synth_powerlaw_rows(uint64_t n, uint64_t e_target, uint64_t max_degree, doub
 int synth_normal(uint64_t count, double scale, uint64_t seed, uint64_t stream, float* out, uint64_t offset);
 int synth_uniform(uint64_t count, double lo, double hi, uint64_t seed, uint64_t stream, float* out);
 
+// Communicator of the multi-GPU forward (comm.cpp). comm_all_gather_device:
+// every rank's `bytes` device bytes, rank-ordered, into recv (device) on
+// `stream`; the NCCL all-gather for world > 1.
+int comm_all_gather_device(gat_b200_comm* c, const void* send, void* recv, size_t bytes, void* stream);
+int comm_world(const gat_b200_comm* c);
+int comm_rank(const gat_b200_comm* c);
+int comm_device(const gat_b200_comm* c);
+
 }  // namespace gatb

@@ -59,6 +59,43 @@ __global__ void convert_vec_kernel(uint64_t n, int width, const float* __restric
     }
 }
 
+// The layer-1 input exchange of the partitioned multi-GPU forward: the
+// conversion of convert_vec_kernel (any input alignment), each 16-byte result
+// stored to `ndst` destinations -- this rank's block of its input table and
+// the same block of every peer's table, mapped over NVLink. Consecutive
+// threads store consecutive 16-byte pieces, so each destination receives
+// whole contiguous rows.
+struct ConvertDst {
+    uint16_t* d[8];
+};
+__global__ void convert_scatter_kernel(uint64_t n, int width, const float* __restrict__ in, int ld_in, bool vec_in,
+                                       ConvertDst dst, int ndst, int ld_out) {
+    const int chunks = ld_out / 8;
+    const uint64_t total = n * uint64_t(chunks);
+    for (uint64_t t = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; t < total;
+         t += uint64_t(gridDim.x) * blockDim.x) {
+        const uint64_t r = t / uint64_t(chunks);
+        const int c = int(t % uint64_t(chunks)) * 8;
+        const float* src = in + r * uint64_t(ld_in) + c;
+        float v[8];
+        if (vec_in && c + 8 <= width) {
+            const float4 a = __ldg(reinterpret_cast<const float4*>(src));
+            const float4 b = __ldg(reinterpret_cast<const float4*>(src + 4));
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+            v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v[k] = c + k < width ? src[k] : 0.f;
+        }
+        const uint4 o = make_uint4(rne_pair(v[0], v[1]), rne_pair(v[2], v[3]), rne_pair(v[4], v[5]),
+                                   rne_pair(v[6], v[7]));
+        const uint64_t off = r * uint64_t(ld_out) + c;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (j < ndst) *reinterpret_cast<uint4*>(dst.d[j] + off) = o;
+    }
+}
+
 // baseline/src/baseline_standard.cpp:44-51 (one warp per row).
 __global__ void max_prescan_kernel(const uint64_t* __restrict__ row, const uint32_t* __restrict__ col,
                                    uint64_t n, int heads, const float* __restrict__ left,
@@ -244,6 +281,24 @@ int convert_launch(uint64_t n, int width, const float* in, int ld_in, uint16_t* 
     else
         convert_kernel<<<grid_for(n * uint64_t(ld_out / 2), 256), 256, 0, st>>>(n, width, in, ld_in, out, ld_out);
     GATB_LAUNCH("convert kernel");
+    return 0;
+}
+
+int convert_scatter_launch(uint64_t n, int width, const float* in, int ld_in, int ndst, uint16_t* const* dst,
+                           int ld_out, cudaStream_t st) {
+    if (!in || !dst) return fail("convert_scatter: null buffer");
+    if (ndst < 1 || ndst > 8) return fail("convert_scatter: 1..8 destinations");
+    if (ld_in < width || ld_out < width || ld_out % 8) return fail("convert_scatter: bad row strides");
+    ConvertDst d{};
+    for (int j = 0; j < ndst; ++j) {
+        if (!dst[j] || (reinterpret_cast<uintptr_t>(dst[j]) & 15)) return fail("convert_scatter: destinations must be 16-byte aligned");
+        d.d[j] = dst[j];
+    }
+    if (n == 0) return 0;
+    const bool vec_in = (reinterpret_cast<uintptr_t>(in) & 15) == 0 && ld_in % 4 == 0;
+    convert_scatter_kernel<<<grid_for(n * uint64_t(ld_out / 8), 256), 256, 0, st>>>(n, width, in, ld_in, vec_in, d,
+                                                                                    ndst, ld_out);
+    GATB_LAUNCH("convert scatter kernel");
     return 0;
 }
 

@@ -112,6 +112,25 @@ SIGNATURES = [
                                               C.POINTER(_vp), C.POINTER(_vp), _vp]),
     ("gat_b200_peer_barrier", C.c_int, [C.POINTER(_vp), C.c_int, C.c_int, C.c_uint32, _vp]),
     ("gat_b200_copy_to_peers", C.c_int, [_vp, C.POINTER(_vp), C.c_int, C.c_uint64, C.POINTER(_vp)]),
+    ("gat_b200_comm_id", C.c_int, [_vp]),
+    ("gat_b200_comm_create", C.c_int, [_vp, C.c_int, C.c_int, C.POINTER(_vp)]),
+    ("gat_b200_comm_create_file", C.c_int, [C.c_char_p, C.c_int, C.c_int, C.c_int, C.POINTER(_vp)]),
+    ("gat_b200_comm_info", C.c_int, [_vp, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+    ("gat_b200_comm_all_gather", C.c_int, [_vp, _vp, _vp, C.c_uint64]),
+    ("gat_b200_comm_barrier", C.c_int, [_vp]),
+    ("gat_b200_comm_destroy", C.c_int, [_vp]),
+    ("gat_b200_partition", C.c_int, [C.c_uint64, _u64p, C.c_int, C.c_int, _u64p, _u64p, _u64p, _u64p]),
+    ("gat_b200_partition_slots", C.c_int, [C.c_uint64, _u64p, C.c_int, C.c_int, C.c_uint64, _u32p, _u32p]),
+    ("gat_b200_part_model_create", C.c_int, [_vp, C.c_uint64, _u64p, _u32p, C.POINTER(_vp), C.c_int, C.c_int, _vp,
+                                             C.POINTER(_vp)]),
+    ("gat_b200_part_model_rows", C.c_int, [_vp, _u64p, _u64p, _u64p]),
+    ("gat_b200_part_model_forward", C.c_int, [_vp, _vp, C.c_int, _vp, C.c_int, _vp]),
+    ("gat_b200_part_model_forward_async", C.c_int, [_vp, _vp, _vp, _vp]),
+    ("gat_b200_part_model_join", C.c_int, [_vp, _vp]),
+    ("gat_b200_part_model_enable_timing", C.c_int, [_vp, C.c_int]),
+    ("gat_b200_part_model_stage_times", C.c_int, [_vp, _f32p]),
+    ("gat_b200_part_model_launches", C.c_int, [_vp]),
+    ("gat_b200_part_model_destroy", C.c_int, [_vp]),
 ]
 for _name, _res, _args in SIGNATURES:
     _fn = getattr(_lib, _name)
@@ -627,3 +646,128 @@ class DeviceModel:
             self.close()
         except Exception:
             pass
+
+
+# ---------------------------------------------------------------- multi-GPU
+COMM_ID_BYTES = 128
+EXCHANGE_P2P, EXCHANGE_NCCL = 0, 1
+PART_STAGES = ("h2d", "input_exchange", "barrier_l1", "projection_l1", "aggregate_l1", "projection_l2",
+               "barrier_l2", "aggregate_l2", "projection_l3", "barrier_l3", "aggregate_l3", "d2h")
+
+
+def comm_id() -> bytes:
+    """A fresh NCCL unique id (rank 0 makes it, every rank passes it to Comm)."""
+    b = C.create_string_buffer(COMM_ID_BYTES)
+    _check(_lib.gat_b200_comm_id(b))
+    return b.raw
+
+
+def partition(row: np.ndarray, world: int, chunks: int = 1):
+    """(cuts[world+1], chunk_cuts[world, chunks+1], block_rows, table_rows) of the partitioned forward."""
+    row = np.ascontiguousarray(row, np.uint64)
+    n = len(row) - 1
+    cuts = np.zeros(world + 1, np.uint64)
+    cc = np.zeros(world * (chunks + 1), np.uint64)
+    br, tr = C.c_uint64(), C.c_uint64()
+    _check(_lib.gat_b200_partition(n, _p(row, _u64p), world, chunks, _p(cuts, _u64p), _p(cc, _u64p), C.byref(br),
+                                   C.byref(tr)))
+    return cuts.astype(np.int64), cc.reshape(world, chunks + 1).astype(np.int64), int(br.value), int(tr.value)
+
+
+def partition_slots(row: np.ndarray, world: int, chunks: int, src: np.ndarray) -> np.ndarray:
+    """Table rows of global source ids under partition(row, world, chunks)."""
+    row = np.ascontiguousarray(row, np.uint64)
+    src = np.ascontiguousarray(src, np.uint32)
+    out = np.empty(len(src), np.uint32)
+    _check(_lib.gat_b200_partition_slots(len(row) - 1, _p(row, _u64p), world, chunks, len(src), _p(src, _u32p),
+                                         _p(out, _u32p)))
+    return out
+
+
+class Comm:
+    """The node's communicator (gat_b200_comm_create): rank `rank` of `world`
+    on the current device, joined with rank 0's unique id (or through `path`)."""
+
+    def __init__(self, world: int, rank: int, uid: Optional[bytes] = None, path: Optional[str] = None,
+                 timeout_ms: int = 60000):
+        h = _vp()
+        if path is not None:
+            _check(_lib.gat_b200_comm_create_file(str(path).encode(), world, rank, timeout_ms, C.byref(h)))
+        else:
+            buf = C.create_string_buffer(uid, COMM_ID_BYTES) if uid is not None else None
+            _check(_lib.gat_b200_comm_create(buf, world, rank, C.byref(h)))
+        self.handle = h
+        self.world, self.rank = world, rank
+
+    def all_gather(self, blob: bytes) -> List[bytes]:
+        out = C.create_string_buffer(len(blob) * self.world)
+        _check(_lib.gat_b200_comm_all_gather(self.handle, C.create_string_buffer(blob, len(blob)), out, len(blob)))
+        return [out.raw[j * len(blob):(j + 1) * len(blob)] for j in range(self.world)]
+
+    def barrier(self):
+        _check(_lib.gat_b200_comm_barrier(self.handle))
+
+    def close(self):
+        if getattr(self, "handle", None):
+            _lib.gat_b200_comm_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class PartModel:
+    """The row-partitioned three-layer forward of this rank
+    (gat_b200_part_model_*): row = all n+1 row pointers, col_rows = the
+    sources of this rank's rows (see rows())."""
+
+    def __init__(self, comm: Comm, row: np.ndarray, col_rows: np.ndarray, layers: Sequence[DeviceLayer],
+                 exchange: int = EXCHANGE_P2P, chunks: int = 1, stream=None):
+        row = np.ascontiguousarray(row, np.uint64)
+        col_rows = np.ascontiguousarray(col_rows, np.uint32)
+        self.layers = list(layers)
+        arr = (_vp * 3)(*[l.handle for l in self.layers])
+        h = _vp()
+        _check(_lib.gat_b200_part_model_create(comm.handle, len(row) - 1, _p(row, _u64p), _p(col_rows, _u32p), arr,
+                                               exchange, chunks, _stream(stream), C.byref(h)))
+        self.handle = h
+        self.comm = comm
+        self.classes = self.layers[2].width
+        self.din = self.layers[0].in_
+        self.lo, self.hi, self.e_loc = self.rows()
+        self.n_loc = self.hi - self.lo
+
+    def rows(self):
+        lo, hi, e = C.c_uint64(), C.c_uint64(), C.c_uint64()
+        _check(_lib.gat_b200_part_model_rows(self.handle, C.byref(lo), C.byref(hi), C.byref(e)))
+        return int(lo.value), int(hi.value), int(e.value)
+
+    def forward(self, x, logits, x_on_host: bool, logits_on_host: bool, stream=None):
+        _check(_lib.gat_b200_part_model_forward(self.handle, _ptr(x), int(x_on_host), _ptr(logits),
+                                                int(logits_on_host), _stream(stream)))
+
+    def forward_async(self, x_host, logits_host, stream=None):
+        _check(_lib.gat_b200_part_model_forward_async(self.handle, _ptr(x_host), _ptr(logits_host), _stream(stream)))
+
+    def join(self, stream=None):
+        _check(_lib.gat_b200_part_model_join(self.handle, _stream(stream)))
+
+    def enable_timing(self, on: bool):
+        _check(_lib.gat_b200_part_model_enable_timing(self.handle, int(on)))
+
+    def stage_times(self) -> dict:
+        buf = np.zeros(len(PART_STAGES), np.float32)
+        _check(_lib.gat_b200_part_model_stage_times(self.handle, _p(buf, _f32p)))
+        return {k: float(v) for k, v in zip(PART_STAGES, buf)}
+
+    def launches(self) -> int:
+        return _lib.gat_b200_part_model_launches(self.handle)
+
+    def close(self):
+        """Collective: every rank calls it."""
+        if getattr(self, "handle", None):
+            h, self.handle = self.handle, None
+            _check(_lib.gat_b200_part_model_destroy(h))

@@ -468,6 +468,96 @@ int gat_b200_copy_to_peers(const void* src, void* const* dst, int ndst, uint64_t
  * next gat_b200_check_device return GAT_B200_ETIMEOUT. world <= 8. */
 int gat_b200_peer_barrier(void* const* flags, int world, int rank, uint32_t epoch, void* stream);
 
+/* ======================================================================== *
+ *  Multi-GPU forward behind the C ABI                                      *
+ * ======================================================================== *
+ * No counterpart in the reference (one CPU process). One process per GPU of
+ * one NVLink/NVSwitch node runs the reference's model loop
+ * (baseline/bench/main.cpp:171-172) on its share of destination rows; the
+ * calls below are everything such a process needs, with no framework around
+ * it. */
+
+/* ---- communicator ------------------------------------------------------ */
+typedef struct gat_b200_comm gat_b200_comm;
+#define GAT_B200_COMM_ID_BYTES 128
+
+/* A fresh NCCL unique id (rank 0), to hand to the other ranks out of band. */
+int gat_b200_comm_id(void* id);
+/* Joins the node's communicator as `rank` of `world` (<= 8) on the current
+ * device; every rank passes rank 0's id. Blocks until all ranks joined. NCCL
+ * (libnccl.so.2) is loaded at run time; NCCL_NVLS_ENABLE defaults to 0. */
+int gat_b200_comm_create(const void* id, int world, int rank, gat_b200_comm** out);
+/* The same, with the id passed through a file: rank 0 writes a fresh id to
+ * `path` (atomically, by rename), the other ranks wait up to timeout_ms for it
+ * (GAT_B200_ETIMEOUT after that). Use a path no earlier run has written. */
+int gat_b200_comm_create_file(const char* path, int world, int rank, int timeout_ms, gat_b200_comm** out);
+int gat_b200_comm_info(const gat_b200_comm* c, int* world, int* rank);
+/* Host-memory all-gather of `bytes` per rank into recv[world * bytes]
+ * (rank order), and a host barrier. Both block until done. */
+int gat_b200_comm_all_gather(gat_b200_comm* c, const void* send, void* recv, uint64_t bytes);
+int gat_b200_comm_barrier(gat_b200_comm* c);
+int gat_b200_comm_destroy(gat_b200_comm* c);
+
+/* ---- row partition (host) ---------------------------------------------- */
+/* The layout of the partitioned forward for a destination-row CSR of n rows
+ * (row pointers only): rank k owns rows [cuts[k], cuts[k+1]), cuts[k] the
+ * first row whose CSR offset reaches k*e/world; each rank's rows are cut again
+ * into `chunks` row chunks balanced by edges (chunk_cuts[k*(chunks+1) + c],
+ * global rows). Every layer's feature table holds chunks*world blocks of
+ * *block_rows rows (the largest chunk, rounded up to 4): chunk c of rank k at
+ * table row (c*world + k) * block_rows; *table_rows = chunks*world*block_rows.
+ * Any output may be NULL. */
+int gat_b200_partition(uint64_t n, const uint64_t* row, int world, int chunks, uint64_t* cuts,
+                       uint64_t* chunk_cuts, uint64_t* block_rows, uint64_t* table_rows);
+/* Table rows of `count` global source ids under that layout. */
+int gat_b200_partition_slots(uint64_t n, const uint64_t* row, int world, int chunks, uint64_t count,
+                             const uint32_t* src, uint32_t* slots);
+
+/* ---- partitioned three-layer model ------------------------------------- */
+typedef struct gat_b200_part_model gat_b200_part_model;
+/* Exchange of each layer's projected features between the ranks:
+ *  P2P  (default): peer memory over NVLink (CUDA IPC). Layer 1's BF16 input
+ *        rows are stored into every rank's input table by the conversion
+ *        kernel itself and every rank projects the whole table; for layers 2
+ *        and 3 the projection kernel stores each H/R tile into every rank's
+ *        table; a bounded cross-GPU flag barrier closes each exchange.
+ *  NCCL: each rank projects its own rows and NCCL all-gathers H and R. */
+#define GAT_B200_EXCHANGE_P2P 0
+#define GAT_B200_EXCHANGE_NCCL 1
+
+/* Collective: every rank calls it with the same n, row (all n+1 row
+ * pointers), chunks, exchange and layer shapes. col_rows holds the sources of
+ * this rank's rows (col[row[cuts[rank]] .. row[cuts[rank+1]]) of the whole
+ * CSR; gat_b200_part_model_rows gives that range). Source ids are remapped to
+ * table rows once, and each chunk's slice is validated and scheduled as
+ * gat_b200_graph_create does. Layers as gat_b200_model_create. */
+int gat_b200_part_model_create(gat_b200_comm* comm, uint64_t n, const uint64_t* row, const uint32_t* col_rows,
+                               const gat_b200_layer* const* layers, int exchange, int chunks, void* stream,
+                               gat_b200_part_model** out);
+/* This rank's destination rows [*lo, *hi) and its edge count. */
+int gat_b200_part_model_rows(const gat_b200_part_model* m, uint64_t* lo, uint64_t* hi, uint64_t* edges);
+/* The forward of this rank's rows: x FP32 [hi-lo][din] (host or device),
+ * logits FP32 [hi-lo][classes] (host or device). Every rank calls it the same
+ * number of times (the exchange pairs the ranks' calls). With host logits the
+ * call returns after the copy. */
+int gat_b200_part_model_forward(gat_b200_part_model* m, const float* x, int x_on_host, float* logits,
+                                int logits_on_host, void* stream);
+/* Pipelined host-to-host requests, as gat_b200_model_forward_async / join. */
+int gat_b200_part_model_forward_async(gat_b200_part_model* m, const float* x, float* logits, void* stream);
+int gat_b200_part_model_join(gat_b200_part_model* m, void* stream);
+/* Per-stage CUDA-event times of the last forward (enable first):
+ * ms[0..11] = {h2d, input exchange, barrier 1, projection L1, aggregation L1,
+ * projection+exchange L2, barrier 2, aggregation L2, projection+exchange L3,
+ * barrier 3, aggregation L3, d2h}. With chunks > 1 a layer's aggregation time
+ * also holds the projections of its earlier chunks. */
+#define GAT_B200_PART_STAGES 12
+int gat_b200_part_model_enable_timing(gat_b200_part_model* m, int on);
+int gat_b200_part_model_stage_times(gat_b200_part_model* m, float* ms);
+int gat_b200_part_model_launches(const gat_b200_part_model* m);
+/* Collective: frees the model after a host barrier (peers may still be
+ * storing into this rank's tables until every rank finished its forward). */
+int gat_b200_part_model_destroy(gat_b200_part_model* m);
+
 #ifdef __cplusplus
 }
 #endif
