@@ -86,10 +86,9 @@ def parse():
                     help="standard: B0 on every layer; adaptive: layer 1 through TFS aggregation (tensor cores)")
     ap.add_argument("--chunks", type=int, default=1,
                     help="N>1: row chunks per rank, each projected and exchanged as soon as it is aggregated")
-    ap.add_argument("--exchange", choices=["p2p", "dma", "nccl"], default="p2p",
-                    help="N>1: p2p = the projection kernel stores H/R into every rank's table over NVLink; "
-                         "dma = copy engines push each projected chunk to the peers while the next chunk "
-                         "is aggregated; nccl = NCCL all-gather per chunk")
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="N>1: p2p = the conversion / projection kernels store every rank's rows into every "
+                         "rank's table over NVLink; nccl = NCCL all-gather of H and R per layer")
     return ap.parse_args()
 
 
@@ -648,21 +647,24 @@ def main():
         model.enable_timing(0)
         parallelism = "single"
     else:
-        # ---- N GPUs: destination rows partitioned by edge count, NCCL all-gather ----
-        import dist as gdist
+        # ---- N GPUs: the C-ABI partitioned model (gat_b200_part_model_*) ----
         log("building rank-local inputs")
         part = configs.make_part(args.config, rank, world)
         log(f"rows [{part.lo}, {part.hi}) of {len(part.row) - 1}")
         n, e, din = len(part.row) - 1, part.e, part.din
-        pm = gdist.PartitionedModel(part.row, part.col_rows, part.model, rank, world, stream, dist, part.cuts,
-                                    chunks=args.chunks, exchange=args.exchange)
+        uid = [G.comm_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = G.Comm(world, rank, uid[0])
+        part_layers = [G.DeviceLayer(p) for p in part.model]
+        exch = G.EXCHANGE_P2P if args.exchange == "p2p" else G.EXCHANGE_NCCL
+        pm = G.PartModel(comm, part.row, part.col_rows, part_layers, exch, args.chunks, stream)
         log("device model ready")
         n_loc, e_loc = pm.n_loc, pm.e_loc
         classes = pm.classes
         x_rows = part.x_rows
         x_dev = torch.from_numpy(x_rows).cuda()
         logits = torch.empty((n_loc, classes), dtype=torch.float32, device="cuda")
-        fwd = pm.forward
+        fwd = lambda x, y, xh, yh: pm.forward(x, y, xh, yh, stream)
         for _ in range(warm):
             fwd(x_dev, logits, False, False)
         torch.cuda.synchronize()
@@ -678,14 +680,13 @@ def main():
         pm.enable_timing(False)
         launches = pm.launches()
         if args.exchange == "p2p":
-            how = ("the projection kernel stores each H/R tile into every rank's table over NVLink (CUDA IPC "
-                   "peer memory), then a cross-GPU flag barrier per layer")
-        elif args.exchange == "dma":
-            how = ("copy engines push each projected chunk into every peer's table (CUDA IPC peer memory) while "
-                   "the next chunk is aggregated, then a cross-GPU flag barrier per layer")
+            how = ("layer 1: the conversion kernel stores every input row into every rank's input table over "
+                   "NVLink (CUDA IPC peer memory) and each rank projects the whole table; layers 2-3: the "
+                   "projection kernel stores each H/R tile into every rank's table; a cross-GPU flag barrier "
+                   "closes each exchange")
         else:
-            how = "each chunk's NCCL all-gather of H and R overlaps the next chunk's aggregation"
-        parallelism = (f"rows{world}: destination rows split by edge count, {len(pm.chunks)} row chunk(s) per "
+            how = "NCCL all-gather of each layer's H and R"
+        parallelism = (f"rows{world}: destination rows split by edge count, {args.chunks} row chunk(s) per "
                        f"rank; {how}")
 
     # roofline of the dominant kernel: the hidden-layer aggregation (agg_kernel,
@@ -697,13 +698,11 @@ def main():
     peak, peak_kind = peaks()
     b_hid = agg_bytes(n_loc, e_loc, 8, 32, 2)
     b_l3 = agg_bytes(n_loc, e_loc, 1, classes, 4)
-    if world == 1:
-        hid = [stage_ms["aggregate_l2"]] if args.path == "adaptive" else [stage_ms["aggregate_l1"],
-                                                                            stage_ms["aggregate_l2"]]
-        l3_ms = stage_ms["aggregate_l3"]
+    if world == 1 and args.path == "adaptive":
+        hid = [stage_ms["aggregate_l2"]]
     else:
-        hid = [stage_ms["layer1"], stage_ms["layer2"]]
-        l3_ms = stage_ms["layer3"]
+        hid = [stage_ms["aggregate_l1"], stage_ms["aggregate_l2"]]
+    l3_ms = stage_ms["aggregate_l3"]
     hid_ms = sum(hid) / len(hid)
     achieved = b_hid / (hid_ms * 1e-3) / 1e9
     traffic = None
@@ -715,6 +714,7 @@ def main():
                                "achieved_gbs": round(b_l3 / (l3_ms * 1e-3) / 1e9, 1),
                                "frac": round(b_l3 / (l3_ms * 1e-3) / 1e9 / peak, 4)}}
     if world == 1:
+        # (N > 1: the projection stages also hold the exchange; stage_ms lists them)
         widths = [(din, 8, 32), (256, 8, 32), (256, 1, classes)]
         for l, (D, K, dd) in enumerate(widths, 1):
             pb = 2 * n_loc * D + 2 * D * (K * dd + 2 * K) + 2 * n_loc * K * dd + 8 * n_loc * K
@@ -743,9 +743,9 @@ def main():
         join = lambda: model.join(stream)
         api = "gat_b200_model_forward_async"
     else:
-        submit = lambda i: pm.forward_async(x_host, l_host[i & 1])
-        join = pm.join
-        api = "PartitionedModel.forward_async on every rank (its rows of X up, its logits down)"
+        submit = lambda i: pm.forward_async(x_host, l_host[i & 1], stream)
+        join = lambda: pm.join(stream)
+        api = "gat_b200_part_model_forward_async on every rank (its rows of X up, its logits down)"
     for i in range(2):
         submit(i)
     join()
@@ -811,7 +811,8 @@ def main():
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
                          "kernel": "agg_kernel, hidden layers (" + ("layer 2" if len(hid) == 1 else "layers 1-2") +
-                                   (", rank 0 rows, layer time incl. next projection and exposed exchange)"
+                                   (", rank 0 rows, last timed step" + (")" if args.chunks == 1 else
+                                                                         ", incl. interleaved projections)")
                                     if world > 1 else ", mean launch over the timed steps)"),
                          "algorithmic_bytes_per_launch": int(b_hid), "others": others,
                          "dram_frac": (round(traffic / (hid_ms * 1e-3) / 1e9 / peak, 4) if traffic else None),
@@ -831,6 +832,9 @@ def main():
         model.close()
     else:
         pm.close()
+        for lay in part_layers:
+            lay.close()
+        comm.close()
         dist.destroy_process_group()
     if rank == 0:
         if args.path == "standard" and not args.no_parity:

@@ -86,8 +86,8 @@ class Part:
 
 def make_part(name: str, rank: int, world: int) -> Part:
     """Generates only what rank `rank` of `world` needs: every rank builds the
-    row pointers, then the sources and features of its own rows."""
-    import dist
+    row pointers, then the sources and features of its own rows (the rows of
+    gat_b200_partition's cut, as the partitioned model takes them)."""
     s = SPECS[name]
     if s["kind"] == "powerlaw":
         row = G.synth_powerlaw_rowptr(s["n"], s["e"], s["max_degree"], s["gamma"], s["seed"])
@@ -95,7 +95,7 @@ def make_part(name: str, rank: int, world: int) -> Part:
         row, _ = _rmat(s, cols=False)  # generated on this rank's GPU
     else:
         raise ValueError("make_part needs a power-law or RMAT configuration")
-    cuts = dist.partition(row, world)
+    cuts = G.partition(row, world)[0]
     lo, hi = int(cuts[rank]), int(cuts[rank + 1])
     if s["kind"] == "rmat":
         _, col = _rmat(s, lo, hi)

@@ -23,6 +23,10 @@
 //    input; or FP32 logits; or the reference's unnormalised out/den/max.
 //  * Hub slices write partial (max, sum, acc) states to scratch; a second small
 //    kernel merges them per hub row.
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+
 #include "device.cuh"
 #include "graph.cuh"
 
@@ -273,8 +277,8 @@ struct Gen {
 //   3. prefetch R of chunk k+1 and col of chunk k+2;
 //   4. consume chunk k-1 (waiting only for this lane's own copies: a lane
 //      consumes exactly the vectors it copied).
-template <class HT, int KT, int C, int LPE, int VPL, bool MIXED, int NVC>
-__global__ void __launch_bounds__(128) agg_kernel(const AggArgs a) {
+template <class HT, int KT, int C, int LPE, int VPL, bool MIXED, int NVC, int MAXT>
+__global__ void __launch_bounds__(MAXT) agg_kernel(const AggArgs a) {
     using V = Vec<HT>;
     constexpr int VEC = V::N;
     constexpr int KM = KT ? KT : 8;
@@ -613,29 +617,223 @@ __global__ void __launch_bounds__(kWarps * 32) hub_merge_kernel(const AggArgs a)
     }
 }
 
+// ---- narrow single-head layers: one lane per work item ---------------------
+// For heads == 1 with a BF16 row of at most 64 features (layer 3, 1 x C with
+// C <= 64: 96 bytes on c4) a whole warp per row spends most of its issue
+// slots on chunk and row bookkeeping. Here each lane owns one work item (a
+// row, or a <= seg_edges segment of a hub row) and walks its edges alone:
+//   pass 1: the row's maximum score m = max_j leaky(L_i + R_j);
+//   pass 2: p_j = exp(s_j - m), den += p_j, acc += p_j * H_j (FP32, in edge
+//           order -- the reference's standard_aggregate order,
+//           baseline/src/baseline_standard.cpp:52-84, with the exact max of
+//           its max_prescan, :44-51).
+// The feature row is NV 16-byte loads per edge (predicated to the row's
+// vectors), the next edge's source, score and row are loaded before the
+// current one is consumed, and the accumulators stay in registers: no shared
+// memory, no cross-lane reductions. Items go to warps 32 at a time, in the
+// same descending-degree order as the warp kernel, so the lanes of a warp
+// have nearly equal edge counts. Hub segments leave their (max, sum, acc)
+// state for hub_merge_kernel, exactly as the warp kernel does.
+template <int NV>
+__global__ void __launch_bounds__(128) agg_lane_kernel(const AggArgs a) {
+    constexpr int NF = NV * 8;
+    const int lane = threadIdx.x & 31;
+    const uint64_t total = uint64_t(a.n_seg) + (a.n - a.n_hub);
+    const uint64_t groups = (total + 31) / 32;
+    const uint64_t G = uint64_t(gridDim.x) * (blockDim.x >> 5);
+    const int nvec = (a.width + 7) / 8;
+    const char* hb = static_cast<const char*>(a.h);
+    const uint64_t rowb = uint64_t(a.ldh) * 2;
+    for (uint64_t grp = blockIdx.x * uint64_t(blockDim.x >> 5) + (threadIdx.x >> 5); grp < groups; grp += G) {
+        const uint64_t it = grp * 32 + lane;
+        if (it >= total) continue;
+        uint64_t r, beg, end;
+        bool partial = false;
+        if (it < a.n_seg) {
+            const Segment sg = a.segs[it];
+            r = sg.row;
+            beg = sg.beg;
+            end = sg.end;
+            partial = true;
+        } else {
+            r = a.perm[a.n - 1 - a.n_hub - (it - a.n_seg)];
+            beg = a.row[r];
+            end = a.row[r + 1];
+        }
+        const float L = a.left[r];
+        // pass 1: the exact row (segment) maximum
+        float m = -INFINITY;
+        for (uint64_t e = beg; e < end; ++e) {
+            const float x = L + __ldg(a.right + __ldg(a.col + e));
+            m = fmaxf(m, fmaxf(x, 0.2f * x));
+        }
+        // pass 2: weights and the weighted sum, one edge ahead
+        unsigned long long acc[NF / 2];
+#pragma unroll
+        for (int k = 0; k < NF / 2; ++k) acc[k] = 0ull;
+        float den = 0.f;
+        uint4 cur[NV];
+        float cur_s = 0.f;
+        if (beg < end) {
+            const uint32_t s0 = __ldg(a.col + beg);
+            const float x = L + __ldg(a.right + s0);
+            cur_s = fmaxf(x, 0.2f * x);
+            const char* src = hb + uint64_t(s0) * rowb;
+#pragma unroll
+            for (int v = 0; v < NV; ++v) cur[v] = v < nvec ? ldg_nc_v4(src + v * 16) : make_uint4(0, 0, 0, 0);
+        }
+        for (uint64_t e = beg; e < end; ++e) {
+            uint4 nxt[NV];
+            float nxt_s = 0.f;
+            if (e + 1 < end) {
+                const uint32_t s1 = __ldg(a.col + e + 1);
+                const float x = L + __ldg(a.right + s1);
+                nxt_s = fmaxf(x, 0.2f * x);
+                const char* src = hb + uint64_t(s1) * rowb;
+#pragma unroll
+                for (int v = 0; v < NV; ++v) nxt[v] = v < nvec ? ldg_nc_v4(src + v * 16) : make_uint4(0, 0, 0, 0);
+            }
+            const float p = __expf(cur_s - m);
+            den += p;
+            const unsigned long long pp = pk(p, p);
+#pragma unroll
+            for (int v = 0; v < NV; ++v) {
+                float f[8];
+                Vec<uint16_t>::unpack(cur[v], f);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) acc[v * 4 + k] = ffma2(pk(f[2 * k], f[2 * k + 1]), pp, acc[v * 4 + k]);
+            }
+            if (e + 1 < end) {
+#pragma unroll
+                for (int v = 0; v < NV; ++v) cur[v] = nxt[v];
+                cur_s = nxt_s;
+            }
+        }
+        if (partial) {
+            float* st = a.seg_state + it * kSegStateFloats;
+            st[0] = m;
+            st[8] = den;
+#pragma unroll
+            for (int k = 0; k < NF / 2; ++k) {
+                const float2 f = upk(acc[k]);
+                if (2 * k < a.width) st[16 + 2 * k] = f.x;
+                if (2 * k + 1 < a.width) st[16 + 2 * k + 1] = f.y;
+            }
+            continue;
+        }
+        const float inv = den > 0.f ? 1.f / den : 0.f;
+        float o[NF];
+#pragma unroll
+        for (int k = 0; k < NF / 2; ++k) {
+            const float2 f = upk(acc[k]);
+            o[2 * k] = f.x;
+            o[2 * k + 1] = f.y;
+        }
+#pragma unroll
+        for (int c = 0; c < NF; ++c) {
+            if (c >= a.ldo) break;
+            float v = c < a.width ? o[c] * inv : 0.f;
+            if (a.hidden && v < 0.f) v = __expf(v) - 1.f;  // the B0 activation (gat.hpp:57-62)
+            if (a.out_bf16)
+                static_cast<uint16_t*>(a.out)[r * a.ldo + c] = uint16_t(pack_bf16x2(v, 0.f) & 0xffffu);
+            else
+                static_cast<float*>(a.out)[r * a.ldo + c] = v;
+        }
+        for (int c = NF; c < a.ldo; ++c) {  // padding columns past the vectors
+            if (a.out_bf16)
+                static_cast<uint16_t*>(a.out)[r * a.ldo + c] = 0;
+            else
+                static_cast<float*>(a.out)[r * a.ldo + c] = 0.f;
+        }
+    }
+}
+
+// Narrow single-head layers run on the warp kernel; the lane-per-item kernel
+// when the environment variable GAT_B200_NARROW_AGG is "lane". Both compute
+// the whole layer. Measured on c4 layer 3 (one B200): warp kernel 3.9 ms,
+// lane kernel 8.2 ms -- the lane kernel issues 6.6 warp instructions per edge
+// against 23, but its per-lane chains of dependent loads (source id, then
+// score and row) leave it latency-bound at 14 % issue activity.
+bool narrow_on_lanes() {
+    static const bool lanes = [] {
+        const char* v = std::getenv("GAT_B200_NARROW_AGG");
+        return v && std::strcmp(v, "lane") == 0;
+    }();
+    return lanes;
+}
+
+template <int NV>
+int launch_agg_lane(const AggArgs& a, cudaStream_t st, int reserve_sms) {
+    int dev = 0, sms = 0;
+    GATB_CUDA(cudaGetDevice(&dev));
+    GATB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    static int per_sm = 0;
+    if (!per_sm) {
+        GATB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, agg_lane_kernel<NV>, 128, 0));
+        if (per_sm < 1) per_sm = 1;
+    }
+    const int usable = reserve_sms > 0 && reserve_sms < sms ? sms - reserve_sms : sms;
+    const uint64_t items = uint64_t(a.n_seg) + (a.n - a.n_hub);
+    const uint64_t need = (items + 127) / 128;
+    const uint64_t cap = uint64_t(usable) * per_sm;
+    const unsigned blocks = unsigned(std::max<uint64_t>(1, std::min(need, cap)));
+    agg_lane_kernel<NV><<<blocks, 128, 0, st>>>(a);
+    GATB_LAUNCH("edge-softmax aggregation kernel (lane per row)");
+    if (a.n_hub) {
+        hub_merge_kernel<<<(a.n_hub + kWarps - 1) / kWarps, kWarps * 32, 0, st>>>(a);
+        GATB_LAUNCH("hub merge kernel");
+    }
+    return 0;
+}
+
+// reserve_sms = 0: blocks of up to 4 warps, as many resident blocks as fit
+// on every SM. reserve_sms > 0 (the multi-GPU forward, where a projection
+// kernel on another stream runs beside the aggregation): one block per SM
+// with as many warps as fit in its shared memory (so no other kernel's CTA
+// can share the SM), on all but reserve_sms SMs, which stay free for the
+// other kernel.
 template <class HT, int KT, int C, int LPE, int VPL, bool MIXED, int NVC>
-int launch_agg(const AggArgs& a, cudaStream_t st) {
+int launch_agg(const AggArgs& a, cudaStream_t st, int reserve_sms) {
     constexpr int KM = KT ? KT : 8;
     constexpr size_t warp_bytes = 2 * sizeof(Slot<C, KM>) + size_t(2) * C * LPE * VPL * 16;
     // Up to 4 warps per block within 200 KB of shared memory.
     constexpr int wpb = warp_bytes * 4 <= 200 * 1024 ? 4 : (warp_bytes * 2 <= 200 * 1024 ? 2 : 1);
-    constexpr size_t smem = warp_bytes * wpb;
-    auto kern = agg_kernel<HT, KT, C, LPE, VPL, MIXED, NVC>;
-    static int grid = 0;  // resident blocks (per process; all B200s are alike)
-    if (!grid) {
-        int dev = 0, sms = 0, per_sm = 0;
-        GATB_CUDA(cudaGetDevice(&dev));
-        GATB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-        GATB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-        GATB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, wpb * 32, smem));
-        grid = sms * (per_sm > 0 ? per_sm : 1);
-    }
+    constexpr int wbig_fit = int((220 * 1024) / warp_bytes);
+    constexpr int wbig = wbig_fit > 16 ? 16 : (wbig_fit < 1 ? 1 : wbig_fit);
+    static_assert(warp_bytes * wbig > 114 * 1024 || wbig == 16, "one block per SM needs most of its shared memory");
     uint64_t items = uint64_t(a.n_seg) + (a.n - a.n_hub);
-    uint64_t need = (items + wpb - 1) / wpb;
-    unsigned blocks = unsigned(need < uint64_t(grid) ? need : uint64_t(grid));
-    if (blocks == 0) blocks = 1;
-    kern<<<blocks, wpb * 32, smem, st>>>(a);
-    GATB_LAUNCH("edge-softmax aggregation kernel");
+    int dev = 0, sms = 0;
+    GATB_CUDA(cudaGetDevice(&dev));
+    GATB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    if (reserve_sms > 0 && reserve_sms < sms) {
+        constexpr size_t smem = warp_bytes * wbig;
+        auto kern = agg_kernel<HT, KT, C, LPE, VPL, MIXED, NVC, wbig * 32>;
+        static bool attr = false;
+        if (!attr) {
+            GATB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+            attr = true;
+        }
+        uint64_t need = (items + wbig - 1) / wbig;
+        unsigned blocks = unsigned(need < uint64_t(sms - reserve_sms) ? need : uint64_t(sms - reserve_sms));
+        if (blocks == 0) blocks = 1;
+        kern<<<blocks, wbig * 32, smem, st>>>(a);
+        GATB_LAUNCH("edge-softmax aggregation kernel");
+    } else {
+        constexpr size_t smem = warp_bytes * wpb;
+        auto kern = agg_kernel<HT, KT, C, LPE, VPL, MIXED, NVC, 128>;
+        static int grid = 0;  // resident blocks (per process; all B200s are alike)
+        if (!grid) {
+            int per_sm = 0;
+            GATB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+            GATB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, wpb * 32, smem));
+            grid = sms * (per_sm > 0 ? per_sm : 1);
+        }
+        uint64_t need = (items + wpb - 1) / wpb;
+        unsigned blocks = unsigned(need < uint64_t(grid) ? need : uint64_t(grid));
+        if (blocks == 0) blocks = 1;
+        kern<<<blocks, wpb * 32, smem, st>>>(a);
+        GATB_LAUNCH("edge-softmax aggregation kernel");
+    }
     if (a.n_hub) {
         hub_merge_kernel<<<(a.n_hub + kWarps - 1) / kWarps, kWarps * 32, 0, st>>>(a);
         GATB_LAUNCH("hub merge kernel");
@@ -656,10 +854,23 @@ int aggregate_check_error() {
     return 0;
 }
 
+int aggregate_dispatch_reserved(const gat_b200_graph* g, int heads, int dim, const void* h, int h_dtype, int ldh,
+                                const float* left, const float* right, const float* fixed_p, const float* fixed_den,
+                                int unnorm, int hidden, void* out, int out_bf16, int ldo, float* den, float* max,
+                                cudaStream_t st, int reserve_sms);
+
 int aggregate_dispatch(const gat_b200_graph* g, int heads, int dim, const void* h, int h_dtype, int ldh,
                        const float* left, const float* right, const float* fixed_p, const float* fixed_den,
                        int unnorm, int hidden, void* out, int out_bf16, int ldo, float* den, float* max,
                        cudaStream_t st) {
+    return aggregate_dispatch_reserved(g, heads, dim, h, h_dtype, ldh, left, right, fixed_p, fixed_den, unnorm, hidden,
+                                       out, out_bf16, ldo, den, max, st, 0);
+}
+
+int aggregate_dispatch_reserved(const gat_b200_graph* g, int heads, int dim, const void* h, int h_dtype, int ldh,
+                                const float* left, const float* right, const float* fixed_p, const float* fixed_den,
+                                int unnorm, int hidden, void* out, int out_bf16, int ldo, float* den, float* max,
+                                cudaStream_t st, int reserve_sms) {
     if (!g) return fail("aggregate: null graph");
     if (heads < 1 || heads > 8 || dim < 1 || dim > 64) return fail("invalid parameter shape (heads <=8, head_dim <=64)");
     const int width = heads * dim;
@@ -705,15 +916,26 @@ int aggregate_dispatch(const gat_b200_graph* g, int heads, int dim, const void* 
     if (h_dtype == GAT_B200_BF16) {
         if (heads == 8 && dim == 32 && (reinterpret_cast<uintptr_t>(left) & 15) == 0 &&
             (reinterpret_cast<uintptr_t>(right) & 15) == 0)
-            return launch_agg<uint16_t, 8, 16, 32, 1, false, 32>(a, st);
-        if (heads == 1 && width <= 64) return launch_agg<uint16_t, 1, 32, 8, 1, false, 0>(a, st);
-        return launch_agg<uint16_t, 0, 16, 32, 2, true, 0>(a, st);
+            return launch_agg<uint16_t, 8, 16, 32, 1, false, 32>(a, st, reserve_sms);
+        if (heads == 1 && width <= 64) {
+            // the lane-per-item kernel serves the fused epilogue (no fixed
+            // weights, no unnormalised outputs); the warp kernel the rest
+            if (!fixed_p && !unnorm && narrow_on_lanes()) {
+                const int nv = (width + 7) / 8;
+                if (nv <= 2) return launch_agg_lane<2>(a, st, reserve_sms);
+                if (nv <= 4) return launch_agg_lane<4>(a, st, reserve_sms);
+                if (nv <= 6) return launch_agg_lane<6>(a, st, reserve_sms);
+                return launch_agg_lane<8>(a, st, reserve_sms);
+            }
+            return launch_agg<uint16_t, 1, 32, 8, 1, false, 0>(a, st, reserve_sms);
+        }
+        return launch_agg<uint16_t, 0, 16, 32, 2, true, 0>(a, st, reserve_sms);
     }
     if (heads == 8 && dim == 32 && (reinterpret_cast<uintptr_t>(left) & 15) == 0 &&
         (reinterpret_cast<uintptr_t>(right) & 15) == 0)
-        return launch_agg<float, 8, 16, 32, 2, false, 64>(a, st);
-    if (heads == 1 && width <= 64) return launch_agg<float, 1, 32, 16, 1, false, 0>(a, st);
-    return launch_agg<float, 0, 16, 32, 4, true, 0>(a, st);
+        return launch_agg<float, 8, 16, 32, 2, false, 64>(a, st, reserve_sms);
+    if (heads == 1 && width <= 64) return launch_agg<float, 1, 32, 16, 1, false, 0>(a, st, reserve_sms);
+    return launch_agg<float, 0, 16, 32, 4, true, 0>(a, st, reserve_sms);
 }
 
 }  // namespace gatb

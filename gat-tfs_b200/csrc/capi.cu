@@ -26,7 +26,7 @@ int projection_simt_launch(const gat_b200_layer* p, uint64_t n, const void* x, i
                            int h_bf16, int ldh, float* left, float* right, cudaStream_t st);
 int projection_tc_launch(const gat_b200_layer* p, uint64_t n, const uint16_t* x, int ldx, uint16_t* h, int ldh,
                          float* z, int ldz, float* left, float* right, cudaStream_t st, int npeer = 0,
-                         uint16_t* const* h_peer = nullptr, float* const* r_peer = nullptr);
+                         uint16_t* const* h_peer = nullptr, float* const* r_peer = nullptr, int max_ctas = 0);
 int projection_tc_check_error();
 int peer_check_error();
 int aggregate_check_error();
@@ -402,6 +402,20 @@ int gat_b200_standard_layer(const gat_b200_graph* g, const gat_b200_layer* p, co
     if (rc) return rc;
     return aggregate_dispatch(g, p->heads, p->dim, h, hd, ldh, left, right, nullptr, nullptr, 0, hidden, out,
                               out_dtype == GAT_B200_BF16, ldo, nullptr, nullptr, st);
+}
+
+int gat_b200_device_count(int* count) {
+    clear_error();
+    if (!count) return fail("device_count: null output");
+    *count = 0;
+    GATB_CUDA(cudaGetDeviceCount(count));
+    return 0;
+}
+
+int gat_b200_set_device(int device) {
+    clear_error();
+    GATB_CUDA(cudaSetDevice(device));
+    return 0;
 }
 
 int gat_b200_check_device(void) {

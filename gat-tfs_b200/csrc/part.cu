@@ -42,16 +42,16 @@
 #include "graph.cuh"
 
 namespace gatb {
-int aggregate_dispatch(const gat_b200_graph* g, int heads, int dim, const void* h, int h_dtype, int ldh,
-                       const float* left, const float* right, const float* fixed_p, const float* fixed_den,
-                       int unnorm, int hidden, void* out, int out_bf16, int ldo, float* den, float* max,
-                       cudaStream_t st);
+int aggregate_dispatch_reserved(const gat_b200_graph* g, int heads, int dim, const void* h, int h_dtype, int ldh,
+                                const float* left, const float* right, const float* fixed_p, const float* fixed_den,
+                                int unnorm, int hidden, void* out, int out_bf16, int ldo, float* den, float* max,
+                                cudaStream_t st, int reserve_sms);
 int convert_launch(uint64_t n, int width, const float* in, int ld_in, uint16_t* out, int ld_out, cudaStream_t st);
 int convert_scatter_launch(uint64_t n, int width, const float* in, int ld_in, int ndst, uint16_t* const* dst,
                            int ld_out, cudaStream_t st);
 int projection_tc_launch(const gat_b200_layer* p, uint64_t n, const uint16_t* x, int ldx, uint16_t* h, int ldh,
                          float* z, int ldz, float* left, float* right, cudaStream_t st, int npeer,
-                         uint16_t* const* h_peer, float* const* r_peer);
+                         uint16_t* const* h_peer, float* const* r_peer, int max_ctas);
 int peer_barrier_launch(void* const* flags, int world, int rank, uint32_t epoch, cudaStream_t st);
 int device_check_errors();
 
@@ -60,6 +60,9 @@ namespace {
 constexpr int kMaxWorld = 8;
 constexpr int kMaxChunks = 64;
 constexpr int kEvents = GAT_B200_PART_STAGES + 1;
+// SMs left to the projection-and-exchange kernel while an aggregation runs
+// beside it (P2P exchange with several row chunks).
+constexpr int kDefaultReserve = 16;
 
 struct Layout {
     int world = 1, chunks = 1;
@@ -149,6 +152,12 @@ struct gat_b200_part_model {
     std::vector<std::array<void*, 8>> tab;
     std::vector<void*> owned, mapped;
     uint32_t epoch = 0;
+    // Overlap (P2P, chunks > 1): the projection and exchange of chunk c run on
+    // xst, on reserve_sms SMs the aggregation of chunk c+1 leaves free.
+    int reserve_sms = 0;
+    cudaStream_t xst = nullptr;
+    std::vector<cudaEvent_t> ev_agg;
+    cudaEvent_t ev_xdone = nullptr;
     // NCCL: full tables and per-chunk send blocks (plain device memory).
     void* h_full[3] = {};
     float* r_full[3] = {};
@@ -185,7 +194,8 @@ void mark(gat_b200_part_model* m, int k, cudaStream_t st) {
 
 // Layers 2 and 3 (l = 1, 2): projection of chunk c's rows of the previous
 // layer's output and its exchange.
-int project_chunk(gat_b200_part_model* m, int l, const gat_b200_part_model::Chunk& ch, cudaStream_t st, int& launches) {
+int project_chunk(gat_b200_part_model* m, int l, const gat_b200_part_model::Chunk& ch, cudaStream_t st, int& launches,
+                  int max_ctas) {
     const gat_b200_layer* p = m->layers[l];
     const int K = p->heads, ldh = m->ldh[l];
     const uint64_t nr = ch.b - ch.a;
@@ -204,7 +214,7 @@ int project_chunk(gat_b200_part_model* m, int l, const gat_b200_part_model::Chun
             ++np;
         }
         rc = projection_tc_launch(p, nr, x, m->ldx, m->H(m->rank, l) + ch.row0 * ldh, ldh, nullptr, 0, left,
-                                  m->R(m->rank, l) + ch.row0 * K, st, np, hp, rp);
+                                  m->R(m->rank, l) + ch.row0 * K, st, np, hp, rp, max_ctas);
         if (rc == GAT_B200_EUNSUPPORTED)
             return fail_code(rc, "part_model: layer outside the tensor-core projection (input or width > 256)");
         ++launches;
@@ -213,7 +223,7 @@ int project_chunk(gat_b200_part_model* m, int l, const gat_b200_part_model::Chun
     // NCCL: own rows into the send block, then the all-gather of chunk c
     const size_t hb = size_t(m->L.block_rows) * ldh * 2, rb = size_t(m->L.block_rows) * K * 4;
     rc = projection_tc_launch(p, nr, x, m->ldx, static_cast<uint16_t*>(m->h_send), ldh, nullptr, 0, left,
-                              m->r_send, st, 0, nullptr, nullptr);
+                              m->r_send, st, 0, nullptr, nullptr, 0);
     if (rc == GAT_B200_EUNSUPPORTED)
         return fail_code(rc, "part_model: layer outside the tensor-core projection (input or width > 256)");
     if (rc) return rc;
@@ -388,6 +398,21 @@ int gat_b200_part_model_create(gat_b200_comm* comm, uint64_t n, const uint64_t* 
         for (int k = 0; k < kEvents && !rc; ++k)
             if (cudaEventCreate(&m->ev[k]) != cudaSuccess) rc = fail("part_model_create: event");
         if (rc) break;
+        // the exchange stream (highest priority) and its events
+        {
+            int least = 0, greatest = 0;
+            cudaError_t e = cudaDeviceGetStreamPriorityRange(&least, &greatest);
+            if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&m->xst, cudaStreamNonBlocking, greatest);
+            m->ev_agg.assign(chunks, nullptr);
+            for (int c = 0; c < chunks && e == cudaSuccess; ++c)
+                e = cudaEventCreateWithFlags(&m->ev_agg[c], cudaEventDisableTiming);
+            if (e == cudaSuccess) e = cudaEventCreateWithFlags(&m->ev_xdone, cudaEventDisableTiming);
+            if (e != cudaSuccess) {
+                rc = cuda_fail(e, "part_model_create: exchange stream");
+                break;
+            }
+        }
+        m->reserve_sms = (exchange == GAT_B200_EXCHANGE_P2P && chunks > 1) ? kDefaultReserve : 0;
         cudaError_t e = cudaStreamSynchronize(st);
         if (e != cudaSuccess) rc = cuda_fail(e, "part_model_create");
     } while (0);
@@ -443,7 +468,7 @@ int gat_b200_part_model_forward(gat_b200_part_model* m, const float* x, int x_on
         // every rank projects the whole input table: H, L and R of every row
         rc = projection_tc_launch(p0, m->L.table_rows, static_cast<const uint16_t*>(m->tab[m->rank][6]), m->ld0,
                                   m->H(m->rank, 0), m->ldh[0], nullptr, 0, m->left0, m->R(m->rank, 0), st, 0,
-                                  nullptr, nullptr);
+                                  nullptr, nullptr, 0);
         if (rc == GAT_B200_EUNSUPPORTED)
             return fail_code(rc, "part_model: layer outside the tensor-core projection (input or width > 256)");
         if (rc) return rc;
@@ -461,7 +486,7 @@ int gat_b200_part_model_forward(gat_b200_part_model* m, const float* x, int x_on
             if (ch.b > ch.a) {
                 rc = projection_tc_launch(p0, ch.b - ch.a, m->x0 + ch.a * m->ld0, m->ld0,
                                           static_cast<uint16_t*>(m->h_send), m->ldh[0], nullptr, 0,
-                                          m->left[0] + ch.a * m->heads[0], m->r_send, st, 0, nullptr, nullptr);
+                                          m->left[0] + ch.a * m->heads[0], m->r_send, st, 0, nullptr, nullptr, 0);
                 if (rc == GAT_B200_EUNSUPPORTED)
                     return fail_code(rc, "part_model: layer outside the tensor-core projection");
                 if (rc) return rc;
@@ -483,20 +508,37 @@ int gat_b200_part_model_forward(gat_b200_part_model* m, const float* x, int x_on
         const bool last = l == 2;
         const void* htab = p2p ? static_cast<const void*>(m->H(m->rank, l)) : m->h_full[l];
         const float* rtab = p2p ? m->R(m->rank, l) : m->r_full[l];
-        for (size_t c = 0; c < m->chunks.size(); ++c) {
+        // overlap: chunk c's projection and exchange (stream xst, reserve_sms
+        // SMs) run while chunk c+1 aggregates on the other SMs; the last
+        // chunk's projection runs alone on every SM
+        const bool overlap = !last && p2p && m->reserve_sms > 0 && m->chunks.size() > 1;
+        const size_t nch = m->chunks.size();
+        for (size_t c = 0; c < nch; ++c) {
             const auto& ch = m->chunks[c];
             if (ch.g) {
                 const float* left = (l == 0 && p2p) ? m->left0 + ch.row0 * K : m->left[l & 1] + ch.a * K;
                 void* o = last ? static_cast<void*>(dst_logits + ch.a * m->classes)
                                : static_cast<void*>(static_cast<uint16_t*>(m->xs[l & 1]) + ch.a * m->ldx);
-                if ((rc = aggregate_dispatch(ch.g, K, p->dim, htab, GAT_B200_BF16, ldh, left, rtab, nullptr, nullptr,
-                                             0, last ? 0 : 1, o, last ? 0 : 1, last ? m->classes : m->ldx, nullptr,
-                                             nullptr, st)))
+                if ((rc = aggregate_dispatch_reserved(ch.g, K, p->dim, htab, GAT_B200_BF16, ldh, left, rtab, nullptr,
+                                                      nullptr, 0, last ? 0 : 1, o, last ? 0 : 1,
+                                                      last ? m->classes : m->ldx, nullptr, nullptr, st,
+                                                      overlap ? m->reserve_sms : 0)))
                     return rc;
                 launches += 1 + (ch.g->n_hub ? 1 : 0);
             }
-            if (c + 1 == m->chunks.size()) mark(m, 5 + 3 * l, st);
-            if (!last && (rc = project_chunk(m, l + 1, ch, st, launches))) return rc;
+            if (c + 1 == nch) mark(m, 5 + 3 * l, st);
+            if (last) continue;
+            if (overlap) {
+                GATB_CUDA(cudaEventRecord(m->ev_agg[c], st));
+                GATB_CUDA(cudaStreamWaitEvent(m->xst, m->ev_agg[c], 0));
+                if ((rc = project_chunk(m, l + 1, ch, m->xst, launches, c + 1 == nch ? 0 : m->reserve_sms))) return rc;
+            } else if ((rc = project_chunk(m, l + 1, ch, st, launches, 0))) {
+                return rc;
+            }
+        }
+        if (overlap) {
+            GATB_CUDA(cudaEventRecord(m->ev_xdone, m->xst));
+            GATB_CUDA(cudaStreamWaitEvent(st, m->ev_xdone, 0));
         }
         if (!last) {
             mark(m, 6 + 3 * l, st);
@@ -580,6 +622,17 @@ int gat_b200_part_model_stage_times(gat_b200_part_model* m, float* ms) {
 
 int gat_b200_part_model_launches(const gat_b200_part_model* m) { return m ? m->launches_last : 0; }
 
+int gat_b200_part_model_set_overlap(gat_b200_part_model* m, int reserved_sms) {
+    clear_error();
+    if (!m) return fail("part_model_set_overlap: null handle");
+    int dev = 0, sms = 0;
+    GATB_CUDA(cudaGetDevice(&dev));
+    GATB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    if (reserved_sms < 0 || reserved_sms >= sms) return fail("part_model_set_overlap: reserved SMs out of range");
+    m->reserve_sms = reserved_sms;
+    return 0;
+}
+
 int gat_b200_part_model_destroy(gat_b200_part_model* m) {
     clear_error();
     if (!m) return 0;
@@ -597,6 +650,10 @@ int gat_b200_part_model_destroy(gat_b200_part_model* m) {
         if (p) cudaFree(p);
     for (auto e : m->ev)
         if (e) cudaEventDestroy(e);
+    for (auto e : m->ev_agg)
+        if (e) cudaEventDestroy(e);
+    if (m->ev_xdone) cudaEventDestroy(m->ev_xdone);
+    if (m->xst) cudaStreamDestroy(m->xst);
     for (int b = 0; b < 2; ++b) {
         if (m->ev_up[b]) cudaEventDestroy(m->ev_up[b]);
         if (m->ev_done[b]) cudaEventDestroy(m->ev_done[b]);

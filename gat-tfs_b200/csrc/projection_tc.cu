@@ -387,9 +387,11 @@ int make_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uin
 
 // Returns GAT_B200_EUNSUPPORTED when the shape is outside the kernel (the
 // caller then uses the CUDA-core projection).
+// max_ctas > 0 caps the persistent grid (the multi-GPU forward runs this
+// kernel beside an aggregation that leaves that many SMs free).
 int projection_tc_launch(const gat_b200_layer* p, uint64_t n, const uint16_t* x, int ldx, uint16_t* h, int ldh,
                          float* z, int ldz, float* left, float* right, cudaStream_t st, int npeer,
-                         uint16_t* const* h_peer, float* const* r_peer) {
+                         uint16_t* const* h_peer, float* const* r_peer, int max_ctas) {
     if (p->np > 256 || p->kp > 256) return GAT_B200_EUNSUPPORTED;
     if (n == 0) return 0;
     if (n > uint64_t(INT32_MAX)) return fail("projection: too many rows");
@@ -461,7 +463,8 @@ int projection_tc_launch(const gat_b200_layer* p, uint64_t n, const uint16_t* x,
     GATB_CUDA(cudaGetDevice(&dev));
     GATB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const uint64_t ntiles = (n + kTileM - 1) / kTileM;
-    const unsigned grid = unsigned(ntiles < uint64_t(sms) ? ntiles : uint64_t(sms));
+    const uint64_t cap = max_ctas > 0 && max_ctas < sms ? uint64_t(max_ctas) : uint64_t(sms);
+    const unsigned grid = unsigned(ntiles < cap ? ntiles : cap);
     // Heads aligned to 16 columns (or a single head, whose columns past the
     // width carry zero coefficients): one head per 16-column block.
     if (p->dim % 16 == 0 || p->heads == 1) {

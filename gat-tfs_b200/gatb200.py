@@ -112,6 +112,8 @@ SIGNATURES = [
                                               C.POINTER(_vp), C.POINTER(_vp), _vp]),
     ("gat_b200_peer_barrier", C.c_int, [C.POINTER(_vp), C.c_int, C.c_int, C.c_uint32, _vp]),
     ("gat_b200_copy_to_peers", C.c_int, [_vp, C.POINTER(_vp), C.c_int, C.c_uint64, C.POINTER(_vp)]),
+    ("gat_b200_device_count", C.c_int, [C.POINTER(C.c_int)]),
+    ("gat_b200_set_device", C.c_int, [C.c_int]),
     ("gat_b200_comm_id", C.c_int, [_vp]),
     ("gat_b200_comm_create", C.c_int, [_vp, C.c_int, C.c_int, C.POINTER(_vp)]),
     ("gat_b200_comm_create_file", C.c_int, [C.c_char_p, C.c_int, C.c_int, C.c_int, C.POINTER(_vp)]),
@@ -131,6 +133,7 @@ SIGNATURES = [
     ("gat_b200_part_model_stage_times", C.c_int, [_vp, _f32p]),
     ("gat_b200_part_model_launches", C.c_int, [_vp]),
     ("gat_b200_part_model_destroy", C.c_int, [_vp]),
+    ("gat_b200_part_model_set_overlap", C.c_int, [_vp, C.c_int]),
 ]
 for _name, _res, _args in SIGNATURES:
     _fn = getattr(_lib, _name)
@@ -765,6 +768,10 @@ class PartModel:
 
     def launches(self) -> int:
         return _lib.gat_b200_part_model_launches(self.handle)
+
+    def set_overlap(self, reserved_sms: int):
+        """SMs left to the exchange while a chunk aggregates (0: no overlap)."""
+        _check(_lib.gat_b200_part_model_set_overlap(self.handle, reserved_sms))
 
     def close(self):
         """Collective: every rank calls it."""

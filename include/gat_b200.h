@@ -353,6 +353,11 @@ int gat_b200_tfs_layer(const gat_b200_graph* g, const gat_b200_layer* p, const v
  * allocation on the current device, its release, and synchronous copies
  * between host and device memory. */
 int gat_b200_device_alloc(uint64_t bytes, void** ptr);
+/* Device selection for the same callers (one process or thread per GPU):
+ * the number of visible devices, and the device the calling thread's later
+ * calls use (cudaSetDevice). */
+int gat_b200_device_count(int* count);
+int gat_b200_set_device(int device);
 int gat_b200_device_free(void* ptr);
 int gat_b200_copy_to_device(void* dst, const void* src, uint64_t bytes);
 int gat_b200_copy_to_host(void* dst, const void* src, uint64_t bytes);
@@ -554,6 +559,12 @@ int gat_b200_part_model_join(gat_b200_part_model* m, void* stream);
 int gat_b200_part_model_enable_timing(gat_b200_part_model* m, int on);
 int gat_b200_part_model_stage_times(gat_b200_part_model* m, float* ms);
 int gat_b200_part_model_launches(const gat_b200_part_model* m);
+/* Overlap of the layer-2/3 exchange with the aggregation (P2P exchange,
+ * chunks > 1): chunk c's projection, which stores into the peers' tables,
+ * runs on its own stream on `reserved_sms` SMs while chunk c+1 aggregates on
+ * the others (one aggregation block per SM). Default 16 when chunks > 1;
+ * 0 runs projection and aggregation one after the other. */
+int gat_b200_part_model_set_overlap(gat_b200_part_model* m, int reserved_sms);
 /* Collective: frees the model after a host barrier (peers may still be
  * storing into this rank's tables until every rank finished its forward). */
 int gat_b200_part_model_destroy(gat_b200_part_model* m);

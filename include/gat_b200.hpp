@@ -716,4 +716,81 @@ inline Fixture load_fixture(const Graph& g, const Param& p, const std::string& p
     return f;
 }
 
+// ---- the model loop on N GPUs of one node -----------------------------------
+// No counterpart in the reference (one CPU process). One process per GPU runs
+// the reference's three-layer loop (baseline/bench/main.cpp:171-172) on its
+// share of destination rows; the ranks exchange each layer's projected
+// features over NVLink (gat_b200_part_model_*).
+class Communicator {
+public:
+    // Rank `rank` of `world` on device `device`; rank 0 writes the NCCL id to
+    // `id_path` (a path no earlier run used), the others wait for it.
+    Communicator(const std::string& id_path, int world, int rank, int device, int timeout_ms = 120000) {
+        check(gat_b200_set_device(device));
+        check(gat_b200_comm_create_file(id_path.c_str(), world, rank, timeout_ms, &c_));
+        world_ = world;
+        rank_ = rank;
+    }
+    Communicator(const Communicator&) = delete;
+    Communicator& operator=(const Communicator&) = delete;
+    ~Communicator() { gat_b200_comm_destroy(c_); }
+    void barrier() { check(gat_b200_comm_barrier(c_)); }
+    int world() const { return world_; }
+    int rank() const { return rank_; }
+    gat_b200_comm* handle() const { return c_; }
+
+private:
+    gat_b200_comm* c_ = nullptr;
+    int world_ = 1, rank_ = 0;
+};
+
+class PartitionedModel {
+public:
+    // Collective. g: the whole graph (every rank reads the same GATBIN1 file);
+    // this rank keeps the sources and features of its own rows only.
+    PartitionedModel(Communicator& comm, const Graph& g, const Model& model,
+                     int exchange = GAT_B200_EXCHANGE_P2P, int chunks = 1)
+        : comm_(comm) {
+        for (int l = 0; l < 3; ++l) {
+            model[l].validate();
+            check(gat_b200_layer_create(model[l].in, model[l].heads, model[l].dim, model[l].w.data(),
+                                        model[l].al.data(), model[l].ar.data(), &layers_[l]));
+        }
+        std::vector<uint64_t> cuts(comm.world() + 1);
+        check(gat_b200_partition(g.n, g.row.data(), comm.world(), chunks, cuts.data(), nullptr, nullptr, nullptr));
+        lo_ = cuts[comm.rank()];
+        hi_ = cuts[comm.rank() + 1];
+        const gat_b200_layer* ls[3] = {layers_[0], layers_[1], layers_[2]};
+        check(gat_b200_part_model_create(comm.handle(), g.n, g.row.data(), g.col.data() + g.row[lo_], ls, exchange,
+                                         chunks, nullptr, &m_));
+        x_.assign(g.x.begin() + checked(lo_, g.din), g.x.begin() + checked(hi_, g.din));
+        classes_ = model[2].width();
+    }
+    PartitionedModel(const PartitionedModel&) = delete;
+    PartitionedModel& operator=(const PartitionedModel&) = delete;
+    // Collective, like the constructor.
+    ~PartitionedModel() {
+        gat_b200_part_model_destroy(m_);
+        for (auto* l : layers_) gat_b200_layer_destroy(l);
+    }
+    uint64_t first_row() const { return lo_; }
+    uint64_t end_row() const { return hi_; }
+    // Logits [end_row()-first_row()][classes] of this rank's rows.
+    std::vector<float> forward() {
+        std::vector<float> out(checked(hi_ - lo_, uint64_t(classes_)));
+        check(gat_b200_part_model_forward(m_, x_.data(), 1, out.data(), 1, nullptr));
+        return out;
+    }
+    gat_b200_part_model* handle() const { return m_; }
+    const std::vector<float>& input() const { return x_; }
+
+private:
+    Communicator& comm_;
+    gat_b200_layer* layers_[3] = {nullptr, nullptr, nullptr};
+    gat_b200_part_model* m_ = nullptr;
+    uint64_t lo_ = 0, hi_ = 0;
+    int classes_ = 0;
+    std::vector<float> x_;
+};
+
 }  // namespace gat_b200

@@ -158,15 +158,24 @@ def test_partitioned_forward_equals_single_process(world, chunks):
     assert np.array_equal(got, _reference_c2())
 
 
-def test_partitioned_model_argument_checks():
-    g = configs.make_graph("c1", features=False)
-    params = G.glorot_model(128, 40, 1)
-    with pytest.raises(ValueError, match="exchange"):
-        gdist.PartitionedModel(g.row, g.col, params, 0, 1, exchange="mpi")
-    with pytest.raises(ValueError, match="up to 8 ranks"):
-        gdist.PartitionedModel(g.row, g.col, params, 0, 9, exchange="p2p")
-    with pytest.raises(ValueError, match="up to 8 ranks"):
-        gdist.PartitionedModel(g.row, g.col, params, 0, 9, exchange="dma")
+def test_multi_gpu_c_abi_host_checks(tmp_path):
+    """Host-side checks of the communicator and the partitioned model (no GPU
+    touched): bad world sizes and ranks are refused, and a rank whose rank 0
+    never publishes the communicator id gives up after its timeout with
+    GAT_B200_ETIMEOUT instead of waiting for ever."""
+    import ctypes as C
+    import time
+    h = C.c_void_p()
+    rc = G._lib.gat_b200_comm_create(None, 9, 0, C.byref(h))
+    assert rc == G.EINVAL and b"world size" in G._lib.gat_b200_last_error()
+    rc = G._lib.gat_b200_comm_create(None, 2, 2, C.byref(h))
+    assert rc == G.EINVAL and b"rank outside" in G._lib.gat_b200_last_error()
+    t0 = time.time()
+    with pytest.raises(G.GatError, match="no unique id") as ei:
+        G.Comm(2, 1, path=str(tmp_path / "never_written"), timeout_ms=300)
+    assert ei.value.code == G.ETIMEOUT and time.time() - t0 < 10
+    rc = G._lib.gat_b200_part_model_create(None, 0, None, None, None, 0, 1, None, C.byref(h))
+    assert rc == G.EINVAL
 
 
 def _rank_fails(rank, world, port, q):
