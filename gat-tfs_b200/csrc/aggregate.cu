@@ -42,6 +42,7 @@ struct AggArgs {
     const uint32_t* perm;
     uint64_t n;
     uint32_t n_hub, n_seg;
+    uint32_t n_wide;         // rows after the hubs with more than kWideRowEdges edges
     const Segment* segs;
     const uint32_t* hub_seg_offset;
     float* seg_state;
@@ -617,173 +618,234 @@ __global__ void __launch_bounds__(kWarps * 32) hub_merge_kernel(const AggArgs a)
     }
 }
 
-// ---- narrow single-head layers: one lane per work item ---------------------
+// ---- narrow single-head layers: two lanes per row -------------------------
 // For heads == 1 with a BF16 row of at most 64 features (layer 3, 1 x C with
-// C <= 64: 96 bytes on c4) a whole warp per row spends most of its issue
-// slots on chunk and row bookkeeping. Here each lane owns one work item (a
-// row, or a <= seg_edges segment of a hub row) and walks its edges alone:
-//   pass 1: the row's maximum score m = max_j leaky(L_i + R_j);
-//   pass 2: p_j = exp(s_j - m), den += p_j, acc += p_j * H_j (FP32, in edge
-//           order -- the reference's standard_aggregate order,
-//           baseline/src/baseline_standard.cpp:52-84, with the exact max of
-//           its max_prescan, :44-51).
-// The feature row is NV 16-byte loads per edge (predicated to the row's
-// vectors), the next edge's source, score and row are loaded before the
-// current one is consumed, and the accumulators stay in registers: no shared
-// memory, no cross-lane reductions. Items go to warps 32 at a time, in the
-// same descending-degree order as the warp kernel, so the lanes of a warp
-// have nearly equal edge counts. Hub segments leave their (max, sum, acc)
-// state for hub_merge_kernel, exactly as the warp kernel does.
-template <int NV>
-__global__ void __launch_bounds__(128) agg_lane_kernel(const AggArgs a) {
-    constexpr int NF = NV * 8;
-    const int lane = threadIdx.x & 31;
-    const uint64_t total = uint64_t(a.n_seg) + (a.n - a.n_hub);
-    const uint64_t groups = (total + 31) / 32;
-    const uint64_t G = uint64_t(gridDim.x) * (blockDim.x >> 5);
-    const int nvec = (a.width + 7) / 8;
-    const char* hb = static_cast<const char*>(a.h);
-    const uint64_t rowb = uint64_t(a.ldh) * 2;
-    for (uint64_t grp = blockIdx.x * uint64_t(blockDim.x >> 5) + (threadIdx.x >> 5); grp < groups; grp += G) {
-        const uint64_t it = grp * 32 + lane;
-        if (it >= total) continue;
-        uint64_t r, beg, end;
-        bool partial = false;
-        if (it < a.n_seg) {
-            const Segment sg = a.segs[it];
-            r = sg.row;
-            beg = sg.beg;
-            end = sg.end;
-            partial = true;
-        } else {
-            r = a.perm[a.n - 1 - a.n_hub - (it - a.n_seg)];
-            beg = a.row[r];
-            end = a.row[r + 1];
-        }
-        const float L = a.left[r];
-        // pass 1: the exact row (segment) maximum
-        float m = -INFINITY;
-        for (uint64_t e = beg; e < end; ++e) {
-            const float x = L + __ldg(a.right + __ldg(a.col + e));
-            m = fmaxf(m, fmaxf(x, 0.2f * x));
-        }
-        // pass 2: weights and the weighted sum, one edge ahead
-        unsigned long long acc[NF / 2];
+// C <= 64: 96 bytes on c4) a whole warp per row and chunk spends most of its
+// issue slots on chunk and row bookkeeping. Here a pair of lanes walks a
+// row's edges in blocks of 4, each lane accumulating its half of the row's
+// 16-byte vectors (NVH of them) in registers:
+//  * the block's four source ids and scores arrive one block ahead;
+//  * the running maximum moves once per block (the sums are rescaled then,
+//    as the warp kernel does per chunk);
+//  * the four rows' half-vectors (4 * NVH loads) are issued together and
+//    consumed in edge order with FP32 FMAs.
+// Work units, dealt round-robin to warps in the warp kernel's order (largest
+// first): a "wide" item -- a hub segment, or a row of more than
+// kWideRowEdges edges -- takes a whole warp, its 16 pairs taking every 16th
+// block and combining their (max, sum, acc) states by shuffles at the end;
+// the remaining rows go 16 to a warp, one pair each (their degrees are nearly
+// equal in that order). Hub segments leave their state for hub_merge_kernel,
+// as the warp kernel does. No shared memory.
+template <int NVH>
+__device__ __forceinline__ void pair_walk(const AggArgs& a, const char* hb, uint64_t rowb, int nvec, int v0,
+                                          float L, uint64_t first, uint64_t end, uint64_t step, float& m,
+                                          float& den, unsigned long long (&acc)[NVH * 4]) {
+    uint32_t src[4];
+    float sco[4];
 #pragma unroll
-        for (int k = 0; k < NF / 2; ++k) acc[k] = 0ull;
-        float den = 0.f;
-        uint4 cur[NV];
-        float cur_s = 0.f;
-        if (beg < end) {
-            const uint32_t s0 = __ldg(a.col + beg);
-            const float x = L + __ldg(a.right + s0);
-            cur_s = fmaxf(x, 0.2f * x);
-            const char* src = hb + uint64_t(s0) * rowb;
+    for (int k = 0; k < 4; ++k) {
+        const bool ok = first + k < end;
+        src[k] = ok ? __ldg(a.col + first + k) : 0u;
+        const float x = ok ? L + __ldg(a.right + src[k]) : 0.f;
+        sco[k] = ok ? fmaxf(x, 0.2f * x) : -INFINITY;
+    }
+    for (uint64_t e = first; e < end; e += step) {
+        uint4 rows[4][NVH];
 #pragma unroll
-            for (int v = 0; v < NV; ++v) cur[v] = v < nvec ? ldg_nc_v4(src + v * 16) : make_uint4(0, 0, 0, 0);
+        for (int k = 0; k < 4; ++k) {
+            const char* sp = hb + uint64_t(src[k]) * rowb;
+            const bool ok = e + k < end;
+#pragma unroll
+            for (int j = 0; j < NVH; ++j)
+                rows[k][j] = (ok && v0 + j < nvec) ? ldg_nc_v4(sp + j * 16) : make_uint4(0, 0, 0, 0);
         }
-        for (uint64_t e = beg; e < end; ++e) {
-            uint4 nxt[NV];
-            float nxt_s = 0.f;
-            if (e + 1 < end) {
-                const uint32_t s1 = __ldg(a.col + e + 1);
-                const float x = L + __ldg(a.right + s1);
-                nxt_s = fmaxf(x, 0.2f * x);
-                const char* src = hb + uint64_t(s1) * rowb;
+        uint32_t nsrc[4];
+        float nsco[4];
 #pragma unroll
-                for (int v = 0; v < NV; ++v) nxt[v] = v < nvec ? ldg_nc_v4(src + v * 16) : make_uint4(0, 0, 0, 0);
-            }
-            const float p = __expf(cur_s - m);
+        for (int k = 0; k < 4; ++k) {
+            const bool ok = e + step + k < end;
+            nsrc[k] = ok ? __ldg(a.col + e + step + k) : 0u;
+            const float x = ok ? L + __ldg(a.right + nsrc[k]) : 0.f;
+            nsco[k] = ok ? fmaxf(x, 0.2f * x) : -INFINITY;
+        }
+        const float bm = fmaxf(fmaxf(sco[0], sco[1]), fmaxf(sco[2], sco[3]));
+        if (bm > m) {
+            const float sc = __expf(m - bm);  // 0 before the first block
+            den *= sc;
+            const unsigned long long ss = pk(sc, sc);
+#pragma unroll
+            for (int k = 0; k < NVH * 4; ++k) acc[k] = fmul2(acc[k], ss);
+            m = bm;
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float p = __expf(sco[k] - m);  // 0 past the end
             den += p;
             const unsigned long long pp = pk(p, p);
 #pragma unroll
-            for (int v = 0; v < NV; ++v) {
+            for (int j = 0; j < NVH; ++j) {
                 float f[8];
-                Vec<uint16_t>::unpack(cur[v], f);
+                Vec<uint16_t>::unpack(rows[k][j], f);
 #pragma unroll
-                for (int k = 0; k < 4; ++k) acc[v * 4 + k] = ffma2(pk(f[2 * k], f[2 * k + 1]), pp, acc[v * 4 + k]);
-            }
-            if (e + 1 < end) {
-#pragma unroll
-                for (int v = 0; v < NV; ++v) cur[v] = nxt[v];
-                cur_s = nxt_s;
+                for (int q = 0; q < 4; ++q) acc[j * 4 + q] = ffma2(pk(f[2 * q], f[2 * q + 1]), pp, acc[j * 4 + q]);
             }
         }
-        if (partial) {
-            float* st = a.seg_state + it * kSegStateFloats;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            src[k] = nsrc[k];
+            sco[k] = nsco[k];
+        }
+    }
+}
+
+// Item `it` of the warp kernel's order: a hub segment (it < n_seg) or a row.
+__device__ __forceinline__ void pair_item(const AggArgs& a, uint64_t it, uint64_t& r, uint64_t& beg, uint64_t& end,
+                                          bool& partial) {
+    if (it < a.n_seg) {
+        const Segment sg = a.segs[it];
+        r = sg.row;
+        beg = sg.beg;
+        end = sg.end;
+        partial = true;
+    } else {
+        r = a.perm[a.n - 1 - a.n_hub - (it - a.n_seg)];
+        beg = a.row[r];
+        end = a.row[r + 1];
+        partial = false;
+    }
+}
+
+template <int NVH>
+__device__ __forceinline__ void pair_emit(const AggArgs& a, uint64_t it, uint64_t r, bool partial, int half, int v0,
+                                          float m, float den, const unsigned long long (&acc)[NVH * 4]) {
+    constexpr int NF = NVH * 8;
+    const int c0 = v0 * 8;
+    if (partial) {
+        float* st = a.seg_state + it * kSegStateFloats;
+        if (half == 0) {
             st[0] = m;
             st[8] = den;
-#pragma unroll
-            for (int k = 0; k < NF / 2; ++k) {
-                const float2 f = upk(acc[k]);
-                if (2 * k < a.width) st[16 + 2 * k] = f.x;
-                if (2 * k + 1 < a.width) st[16 + 2 * k + 1] = f.y;
-            }
-            continue;
         }
-        const float inv = den > 0.f ? 1.f / den : 0.f;
-        float o[NF];
 #pragma unroll
         for (int k = 0; k < NF / 2; ++k) {
             const float2 f = upk(acc[k]);
-            o[2 * k] = f.x;
-            o[2 * k + 1] = f.y;
+            if (c0 + 2 * k < a.width) st[16 + c0 + 2 * k] = f.x;
+            if (c0 + 2 * k + 1 < a.width) st[16 + c0 + 2 * k + 1] = f.y;
         }
+        return;
+    }
+    const float inv = den > 0.f ? 1.f / den : 0.f;
 #pragma unroll
-        for (int c = 0; c < NF; ++c) {
-            if (c >= a.ldo) break;
-            float v = c < a.width ? o[c] * inv : 0.f;
+    for (int k = 0; k < NF / 2; ++k) {
+        const float2 f = upk(acc[k]);
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+            const int c = c0 + 2 * k + t;
+            if (c >= a.ldo) continue;
+            float v = c < a.width ? (t ? f.y : f.x) * inv : 0.f;
             if (a.hidden && v < 0.f) v = __expf(v) - 1.f;  // the B0 activation (gat.hpp:57-62)
             if (a.out_bf16)
                 static_cast<uint16_t*>(a.out)[r * a.ldo + c] = uint16_t(pack_bf16x2(v, 0.f) & 0xffffu);
             else
                 static_cast<float*>(a.out)[r * a.ldo + c] = v;
         }
-        for (int c = NF; c < a.ldo; ++c) {  // padding columns past the vectors
+    }
+    if (half == 1)  // padding columns past both lanes' vectors
+        for (int c = 2 * NF; c < a.ldo; ++c) {
             if (a.out_bf16)
                 static_cast<uint16_t*>(a.out)[r * a.ldo + c] = 0;
             else
                 static_cast<float*>(a.out)[r * a.ldo + c] = 0.f;
         }
+}
+
+template <int NVH>
+__global__ void __launch_bounds__(128) agg_pair_kernel(const AggArgs a) {
+    const int lane = threadIdx.x & 31, half = lane & 1, pair = lane >> 1;
+    const uint64_t total = uint64_t(a.n_seg) + (a.n - a.n_hub);
+    const uint64_t n_big = uint64_t(a.n_seg) + a.n_wide;
+    const uint64_t units = n_big + (total - n_big + 15) / 16;
+    const uint64_t G = uint64_t(gridDim.x) * (blockDim.x >> 5);
+    const int nvec = (a.width + 7) / 8;
+    const int v0 = half * NVH;  // first vector of this lane
+    const char* hb = static_cast<const char*>(a.h) + v0 * 16;
+    const uint64_t rowb = uint64_t(a.ldh) * 2;
+    for (uint64_t u = blockIdx.x * uint64_t(blockDim.x >> 5) + (threadIdx.x >> 5); u < units; u += G) {
+        unsigned long long acc[NVH * 4];
+#pragma unroll
+        for (int k = 0; k < NVH * 4; ++k) acc[k] = 0ull;
+        float m = -INFINITY, den = 0.f;
+        uint64_t r, beg, end;
+        bool partial;
+        if (u < n_big) {
+            // a wide item: pair q takes blocks q, q+16, ... of its edges
+            pair_item(a, u, r, beg, end, partial);
+            const float L = a.left[r];
+            pair_walk<NVH>(a, hb, rowb, nvec, v0, L, beg + 4 * uint64_t(pair), end, 64, m, den, acc);
+#pragma unroll
+            for (int o = 2; o < 32; o <<= 1) {  // combine the 16 pairs' states (same half)
+                const float mo = __shfl_xor_sync(kFull, m, o);
+                const float dn = __shfl_xor_sync(kFull, den, o);
+                const float M = fmaxf(m, mo);
+                const float fa = m == -INFINITY ? 0.f : __expf(m - M);
+                const float fb = mo == -INFINITY ? 0.f : __expf(mo - M);
+                den = den * fa + dn * fb;
+                const unsigned long long pa = pk(fa, fa), pb = pk(fb, fb);
+#pragma unroll
+                for (int k = 0; k < NVH * 4; ++k) {
+                    const float2 x = upk(acc[k]);
+                    const unsigned long long other =
+                        pk(__shfl_xor_sync(kFull, x.x, o), __shfl_xor_sync(kFull, x.y, o));
+                    acc[k] = ffma2(other, pb, fmul2(acc[k], pa));
+                }
+                m = M;
+            }
+            if (pair == 0) pair_emit<NVH>(a, u, r, partial, half, v0, m, den, acc);
+        } else {
+            const uint64_t it = n_big + (u - n_big) * 16 + pair;
+            if (it >= total) continue;
+            pair_item(a, it, r, beg, end, partial);
+            const float L = a.left[r];
+            pair_walk<NVH>(a, hb, rowb, nvec, v0, L, beg, end, 4, m, den, acc);
+            pair_emit<NVH>(a, it, r, partial, half, v0, m, den, acc);
+        }
     }
 }
 
-// Narrow single-head layers run on the warp kernel; the lane-per-item kernel
-// when the environment variable GAT_B200_NARROW_AGG is "lane". Both compute
-// the whole layer. Measured on c4 layer 3 (one B200): warp kernel 3.9 ms,
-// lane kernel 8.2 ms -- the lane kernel issues 6.6 warp instructions per edge
-// against 23, but its per-lane chains of dependent loads (source id, then
-// score and row) leave it latency-bound at 14 % issue activity.
-bool narrow_on_lanes() {
-    static const bool lanes = [] {
-        const char* v = std::getenv("GAT_B200_NARROW_AGG");
-        return v && std::strcmp(v, "lane") == 0;
-    }();
-    return lanes;
-}
-
-template <int NV>
-int launch_agg_lane(const AggArgs& a, cudaStream_t st, int reserve_sms) {
+template <int NVH>
+int launch_agg_pair(const AggArgs& a, cudaStream_t st, int reserve_sms) {
     int dev = 0, sms = 0;
     GATB_CUDA(cudaGetDevice(&dev));
     GATB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     static int per_sm = 0;
     if (!per_sm) {
-        GATB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, agg_lane_kernel<NV>, 128, 0));
+        GATB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, agg_pair_kernel<NVH>, 128, 0));
         if (per_sm < 1) per_sm = 1;
     }
     const int usable = reserve_sms > 0 && reserve_sms < sms ? sms - reserve_sms : sms;
     const uint64_t items = uint64_t(a.n_seg) + (a.n - a.n_hub);
-    const uint64_t need = (items + 127) / 128;
+    const uint64_t n_big = uint64_t(a.n_seg) + a.n_wide;
+    const uint64_t need = (n_big + (items - n_big + 15) / 16 + 3) / 4;  // 4 warps per block
     const uint64_t cap = uint64_t(usable) * per_sm;
     const unsigned blocks = unsigned(std::max<uint64_t>(1, std::min(need, cap)));
-    agg_lane_kernel<NV><<<blocks, 128, 0, st>>>(a);
-    GATB_LAUNCH("edge-softmax aggregation kernel (lane per row)");
+    agg_pair_kernel<NVH><<<blocks, 128, 0, st>>>(a);
+    GATB_LAUNCH("edge-softmax aggregation kernel (lane pair per row)");
     if (a.n_hub) {
         hub_merge_kernel<<<(a.n_hub + kWarps - 1) / kWarps, kWarps * 32, 0, st>>>(a);
         GATB_LAUNCH("hub merge kernel");
     }
     return 0;
+}
+
+// Narrow single-head layers run on the lane-pair kernel unless the
+// environment variable GAT_B200_NARROW_AGG is "warp" (the warp kernel, kept
+// for comparison; both compute the whole layer).
+bool narrow_on_pairs() {
+    static const bool pairs = [] {
+        const char* v = std::getenv("GAT_B200_NARROW_AGG");
+        return !(v && std::strcmp(v, "warp") == 0);
+    }();
+    return pairs;
 }
 
 // reserve_sms = 0: blocks of up to 4 warps, as many resident blocks as fit
@@ -890,6 +952,7 @@ int aggregate_dispatch_reserved(const gat_b200_graph* g, int heads, int dim, con
     a.n = g->n;
     a.n_hub = g->n_hub;
     a.n_seg = g->n_seg;
+    a.n_wide = g->n_wide;
     a.segs = g->segs;
     a.hub_seg_offset = g->hub_seg_offset;
     a.seg_state = g->seg_state;
@@ -918,14 +981,14 @@ int aggregate_dispatch_reserved(const gat_b200_graph* g, int heads, int dim, con
             (reinterpret_cast<uintptr_t>(right) & 15) == 0)
             return launch_agg<uint16_t, 8, 16, 32, 1, false, 32>(a, st, reserve_sms);
         if (heads == 1 && width <= 64) {
-            // the lane-per-item kernel serves the fused epilogue (no fixed
+            // the lane-pair kernel serves the fused epilogue (no fixed
             // weights, no unnormalised outputs); the warp kernel the rest
-            if (!fixed_p && !unnorm && narrow_on_lanes()) {
-                const int nv = (width + 7) / 8;
-                if (nv <= 2) return launch_agg_lane<2>(a, st, reserve_sms);
-                if (nv <= 4) return launch_agg_lane<4>(a, st, reserve_sms);
-                if (nv <= 6) return launch_agg_lane<6>(a, st, reserve_sms);
-                return launch_agg_lane<8>(a, st, reserve_sms);
+            if (!fixed_p && !unnorm && narrow_on_pairs()) {
+                const int nvh = ((width + 7) / 8 + 1) / 2;
+                if (nvh <= 1) return launch_agg_pair<1>(a, st, reserve_sms);
+                if (nvh <= 2) return launch_agg_pair<2>(a, st, reserve_sms);
+                if (nvh <= 3) return launch_agg_pair<3>(a, st, reserve_sms);
+                return launch_agg_pair<4>(a, st, reserve_sms);
             }
             return launch_agg<uint16_t, 1, 32, 8, 1, false, 0>(a, st, reserve_sms);
         }

@@ -129,6 +129,32 @@ inline void mark(gat_b200_model* m, int stage, cudaStream_t st) {
 
 using namespace gatb;
 
+namespace gatb {
+// gat_b200_graph_create_part with the segment length of a graph of basis_e
+// edges (0: e). The partitioned model passes the whole graph's edge count.
+int graph_create_part_basis(uint64_t n, uint64_t n_src, uint64_t e, const uint64_t* row, const uint32_t* col,
+                            void* stream, uint64_t basis_e, gat_b200_graph** out) {
+    if (!out) return fail("graph_create_part: null output handle");
+    *out = nullptr;
+    if (!n || n > uint64_t(INT32_MAX) || !n_src || n_src > uint64_t(UINT32_MAX)) return fail("invalid graph sizes");
+    if (!row || (e && !col)) return fail("invalid graph sizes");
+    gat_b200_graph* g = new (std::nothrow) gat_b200_graph();
+    if (!g) return fail("graph_create_part: out of host memory");
+    g->n = n;
+    g->e = e;
+    g->n_src = n_src;
+    g->seg_basis_e = basis_e;
+    int rc = graph_build(g, row, col, as_stream(stream));
+    if (rc) {
+        graph_release(g);
+        delete g;
+        return rc;
+    }
+    *out = g;
+    return 0;
+}
+}  // namespace gatb
+
 extern "C" {
 
 int gat_b200_graph_create(uint64_t n, uint64_t e, const uint64_t* row, const uint32_t* col, void* stream,
@@ -152,26 +178,11 @@ int gat_b200_graph_create(uint64_t n, uint64_t e, const uint64_t* row, const uin
     return 0;
 }
 
+
 int gat_b200_graph_create_part(uint64_t n, uint64_t n_src, uint64_t e, const uint64_t* row, const uint32_t* col,
                                void* stream, gat_b200_graph** out) {
     clear_error();
-    if (!out) return fail("graph_create_part: null output handle");
-    *out = nullptr;
-    if (!n || n > uint64_t(INT32_MAX) || !n_src || n_src > uint64_t(UINT32_MAX)) return fail("invalid graph sizes");
-    if (!row || (e && !col)) return fail("invalid graph sizes");
-    gat_b200_graph* g = new (std::nothrow) gat_b200_graph();
-    if (!g) return fail("graph_create_part: out of host memory");
-    g->n = n;
-    g->e = e;
-    g->n_src = n_src;
-    int rc = graph_build(g, row, col, as_stream(stream));
-    if (rc) {
-        graph_release(g);
-        delete g;
-        return rc;
-    }
-    *out = g;
-    return 0;
+    return graph_create_part_basis(n, n_src, e, row, col, stream, 0, out);
 }
 
 int gat_b200_graph_destroy(gat_b200_graph* g) {

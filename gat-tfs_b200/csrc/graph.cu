@@ -66,26 +66,31 @@ __global__ void validate_cols(const uint32_t* __restrict__ col, uint64_t e, uint
 __global__ void schedule_stats(const uint32_t* __restrict__ sorted_deg, uint64_t n, uint32_t seg_edges,
                                unsigned long long* __restrict__ steps,
                                unsigned long long* __restrict__ n_hub,
-                               unsigned long long* __restrict__ n_seg) {
+                               unsigned long long* __restrict__ n_seg,
+                               unsigned long long* __restrict__ n_wide) {
     uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
-    unsigned long long s = 0, h = 0, g = 0;
+    unsigned long long s = 0, h = 0, g = 0, w = 0;
     for (uint64_t t = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; t < n; t += stride) {
         uint32_t d = sorted_deg[t];
         if (t % 16 == 15 || t == n - 1) s += d;  // last row of each 16-row tile
         if (d > seg_edges) {
             ++h;
             g += (d + seg_edges - 1) / seg_edges;
+        } else if (d > kWideRowEdges) {
+            ++w;
         }
     }
     for (int o = 16; o > 0; o >>= 1) {
         s += __shfl_xor_sync(0xffffffffu, s, o);
         h += __shfl_xor_sync(0xffffffffu, h, o);
         g += __shfl_xor_sync(0xffffffffu, g, o);
+        w += __shfl_xor_sync(0xffffffffu, w, o);
     }
     if ((threadIdx.x & 31) == 0) {
         atomicAdd(steps, s);
         atomicAdd(n_hub, h);
         atomicAdd(n_seg, g);
+        atomicAdd(n_wide, w);
     }
 }
 
@@ -138,9 +143,9 @@ int graph_build(gat_b200_graph* g, const uint64_t* row_h, const uint32_t* col_h,
         if ((rc = dalloc((void**)&ids, n * sizeof(uint32_t), "cudaMalloc ids"))) break;
         if ((rc = dalloc((void**)&sorted_deg, n * sizeof(uint32_t), "cudaMalloc sorted"))) break;
         if ((rc = dalloc((void**)&flags, sizeof(unsigned), "cudaMalloc flags"))) break;
-        if ((rc = dalloc((void**)&stats, 3 * sizeof(unsigned long long), "cudaMalloc stats"))) break;
+        if ((rc = dalloc((void**)&stats, 4 * sizeof(unsigned long long), "cudaMalloc stats"))) break;
         cudaMemsetAsync(flags, 0, sizeof(unsigned), st);
-        cudaMemsetAsync(stats, 0, 3 * sizeof(unsigned long long), st);
+        cudaMemsetAsync(stats, 0, 4 * sizeof(unsigned long long), st);
         validate_rows<<<unsigned((n + 255) / 256), 256, 0, st>>>(g->row, n, e, deg, ids, flags);
         if (e) validate_cols<<<1184, 256, 0, st>>>(g->col, e, g->n_src ? g->n_src : n, flags);
         unsigned hflags = 0;
@@ -158,7 +163,7 @@ int graph_build(gat_b200_graph* g, const uint64_t* row_h, const uint32_t* col_h,
         {
             int sms = 148;
             cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, g->device);
-            uint64_t per = e / (uint64_t(sms) * 24 * 8);
+            uint64_t per = (g->seg_basis_e ? g->seg_basis_e : e) / (uint64_t(sms) * 24 * 8);
             uint32_t seg = 128;
             while (seg < 8192 && uint64_t(seg) * 2 <= per) seg *= 2;
             g->seg_edges = seg;
@@ -171,8 +176,8 @@ int graph_build(gat_b200_graph* g, const uint64_t* row_h, const uint32_t* col_h,
         if ((rc = dalloc((void**)&temp, temp_bytes, "cudaMalloc sort temp"))) break;
         ce = cub::DeviceRadixSort::SortPairs(temp, temp_bytes, deg, sorted_deg, ids, g->perm, int(n), 0, end_bit, st);
         if (ce != cudaSuccess) { rc = cuda_fail(ce, "degree sort"); break; }
-        schedule_stats<<<592, 256, 0, st>>>(sorted_deg, n, g->seg_edges, stats, stats + 1, stats + 2);
-        unsigned long long hs[3];
+        schedule_stats<<<592, 256, 0, st>>>(sorted_deg, n, g->seg_edges, stats, stats + 1, stats + 2, stats + 3);
+        unsigned long long hs[4];
         cudaMemcpyAsync(hs, stats, sizeof(hs), cudaMemcpyDeviceToHost, st);
         cudaMemcpyAsync(&g->max_degree, sorted_deg + (n - 1), sizeof(uint32_t), cudaMemcpyDeviceToHost, st);
         ce = cudaStreamSynchronize(st);
@@ -180,6 +185,7 @@ int graph_build(gat_b200_graph* g, const uint64_t* row_h, const uint32_t* col_h,
         g->neighbor_steps = hs[0];
         g->n_hub = uint32_t(hs[1]);
         g->n_seg = uint32_t(hs[2]);
+        g->n_wide = uint32_t(hs[3]);
         if (g->n_hub) {
             // Segment offsets: exclusive prefix over the hub rows (host side; few rows).
             std::vector<uint32_t> hub_deg(g->n_hub), off(g->n_hub + 1);

@@ -29,7 +29,15 @@ struct gat_b200_graph {
     // Rows with degree > seg_edges are hubs; they are perm[n-1-k], k < n_hub,
     // cut into n_seg segments (segs, ordered by hub then edge position).
     uint32_t seg_edges = 256;
+    // Edge count the segment length is derived from (0: this graph's e). The
+    // slices of a partitioned graph take the whole graph's, so their hub rows
+    // are cut where the one-GPU graph cuts them and the sums run in the same
+    // order on any number of GPUs.
+    uint64_t seg_basis_e = 0;
     uint32_t n_hub = 0, n_seg = 0;
+    // Rows with more than kWideRowEdges edges that are not hubs: in the degree
+    // order they follow the hubs, perm[n-1-n_hub-k] for k < n_wide.
+    uint32_t n_wide = 0;
     gatb::Segment* segs = nullptr;       // device [n_seg]
     uint32_t* hub_seg_offset = nullptr;  // device [n_hub+1]
     // Device scratch for the segments' partial softmax states: kSegStateFloats
@@ -52,4 +60,6 @@ namespace gatb {
 int graph_build(gat_b200_graph* g, const uint64_t* row_h, const uint32_t* col_h, cudaStream_t st);
 void graph_release(gat_b200_graph* g);
 constexpr int kSegStateFloats = 8 * 64 + 2 * 8;
+// Rows above this many edges get a whole warp in the narrow-layer kernel.
+constexpr uint32_t kWideRowEdges = 64;
 }  // namespace gatb

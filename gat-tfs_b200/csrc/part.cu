@@ -53,6 +53,8 @@ int projection_tc_launch(const gat_b200_layer* p, uint64_t n, const uint16_t* x,
                          float* z, int ldz, float* left, float* right, cudaStream_t st, int npeer,
                          uint16_t* const* h_peer, float* const* r_peer, int max_ctas);
 int peer_barrier_launch(void* const* flags, int world, int rank, uint32_t epoch, cudaStream_t st);
+int graph_create_part_basis(uint64_t n, uint64_t n_src, uint64_t e, const uint64_t* row, const uint32_t* col,
+                            void* stream, uint64_t basis_e, gat_b200_graph** out);
 int device_check_errors();
 
 namespace {
@@ -344,7 +346,11 @@ int gat_b200_part_model_create(gat_b200_comm* comm, uint64_t n, const uint64_t* 
                 cl[k] = layout_slot(L, s);
             }
             if (rc) break;
-            if ((rc = gat_b200_graph_create_part(B - A, nt, cl.size(), rl.data(), cl.data(), stream, &ch.g))) break;
+            // hub rows cut where the one-GPU graph cuts them (segment length
+            // from the whole graph's edge count): the same sums, in the same
+            // order, on any number of GPUs
+            if ((rc = graph_create_part_basis(B - A, nt, cl.size(), rl.data(), cl.data(), stream, row[n], &ch.g)))
+                break;
         }
         if (rc) break;
         const int K0 = m->heads[0];
