@@ -86,6 +86,9 @@ def parse():
                     help="standard: B0 on every layer; adaptive: layer 1 through TFS aggregation (tensor cores)")
     ap.add_argument("--chunks", type=int, default=1,
                     help="N>1: row chunks per rank, each projected and exchanged as soon as it is aggregated")
+    ap.add_argument("--reserve-sms", type=int, default=None,
+                    help="N>1, chunks>1: SMs left to each chunk's projection and exchange while the next chunk "
+                         "aggregates (default 16; 0 = no overlap)")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="N>1: p2p = the conversion / projection kernels store every rank's rows into every "
                          "rank's table over NVLink; nccl = NCCL all-gather of H and R per layer")
@@ -658,6 +661,8 @@ def main():
         part_layers = [G.DeviceLayer(p) for p in part.model]
         exch = G.EXCHANGE_P2P if args.exchange == "p2p" else G.EXCHANGE_NCCL
         pm = G.PartModel(comm, part.row, part.col_rows, part_layers, exch, args.chunks, stream)
+        if args.reserve_sms is not None:
+            pm.set_overlap(args.reserve_sms)
         log("device model ready")
         n_loc, e_loc = pm.n_loc, pm.e_loc
         classes = pm.classes
@@ -686,6 +691,9 @@ def main():
                    "closes each exchange")
         else:
             how = "NCCL all-gather of each layer's H and R"
+        if args.chunks > 1 and args.exchange == "p2p" and args.reserve_sms != 0:
+            how += (f"; chunk c's projection and exchange overlap chunk c+1's aggregation on "
+                    f"{16 if args.reserve_sms is None else args.reserve_sms} reserved SMs")
         parallelism = (f"rows{world}: destination rows split by edge count, {args.chunks} row chunk(s) per "
                        f"rank; {how}")
 
@@ -737,7 +745,7 @@ def main():
     e2e_sync_ms = timed(e2e_step, max(1, min(args.steps, 5)))
     # Throughput: a stream of requests through gat_b200_model_forward_async, where request
     # k's download and request k+1's upload overlap compute (one GPU only).
-    k_pipe = max(2, min(args.steps, 10))
+    k_pipe = max(2, min(args.steps, 20))
     if world == 1:
         submit = lambda i: model.forward_async(x_host, l_host[i & 1], stream)
         join = lambda: model.join(stream)

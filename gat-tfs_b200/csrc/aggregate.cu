@@ -837,15 +837,21 @@ int launch_agg_pair(const AggArgs& a, cudaStream_t st, int reserve_sms) {
     return 0;
 }
 
-// Narrow single-head layers run on the lane-pair kernel unless the
-// environment variable GAT_B200_NARROW_AGG is "warp" (the warp kernel, kept
-// for comparison; both compute the whole layer).
+// Narrow single-head layers (heads == 1, width <= 64, BF16) run on the warp
+// kernel (eight lanes per gathered row, one 16-byte vector each);
+// GAT_B200_NARROW_AGG=pair selects the lane-pair kernel above instead (both
+// compute the whole layer). Measured on c4 layer 3 (1 x 47, one B200): warp
+// kernel 3.76-4.06 ms, lane pair 4.02-4.21 ms. Two other layouts were
+// measured and dropped: one lane per row (8.2 ms: each lane's chain of
+// dependent loads -- source id, then score and row -- leaves it
+// latency-bound at 14 % issue activity) and the warp kernel with two lanes
+// per row and three vectors each (7.6 ms: 166 registers, 12 warps per SM).
 bool narrow_on_pairs() {
-    static const bool pairs = [] {
-        const char* v = std::getenv("GAT_B200_NARROW_AGG");
-        return !(v && std::strcmp(v, "warp") == 0);
+    static const bool v = [] {
+        const char* e = std::getenv("GAT_B200_NARROW_AGG");
+        return e && std::strcmp(e, "pair") == 0;
     }();
-    return pairs;
+    return v;
 }
 
 // reserve_sms = 0: blocks of up to 4 warps, as many resident blocks as fit
@@ -981,10 +987,10 @@ int aggregate_dispatch_reserved(const gat_b200_graph* g, int heads, int dim, con
             (reinterpret_cast<uintptr_t>(right) & 15) == 0)
             return launch_agg<uint16_t, 8, 16, 32, 1, false, 32>(a, st, reserve_sms);
         if (heads == 1 && width <= 64) {
-            // the lane-pair kernel serves the fused epilogue (no fixed
-            // weights, no unnormalised outputs); the warp kernel the rest
-            if (!fixed_p && !unnorm && narrow_on_pairs()) {
-                const int nvh = ((width + 7) / 8 + 1) / 2;
+            const int nv = (width + 7) / 8;
+            if (narrow_on_pairs() && !fixed_p && !unnorm) {
+                // the lane-pair kernel serves the fused epilogue only
+                const int nvh = (nv + 1) / 2;
                 if (nvh <= 1) return launch_agg_pair<1>(a, st, reserve_sms);
                 if (nvh <= 2) return launch_agg_pair<2>(a, st, reserve_sms);
                 if (nvh <= 3) return launch_agg_pair<3>(a, st, reserve_sms);
