@@ -27,10 +27,15 @@
 #include <cstdlib>
 #include <cstring>
 
+#include <cuda.h>
+
 #include "device.cuh"
 #include "graph.cuh"
+#include "tc.cuh"
 
 namespace gatb {
+int make_row_gather_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint64_t ld,
+                        uint32_t box_cols);
 namespace {
 
 constexpr int kWarps = 8;  // warps per block
@@ -41,6 +46,7 @@ struct AggArgs {
     const uint32_t* col;
     const uint32_t* perm;
     uint64_t n;
+    uint64_t n_src;          // rows of the feature table the source ids index
     uint32_t n_hub, n_seg;
     uint32_t n_wide;         // rows after the hubs with more than kWideRowEdges edges
     const Segment* segs;
@@ -278,8 +284,42 @@ struct Gen {
 //   3. prefetch R of chunk k+1 and col of chunk k+2;
 //   4. consume chunk k-1 (waiting only for this lane's own copies: a lane
 //      consumes exactly the vectors it copied).
-template <class HT, int KT, int C, int LPE, int VPL, bool MIXED, int NVC, int MAXT>
-__global__ void __launch_bounds__(MAXT) agg_kernel(const AggArgs a) {
+// Shared memory of one warp: the two chunk slots, the two row buffers and,
+// with TG, the buffers' two mbarriers (128-byte aligned regions).
+template <int C, int KM, int RV, bool TG>
+__host__ __device__ constexpr size_t agg_slot_bytes() {
+    return TG ? (2 * sizeof(Slot<C, KM>) + 127) / 128 * 128 : 2 * sizeof(Slot<C, KM>);
+}
+template <int C, int KM, int RV, bool TG>
+__host__ __device__ constexpr size_t agg_warp_bytes() {
+    return TG ? (agg_slot_bytes<C, KM, RV, TG>() + size_t(2) * C * RV * 16 + 16 + 127) / 128 * 128
+              : agg_slot_bytes<C, KM, RV, TG>() + size_t(2) * C * RV * 16;
+}
+
+// Bounded wait on a row buffer's mbarrier (TG): false after ~1 s, with the
+// error flag raised.
+__device__ __forceinline__ bool agg_wait(uint64_t* bar, uint32_t parity) {
+    if (tc::mbar_try(bar, parity)) return true;
+    const long long t0 = clock64();
+    for (uint32_t it = 0;; ++it) {
+        if (tc::mbar_try(bar, parity)) return true;
+        if ((it & 63) == 63) {
+            __nanosleep(32);
+            if (clock64() - t0 > (1ll << 31)) {
+                atomicOr(&g_agg_error, 1u);
+                return false;
+            }
+        }
+    }
+}
+
+// TG (hidden layers, 8 heads x 32, BF16 rows of 512 bytes): each chunk's 16
+// rows are fetched by the tensor memory accelerator instead of per-lane
+// cp.async -- lanes 0..3 each issue one tile::gather4 of four rows (source
+// ids past the chunk's end point outside the table and read as zeros), the
+// buffer's mbarrier counts the bytes, and the consumer waits on it (bounded).
+template <class HT, int KT, int C, int LPE, int VPL, bool MIXED, int NVC, int MAXT, bool TG>
+__global__ void __launch_bounds__(MAXT) agg_kernel(const AggArgs a, const __grid_constant__ CUtensorMap tmh) {
     using V = Vec<HT>;
     constexpr int VEC = V::N;
     constexpr int KM = KT ? KT : 8;
@@ -294,13 +334,26 @@ __global__ void __launch_bounds__(MAXT) agg_kernel(const AggArgs a) {
     static_assert(HS == 1 || LPE == 32, "8 head slots need whole-warp rows");
     using SlotT = Slot<C, KM>;
 
-    extern __shared__ __align__(16) uint8_t agg_smem[];
+    static_assert(!TG || (sizeof(HT) == 2 && KT == 8 && C == 16 && LPE == 32 && VPL == 1 && NVC == 32),
+                  "the row gather serves the 8 x 32 BF16 layout");
+    extern __shared__ __align__(128) uint8_t agg_smem[];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-    constexpr size_t kWarpBytes = 2 * sizeof(SlotT) + size_t(2) * C * RV * 16;
+    constexpr size_t kSlotBytes = agg_slot_bytes<C, KM, RV, TG>();
+    constexpr size_t kWarpBytes = agg_warp_bytes<C, KM, RV, TG>();
     uint8_t* wbase = agg_smem + wib * kWarpBytes;
     SlotT* slots = reinterpret_cast<SlotT*>(wbase);
-    const uint4* bufs = reinterpret_cast<const uint4*>(wbase + 2 * sizeof(SlotT));
+    const uint4* bufs = reinterpret_cast<const uint4*>(wbase + kSlotBytes);
     const uint32_t bufs_s = static_cast<uint32_t>(__cvta_generic_to_shared(bufs));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(wbase + kSlotBytes + size_t(2) * C * RV * 16);
+    uint32_t par = 0;  // TG: phase parity of the two buffers' barriers
+    if constexpr (TG) {
+        if (lane == 0) {
+            tc::mbar_init(bars, 1);
+            tc::mbar_init(bars + 1, 1);
+            tc::fence_mbarrier_init();
+        }
+        __syncwarp();
+    }
 
     const int K = KT ? KT : a.heads;
     const int eo = lane / HS, hh = lane % HS;    // scoring role
@@ -539,37 +592,68 @@ __global__ void __launch_bounds__(MAXT) agg_kernel(const AggArgs a) {
         // zero-filled without reading memory) ----
         // Groups of 4 steps, as in consume: slots up to the end of the last
         // group holding an edge are written, later groups are skipped.
-        const uint32_t bs = bufs_s + uint32_t(sl) * C * RV * 16 + uint32_t(vl) * 16;
+        if constexpr (TG) {
+            // edge g*4+j of the chunk is held by lane j*HS in colS[g]; lane q
+            // gathers edges 4q..4q+3
+            const uint32_t oob = uint32_t(a.n_src);
+            uint32_t y[4] = {oob, oob, oob, oob};
 #pragma unroll
-        for (int i0 = 0; i0 < NT; i0 += 4) {
-            if (i0 * EPS >= S.cnt) break;
+            for (int g = 0; g < NG; ++g)
 #pragma unroll
-            for (int u = 0; u < 4 && i0 + u < NT; ++u) {
-                const int i = i0 + u;
-                const int tt = es + i * EPS;
-                const int g = (i * EPS) / EG;  // static: EPS == 1 or NG == 1
-                const uint32_t c = __shfl_sync(kFull, colS[g], (tt % EG) * HS);
-                const uint32_t nb = tt < S.cnt ? 16u : 0u;
-                const char* src = hbase + uint64_t(c) * row_bytes;
+                for (int j = 0; j < EG; ++j) {
+                    const uint32_t v = __shfl_sync(kFull, colS[g], j * HS);
+                    if (g == lane && g * EG + j < S.cnt) y[j] = v;
+                }
+            const int ngrp = (S.cnt + 3) >> 2;
+            if (lane == 0) tc::mbar_expect_tx(bars + sl, uint32_t(ngrp) * 4u * RV * 16u);
+            __syncwarp();
+            if (lane < ngrp) {
+                tc::fence_proxy_async_smem();
+                tc::tma_gather4(const_cast<uint4*>(bufs) + (size_t(sl) * C + size_t(lane) * 4) * RV, &tmh, bars + sl,
+                                0, int(y[0]), int(y[1]), int(y[2]), int(y[3]));
+            }
+        } else {
+            const uint32_t bs = bufs_s + uint32_t(sl) * C * RV * 16 + uint32_t(vl) * 16;
 #pragma unroll
-                for (int j = 0; j < VPL; ++j) {
-                    const int v = vl + j * LPE;
-                    if (NVC != 0 || v < nvec)
-                        cp_async16(bs + uint32_t(tt * RV + j * LPE) * 16, src + j * LPE * 16, nb);
+            for (int i0 = 0; i0 < NT; i0 += 4) {
+                if (i0 * EPS >= S.cnt) break;
+#pragma unroll
+                for (int u = 0; u < 4 && i0 + u < NT; ++u) {
+                    const int i = i0 + u;
+                    const int tt = es + i * EPS;
+                    const int g = (i * EPS) / EG;  // static: EPS == 1 or NG == 1
+                    const uint32_t c = __shfl_sync(kFull, colS[g], (tt % EG) * HS);
+                    const uint32_t nb = tt < S.cnt ? 16u : 0u;
+                    const char* src = hbase + uint64_t(c) * row_bytes;
+#pragma unroll
+                    for (int j = 0; j < VPL; ++j) {
+                        const int v = vl + j * LPE;
+                        if (NVC != 0 || v < nvec)
+                            cp_async16(bs + uint32_t(tt * RV + j * LPE) * 16, src + j * LPE * 16, nb);
+                    }
                 }
             }
+            cp_commit();
         }
-        cp_commit();
         __syncwarp();
         // ---- 4. consume chunk k-1 ----
         if (prev >= 0) {
-            cp_wait<1>();
+            if constexpr (TG) {
+                if (!agg_wait(bars + prev, (par >> prev) & 1u)) return;
+                par ^= 1u << prev;
+            } else {
+                cp_wait<1>();
+            }
             consume(prev);
         }
         prev = sl;
     }
     if (prev >= 0) {
-        cp_wait<0>();
+        if constexpr (TG) {
+            if (!agg_wait(bars + prev, (par >> prev) & 1u)) return;
+        } else {
+            cp_wait<0>();
+        }
         consume(prev);
     }
 }
@@ -846,6 +930,17 @@ int launch_agg_pair(const AggArgs& a, cudaStream_t st, int reserve_sms) {
 // dependent loads -- source id, then score and row -- leaves it
 // latency-bound at 14 % issue activity) and the warp kernel with two lanes
 // per row and three vectors each (7.6 ms: 166 registers, 12 warps per SM).
+// Hidden layers (8 x 32 BF16) fetch their rows with per-lane cp.async; with
+// GAT_B200_HIDDEN_AGG=gather4 the tensor memory accelerator's row gather
+// (tile::gather4) does it. Both compute the whole layer.
+bool hidden_row_gather() {
+    static const bool v = [] {
+        const char* e = std::getenv("GAT_B200_HIDDEN_AGG");
+        return e && std::strcmp(e, "gather4") == 0;
+    }();
+    return v;
+}
+
 bool narrow_on_pairs() {
     static const bool v = [] {
         const char* e = std::getenv("GAT_B200_NARROW_AGG");
@@ -860,10 +955,16 @@ bool narrow_on_pairs() {
 // with as many warps as fit in its shared memory (so no other kernel's CTA
 // can share the SM), on all but reserve_sms SMs, which stay free for the
 // other kernel.
-template <class HT, int KT, int C, int LPE, int VPL, bool MIXED, int NVC>
+template <class HT, int KT, int C, int LPE, int VPL, bool MIXED, int NVC, bool TG = false>
 int launch_agg(const AggArgs& a, cudaStream_t st, int reserve_sms) {
     constexpr int KM = KT ? KT : 8;
-    constexpr size_t warp_bytes = 2 * sizeof(Slot<C, KM>) + size_t(2) * C * LPE * VPL * 16;
+    constexpr size_t warp_bytes = agg_warp_bytes<C, KM, LPE * VPL, TG>();
+    CUtensorMap tmh;
+    std::memset(&tmh, 0, sizeof(tmh));
+    if constexpr (TG) {
+        int rc = make_row_gather_map(&tmh, a.h, uint64_t(a.ldh), a.n_src, uint64_t(a.ldh), 256);
+        if (rc) return rc;
+    }
     // Up to 4 warps per block within 200 KB of shared memory.
     constexpr int wpb = warp_bytes * 4 <= 200 * 1024 ? 4 : (warp_bytes * 2 <= 200 * 1024 ? 2 : 1);
     constexpr int wbig_fit = int((220 * 1024) / warp_bytes);
@@ -875,7 +976,7 @@ int launch_agg(const AggArgs& a, cudaStream_t st, int reserve_sms) {
     GATB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     if (reserve_sms > 0 && reserve_sms < sms) {
         constexpr size_t smem = warp_bytes * wbig;
-        auto kern = agg_kernel<HT, KT, C, LPE, VPL, MIXED, NVC, wbig * 32>;
+        auto kern = agg_kernel<HT, KT, C, LPE, VPL, MIXED, NVC, wbig * 32, TG>;
         static bool attr = false;
         if (!attr) {
             GATB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
@@ -884,11 +985,11 @@ int launch_agg(const AggArgs& a, cudaStream_t st, int reserve_sms) {
         uint64_t need = (items + wbig - 1) / wbig;
         unsigned blocks = unsigned(need < uint64_t(sms - reserve_sms) ? need : uint64_t(sms - reserve_sms));
         if (blocks == 0) blocks = 1;
-        kern<<<blocks, wbig * 32, smem, st>>>(a);
+        kern<<<blocks, wbig * 32, smem, st>>>(a, tmh);
         GATB_LAUNCH("edge-softmax aggregation kernel");
     } else {
         constexpr size_t smem = warp_bytes * wpb;
-        auto kern = agg_kernel<HT, KT, C, LPE, VPL, MIXED, NVC, 128>;
+        auto kern = agg_kernel<HT, KT, C, LPE, VPL, MIXED, NVC, 128, TG>;
         static int grid = 0;  // resident blocks (per process; all B200s are alike)
         if (!grid) {
             int per_sm = 0;
@@ -899,7 +1000,7 @@ int launch_agg(const AggArgs& a, cudaStream_t st, int reserve_sms) {
         uint64_t need = (items + wpb - 1) / wpb;
         unsigned blocks = unsigned(need < uint64_t(grid) ? need : uint64_t(grid));
         if (blocks == 0) blocks = 1;
-        kern<<<blocks, wpb * 32, smem, st>>>(a);
+        kern<<<blocks, wpb * 32, smem, st>>>(a, tmh);
         GATB_LAUNCH("edge-softmax aggregation kernel");
     }
     if (a.n_hub) {
@@ -956,6 +1057,7 @@ int aggregate_dispatch_reserved(const gat_b200_graph* g, int heads, int dim, con
     a.col = g->col;
     a.perm = g->perm;
     a.n = g->n;
+    a.n_src = g->n_src ? g->n_src : g->n;
     a.n_hub = g->n_hub;
     a.n_seg = g->n_seg;
     a.n_wide = g->n_wide;
@@ -984,8 +1086,11 @@ int aggregate_dispatch_reserved(const gat_b200_graph* g, int heads, int dim, con
     a.max_out = max;
     if (h_dtype == GAT_B200_BF16) {
         if (heads == 8 && dim == 32 && (reinterpret_cast<uintptr_t>(left) & 15) == 0 &&
-            (reinterpret_cast<uintptr_t>(right) & 15) == 0)
+            (reinterpret_cast<uintptr_t>(right) & 15) == 0) {
+            if (ldh >= 256 && a.n_src < (1ull << 31) && hidden_row_gather())
+                return launch_agg<uint16_t, 8, 16, 32, 1, false, 32, true>(a, st, reserve_sms);
             return launch_agg<uint16_t, 8, 16, 32, 1, false, 32>(a, st, reserve_sms);
+        }
         if (heads == 1 && width <= 64) {
             const int nv = (width + 7) / 8;
             if (narrow_on_pairs() && !fixed_p && !unnorm) {

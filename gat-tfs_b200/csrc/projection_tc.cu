@@ -385,6 +385,25 @@ int make_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uin
 
 }  // namespace
 
+// Row-gather map of a BF16 feature table (the aggregation's tile::gather4
+// loads): `rows` rows of `cols` elements at a pitch of `ld` elements, boxes of
+// one row of box_cols elements, no swizzle, zeros outside the table.
+int make_row_gather_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint64_t ld,
+                        uint32_t box_cols) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail_code(GAT_B200_ECUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {ld * 2};
+    cuuint32_t box[2] = {box_cols, 1};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail_code(GAT_B200_ECUDA, "cuTensorMapEncodeTiled (row gather) failed (" + std::to_string(int(r)) + ")");
+    return 0;
+}
+
 // Returns GAT_B200_EUNSUPPORTED when the shape is outside the kernel (the
 // caller then uses the CUDA-core projection).
 // max_ctas > 0 caps the persistent grid (the multi-GPU forward runs this

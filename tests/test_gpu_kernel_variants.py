@@ -1,6 +1,7 @@
-"""The aggregation kernel variant that is not the default for its shape,
+"""The aggregation kernel variants that are not the default for their shape,
 selected per process by environment variable (GAT_B200_NARROW_AGG=pair: the
-lane-pair kernel for narrow single-head layers), runs in a child process on
+lane-pair kernel for narrow single-head layers; GAT_B200_HIDDEN_AGG=gather4:
+hidden-layer rows fetched by the TMA row gather), each in a child process on
 the c2 graph (hubs split into segments, wide rows, short rows): the
 three-layer BF16 forward against the R0 oracle (relative L2 <= 1e-2) and
 against the default kernels' forward (relative L2 <= 2e-3: the same math in
@@ -49,7 +50,8 @@ def reference_logits():
     return O.ref_chain(cfg.graph.row, cfg.graph.col, cfg.graph.x, model)[2]["out"]
 
 
-@pytest.mark.parametrize("name,env", [("default", {}), ("narrow_pair", {"GAT_B200_NARROW_AGG": "pair"})])
+@pytest.mark.parametrize("name,env", [("default", {}), ("narrow_pair", {"GAT_B200_NARROW_AGG": "pair"}),
+                                      ("hidden_gather4", {"GAT_B200_HIDDEN_AGG": "gather4"})])
 def test_variant_forward(tmp_path, reference_logits, name, env):
     got = _forward(tmp_path, name, env)
     ref = reference_logits
