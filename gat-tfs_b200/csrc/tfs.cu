@@ -134,32 +134,59 @@ struct TfsArgs {
     float* max_out;
 };
 
-constexpr int kGenWarps = 4;
+constexpr int kGenWarps = 4;    // warps per block, W read from global memory
+constexpr int kGenWarpsWs = 16;  // warps per block with W staged in shared memory
 
 // V[c] (lane owns c = lane, lane+32) += sum_k a[k] * W[k][h*dim+c], sequential
 // FP32 over k with exact BF16 x BF16 products (the order of AMX tdpbf16ps).
-__device__ __forceinline__ void gen_accumulate(const TfsArgs& a, int h, const float* s_a, float* v, int lane) {
+// WS: W read from the block's shared copy w_s[k][col] (consecutive lanes read
+// consecutive columns), else from the global W^T rows. Same products, same
+// order: the two give identical bits.
+template <bool WS>
+__device__ __forceinline__ void gen_accumulate(const TfsArgs& a, int h, const float* s_a, float* v, int lane,
+                                               const uint16_t* w_s) {
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
         const int c = lane + 32 * j;
         if (c < a.dim) {
-            const uint16_t* w = a.wt + size_t(h * a.dim + c) * a.kp;
             float acc = v[j];
-            for (int k = 0; k < a.in; ++k) acc = fmaf(s_a[k], bf(w[k]), acc);
+            if constexpr (WS) {
+                const uint16_t* w = w_s + h * a.dim + c;
+                for (int k = 0; k < a.in; ++k) acc = fmaf(s_a[k], bf(w[size_t(k) * a.width]), acc);
+            } else {
+                const uint16_t* w = a.wt + size_t(h * a.dim + c) * a.kp;
+                for (int k = 0; k < a.in; ++k) acc = fmaf(s_a[k], bf(w[k]), acc);
+            }
             v[j] = acc;
         }
     }
 }
 
-// One warp per destination row, heads in turn, neighbours in CSR order.
-__global__ void __launch_bounds__(32 * kGenWarps) tfs_generic_kernel(const TfsArgs a) {
+// One warp per destination row, heads in turn, neighbours in CSR order. With
+// WS the block first copies RNE(W) (in x width BF16, row-major) into shared
+// memory, so the FMA chains read W from there.
+template <int NW, bool WS>
+__global__ void __launch_bounds__(32 * NW) tfs_generic_kernel(const TfsArgs a) {
     extern __shared__ float gen_smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float* s_a = gen_smem + size_t(warp) * (2 * a.in_pad + 64);  // RNE(.) vector [in_pad]
+    const uint16_t* w_s = nullptr;
+    float* wbase = gen_smem;
+    if constexpr (WS) {
+        uint16_t* ws = reinterpret_cast<uint16_t*>(gen_smem);
+        const size_t wcount = size_t(a.in) * a.width;
+        for (size_t t = threadIdx.x; t < wcount; t += blockDim.x) {
+            const int k = int(t / a.width), c = int(t % a.width);
+            ws[t] = a.wt[size_t(c) * a.kp + k];
+        }
+        __syncthreads();
+        w_s = ws;
+        wbase = gen_smem + (wcount * 2 + 15) / 16 * 4;  // past W, 16-byte aligned
+    }
+    float* s_a = wbase + size_t(warp) * (2 * a.in_pad + 64);  // RNE(.) vector [in_pad]
     float* s_u = s_a + a.in_pad;                                 // U accumulator [in_pad]
     float* s_p = s_u + a.in_pad;                                 // weights of a 32-neighbour chunk
     uint32_t* s_src = reinterpret_cast<uint32_t*>(s_p + 32);     // their sources
-    for (uint64_t i = (uint64_t(blockIdx.x) * kGenWarps + warp); i < a.n; i += uint64_t(gridDim.x) * kGenWarps) {
+    for (uint64_t i = (uint64_t(blockIdx.x) * NW + warp); i < a.n; i += uint64_t(gridDim.x) * NW) {
         const uint64_t beg = a.row[i], deg = a.row[i + 1] - beg;
         // block 0: one block per row; with BLOCK/SPLIT rounding a row longer than
         // the graph's segment length takes one block per segment, as the
@@ -222,7 +249,7 @@ __global__ void __launch_bounds__(32 * kGenWarps) tfs_generic_kernel(const TfsAr
                                 // hbuf = RNE(x * p) (baseline_tfs.cpp:67-69), then V += hbuf . W
                                 for (int k = lane; k < a.in; k += 32) s_a[k] = bf(rne16(__fmul_rn(bf(xr[k]), p)));
                                 __syncwarp();
-                                gen_accumulate(a, h, s_a, v, lane);
+                                gen_accumulate<WS>(a, h, s_a, v, lane, w_s);
                                 __syncwarp();
                             } else if (!split) {
                                 for (int k = lane; k < a.in; k += 32) s_u[k] = fmaf(p, bf(xr[k]), s_u[k]);
@@ -238,7 +265,7 @@ __global__ void __launch_bounds__(32 * kGenWarps) tfs_generic_kernel(const TfsAr
                     __syncwarp();
                     for (int k = lane; k < a.in; k += 32) s_a[k] = bf(rne16(s_u[k]));
                     __syncwarp();
-                    gen_accumulate(a, h, s_a, v, lane);
+                    gen_accumulate<WS>(a, h, s_a, v, lane, w_s);
                 }
             }
             if (a.fixed_den) den = a.fixed_den[i * a.heads + h];
@@ -447,11 +474,27 @@ int tfs_generic_launch(const gat_b200_graph* g, const gat_b200_layer* p, const u
     a.den = den;
     a.max_out = max_out;
     if (g->n == 0) return 0;
+    // W staged in shared memory when it fits beside 16 warps' vectors: one
+    // block per SM, four FMA chains per scheduler
+    const size_t w_bytes = (size_t(a.in) * a.width * 2 + 15) / 16 * 16;
+    const size_t smem_ws = w_bytes + size_t(kGenWarpsWs) * (2 * a.in_pad + 64) * sizeof(float);
+    if (smem_ws <= 200 * 1024) {
+        auto k = tfs_generic_kernel<kGenWarpsWs, true>;
+        GATB_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem_ws)));
+        int dev = 0, sms = 0;
+        GATB_CUDA(cudaGetDevice(&dev));
+        GATB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        unsigned blocks = unsigned(std::min<uint64_t>((g->n + kGenWarpsWs - 1) / kGenWarpsWs, uint64_t(sms)));
+        k<<<blocks, 32 * kGenWarpsWs, smem_ws, st>>>(a);
+        GATB_LAUNCH("TFS aggregation kernel");
+        return 0;
+    }
     const size_t smem = size_t(kGenWarps) * (2 * a.in_pad + 64) * sizeof(float);
     if (smem > 200 * 1024) return fail_code(GAT_B200_EUNSUPPORTED, "tfs: input width too large");
-    GATB_CUDA(cudaFuncSetAttribute(tfs_generic_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+    auto k = tfs_generic_kernel<kGenWarps, false>;
+    GATB_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
     unsigned blocks = unsigned(std::min<uint64_t>((g->n + kGenWarps - 1) / kGenWarps, 148ull * 32));
-    tfs_generic_kernel<<<blocks, 32 * kGenWarps, smem, st>>>(a);
+    k<<<blocks, 32 * kGenWarps, smem, st>>>(a);
     GATB_LAUNCH("TFS aggregation kernel");
     return 0;
 }
