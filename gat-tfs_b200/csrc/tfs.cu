@@ -114,6 +114,7 @@ __global__ void __launch_bounds__(kLrRows)
 struct TfsArgs {
     const uint64_t* row;
     const uint32_t* col;
+    const uint32_t* perm;  // degree order (ascending); rows are taken from its end
     uint64_t n;
     int in, heads, dim, width, in_pad;
     const uint16_t* x;
@@ -186,14 +187,21 @@ __global__ void __launch_bounds__(32 * NW) tfs_generic_kernel(const TfsArgs a) {
     float* s_u = s_a + a.in_pad;                                 // U accumulator [in_pad]
     float* s_p = s_u + a.in_pad;                                 // weights of a 32-neighbour chunk
     uint32_t* s_src = reinterpret_cast<uint32_t*>(s_p + 32);     // their sources
-    for (uint64_t i = (uint64_t(blockIdx.x) * NW + warp); i < a.n; i += uint64_t(gridDim.x) * NW) {
+    // Work items are (row, head) pairs, rows from the largest degree down (the
+    // degree order), so the heads of a hub row run on different warps at once;
+    // every (row, head) keeps its neighbour order, so the sums are unchanged.
+    const uint64_t items = a.n * uint64_t(a.heads);
+    for (uint64_t item = (uint64_t(blockIdx.x) * NW + warp); item < items; item += uint64_t(gridDim.x) * NW) {
+        const uint64_t ri = item / uint64_t(a.heads);
+        const int h = int(item % uint64_t(a.heads));
+        const uint64_t i = a.perm ? a.perm[a.n - 1 - ri] : ri;
         const uint64_t beg = a.row[i], deg = a.row[i + 1] - beg;
         // block 0: one block per row; with BLOCK/SPLIT rounding a row longer than
         // the graph's segment length takes one block per segment, as the
         // tensor-core kernel does (it rounds U once per segment).
         const uint64_t B = a.block > 0 ? uint64_t(a.block)
                                        : (a.rounding != 0 && deg > a.seg ? a.seg : (deg ? deg : 1));
-        for (int h = 0; h < a.heads; ++h) {
+        {
             const float L = a.left ? a.left[i * a.heads + h] : 0.f;
             float v[2] = {0.f, 0.f};
             float den = 0.f, m = -INFINITY;
@@ -294,7 +302,7 @@ __global__ void __launch_bounds__(32 * NW) tfs_generic_kernel(const TfsArgs a) {
                 if (a.max_out) a.max_out[i * a.heads + h] = m;
             }
         }
-        if (a.norm && a.out_bf16) {
+        if (a.norm && a.out_bf16 && h == 0) {
             // zero the padding columns of a BF16 row (the next layer gathers whole rows)
             uint16_t* o = static_cast<uint16_t*>(a.out) + i * uint64_t(a.ldo);
             for (int c = a.width + lane; c < a.ldo; c += 32) o[c] = 0;
@@ -447,6 +455,7 @@ int tfs_generic_launch(const gat_b200_graph* g, const gat_b200_layer* p, const u
     TfsArgs a{};
     a.row = g->row;
     a.col = g->col;
+    a.perm = g->perm;
     a.n = g->n;
     a.in = p->in;
     a.heads = p->heads;
@@ -484,7 +493,8 @@ int tfs_generic_launch(const gat_b200_graph* g, const gat_b200_layer* p, const u
         int dev = 0, sms = 0;
         GATB_CUDA(cudaGetDevice(&dev));
         GATB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-        unsigned blocks = unsigned(std::min<uint64_t>((g->n + kGenWarpsWs - 1) / kGenWarpsWs, uint64_t(sms)));
+        const uint64_t items = g->n * uint64_t(p->heads);
+        unsigned blocks = unsigned(std::min<uint64_t>((items + kGenWarpsWs - 1) / kGenWarpsWs, uint64_t(sms)));
         k<<<blocks, 32 * kGenWarpsWs, smem_ws, st>>>(a);
         GATB_LAUNCH("TFS aggregation kernel");
         return 0;
@@ -493,7 +503,8 @@ int tfs_generic_launch(const gat_b200_graph* g, const gat_b200_layer* p, const u
     if (smem > 200 * 1024) return fail_code(GAT_B200_EUNSUPPORTED, "tfs: input width too large");
     auto k = tfs_generic_kernel<kGenWarps, false>;
     GATB_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-    unsigned blocks = unsigned(std::min<uint64_t>((g->n + kGenWarps - 1) / kGenWarps, 148ull * 32));
+    unsigned blocks =
+        unsigned(std::min<uint64_t>((g->n * uint64_t(p->heads) + kGenWarps - 1) / kGenWarps, 148ull * 32));
     k<<<blocks, 32 * kGenWarps, smem, st>>>(a);
     GATB_LAUNCH("TFS aggregation kernel");
     return 0;

@@ -79,3 +79,8 @@ def test_gpu_arm_line():
     assert d["gpu_launches"] > 0
     assert {"sm_mhz", "sm_max_mhz", "reasons"} <= set(d["clocks"])
     assert "cpu_baseline" in d
+    # the timed forward's own output, checked outside the timed region
+    par = d["parity"]
+    assert par["vs_1gpu"]["rows"] == 1024 and par["vs_1gpu"]["relative_l2"] <= 1e-5
+    assert par["vs_fp64"]["relative_l2"] <= 1e-2 and par["vs_fp64"]["layer"] == 3
+    assert "others" in rf and "aggregate_l3" in rf["others"]
