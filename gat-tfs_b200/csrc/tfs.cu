@@ -152,8 +152,27 @@ __device__ __forceinline__ void gen_accumulate(const TfsArgs& a, int h, const fl
         if (c < a.dim) {
             float acc = v[j];
             if constexpr (WS) {
+                // eight features at a time: their s_a and W values are loaded
+                // together, then the FMAs run in feature order
                 const uint16_t* w = w_s + h * a.dim + c;
-                for (int k = 0; k < a.in; ++k) acc = fmaf(s_a[k], bf(w[size_t(k) * a.width]), acc);
+                const int ws = a.width;
+                int k = 0;
+                for (; k + 8 <= a.in; k += 8) {
+                    const float4 s0 = *reinterpret_cast<const float4*>(s_a + k);
+                    const float4 s1 = *reinterpret_cast<const float4*>(s_a + k + 4);
+                    float wv[8];
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) wv[q] = bf(w[size_t(k + q) * ws]);
+                    acc = fmaf(s0.x, wv[0], acc);
+                    acc = fmaf(s0.y, wv[1], acc);
+                    acc = fmaf(s0.z, wv[2], acc);
+                    acc = fmaf(s0.w, wv[3], acc);
+                    acc = fmaf(s1.x, wv[4], acc);
+                    acc = fmaf(s1.y, wv[5], acc);
+                    acc = fmaf(s1.z, wv[6], acc);
+                    acc = fmaf(s1.w, wv[7], acc);
+                }
+                for (; k < a.in; ++k) acc = fmaf(s_a[k], bf(w[size_t(k) * ws]), acc);
             } else {
                 const uint16_t* w = a.wt + size_t(h * a.dim + c) * a.kp;
                 for (int k = 0; k < a.in; ++k) acc = fmaf(s_a[k], bf(w[k]), acc);
@@ -167,7 +186,7 @@ __device__ __forceinline__ void gen_accumulate(const TfsArgs& a, int h, const fl
 // WS the block first copies RNE(W) (in x width BF16, row-major) into shared
 // memory, so the FMA chains read W from there.
 template <int NW, bool WS>
-__global__ void __launch_bounds__(32 * NW) tfs_generic_kernel(const TfsArgs a) {
+__global__ void __launch_bounds__(32 * NW, 1) tfs_generic_kernel(const TfsArgs a) {
     extern __shared__ float gen_smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint16_t* w_s = nullptr;
@@ -191,6 +210,9 @@ __global__ void __launch_bounds__(32 * NW) tfs_generic_kernel(const TfsArgs a) {
     // degree order), so the heads of a hub row run on different warps at once;
     // every (row, head) keeps its neighbour order, so the sums are unchanged.
     const uint64_t items = a.n * uint64_t(a.heads);
+    // rows of at most 256 features, 8-feature aligned, in 16-byte pieces
+    const bool vec_rows = a.in <= 256 && a.in % 8 == 0 && a.ldx % 8 == 0 &&
+                          (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
     for (uint64_t item = (uint64_t(blockIdx.x) * NW + warp); item < items; item += uint64_t(gridDim.x) * NW) {
         const uint64_t ri = item / uint64_t(a.heads);
         const int h = int(item % uint64_t(a.heads));
@@ -249,6 +271,34 @@ __global__ void __launch_bounds__(32 * NW) tfs_generic_kernel(const TfsArgs a) {
                             if (lane == 0)
                                 for (int b = 0; b < cn; ++b) den = den + s_p[b];
                             den = __shfl_sync(0xffffffffu, den, 0);
+                        }
+                        if (a.rounding == 0 && vec_rows) {
+                            // per-edge rounding with the rows read as one 16-byte piece
+                            // per lane (8 features), the next neighbour's row in flight
+                            // while this one's FMA chains run
+                            const int k0 = lane * 8;
+                            const bool mine = k0 < a.in;
+                            uint4 cur = mine ? ldg_nc_v4(a.x + uint64_t(s_src[0]) * a.ldx + k0)
+                                             : make_uint4(0, 0, 0, 0);
+                            for (int b = 0; b < cn; ++b) {
+                                uint4 nxt = make_uint4(0, 0, 0, 0);
+                                if (b + 1 < cn && mine) nxt = ldg_nc_v4(a.x + uint64_t(s_src[b + 1]) * a.ldx + k0);
+                                const float p = s_p[b];
+                                if (mine) {
+                                    const uint32_t w4[4] = {cur.x, cur.y, cur.z, cur.w};
+#pragma unroll
+                                    for (int q = 0; q < 4; ++q) {
+                                        s_a[k0 + 2 * q] = bf(rne16(__fmul_rn(__uint_as_float(w4[q] << 16), p)));
+                                        s_a[k0 + 2 * q + 1] =
+                                            bf(rne16(__fmul_rn(__uint_as_float(w4[q] & 0xffff0000u), p)));
+                                    }
+                                }
+                                __syncwarp();
+                                gen_accumulate<WS>(a, h, s_a, v, lane, w_s);
+                                __syncwarp();
+                                cur = nxt;
+                            }
+                            continue;
                         }
                         for (int b = 0; b < cn; ++b) {
                             const float p = s_p[b];
