@@ -152,27 +152,32 @@ __device__ __forceinline__ void gen_accumulate(const TfsArgs& a, int h, const fl
         if (c < a.dim) {
             float acc = v[j];
             if constexpr (WS) {
-                // eight features at a time: their s_a and W values are loaded
-                // together, then the FMAs run in feature order
-                const uint16_t* w = w_s + h * a.dim + c;
+                // W in shared memory as groups of four features per column
+                // (w_s viewed as uint2 [in/4][width]: W[4g..4g+3][col] in one
+                // 8-byte word); eight features at a time, their s_a and W values
+                // loaded together, the FMAs in feature order
+                const uint2* w4 = reinterpret_cast<const uint2*>(w_s) + h * a.dim + c;
                 const int ws = a.width;
                 int k = 0;
                 for (; k + 8 <= a.in; k += 8) {
                     const float4 s0 = *reinterpret_cast<const float4*>(s_a + k);
                     const float4 s1 = *reinterpret_cast<const float4*>(s_a + k + 4);
-                    float wv[8];
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) wv[q] = bf(w[size_t(k + q) * ws]);
-                    acc = fmaf(s0.x, wv[0], acc);
-                    acc = fmaf(s0.y, wv[1], acc);
-                    acc = fmaf(s0.z, wv[2], acc);
-                    acc = fmaf(s0.w, wv[3], acc);
-                    acc = fmaf(s1.x, wv[4], acc);
-                    acc = fmaf(s1.y, wv[5], acc);
-                    acc = fmaf(s1.z, wv[6], acc);
-                    acc = fmaf(s1.w, wv[7], acc);
+                    const uint2 wa = w4[size_t(k / 4) * ws];
+                    const uint2 wb = w4[size_t(k / 4 + 1) * ws];
+                    acc = fmaf(s0.x, bf16lo(wa.x), acc);
+                    acc = fmaf(s0.y, bf16hi(wa.x), acc);
+                    acc = fmaf(s0.z, bf16lo(wa.y), acc);
+                    acc = fmaf(s0.w, bf16hi(wa.y), acc);
+                    acc = fmaf(s1.x, bf16lo(wb.x), acc);
+                    acc = fmaf(s1.y, bf16hi(wb.x), acc);
+                    acc = fmaf(s1.z, bf16lo(wb.y), acc);
+                    acc = fmaf(s1.w, bf16hi(wb.y), acc);
                 }
-                for (; k < a.in; ++k) acc = fmaf(s_a[k], bf(w[size_t(k) * ws]), acc);
+                for (; k < a.in; ++k) {
+                    const uint2 wq = w4[size_t(k / 4) * ws];
+                    const uint32_t word = (k & 2) ? wq.y : wq.x;
+                    acc = fmaf(s_a[k], (k & 1) ? bf16hi(word) : bf16lo(word), acc);
+                }
             } else {
                 const uint16_t* w = a.wt + size_t(h * a.dim + c) * a.kp;
                 for (int k = 0; k < a.in; ++k) acc = fmaf(s_a[k], bf(w[k]), acc);
@@ -192,11 +197,15 @@ __global__ void __launch_bounds__(32 * NW, 1) tfs_generic_kernel(const TfsArgs a
     const uint16_t* w_s = nullptr;
     float* wbase = gen_smem;
     if constexpr (WS) {
+        // element (k, col) at uint16 index ((k/4) * width + col) * 4 + k%4;
+        // features past `in` (up to a multiple of 4) hold zeros and are never used
         uint16_t* ws = reinterpret_cast<uint16_t*>(gen_smem);
-        const size_t wcount = size_t(a.in) * a.width;
+        const int in4 = (a.in + 3) / 4 * 4;
+        const size_t wcount = size_t(in4) * a.width;
         for (size_t t = threadIdx.x; t < wcount; t += blockDim.x) {
-            const int k = int(t / a.width), c = int(t % a.width);
-            ws[t] = a.wt[size_t(c) * a.kp + k];
+            const int g = int(t / (size_t(a.width) * 4)), rem = int(t % (size_t(a.width) * 4));
+            const int c = rem / 4, k = g * 4 + rem % 4;
+            ws[t] = k < a.in ? a.wt[size_t(c) * a.kp + k] : uint16_t(0);
         }
         __syncthreads();
         w_s = ws;
@@ -285,13 +294,15 @@ __global__ void __launch_bounds__(32 * NW, 1) tfs_generic_kernel(const TfsArgs a
                                 if (b + 1 < cn && mine) nxt = ldg_nc_v4(a.x + uint64_t(s_src[b + 1]) * a.ldx + k0);
                                 const float p = s_p[b];
                                 if (mine) {
-                                    const uint32_t w4[4] = {cur.x, cur.y, cur.z, cur.w};
+                                    const uint32_t xw[4] = {cur.x, cur.y, cur.z, cur.w};
+                                    float o[8];
 #pragma unroll
                                     for (int q = 0; q < 4; ++q) {
-                                        s_a[k0 + 2 * q] = bf(rne16(__fmul_rn(__uint_as_float(w4[q] << 16), p)));
-                                        s_a[k0 + 2 * q + 1] =
-                                            bf(rne16(__fmul_rn(__uint_as_float(w4[q] & 0xffff0000u), p)));
+                                        o[2 * q] = bf(rne16(__fmul_rn(bf16lo(xw[q]), p)));
+                                        o[2 * q + 1] = bf(rne16(__fmul_rn(bf16hi(xw[q]), p)));
                                     }
+                                    *reinterpret_cast<float4*>(s_a + k0) = make_float4(o[0], o[1], o[2], o[3]);
+                                    *reinterpret_cast<float4*>(s_a + k0 + 4) = make_float4(o[4], o[5], o[6], o[7]);
                                 }
                                 __syncwarp();
                                 gen_accumulate<WS>(a, h, s_a, v, lane, w_s);
@@ -535,7 +546,7 @@ int tfs_generic_launch(const gat_b200_graph* g, const gat_b200_layer* p, const u
     if (g->n == 0) return 0;
     // W staged in shared memory when it fits beside 16 warps' vectors: one
     // block per SM, four FMA chains per scheduler
-    const size_t w_bytes = (size_t(a.in) * a.width * 2 + 15) / 16 * 16;
+    const size_t w_bytes = (size_t((a.in + 3) / 4 * 4) * a.width * 2 + 15) / 16 * 16;
     const size_t smem_ws = w_bytes + size_t(kGenWarpsWs) * (2 * a.in_pad + 64) * sizeof(float);
     if (smem_ws <= 200 * 1024) {
         auto k = tfs_generic_kernel<kGenWarpsWs, true>;
