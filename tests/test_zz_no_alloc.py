@@ -83,6 +83,38 @@ def test_noalloc_matches_regular_entry_point(dev, kind, K, d, out_dtype, h_dtype
         assert np.all(np.abs(a - b) <= tol), (call, float(np.abs(a - b).max()))
 
 
+@pytest.mark.parametrize("kind,K,d", [("hubs", 8, 32), ("powerlaw", 1, 47), ("uniform", 4, 40)])
+def test_noalloc_matches_oracle(dev, kind, K, d):
+    """The same entry point against the CPU oracle's max prescan, standard
+    aggregate and finish (the reference's B0 stages) on the same inputs:
+    FP32 output within 1e-5 relative to the largest value (the same math,
+    another summation order)."""
+    import torch
+    import oracle as O
+    row, col = _graph(kind)
+    n, e, W = len(row) - 1, len(col), K * d
+    rng = np.random.default_rng(K * 100 + d)
+    ldh = G.padded_ld(W, G.BF16)
+    hb = G.rne(rng.standard_normal((n, W)).astype(np.float32))
+    hz = np.zeros((n, ldh), np.uint16)
+    hz[:, :W] = hb
+    L = rng.standard_normal((n, K)).astype(np.float32)
+    R = rng.standard_normal((n, K)).astype(np.float32)
+    z = G.bf16_to_f32(hb)
+    mx = O.max_prescan(row, col, L, R, K)
+    agg, den = O.standard_aggregate(row, col, z, L, R, mx, K, d)
+    want = O.finish(agg, den, K, d, True)
+    out = torch.zeros((n, W), dtype=torch.float32, device="cuda")
+    G.aggregate_fused_noalloc(n, e, torch.from_numpy(row.view(np.int64)).cuda(),
+                              torch.from_numpy(col.view(np.int32)).cuda(), K, d,
+                              torch.from_numpy(hz.view(np.int16)).cuda(), G.BF16, ldh, torch.from_numpy(L).cuda(),
+                              torch.from_numpy(R).cuda(), True, out, G.F32, W)
+    torch.cuda.synchronize()
+    G.check_device()
+    got = out.cpu().numpy()
+    assert np.abs(got - want).max() <= 1e-5 * max(1.0, float(np.abs(want).max())), float(np.abs(got - want).max())
+
+
 def test_noalloc_rejects_bad_arguments(dev):
     import torch
     row, col = _graph("uniform")
