@@ -89,6 +89,10 @@ def parse():
     ap.add_argument("--reserve-sms", type=int, default=None,
                     help="N>1, chunks>1: SMs left to each chunk's projection and exchange while the next chunk "
                          "aggregates (default 16; 0 = no overlap)")
+    ap.add_argument("--layer2-exchange", choices=["inputs", "h"], default="inputs",
+                    help="N>1, p2p: inputs = layer 2's input rows travel in the layer-1 aggregation's epilogue "
+                         "and every rank projects the whole table; h = the layer-2 projection stores H and R "
+                         "into every rank's table")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="N>1: p2p = the conversion / projection kernels store every rank's rows into every "
                          "rank's table over NVLink; nccl = NCCL all-gather of H and R per layer")
@@ -663,6 +667,8 @@ def main():
         pm = G.PartModel(comm, part.row, part.col_rows, part_layers, exch, args.chunks, stream)
         if args.reserve_sms is not None:
             pm.set_overlap(args.reserve_sms)
+        if args.exchange == "p2p" and args.layer2_exchange == "h":
+            pm.set_layer2_exchange(False)
         log("device model ready")
         n_loc, e_loc = pm.n_loc, pm.e_loc
         classes = pm.classes
@@ -685,10 +691,13 @@ def main():
         pm.enable_timing(False)
         launches = pm.launches()
         if args.exchange == "p2p":
+            l2 = ("layer 2: the layer-1 aggregation stores every output row into every rank's layer-2 input "
+                  "table and each rank projects the whole table; layer 3"
+                  if args.layer2_exchange == "inputs" else "layers 2-3")
             how = ("layer 1: the conversion kernel stores every input row into every rank's input table over "
-                   "NVLink (CUDA IPC peer memory) and each rank projects the whole table; layers 2-3: the "
-                   "projection kernel stores each H/R tile into every rank's table; a cross-GPU flag barrier "
-                   "closes each exchange")
+                   "NVLink (CUDA IPC peer memory) and each rank projects the whole table; " + l2 +
+                   ": the projection kernel stores each H/R tile into every rank's table; a cross-GPU flag "
+                   "barrier closes each exchange")
         else:
             how = "NCCL all-gather of each layer's H and R"
         if args.chunks > 1 and args.exchange == "p2p" and args.reserve_sms != 0:

@@ -67,6 +67,11 @@ struct AggArgs {
     int ldo;
     float* den_out;
     float* max_out;
+    // BF16 outputs only: every output row is also stored, at the same row and
+    // stride, into out_peer[j], j < npeer (other GPUs' tables mapped over
+    // NVLink; the multi-GPU forward's layer-2 input exchange)
+    int npeer;
+    uint16_t* out_peer[7];
 };
 
 template <class HT>
@@ -100,20 +105,29 @@ __device__ __forceinline__ float pick(const float (&a)[KM], int h) {
 template <int VECN>
 __device__ __forceinline__ void store_out(const AggArgs& a, uint64_t r, int c0, const float* v) {
     if (a.out_bf16) {
-        uint16_t* o = static_cast<uint16_t*>(a.out) + r * uint64_t(a.ldo) + c0;
+        const uint64_t off = r * uint64_t(a.ldo) + c0;
+        uint16_t* o = static_cast<uint16_t*>(a.out) + off;
         if (a.out_vec && c0 + VECN <= a.ldo) {
             uint32_t w[VECN / 2];
 #pragma unroll
             for (int k = 0; k < VECN / 2; ++k) w[k] = pack_bf16x2(v[2 * k], v[2 * k + 1]);
             if constexpr (VECN == 8) {
-                *reinterpret_cast<uint4*>(o) = make_uint4(w[0], w[1], w[2], w[3]);
+                const uint4 q = make_uint4(w[0], w[1], w[2], w[3]);
+                *reinterpret_cast<uint4*>(o) = q;
+                for (int j = 0; j < a.npeer; ++j) *reinterpret_cast<uint4*>(a.out_peer[j] + off) = q;
             } else {
-                *reinterpret_cast<uint2*>(o) = make_uint2(w[0], w[1]);
+                const uint2 q = make_uint2(w[0], w[1]);
+                *reinterpret_cast<uint2*>(o) = q;
+                for (int j = 0; j < a.npeer; ++j) *reinterpret_cast<uint2*>(a.out_peer[j] + off) = q;
             }
         } else {
 #pragma unroll
             for (int k = 0; k < VECN; ++k)
-                if (c0 + k < a.ldo) o[k] = uint16_t(pack_bf16x2(v[k], 0.f) & 0xffffu);
+                if (c0 + k < a.ldo) {
+                    const uint16_t b = uint16_t(pack_bf16x2(v[k], 0.f) & 0xffffu);
+                    o[k] = b;
+                    for (int j = 0; j < a.npeer; ++j) a.out_peer[j][off + k] = b;
+                }
         }
     } else {
         float* o = static_cast<float*>(a.out) + r * uint64_t(a.ldo) + c0;
@@ -695,10 +709,13 @@ __global__ void __launch_bounds__(kWarps * 32) hub_merge_kernel(const AggArgs a)
             d = pick(den, hh);
         }
         float v = finalize(a, c, accv, d);
-        if (a.out_bf16)
-            static_cast<uint16_t*>(a.out)[r * a.ldo + c] = uint16_t(pack_bf16x2(v, 0.f) & 0xffffu);
-        else
+        if (a.out_bf16) {
+            const uint16_t b = uint16_t(pack_bf16x2(v, 0.f) & 0xffffu);
+            static_cast<uint16_t*>(a.out)[r * a.ldo + c] = b;
+            for (int j = 0; j < a.npeer; ++j) a.out_peer[j][r * a.ldo + c] = b;
+        } else {
             static_cast<float*>(a.out)[r * a.ldo + c] = v;
+        }
     }
 }
 
@@ -1026,7 +1043,7 @@ int aggregate_check_error() {
 int aggregate_dispatch_reserved(const gat_b200_graph* g, int heads, int dim, const void* h, int h_dtype, int ldh,
                                 const float* left, const float* right, const float* fixed_p, const float* fixed_den,
                                 int unnorm, int hidden, void* out, int out_bf16, int ldo, float* den, float* max,
-                                cudaStream_t st, int reserve_sms);
+                                cudaStream_t st, int reserve_sms, int npeer = 0, uint16_t* const* out_peer = nullptr);
 
 int aggregate_dispatch(const gat_b200_graph* g, int heads, int dim, const void* h, int h_dtype, int ldh,
                        const float* left, const float* right, const float* fixed_p, const float* fixed_den,
@@ -1036,10 +1053,14 @@ int aggregate_dispatch(const gat_b200_graph* g, int heads, int dim, const void* 
                                        out, out_bf16, ldo, den, max, st, 0);
 }
 
+// npeer > 0 (BF16 hidden outputs only): every output row is also stored into
+// out_peer[j] (other GPUs' tables, each offset like out), by the warp kernel.
 int aggregate_dispatch_reserved(const gat_b200_graph* g, int heads, int dim, const void* h, int h_dtype, int ldh,
                                 const float* left, const float* right, const float* fixed_p, const float* fixed_den,
                                 int unnorm, int hidden, void* out, int out_bf16, int ldo, float* den, float* max,
-                                cudaStream_t st, int reserve_sms) {
+                                cudaStream_t st, int reserve_sms, int npeer, uint16_t* const* out_peer) {
+    if (npeer < 0 || npeer > 7) return fail("aggregate: at most 7 peer outputs");
+    if (npeer && (!out_bf16 || unnorm || !out_peer)) return fail("aggregate: peer outputs need BF16 output rows");
     if (!g) return fail("aggregate: null graph");
     if (heads < 1 || heads > 8 || dim < 1 || dim > 64) return fail("invalid parameter shape (heads <=8, head_dim <=64)");
     const int width = heads * dim;
@@ -1084,6 +1105,11 @@ int aggregate_dispatch_reserved(const gat_b200_graph* g, int heads, int dim, con
     }
     a.den_out = den;
     a.max_out = max;
+    a.npeer = npeer;
+    for (int j = 0; j < npeer; ++j) {
+        if (!out_peer[j]) return fail("aggregate: null peer output");
+        a.out_peer[j] = static_cast<uint16_t*>(out_peer[j]);
+    }
     if (h_dtype == GAT_B200_BF16) {
         if (heads == 8 && dim == 32 && (reinterpret_cast<uintptr_t>(left) & 15) == 0 &&
             (reinterpret_cast<uintptr_t>(right) & 15) == 0) {
@@ -1093,7 +1119,7 @@ int aggregate_dispatch_reserved(const gat_b200_graph* g, int heads, int dim, con
         }
         if (heads == 1 && width <= 64) {
             const int nv = (width + 7) / 8;
-            if (narrow_on_pairs() && !fixed_p && !unnorm) {
+            if (narrow_on_pairs() && !fixed_p && !unnorm && npeer == 0) {
                 // the lane-pair kernel serves the fused epilogue only
                 const int nvh = (nv + 1) / 2;
                 if (nvh <= 1) return launch_agg_pair<1>(a, st, reserve_sms);

@@ -45,7 +45,7 @@ namespace gatb {
 int aggregate_dispatch_reserved(const gat_b200_graph* g, int heads, int dim, const void* h, int h_dtype, int ldh,
                                 const float* left, const float* right, const float* fixed_p, const float* fixed_den,
                                 int unnorm, int hidden, void* out, int out_bf16, int ldo, float* den, float* max,
-                                cudaStream_t st, int reserve_sms);
+                                cudaStream_t st, int reserve_sms, int npeer, uint16_t* const* out_peer);
 int convert_launch(uint64_t n, int width, const float* in, int ld_in, uint16_t* out, int ld_out, cudaStream_t st);
 int convert_scatter_launch(uint64_t n, int width, const float* in, int ld_in, int ndst, uint16_t* const* dst,
                            int ld_out, cudaStream_t st);
@@ -65,6 +65,9 @@ constexpr int kEvents = GAT_B200_PART_STAGES + 1;
 // SMs left to the projection-and-exchange kernel while an aggregation runs
 // beside it (P2P exchange with several row chunks).
 constexpr int kDefaultReserve = 16;
+// P2P tables per rank: H of layers 1-3, R of layers 1-3, layer-1 BF16 input,
+// barrier flags, layer-2 BF16 input
+constexpr int kTables = 9;
 
 struct Layout {
     int world = 1, chunks = 1;
@@ -151,7 +154,10 @@ struct gat_b200_part_model {
     std::vector<Chunk> chunks;
     // P2P: tables t = 0..2 H of layer t+1, 3..5 R of layer t-2, 6 the layer-1
     // BF16 input, 7 the barrier flags; tab[j][t] = rank j's table t as mapped here.
-    std::vector<std::array<void*, 8>> tab;
+    std::vector<std::array<void*, kTables>> tab;
+    // P2P: layer 2's input rows reach every rank through the layer-1
+    // aggregation's epilogue (table 8) and every rank projects the whole table
+    bool x2x = false;
     std::vector<void*> owned, mapped;
     uint32_t epoch = 0;
     // Overlap (P2P, chunks > 1): the projection and exchange of chunk c run on
@@ -364,32 +370,34 @@ int gat_b200_part_model_create(gat_b200_comm* comm, uint64_t n, const uint64_t* 
         if (exchange == GAT_B200_EXCHANGE_P2P) {
             if ((rc = dalloc((void**)&m->left0, nt * K0 * 4))) break;
             // this rank's tables, their IPC handles to every rank, the peers' mapped
-            const uint64_t bytes[8] = {nt * m->ldh[0] * 2, nt * m->ldh[1] * 2, nt * m->ldh[2] * 2,
-                                       nt * m->heads[0] * 4, nt * m->heads[1] * 4, nt * m->heads[2] * 4,
-                                       nt * m->ld0 * 2, 64};
-            std::vector<unsigned char> handles(8 * GAT_B200_PEER_HANDLE_BYTES);
-            std::array<void*, 8> own{};
-            for (int t = 0; t < 8 && !rc; ++t) {
+            const uint64_t bytes[kTables] = {nt * m->ldh[0] * 2, nt * m->ldh[1] * 2, nt * m->ldh[2] * 2,
+                                             nt * m->heads[0] * 4, nt * m->heads[1] * 4, nt * m->heads[2] * 4,
+                                             nt * m->ld0 * 2, 64, nt * m->ldx * 2};
+            std::vector<unsigned char> handles(kTables * GAT_B200_PEER_HANDLE_BYTES);
+            std::array<void*, kTables> own{};
+            for (int t = 0; t < kTables && !rc; ++t) {
                 rc = gat_b200_peer_alloc(bytes[t], &own[t], &handles[t * GAT_B200_PEER_HANDLE_BYTES]);
                 if (!rc) m->owned.push_back(own[t]);
             }
             if (rc) break;
             std::vector<unsigned char> all(handles.size() * m->world);
             if ((rc = gat_b200_comm_all_gather(comm, handles.data(), all.data(), handles.size()))) break;
-            m->tab.assign(m->world, std::array<void*, 8>{});
+            m->tab.assign(m->world, std::array<void*, kTables>{});
             for (int j = 0; j < m->world && !rc; ++j) {
                 if (j == m->rank) {
                     m->tab[j] = own;
                     continue;
                 }
-                for (int t = 0; t < 8 && !rc; ++t) {
-                    rc = gat_b200_peer_open(&all[(size_t(j) * 8 + t) * GAT_B200_PEER_HANDLE_BYTES], &m->tab[j][t]);
+                for (int t = 0; t < kTables && !rc; ++t) {
+                    rc = gat_b200_peer_open(&all[(size_t(j) * kTables + t) * GAT_B200_PEER_HANDLE_BYTES],
+                                            &m->tab[j][t]);
                     if (!rc) m->mapped.push_back(m->tab[j][t]);
                 }
             }
             if (rc) break;
             // every rank's tables exist and are zeroed before any rank stores into them
             if ((rc = gat_b200_comm_barrier(comm))) break;
+            m->x2x = m->world > 1 && m->heads[1] <= m->heads[0];
         } else {
             if ((rc = dalloc((void**)&m->x0, nl * size_t(m->ld0) * 2))) break;
             int ldm = std::max(m->ldh[0], std::max(m->ldh[1], m->ldh[2]));
@@ -517,23 +525,33 @@ int gat_b200_part_model_forward(gat_b200_part_model* m, const float* x, int x_on
         // overlap: chunk c's projection and exchange (stream xst, reserve_sms
         // SMs) run while chunk c+1 aggregates on the other SMs; the last
         // chunk's projection runs alone on every SM
-        const bool overlap = !last && p2p && m->reserve_sms > 0 && m->chunks.size() > 1;
+        // x2 exchange: layer 1's aggregation stores each output row into every
+        // rank's layer-2 input table; layer 2 then projects the whole table
+        const bool x2 = p2p && m->x2x && l == 0;
+        const bool overlap = !last && !x2 && p2p && m->reserve_sms > 0 && m->chunks.size() > 1;
         const size_t nch = m->chunks.size();
         for (size_t c = 0; c < nch; ++c) {
             const auto& ch = m->chunks[c];
             if (ch.g) {
-                const float* left = (l == 0 && p2p) ? m->left0 + ch.row0 * K : m->left[l & 1] + ch.a * K;
+                const bool table_left = p2p && (l == 0 || (l == 1 && m->x2x));
+                const float* left = table_left ? m->left0 + ch.row0 * K : m->left[l & 1] + ch.a * K;
                 void* o = last ? static_cast<void*>(dst_logits + ch.a * m->classes)
-                               : static_cast<void*>(static_cast<uint16_t*>(m->xs[l & 1]) + ch.a * m->ldx);
+                               : x2 ? static_cast<void*>(static_cast<uint16_t*>(m->tab[m->rank][8]) + ch.row0 * m->ldx)
+                                    : static_cast<void*>(static_cast<uint16_t*>(m->xs[l & 1]) + ch.a * m->ldx);
+                uint16_t* peers[7];
+                int np = 0;
+                if (x2)
+                    for (int j = 0; j < m->world; ++j)
+                        if (j != m->rank) peers[np++] = static_cast<uint16_t*>(m->tab[j][8]) + ch.row0 * m->ldx;
                 if ((rc = aggregate_dispatch_reserved(ch.g, K, p->dim, htab, GAT_B200_BF16, ldh, left, rtab, nullptr,
                                                       nullptr, 0, last ? 0 : 1, o, last ? 0 : 1,
                                                       last ? m->classes : m->ldx, nullptr, nullptr, st,
-                                                      overlap ? m->reserve_sms : 0)))
+                                                      overlap ? m->reserve_sms : 0, np, peers)))
                     return rc;
                 launches += 1 + (ch.g->n_hub ? 1 : 0);
             }
             if (c + 1 == nch) mark(m, 5 + 3 * l, st);
-            if (last) continue;
+            if (last || x2) continue;
             if (overlap) {
                 GATB_CUDA(cudaEventRecord(m->ev_agg[c], st));
                 GATB_CUDA(cudaStreamWaitEvent(m->xst, m->ev_agg[c], 0));
@@ -546,7 +564,20 @@ int gat_b200_part_model_forward(gat_b200_part_model* m, const float* x, int x_on
             GATB_CUDA(cudaEventRecord(m->ev_xdone, m->xst));
             GATB_CUDA(cudaStreamWaitEvent(st, m->ev_xdone, 0));
         }
-        if (!last) {
+        if (x2) {
+            // every rank's layer-2 input rows have landed: project the whole table
+            if ((rc = barrier(m, st, launches))) return rc;
+            mark(m, 6, st);
+            const gat_b200_layer* p1 = m->layers[1];
+            rc = projection_tc_launch(p1, m->L.table_rows, static_cast<const uint16_t*>(m->tab[m->rank][8]), m->ldx,
+                                      m->H(m->rank, 1), m->ldh[1], nullptr, 0, m->left0, m->R(m->rank, 1), st, 0,
+                                      nullptr, nullptr, 0);
+            if (rc == GAT_B200_EUNSUPPORTED)
+                return fail_code(rc, "part_model: layer outside the tensor-core projection (input or width > 256)");
+            if (rc) return rc;
+            ++launches;
+            mark(m, 7, st);
+        } else if (!last) {
             mark(m, 6 + 3 * l, st);
             if ((rc = barrier(m, st, launches))) return rc;
             mark(m, 7 + 3 * l, st);
@@ -627,6 +658,15 @@ int gat_b200_part_model_stage_times(gat_b200_part_model* m, float* ms) {
 }
 
 int gat_b200_part_model_launches(const gat_b200_part_model* m) { return m ? m->launches_last : 0; }
+
+int gat_b200_part_model_set_layer2_exchange(gat_b200_part_model* m, int inputs) {
+    clear_error();
+    if (!m) return fail("part_model_set_layer2_exchange: null handle");
+    if (inputs && (m->exchange != GAT_B200_EXCHANGE_P2P || m->heads[1] > m->heads[0]))
+        return fail("part_model_set_layer2_exchange: needs the P2P exchange and layer 2 heads <= layer 1 heads");
+    m->x2x = inputs != 0 && m->world > 1;
+    return 0;
+}
 
 int gat_b200_part_model_set_overlap(gat_b200_part_model* m, int reserved_sms) {
     clear_error();

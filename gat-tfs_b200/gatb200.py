@@ -134,6 +134,7 @@ SIGNATURES = [
     ("gat_b200_part_model_launches", C.c_int, [_vp]),
     ("gat_b200_part_model_destroy", C.c_int, [_vp]),
     ("gat_b200_part_model_set_overlap", C.c_int, [_vp, C.c_int]),
+    ("gat_b200_part_model_set_layer2_exchange", C.c_int, [_vp, C.c_int]),
 ]
 for _name, _res, _args in SIGNATURES:
     _fn = getattr(_lib, _name)
@@ -772,6 +773,12 @@ class PartModel:
     def set_overlap(self, reserved_sms: int):
         """SMs left to the exchange while a chunk aggregates (0: no overlap)."""
         _check(_lib.gat_b200_part_model_set_overlap(self.handle, reserved_sms))
+
+    def set_layer2_exchange(self, inputs: bool):
+        """True: layer 2's input rows travel in the layer-1 aggregation's epilogue
+        and every rank projects the whole table; False: the layer-2 projection
+        stores H and R into every rank's table."""
+        _check(_lib.gat_b200_part_model_set_layer2_exchange(self.handle, int(inputs)))
 
     def close(self):
         """Collective: every rank calls it."""

@@ -523,9 +523,11 @@ typedef struct gat_b200_part_model gat_b200_part_model;
 /* Exchange of each layer's projected features between the ranks:
  *  P2P  (default): peer memory over NVLink (CUDA IPC). Layer 1's BF16 input
  *        rows are stored into every rank's input table by the conversion
- *        kernel itself and every rank projects the whole table; for layers 2
- *        and 3 the projection kernel stores each H/R tile into every rank's
- *        table; a bounded cross-GPU flag barrier closes each exchange.
+ *        kernel itself and every rank projects the whole table; layer 2's
+ *        input rows likewise by the layer-1 aggregation's epilogue (see
+ *        gat_b200_part_model_set_layer2_exchange); for layer 3 the
+ *        projection kernel stores each H/R tile into every rank's table; a
+ *        bounded cross-GPU flag barrier closes each exchange.
  *  NCCL: each rank projects its own rows and NCCL all-gathers H and R. */
 #define GAT_B200_EXCHANGE_P2P 0
 #define GAT_B200_EXCHANGE_NCCL 1
@@ -565,6 +567,15 @@ int gat_b200_part_model_launches(const gat_b200_part_model* m);
  * the others (one aggregation block per SM). Default 16 when chunks > 1;
  * 0 runs projection and aggregation one after the other. */
 int gat_b200_part_model_set_overlap(gat_b200_part_model* m, int reserved_sms);
+/* How layer 2's features reach the ranks under the P2P exchange. 1 (the
+ * default with more than one rank): the layer-1 aggregation stores every
+ * output row (layer 2's BF16 input) into every rank's layer-2 input table as
+ * it writes it, so the exchange runs inside the aggregation; after the
+ * barrier every rank projects the whole table (stage 5 of
+ * gat_b200_part_model_stage_times is then the barrier, stage 6 the
+ * projection). 0: each rank projects its own rows and the projection stores
+ * H and R into every rank's table, as for layer 3. */
+int gat_b200_part_model_set_layer2_exchange(gat_b200_part_model* m, int inputs);
 /* Collective: frees the model after a host barrier (peers may still be
  * storing into this rank's tables until every rank finished its forward). */
 int gat_b200_part_model_destroy(gat_b200_part_model* m);

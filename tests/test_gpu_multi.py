@@ -6,7 +6,9 @@
   (bit for bit): P2P exchange with 1 and 3 row chunks, NCCL with 2.
 * The Python binding (gatb200.Comm / PartModel) under torch.distributed, as
   bench.py drives it: the ranks' logits gathered on rank 0 against the
-  one-GPU model (relative L2 <= 1e-5).
+  one-GPU model (relative L2 <= 1e-5), with layer 2's input rows exchanged in
+  the layer-1 aggregation (the default) and with H exchanged by the layer-2
+  projection.
 
 Skipped with fewer than two GPUs. NCCL's NVLink SHARP (NVLS) is off, every
 wait is bounded (process-group timeout, subprocess timeouts, the peer
@@ -83,7 +85,7 @@ def test_cpp_mirror_partitioned_forward(part_bin, c2_files, tmp_path, exchange, 
         assert rc == 0 and "PASS" in o, o + e
 
 
-def _rank_main(rank, world, port, q, exchange, chunks):
+def _rank_main(rank, world, port, q, exchange, chunks, layer2_inputs=True):
     import datetime
     import torch
     import torch.distributed as tdist
@@ -100,6 +102,8 @@ def _rank_main(rank, world, port, q, exchange, chunks):
         part = configs.make_part("c2", rank, world)
         layers = [G.DeviceLayer(p) for p in part.model]
         pm = G.PartModel(comm, part.row, part.col_rows, layers, exchange, chunks, torch.cuda.current_stream())
+        if exchange == G.EXCHANGE_P2P:
+            pm.set_layer2_exchange(layer2_inputs)
         assert (pm.lo, pm.hi) == (part.lo, part.hi)
         x = torch.from_numpy(part.x_rows).cuda()
         logits = torch.empty((pm.n_loc, pm.classes), dtype=torch.float32, device="cuda")
@@ -123,8 +127,8 @@ def _rank_main(rank, world, port, q, exchange, chunks):
         tdist.destroy_process_group()
 
 
-@pytest.mark.parametrize("exchange,chunks", [(0, 1), (1, 1)])
-def test_python_binding_partitioned_forward(exchange, chunks):
+@pytest.mark.parametrize("exchange,chunks,layer2_inputs", [(0, 1, True), (0, 2, False), (1, 1, True)])
+def test_python_binding_partitioned_forward(exchange, chunks, layer2_inputs):
     import torch
     import torch.multiprocessing as mp
     if _gpus() < 2:
@@ -143,7 +147,8 @@ def test_python_binding_partitioned_forward(exchange, chunks):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q, exchange, chunks)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q, exchange, chunks, layer2_inputs))
+             for r in range(2)]
     for p in procs:
         p.start()
     import queue
