@@ -781,6 +781,10 @@ public:
         check(gat_b200_part_model_forward(m_, x_.data(), 1, out.data(), 1, nullptr));
         return out;
     }
+    // P2P exchange only: true (the default on more than one GPU) sends layer
+    // 2's input rows from the layer-1 aggregation; false sends layer 2's
+    // projected rows from its projection, like layers 1 and 3.
+    void set_layer2_exchange(bool inputs) { check(gat_b200_part_model_set_layer2_exchange(m_, inputs ? 1 : 0)); }
     gat_b200_part_model* handle() const { return m_; }
     const std::vector<float>& input() const { return x_; }
 

@@ -1,7 +1,10 @@
 // The three-layer forward on `world` GPUs of one node through the C++ mirror
 // (gat_b200::Communicator / gat_b200::PartitionedModel), one process per rank:
 //
-//   part_test GRAPH WEIGHTS RANK WORLD ID_PATH EXCHANGE CHUNKS
+//   part_test GRAPH WEIGHTS RANK WORLD ID_PATH EXCHANGE CHUNKS [LAYER2_INPUTS]
+//
+// LAYER2_INPUTS (P2P exchange only, default 1): 1 sends layer 2's input rows
+// from the layer-1 aggregation, 0 sends its projected rows.
 //
 // Each rank checks its rows of the partitioned logits against the one-GPU
 // model (gat_b200_model_*) of the whole graph run on its own GPU: relative L2
@@ -20,13 +23,14 @@
 namespace gat = gat_b200;
 
 int main(int argc, char** argv) {
-    if (argc != 8) {
-        std::fprintf(stderr, "usage: %s GRAPH WEIGHTS RANK WORLD ID_PATH EXCHANGE CHUNKS\n", argv[0]);
+    if (argc != 8 && argc != 9) {
+        std::fprintf(stderr, "usage: %s GRAPH WEIGHTS RANK WORLD ID_PATH EXCHANGE CHUNKS [LAYER2_INPUTS]\n", argv[0]);
         return 2;
     }
     try {
         const int rank = std::atoi(argv[3]), world = std::atoi(argv[4]);
         const int exchange = std::atoi(argv[6]), chunks = std::atoi(argv[7]);
+        const bool layer2_inputs = argc == 9 ? std::atoi(argv[8]) != 0 : true;
         const gat::Graph g = gat::load_graph(argv[1]);
         const gat::Model model = gat::load_model(argv[2], g.din, g.classes);
         gat::Communicator comm(argv[5], world, rank, rank);
@@ -35,6 +39,7 @@ int main(int argc, char** argv) {
         bool async_equal = true;
         {
             gat::PartitionedModel pm(comm, g, model, exchange, chunks);
+            if (exchange == GAT_B200_EXCHANGE_P2P) pm.set_layer2_exchange(layer2_inputs);
             lo = pm.first_row();
             hi = pm.end_row();
             for (int i = 0; i < 3; ++i) got = pm.forward();
@@ -69,9 +74,9 @@ int main(int argc, char** argv) {
         gat_b200_graph_destroy(gg);
         const double rel = r2 > 0 ? std::sqrt(d2 / r2) : std::sqrt(d2);
         const bool ok = std::isfinite(rel) && rel <= 1e-5 && async_equal;
-        std::printf("PART_TEST rank=%d world=%d exchange=%d chunks=%d rows=%llu..%llu rel_l2=%.3e max_abs=%.3e "
-                    "async_equal=%d %s\n",
-                    rank, world, exchange, chunks, (unsigned long long)lo, (unsigned long long)hi, rel, mx,
+        std::printf("PART_TEST rank=%d world=%d exchange=%d chunks=%d layer2_inputs=%d rows=%llu..%llu rel_l2=%.3e "
+                    "max_abs=%.3e async_equal=%d %s\n",
+                    rank, world, exchange, chunks, int(layer2_inputs), (unsigned long long)lo, (unsigned long long)hi, rel, mx,
                     int(async_equal), ok ? "PASS" : "FAIL");
         return ok ? 0 : 1;
     } catch (const std::exception& e) {

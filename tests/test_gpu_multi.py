@@ -3,7 +3,8 @@
 * The C++ mirror program tests/cpp/part_test.cpp, one process per rank, each
   checking its rows against the one-GPU model of the whole graph on its own
   GPU (relative L2 <= 1e-5) and its pipelined requests against its forward
-  (bit for bit): P2P exchange with 1 and 3 row chunks, NCCL with 2.
+  (bit for bit): P2P exchange with 1 and 3 row chunks and with either layer-2
+  exchange, NCCL with 2.
 * The Python binding (gatb200.Comm / PartModel) under torch.distributed, as
   bench.py drives it: the ranks' logits gathered on rank 0 against the
   one-GPU model (relative L2 <= 1e-5), with layer 2's input rows exchanged in
@@ -62,15 +63,15 @@ def part_bin(tmp_path_factory):
     return out
 
 
-@pytest.mark.parametrize("exchange,chunks", [(0, 1), (0, 3), (1, 2)])
-def test_cpp_mirror_partitioned_forward(part_bin, c2_files, tmp_path, exchange, chunks):
+@pytest.mark.parametrize("exchange,chunks,layer2_inputs", [(0, 1, 1), (0, 3, 1), (0, 1, 0), (1, 2, 1)])
+def test_cpp_mirror_partitioned_forward(part_bin, c2_files, tmp_path, exchange, chunks, layer2_inputs):
     if _gpus() < 2:
         pytest.skip("needs 2 GPUs")
     world = 2
     idp = tmp_path / f"nccl_id_{uuid.uuid4().hex}"
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     procs = [subprocess.Popen([str(part_bin), str(c2_files[0]), str(c2_files[1]), str(r), str(world), str(idp),
-                               str(exchange), str(chunks)], stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True,
+                               str(exchange), str(chunks), str(layer2_inputs)], stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True,
                               env=env) for r in range(world)]
     outs = []
     try:
