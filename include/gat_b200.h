@@ -572,8 +572,8 @@ int gat_b200_part_model_set_overlap(gat_b200_part_model* m, int reserved_sms);
  * output row (layer 2's BF16 input) into every rank's layer-2 input table as
  * it writes it, so the exchange runs inside the aggregation; after the
  * barrier every rank projects the whole table (stage 5 of
- * gat_b200_part_model_stage_times is then the barrier, stage 6 the
- * projection). 0: each rank projects its own rows and the projection stores
+ * gat_b200_part_model_stage_times is that projection, stage 6 the barrier
+ * before it). 0: each rank projects its own rows and the projection stores
  * H and R into every rank's table, as for layer 3. */
 int gat_b200_part_model_set_layer2_exchange(gat_b200_part_model* m, int inputs);
 /* Collective: frees the model after a host barrier (peers may still be
