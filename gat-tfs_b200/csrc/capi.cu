@@ -279,6 +279,8 @@ int gat_b200_layer_create(int in, int heads, int dim, const float* w, const floa
     p->width = width;
     p->kp = (in + 63) / 64 * 64;
     p->np = (width + 15) / 16 * 16;
+    p->al_host.assign(al, al + width);
+    p->ar_host.assign(ar, ar + width);
     // BF16 RNE(W) transposed to [np][kp] (K-major B operand), zero padded;
     // prepare() converts W with the same rounding (common.cpp:99).
     std::vector<uint16_t> wt(size_t(p->np) * p->kp, 0);

@@ -1,6 +1,7 @@
 // Device-resident graph, prepared layer and model objects behind the opaque
 // handles of include/gat_b200.h.
 #pragma once
+#include <vector>
 #include <cuda_runtime.h>
 #include <cstdint>
 
@@ -54,6 +55,7 @@ struct gat_b200_layer {
     float* al = nullptr;         // device [width]
     float* ar = nullptr;         // device [width]
     float* blr = nullptr;        // device [in][2*heads] = W.a (common.cpp:100-108)
+    std::vector<float> al_host, ar_host;  // host copies of aL / aR [width]
 };
 
 namespace gatb {

@@ -44,6 +44,7 @@ constexpr int kStageBytes = kStageRows * 128;     // 4 KB
 constexpr int kThreads = 320;
 constexpr int kEpiWarps = 8;
 constexpr int kMaxPeers = 7;
+constexpr int kMaxCoef = 256;  // attention coefficients carried in the launch parameters
 
 struct ProjArgs {
     uint64_t n;
@@ -66,6 +67,10 @@ struct ProjArgs {
     int ldh;
     uint16_t* hp[kMaxPeers];
     float* rp[kMaxPeers];
+    // aL / aR (zero past the width) for the shape-specialised epilogues, which
+    // read them as constant operands instead of from shared memory
+    float alc[kMaxCoef];
+    float arc[kMaxCoef];
 };
 
 // ---- PTX wrappers (tc.cuh) -------------------------------------------------
@@ -90,14 +95,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // K-major operand in the 128-byte swizzle layout: 8-row groups 1024 bytes apart.
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) { return tc::desc_sw128(saddr, 16, 1024); }
 
-template <bool ALIGNED16>
+// ALIGNED16: every 16-column block lies in one head. NPT / KT: the padded
+// width and the head count at compile time (0 = read from the arguments);
+// with both known the epilogue's loops unroll completely, the coefficients
+// are constant operands and each block's head is a constant.
+template <bool ALIGNED16, int NPT, int KT>
 __global__ void __launch_bounds__(kThreads, 1)
     proj_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
-                   const __grid_constant__ CUtensorMap tm_h, const ProjArgs a) {
+                   const __grid_constant__ CUtensorMap tm_h, const __grid_constant__ ProjArgs a) {
+    static_assert(NPT == 0 || (ALIGNED16 && KT != 0 && NPT <= kMaxCoef && NPT % 16 == 0), "bad specialisation");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte alignment for the swizzled tiles.
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const int S = a.stages, NP = a.np, KB = a.kb;
+    const int S = a.stages, NP = NPT ? NPT : a.np, KB = a.kb;
     uint8_t* w_s = smem;                                         // KB x [NP x 128 B]
     uint8_t* a_s = w_s + size_t(KB) * NP * 128;                   // S x 16 KB
     uint8_t* st_s = a_s + size_t(S) * kABytes;                    // 8 warps x sb x 4 KB
@@ -222,6 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             float L[8], R[8];
 #pragma unroll
             for (int h = 0; h < 8; ++h) { L[h] = 0.f; R[h] = 0.f; }
+#pragma unroll
             for (int g = 0; g < NP; g += 64) {
                 uint8_t* sb = stage0 + toggle * kStageBytes;
                 if (lane == 0 && a.store_h) {
@@ -234,12 +245,34 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // 16 accumulator columns c..c+15 of this row (sub-block cc of the group)
                 auto col16 = [&](int cc, const float* v) {
                     const int c = g + cc * 16;
-                    if constexpr (ALIGNED16) {
+                    if constexpr (ALIGNED16 && NPT != 0) {
+                        // c is a constant here: the same FMA chains as below
                         float pl = 0.f, pr = 0.f;
 #pragma unroll
                         for (int j = 0; j < 16; ++j) {
-                            pl = fmaf(v[j], al_s[c + j], pl);
-                            pr = fmaf(v[j], ar_s[c + j], pr);
+                            pl = fmaf(v[j], a.alc[c + j], pl);
+                            pr = fmaf(v[j], a.arc[c + j], pr);
+                        }
+                        const int hh = KT == 1 ? 0 : c / (NPT / KT);
+                        L[hh] += pl;
+                        R[hh] += pr;
+                    } else if constexpr (ALIGNED16) {
+                        // the block's 16 coefficients as four 16-byte reads
+                        const float4* l4 = reinterpret_cast<const float4*>(al_s + c);
+                        const float4* r4 = reinterpret_cast<const float4*>(ar_s + c);
+                        float pl = 0.f, pr = 0.f;
+#pragma unroll
+                        for (int j4 = 0; j4 < 4; ++j4) {
+                            const float4 x = l4[j4], y = r4[j4];
+                            const float* vv = v + 4 * j4;
+                            pl = fmaf(vv[0], x.x, pl);
+                            pl = fmaf(vv[1], x.y, pl);
+                            pl = fmaf(vv[2], x.z, pl);
+                            pl = fmaf(vv[3], x.w, pl);
+                            pr = fmaf(vv[0], y.x, pr);
+                            pr = fmaf(vv[1], y.y, pr);
+                            pr = fmaf(vv[2], y.z, pr);
+                            pr = fmaf(vv[3], y.w, pr);
                         }
                         const int hh = c / a.dim;
 #pragma unroll
@@ -277,6 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int cc = 0; cc < 4; ++cc) col16(cc, v64 + cc * 16);
                 } else {
+#pragma unroll
                     for (int cc = 0; cc < 4 && g + cc * 16 < NP; ++cc) {
                         float v[16];
                         tmem_ld16(taddr + uint32_t(g + cc * 16), v);
@@ -486,15 +520,29 @@ int projection_tc_launch(const gat_b200_layer* p, uint64_t n, const uint16_t* x,
     const unsigned grid = unsigned(ntiles < cap ? ntiles : cap);
     // Heads aligned to 16 columns (or a single head, whose columns past the
     // width carry zero coefficients): one head per 16-column block.
-    if (p->dim % 16 == 0 || p->heads == 1) {
-        auto k = proj_tc_kernel<true>;
-        GATB_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-        k<<<grid, kThreads, smem, st>>>(tm_x, tm_w, tm_h, a);
-    } else {
-        auto k = proj_tc_kernel<false>;
-        GATB_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-        k<<<grid, kThreads, smem, st>>>(tm_x, tm_w, tm_h, a);
+    // Shape-specialised epilogues: 8 heads x 32 (the hidden layers) and one
+    // head of 48 or 64 padded columns (class logits).
+    for (int c = 0; c < kMaxCoef; ++c) {
+        a.alc[c] = c < p->width && c < int(p->al_host.size()) ? p->al_host[c] : 0.f;
+        a.arc[c] = c < p->width && c < int(p->ar_host.size()) ? p->ar_host[c] : 0.f;
     }
+    const bool coef = int(p->al_host.size()) == p->width && int(p->ar_host.size()) == p->width;
+    auto launch = [&](auto kern) -> int {
+        GATB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+        kern<<<grid, kThreads, smem, st>>>(tm_x, tm_w, tm_h, a);
+        return 0;
+    };
+    if (coef && p->heads == 8 && p->dim == 32 && p->np == 256)
+        rc = launch(proj_tc_kernel<true, 256, 8>);
+    else if (coef && p->heads == 1 && p->np == 48)
+        rc = launch(proj_tc_kernel<true, 48, 1>);
+    else if (coef && p->heads == 1 && p->np == 64)
+        rc = launch(proj_tc_kernel<true, 64, 1>);
+    else if (p->dim % 16 == 0 || p->heads == 1)
+        rc = launch(proj_tc_kernel<true, 0, 0>);
+    else
+        rc = launch(proj_tc_kernel<false, 0, 0>);
+    if (rc) return rc;
     GATB_LAUNCH("projection (tcgen05) kernel");
     return 0;
 }
