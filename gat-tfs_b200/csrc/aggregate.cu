@@ -115,10 +115,14 @@ __device__ __forceinline__ void store_out(const AggArgs& a, uint64_t r, int c0, 
                 const uint4 q = make_uint4(w[0], w[1], w[2], w[3]);
                 *reinterpret_cast<uint4*>(o) = q;
                 for (int j = 0; j < a.npeer; ++j) *reinterpret_cast<uint4*>(a.out_peer[j] + off) = q;
-            } else {
+            } else if constexpr (VECN == 4) {
                 const uint2 q = make_uint2(w[0], w[1]);
                 *reinterpret_cast<uint2*>(o) = q;
                 for (int j = 0; j < a.npeer; ++j) *reinterpret_cast<uint2*>(a.out_peer[j] + off) = q;
+            } else {
+                static_assert(VECN == 2, "2, 4 or 8 values");
+                *reinterpret_cast<uint32_t*>(o) = w[0];
+                for (int j = 0; j < a.npeer; ++j) *reinterpret_cast<uint32_t*>(a.out_peer[j] + off) = w[0];
             }
         } else {
 #pragma unroll
@@ -132,14 +136,44 @@ __device__ __forceinline__ void store_out(const AggArgs& a, uint64_t r, int c0, 
     } else {
         float* o = static_cast<float*>(a.out) + r * uint64_t(a.ldo) + c0;
         if (a.out_vec && c0 + VECN <= a.ldo) {
+            if constexpr (VECN % 4 == 0) {
 #pragma unroll
-            for (int k = 0; k < VECN; k += 4)
-                *reinterpret_cast<float4*>(o + k) = make_float4(v[k], v[k + 1], v[k + 2], v[k + 3]);
+                for (int k = 0; k < VECN; k += 4)
+                    *reinterpret_cast<float4*>(o + k) = make_float4(v[k], v[k + 1], v[k + 2], v[k + 3]);
+            } else {
+                static_assert(VECN == 2, "2 or a multiple of 4 values");
+                *reinterpret_cast<float2*>(o) = make_float2(v[0], v[1]);
+            }
         } else {
 #pragma unroll
             for (int k = 0; k < VECN; ++k)
                 if (c0 + k < a.ldo) o[k] = v[k];
         }
+    }
+}
+
+// Sum of n values over the lanes lane ^ O, lane ^ 2O, ... < 32 (the edge groups
+// of a warp that share a feature vector), scattered: each lane ends with n /
+// (32 / O) of the sums, starting at value k0. Each step adds the partner's
+// half to the half this lane keeps, own value first, so every sum has the
+// same operands in the same order as a butterfly over all n values.
+template <int N, int O>
+__device__ __forceinline__ void reduce_scatter(const float* in, float* out, int lane, int& k0) {
+    if constexpr (O >= 32) {
+#pragma unroll
+        for (int i = 0; i < N; ++i) out[i] = in[i];
+    } else {
+        static_assert(N % 2 == 0, "values must halve at every step");
+        const bool hi = (lane & O) != 0;
+        float t[N / 2];
+#pragma unroll
+        for (int i = 0; i < N / 2; ++i) {
+            const float keep = hi ? in[N / 2 + i] : in[i];
+            const float send = hi ? in[i] : in[N / 2 + i];
+            t[i] = keep + __shfl_xor_sync(0xffffffffu, send, O);
+        }
+        if (hi) k0 += N / 2;
+        reduce_scatter<N / 2, 2 * O>(t, out, lane, k0);
     }
 }
 
@@ -488,12 +522,51 @@ __global__ void __launch_bounds__(MAXT) agg_kernel(const AggArgs a, const __grid
                 out[j][2 * k] = f.x;
                 out[j][2 * k + 1] = f.y;
             }
+        if constexpr (EPS > 1) {
+            // Narrow rows (EPS edge groups): the groups' sums are reduced and
+            // scattered so that each lane finishes and stores VEC / EPS values
+            // of its vector (the butterfly's sums, without its redundant copies).
+            static_assert(!MIXED && VEC % EPS == 0, "narrow rows hold one head per vector");
+            constexpr int VR = VEC / EPS;
+            float red[VPL][VR];
+            int k0 = 0;
 #pragma unroll
-        for (int o = LPE; o < 32; o <<= 1)
+            for (int j = 0; j < VPL; ++j) {
+                k0 = 0;
+                reduce_scatter<VEC, LPE>(out[j], red[j], lane, k0);
+            }
+            if (flags & kPartial) {
+                float* st = a.seg_state + uint64_t(S.item) * kSegStateFloats;
+                if (lane < K) {
+                    st[lane] = S.m[lane];
+                    st[8 + lane] = S.den[lane];
+                }
 #pragma unroll
-            for (int j = 0; j < VPL; ++j)
+                for (int j = 0; j < VPL; ++j) {
+                    const int v = vl + j * LPE;
+                    if (v < nvec)
 #pragma unroll
-                for (int k = 0; k < VEC; ++k) out[j][k] += __shfl_xor_sync(kFull, out[j][k], o);
+                        for (int i = 0; i < VR; ++i) st[16 + v * VEC + k0 + i] = red[j][i];
+                }
+                return;
+            }
+            const uint64_t r = S.r;
+            if (a.unnorm && lane < K) {
+                a.den_out[r * K + lane] = a.fixed_den ? a.fixed_den[r * K + lane] : S.den[lane];
+                if (a.max_out && !fixed) a.max_out[r * K + lane] = S.m[lane];
+            }
+#pragma unroll
+            for (int j = 0; j < VPL; ++j) {
+                const int v = vl + j * LPE;
+                if (v * VEC >= a.ldo) continue;
+                float o[VR];
+#pragma unroll
+                for (int i = 0; i < VR; ++i) o[i] = finalize(a, v * VEC + k0 + i, red[j][i], S.den[hv[j]]);
+                store_out<VR>(a, r, v * VEC + k0, o);
+            }
+            return;
+        }
+        // whole-warp rows (EPS == 1): every lane holds its vector's sums
         if (flags & kPartial) {
             float* st = a.seg_state + uint64_t(S.item) * kSegStateFloats;
             if (lane < K) {
