@@ -333,15 +333,25 @@ struct Gen {
 //   4. consume chunk k-1 (waiting only for this lane's own copies: a lane
 //      consumes exactly the vectors it copied).
 // Shared memory of one warp: the two chunk slots, the two row buffers and,
-// with TG, the buffers' two mbarriers (128-byte aligned regions).
-template <int C, int KM, int RV, bool TG>
+// with TG, the buffers' two mbarriers (128-byte aligned regions). A buffer
+// holds C rows of RP 16-byte vectors in groups of four rows; with TG each
+// group (one tile::gather4) starts on a 128-byte boundary.
+template <int RP, bool TG>
+__host__ __device__ constexpr int agg_group_bytes() {
+    return TG ? (64 * RP + 127) / 128 * 128 : 64 * RP;
+}
+template <int C, int RP, bool TG>
+__host__ __device__ constexpr size_t agg_buf_bytes() {
+    return size_t(C / 4) * agg_group_bytes<RP, TG>();
+}
+template <int C, int KM, bool TG>
 __host__ __device__ constexpr size_t agg_slot_bytes() {
     return TG ? (2 * sizeof(Slot<C, KM>) + 127) / 128 * 128 : 2 * sizeof(Slot<C, KM>);
 }
-template <int C, int KM, int RV, bool TG>
+template <int C, int KM, int RP, bool TG>
 __host__ __device__ constexpr size_t agg_warp_bytes() {
-    return TG ? (agg_slot_bytes<C, KM, RV, TG>() + size_t(2) * C * RV * 16 + 16 + 127) / 128 * 128
-              : agg_slot_bytes<C, KM, RV, TG>() + size_t(2) * C * RV * 16;
+    return TG ? (agg_slot_bytes<C, KM, TG>() + 2 * agg_buf_bytes<C, RP, TG>() + 16 + 127) / 128 * 128
+              : agg_slot_bytes<C, KM, TG>() + 2 * agg_buf_bytes<C, RP, TG>();
 }
 
 // Bounded wait on a row buffer's mbarrier (TG): false after ~1 s, with the
@@ -361,11 +371,13 @@ __device__ __forceinline__ bool agg_wait(uint64_t* bar, uint32_t parity) {
     }
 }
 
-// TG (hidden layers, 8 heads x 32, BF16 rows of 512 bytes): each chunk's 16
-// rows are fetched by the tensor memory accelerator instead of per-lane
-// cp.async -- lanes 0..3 each issue one tile::gather4 of four rows (source
-// ids past the chunk's end point outside the table and read as zeros), the
-// buffer's mbarrier counts the bytes, and the consumer waits on it (bounded).
+// TG (BF16 rows: the hidden layers' 8 heads x 32, 512 bytes, or a single
+// head of NVC 16-byte vectors): each chunk's rows are fetched by the tensor
+// memory accelerator instead of per-lane cp.async -- lane q issues one
+// tile::gather4 of rows 4q..4q+3 (source ids past the chunk's end point
+// outside the table and read as zeros, up to the consumer's granule of 4
+// steps), the buffer's mbarrier counts the bytes, and the consumer waits on
+// it (bounded).
 template <class HT, int KT, int C, int LPE, int VPL, bool MIXED, int NVC, int MAXT, bool TG>
 __global__ void __launch_bounds__(MAXT) agg_kernel(const AggArgs a, const __grid_constant__ CUtensorMap tmh) {
     using V = Vec<HT>;
@@ -376,23 +388,30 @@ __global__ void __launch_bounds__(MAXT) agg_kernel(const AggArgs a, const __grid
     constexpr int NG = C / EG;           // score groups per chunk
     constexpr int EPS = 32 / LPE;        // edges per copy/consume step
     constexpr int NT = C / EPS;          // copy/consume steps per chunk
-    constexpr int RV = LPE * VPL;        // 16-byte vectors per buffered row
+    constexpr int RV = LPE * VPL;        // 16-byte vectors a lane group covers
+    constexpr int RP = TG ? NVC : RV;    // 16-byte vectors per buffered row
+    constexpr int GPB = agg_group_bytes<RP, TG>();
+    constexpr int BUFV = int(agg_buf_bytes<C, RP, TG>() / 16);  // vectors per row buffer
     constexpr int PS = C + 4;            // p row stride (Slot::p): conflict-free for 8 heads x 4 offsets
     static_assert(NG >= 1 && NG * EG == C && NT * EPS == C, "bad tiling");
     static_assert(HS == 1 || LPE == 32, "8 head slots need whole-warp rows");
     using SlotT = Slot<C, KM>;
 
-    static_assert(!TG || (sizeof(HT) == 2 && KT == 8 && C == 16 && LPE == 32 && VPL == 1 && NVC == 32),
-                  "the row gather serves the 8 x 32 BF16 layout");
+    static_assert(!TG || (sizeof(HT) == 2 && VPL == 1 &&
+                          ((KT == 8 && C == 16 && LPE == 32 && NVC == 32) ||
+                           (KT == 1 && C == 32 && LPE == 8 && NVC >= 1 && NVC <= 8))),
+                  "the row gather serves BF16 rows of 8 x 32 or of one head up to 64 columns");
+    // first vector of buffered row tt
+    auto row_vec = [](int tt) { return ((tt >> 2) * GPB + (tt & 3) * RP * 16) / 16; };
     extern __shared__ __align__(128) uint8_t agg_smem[];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-    constexpr size_t kSlotBytes = agg_slot_bytes<C, KM, RV, TG>();
-    constexpr size_t kWarpBytes = agg_warp_bytes<C, KM, RV, TG>();
+    constexpr size_t kSlotBytes = agg_slot_bytes<C, KM, TG>();
+    constexpr size_t kWarpBytes = agg_warp_bytes<C, KM, RP, TG>();
     uint8_t* wbase = agg_smem + wib * kWarpBytes;
     SlotT* slots = reinterpret_cast<SlotT*>(wbase);
     const uint4* bufs = reinterpret_cast<const uint4*>(wbase + kSlotBytes);
     const uint32_t bufs_s = static_cast<uint32_t>(__cvta_generic_to_shared(bufs));
-    uint64_t* bars = reinterpret_cast<uint64_t*>(wbase + kSlotBytes + size_t(2) * C * RV * 16);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(wbase + kSlotBytes + size_t(2) * BUFV * 16);
     uint32_t par = 0;  // TG: phase parity of the two buffers' barriers
     if constexpr (TG) {
         if (lane == 0) {
@@ -481,7 +500,7 @@ __global__ void __launch_bounds__(MAXT) agg_kernel(const AggArgs a, const __grid
                     acc[j][k] = fmul2(acc[j][k], pk(S.sc[MIXED ? hk[j][2 * k] : hv[j]],
                                                     S.sc[MIXED ? hk[j][2 * k + 1] : hv[j]]));
         }
-        const uint4* buf = bufs + size_t(sl) * C * RV;
+        const uint4* buf = bufs + size_t(sl) * BUFV;
         // Slots past cnt hold zero rows and p = 0, so groups of 4 steps run
         // without per-edge predicates.
 #pragma unroll
@@ -493,9 +512,9 @@ __global__ void __launch_bounds__(MAXT) agg_kernel(const AggArgs a, const __grid
 #pragma unroll
                 for (int j = 0; j < VPL; ++j) {
                     const int v = vl + j * LPE;
-                    if (NVC == 0 && v >= nvec) continue;
+                    if ((NVC == 0 || NVC < RV) && v >= nvec) continue;
                     float f[VEC];
-                    V::unpack(buf[tt * RV + v], f);
+                    V::unpack(buf[row_vec(tt) + v], f);
                     if constexpr (MIXED) {
 #pragma unroll
                         for (int k = 0; k < VEC / 2; ++k)
@@ -680,27 +699,39 @@ __global__ void __launch_bounds__(MAXT) agg_kernel(const AggArgs a, const __grid
         // Groups of 4 steps, as in consume: slots up to the end of the last
         // group holding an edge are written, later groups are skipped.
         if constexpr (TG) {
-            // edge g*4+j of the chunk is held by lane j*HS in colS[g]; lane q
-            // gathers edges 4q..4q+3
+            // lane q gathers edges 4q..4q+3; rows are fetched up to the end
+            // of the consumer's last granule of 4 steps (4*EPS edges), those
+            // past cnt as zeros from outside the table
             const uint32_t oob = uint32_t(a.n_src);
             uint32_t y[4] = {oob, oob, oob, oob};
+            if constexpr (HS == 1) {
+                // edge e is held by lane e in colS[0]
 #pragma unroll
-            for (int g = 0; g < NG; ++g)
-#pragma unroll
-                for (int j = 0; j < EG; ++j) {
-                    const uint32_t v = __shfl_sync(kFull, colS[g], j * HS);
-                    if (g == lane && g * EG + j < S.cnt) y[j] = v;
+                for (int j = 0; j < 4; ++j) {
+                    const int e = 4 * lane + j;
+                    const uint32_t v = __shfl_sync(kFull, colS[0], e & 31);
+                    if (e < S.cnt) y[j] = v;
                 }
-            const int ngrp = (S.cnt + 3) >> 2;
-            if (lane == 0) tc::mbar_expect_tx(bars + sl, uint32_t(ngrp) * 4u * RV * 16u);
+            } else {
+                // edge g*4+j is held by lane j*HS in colS[g]
+#pragma unroll
+                for (int g = 0; g < NG; ++g)
+#pragma unroll
+                    for (int j = 0; j < EG; ++j) {
+                        const uint32_t v = __shfl_sync(kFull, colS[g], j * HS);
+                        if (g == lane && g * EG + j < S.cnt) y[j] = v;
+                    }
+            }
+            const int ngrp = (S.cnt + 4 * EPS - 1) / (4 * EPS) * EPS;
+            if (lane == 0) tc::mbar_expect_tx(bars + sl, uint32_t(ngrp) * 4u * RP * 16u);
             __syncwarp();
             if (lane < ngrp) {
                 tc::fence_proxy_async_smem();
-                tc::tma_gather4(const_cast<uint4*>(bufs) + (size_t(sl) * C + size_t(lane) * 4) * RV, &tmh, bars + sl,
-                                0, int(y[0]), int(y[1]), int(y[2]), int(y[3]));
+                tc::tma_gather4(const_cast<uint4*>(bufs) + size_t(sl) * BUFV + size_t(lane) * (GPB / 16), &tmh,
+                                bars + sl, 0, int(y[0]), int(y[1]), int(y[2]), int(y[3]));
             }
         } else {
-            const uint32_t bs = bufs_s + uint32_t(sl) * C * RV * 16 + uint32_t(vl) * 16;
+            const uint32_t bs = bufs_s + uint32_t(sl) * BUFV * 16 + uint32_t(vl) * 16;
 #pragma unroll
             for (int i0 = 0; i0 < NT; i0 += 4) {
                 if (i0 * EPS >= S.cnt) break;
@@ -1039,6 +1070,14 @@ bool narrow_on_pairs() {
     return v;
 }
 
+bool narrow_row_gather() {
+    static const bool v = [] {
+        const char* e = std::getenv("GAT_B200_NARROW_AGG");
+        return e && std::strcmp(e, "gather4") == 0;
+    }();
+    return v;
+}
+
 // reserve_sms = 0: blocks of up to 4 warps, as many resident blocks as fit
 // on every SM. reserve_sms > 0 (the multi-GPU forward, where a projection
 // kernel on another stream runs beside the aggregation): one block per SM
@@ -1048,11 +1087,13 @@ bool narrow_on_pairs() {
 template <class HT, int KT, int C, int LPE, int VPL, bool MIXED, int NVC, bool TG = false>
 int launch_agg(const AggArgs& a, cudaStream_t st, int reserve_sms) {
     constexpr int KM = KT ? KT : 8;
-    constexpr size_t warp_bytes = agg_warp_bytes<C, KM, LPE * VPL, TG>();
+    constexpr int RP = TG ? NVC : LPE * VPL;  // 16-byte vectors per buffered row
+    constexpr size_t warp_bytes = agg_warp_bytes<C, KM, RP, TG>();
     CUtensorMap tmh;
     std::memset(&tmh, 0, sizeof(tmh));
     if constexpr (TG) {
-        int rc = make_row_gather_map(&tmh, a.h, uint64_t(a.ldh), a.n_src, uint64_t(a.ldh), 256);
+        // boxes of one row of RP vectors (8 BF16 each)
+        int rc = make_row_gather_map(&tmh, a.h, uint64_t(a.ldh), a.n_src, uint64_t(a.ldh), uint32_t(RP * 8));
         if (rc) return rc;
     }
     // Up to 4 warps per block within 200 KB of shared memory.
@@ -1199,6 +1240,19 @@ int aggregate_dispatch_reserved(const gat_b200_graph* g, int heads, int dim, con
                 if (nvh <= 2) return launch_agg_pair<2>(a, st, reserve_sms);
                 if (nvh <= 3) return launch_agg_pair<3>(a, st, reserve_sms);
                 return launch_agg_pair<4>(a, st, reserve_sms);
+            }
+            if (narrow_row_gather() && ldh >= nv * 8 && a.n_src < (1ull << 31)) {
+                // rows of nv vectors through the TMA row gather
+                switch (nv) {
+                    case 1: return launch_agg<uint16_t, 1, 32, 8, 1, false, 1, true>(a, st, reserve_sms);
+                    case 2: return launch_agg<uint16_t, 1, 32, 8, 1, false, 2, true>(a, st, reserve_sms);
+                    case 3: return launch_agg<uint16_t, 1, 32, 8, 1, false, 3, true>(a, st, reserve_sms);
+                    case 4: return launch_agg<uint16_t, 1, 32, 8, 1, false, 4, true>(a, st, reserve_sms);
+                    case 5: return launch_agg<uint16_t, 1, 32, 8, 1, false, 5, true>(a, st, reserve_sms);
+                    case 6: return launch_agg<uint16_t, 1, 32, 8, 1, false, 6, true>(a, st, reserve_sms);
+                    case 7: return launch_agg<uint16_t, 1, 32, 8, 1, false, 7, true>(a, st, reserve_sms);
+                    default: return launch_agg<uint16_t, 1, 32, 8, 1, false, 8, true>(a, st, reserve_sms);
+                }
             }
             return launch_agg<uint16_t, 1, 32, 8, 1, false, 0>(a, st, reserve_sms);
         }

@@ -1,7 +1,9 @@
 """The aggregation kernel variants that are not the default for their shape,
 selected per process by environment variable (GAT_B200_NARROW_AGG=pair: the
-lane-pair kernel for narrow single-head layers; GAT_B200_HIDDEN_AGG=gather4:
-hidden-layer rows fetched by the TMA row gather), each in a child process on
+lane-pair kernel for narrow single-head layers; GAT_B200_NARROW_AGG=gather4:
+single-head rows fetched by the TMA row gather, here 40 columns = 5 vectors
+per row; GAT_B200_HIDDEN_AGG=gather4: hidden-layer rows fetched by the TMA row
+gather), each in a child process on
 the c2 graph (hubs split into segments, wide rows, short rows): the
 three-layer BF16 forward against the R0 oracle (relative L2 <= 1e-2) and
 against the default kernels' forward (relative L2 <= 2e-3: the same math in
@@ -51,6 +53,7 @@ def reference_logits():
 
 
 @pytest.mark.parametrize("name,env", [("default", {}), ("narrow_pair", {"GAT_B200_NARROW_AGG": "pair"}),
+                                      ("narrow_gather4", {"GAT_B200_NARROW_AGG": "gather4"}),
                                       ("hidden_gather4", {"GAT_B200_HIDDEN_AGG": "gather4"})])
 def test_variant_forward(tmp_path, reference_logits, name, env):
     got = _forward(tmp_path, name, env)
