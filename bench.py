@@ -709,13 +709,15 @@ def main():
     # roofline of the dominant kernel: the hidden-layer aggregation (agg_kernel,
     # launches of layers 1 and 2, the same bytes each), averaged over the timed
     # steps. Layer 3's aggregation and the projections are reported beside it.
-    # Under the multi-GPU pipeline a layer's time also holds the next layer's
-    # projection and any exchange not overlapped, so the figure is a lower
-    # bound there.
+    # Under the multi-GPU pipeline with the layer-2 input exchange, layer 1's
+    # aggregation also stores every output row to the peers, so layer 2's launch
+    # alone is the kernel's figure; with chunks > 1 a layer's time also holds the
+    # projections of its earlier chunks, and the figure is a lower bound.
     peak, peak_kind = peaks()
     b_hid = agg_bytes(n_loc, e_loc, 8, 32, 2)
     b_l3 = agg_bytes(n_loc, e_loc, 1, classes, 4)
-    if world == 1 and args.path == "adaptive":
+    x2_inputs = world > 1 and args.exchange == "p2p" and args.layer2_exchange == "inputs"
+    if (world == 1 and args.path == "adaptive") or x2_inputs:
         hid = [stage_ms["aggregate_l2"]]
     else:
         hid = [stage_ms["aggregate_l1"], stage_ms["aggregate_l2"]]
