@@ -176,6 +176,11 @@ def test_multi_gpu_c_abi_host_checks(tmp_path):
     assert ei.value.code == G.ETIMEOUT and time.time() - t0 < 10
     rc = G._lib.gat_b200_part_model_create(None, 0, None, None, None, 0, 1, None, C.byref(h))
     assert rc == G.EINVAL
+    # the model's switches refuse a null handle with a message
+    for fn, arg, what in ((G._lib.gat_b200_part_model_set_layer2_exchange, 1, b"set_layer2_exchange"),
+                          (G._lib.gat_b200_part_model_set_overlap, 0, b"set_overlap"),
+                          (G._lib.gat_b200_part_model_enable_timing, 1, b"enable_timing")):
+        assert fn(None, arg) == G.EINVAL and what in G._lib.gat_b200_last_error()
 
 
 def _rank_fails(rank, world, port, q):
