@@ -812,6 +812,13 @@ def main():
             got = np.concatenate([fh[k * n_max:k * n_max + int(part.cuts[k + 1] - part.cuts[k])]
                                   for k in range(world)])
         del full, pad
+        # every rank's stage times of its last timed step (rank balance)
+        names = list(stage_ms)
+        mine = torch.tensor([float(stage_ms[k]) for k in names], dtype=torch.float32, device="cuda")
+        allst = torch.empty(world * len(names), dtype=torch.float32, device="cuda")
+        dist.all_gather_into_tensor(allst, mine)
+        allst = allst.view(world, len(names))
+        stage_ranks = {k: [round(float(v), 4) for v in allst[:, i].tolist()] for i, k in enumerate(names)}
 
     line = None
     if rank == 0:
@@ -827,6 +834,7 @@ def main():
                        "l2": f"inputs larger than L2 (H is {n * 512 / 1e9:.2f} GB per layer)",
                        "parallelism": parallelism, "path": args.path if world == 1 else "standard"},
             "stage_ms": {k: round(float(v), 4) for k, v in stage_ms.items()},
+            **({"stage_ms_by_rank": stage_ranks} if world > 1 else {}),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
                          "kernel": "agg_kernel, hidden layers (" + ("layer 2" if len(hid) == 1 else "layers 1-2") +
